@@ -1,0 +1,82 @@
+"""ctypes binding of ``libf16env.so`` (the sm_100a kernels behind the C ABI in include/f16env.h).
+
+The library is built in-tree by ``build.py``.  There is no fallback: if the library is
+missing or cannot be loaded, importing the GPU entry points raises, so a GPU run can never
+silently take a CPU path.
+"""
+import ctypes as C
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libf16env.so"
+
+STATE_N = 101
+OBS17_N = 17
+IC_N = 12
+LAYOUT_SOA = 0
+LAYOUT_AOS = 1
+
+_P = C.c_void_p
+_I64 = C.c_int64
+
+# name -> (argtypes, restype); keep in step with include/f16env.h
+_SIGS = {
+    "f16_fdm_step": ([_P, C.c_int, _I64, _I64, _P, C.c_int, C.c_double, _P, _P], C.c_int),
+    "f16_fdm_step_bins": ([_P, C.c_int, _I64, _I64, _P, C.c_int, C.c_int, C.c_double, _P, _P], C.c_int),
+    "f16_seed_ic": ([_P, _I64, _P, C.c_int, _I64, C.c_double, _P], C.c_int),
+    "f16_probe_fp64": ([_P, _I64, C.c_int, C.POINTER(C.c_double), _P], C.c_int),
+    "f16_version": ([], C.c_char_p),
+    "f16_status_string": ([C.c_int], C.c_char_p),
+}
+
+_lib = None
+
+
+def exported_symbols():
+    return list(_SIGS)
+
+
+def load(path=None):
+    """Load (once) and return the library; raises OSError/FileNotFoundError if unavailable."""
+    global _lib
+    if _lib is None:
+        p = Path(path) if path else LIB_PATH
+        if not p.exists():
+            raise FileNotFoundError(
+                f"{p} is missing: build it with `python {HERE.name}/build.py` (no CPU fallback exists)")
+        lib = C.CDLL(str(p))
+        for name, (args, res) in _SIGS.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = lib
+    return _lib
+
+
+def check(rc, what):
+    if rc != 0:
+        msg = load().f16_status_string(int(rc)).decode()
+        raise RuntimeError(f"{what} failed: status {rc} ({msg})")
+
+
+def ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def stream_of(t):
+    """Raw handle of the torch current stream on the tensor's device."""
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def require_cuda_tensor(t, dtype, shape, label, device=None):
+    """Raise before any launch if a raw-pointer argument is not what the kernel reads
+    (same contract as the reference's _kernel_input, R/cuda_fdm/obs_reward.py:391-401)."""
+    if not torch.is_tensor(t) or t.dtype not in (dtype if isinstance(dtype, tuple) else (dtype,)):
+        raise TypeError(f"{label} requires dtype {dtype}; no implicit pointer cast")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{label} shape {tuple(t.shape)} != {tuple(shape)}")
+    if t.device.type != "cuda" or (device is not None and t.device != device):
+        raise ValueError(f"{label} must be a CUDA tensor on {device}")
+    return t

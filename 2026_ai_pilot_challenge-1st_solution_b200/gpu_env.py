@@ -1,0 +1,114 @@
+"""``GpuDogfight``: drop-in for the reference's batched F-16 physics object (cuda_fdm/gpu_env.py:25-112).
+
+Same constructor, attributes and methods (``states (nac,101)``, ``obs (nac,17)``, ``actions
+(nac,4)``, ``load_seed``, ``reset_ic``, ``step``, ``get_state``, ``get_obs``), backed by the
+AOT-built sm_100a kernel ``f16_fdm_step`` instead of an NVRTC compile.
+
+Memory layout: the state lives in a (101, nac) structure-of-arrays buffer so every column is
+read and written with coalesced accesses; ``states`` is the (nac, 101) transposed *view* of
+it, so the reference's indexing (``states[:, 0:3]``, ``torch.where(mask, rows, states)``,
+``states[idx] = rows``, ``.view(nenv, 2, 101)``) works unchanged on the same memory.
+"""
+import numpy as np
+import torch
+
+from . import _lib
+from .ic import ic_rows, seed_states
+
+STATE_N = _lib.STATE_N
+OBS_N = _lib.OBS17_N
+# obs17 columns (cuda_fdm/gpu_env.py:19-22)
+OBS = dict(eci_pos=slice(0, 3), eci_vel=slice(3, 6), euler=slice(6, 9),
+           vUVW=slice(9, 12), alpha=12, beta=13, mach=14, Vt=15, alt_asl=16)
+
+FCS_DT_ROOT = 1.0 / 120.0     # cuda_fdm/gen/fdm.cuh:23 (golden contract)
+FCS_DT_R36 = 1.0 / 60.0       # research/competition_36500 lineage (184-D env)
+
+
+class GpuDogfight:
+    """nenv one-vs-one engagements, planes_per_env aircraft each (a = ppe*e + k)."""
+
+    def __init__(self, nenv, substeps=1, planes_per_env=2, block=128, precision="fp64",
+                 max_registers="auto", fcs_dt=FCS_DT_ROOT, device="cuda"):
+        if precision != "fp64":
+            raise NotImplementedError("only precision='fp64' is implemented on the B200 path")
+        if not torch.cuda.is_available():
+            raise RuntimeError("GpuDogfight needs a CUDA device")
+        self.lib = _lib.load()
+        self.nenv = int(nenv)
+        self.ppe = int(planes_per_env)
+        self.nac = self.nenv * self.ppe
+        self.substeps = int(substeps)
+        self.block = block                 # accepted for API parity; launch shape is chosen by the library
+        self.max_registers = max_registers
+        self.precision = precision
+        self.dtype = torch.float64
+        self.fcs_dt = float(fcs_dt)
+        self.device = torch.device(device) if not isinstance(device, torch.device) else device
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.states_soa = torch.zeros(STATE_N, self.nac, dtype=torch.float64, device=self.device)
+        self.states = self.states_soa.t()              # (nac, 101) view, stride (1, nac)
+        self.obs = torch.zeros(self.nac, OBS_N, dtype=torch.float64, device=self.device)
+        self.actions = torch.zeros(self.nac, 4, dtype=torch.float64, device=self.device)
+
+    # ---- reset ----
+    def load_seed(self, seed):
+        """seed: (nac,101), (101,) broadcast, (ppe,101) per-plane, or (nenv,ppe,101)."""
+        t = torch.as_tensor(seed, dtype=torch.float64)
+        if t.ndim == 1:
+            t = t.unsqueeze(0).expand(self.nac, -1)
+        elif t.ndim == 3:
+            t = t.reshape(self.nac, STATE_N)
+        elif t.shape[0] != self.nac:
+            t = t.unsqueeze(0).expand(self.nenv, -1, -1).reshape(self.nac, STATE_N)
+        self.states.copy_(t.to(self.device))
+
+    def reset_ic(self, ic_list):
+        """ic_list: nac IC dicts (or (nenv, ppe) nested), keyword names of cuda_fdm/ic.py
+        build_seed_vector.  Seeds are built on the GPU (f16_seed_ic)."""
+        flat = []
+        for item in ic_list:
+            if isinstance(item, dict):
+                flat.append(item)
+            else:
+                flat.extend(item)
+        if len(flat) != self.nac:
+            raise ValueError(f"{len(flat)} != nac {self.nac}")
+        seed_states(ic_rows(flat), self.fcs_dt, device=self.device, out=self.states_soa)
+
+    def reset_ic_rows(self, rows):
+        """(nac, 12) IC rows (include/f16env.h F16_IC_* columns) -> seeded states, on the GPU."""
+        rows = np.asarray(rows, dtype=np.float64) if not torch.is_tensor(rows) else rows
+        if rows.shape[0] != self.nac:
+            raise ValueError(f"{rows.shape[0]} != nac {self.nac}")
+        seed_states(rows, self.fcs_dt, device=self.device, out=self.states_soa)
+
+    # ---- step ----
+    def step(self, actions, substeps=None):
+        """actions: (nac,4) or (nenv,ppe,4) [aileron, elevator, rudder, throttle].
+        Returns obs (nenv, ppe, 17), a view of self.obs."""
+        ss = self.substeps if substeps is None else int(substeps)
+        a = torch.as_tensor(actions, dtype=torch.float64, device=self.device).reshape(self.nac, 4)
+        self.actions.copy_(a)
+        _lib.check(self.lib.f16_fdm_step(_lib.ptr(self.states_soa), _lib.LAYOUT_SOA, self.nac, self.nac,
+                                         _lib.ptr(self.actions), ss, self.fcs_dt, _lib.ptr(self.obs),
+                                         _lib.stream_of(self.states_soa)), "f16_fdm_step")
+        return self.obs.view(self.nenv, self.ppe, OBS_N)
+
+    def step_bins(self, bins, num_bins=21, substeps=None, write_obs=True):
+        """Fused action mapping: bins (nac,4) uint8 -> reference action_to_env grid -> FDM."""
+        ss = self.substeps if substeps is None else int(substeps)
+        _lib.require_cuda_tensor(bins, torch.uint8, (self.nac, 4), "action bins", self.device)
+        b = bins.contiguous()
+        _lib.check(self.lib.f16_fdm_step_bins(_lib.ptr(self.states_soa), _lib.LAYOUT_SOA, self.nac, self.nac,
+                                              _lib.ptr(b), int(num_bins), ss, self.fcs_dt,
+                                              _lib.ptr(self.obs) if write_obs else None,
+                                              _lib.stream_of(self.states_soa)), "f16_fdm_step_bins")
+        return self.obs.view(self.nenv, self.ppe, OBS_N)
+
+    def get_state(self):
+        return self.states.view(self.nenv, self.ppe, STATE_N)
+
+    def get_obs(self):
+        return self.obs.view(self.nenv, self.ppe, OBS_N)

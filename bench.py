@@ -1,0 +1,345 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200-native F-16 environment hot path (one JSON line on rank 0).
+
+Workload: FDM+FCS step only, 65,536 envs x 2 F-16s per GPU,
+seeded synthetic ICs (altitude U(6,9) km, Mach U(0.6,0.9), head-on 10 km, heading offsets
+U(-30,30) deg), uniform random 4 x 21-bin actions held for 6 frames (one decision = one
+step), fp64.  value = aircraft-FDM-frames/s over all ranks (weak scaling: every rank owns
+its own 131,072 aircraft; no collective on the data path).
+
+Arms:
+  default             this repository's sm_100a kernel (f16_fdm_step)
+  --impl reference    the reference's own CPU implementation of the path (its fdm.cuh,
+                      host-compiled into oracle/_ref) on all host threads, same metric.
+"""
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+PKG = "2026_ai_pilot_challenge-1st_solution_b200"
+
+NENV = 65_536
+SUBSTEPS = 6
+FCS_DT = 1.0 / 120.0
+NUM_BINS = 21
+FLOP_PER_FRAME = 1493          # FP64 add+mul+div+sqrt per aircraft-frame (op-counting probe)
+REF_PUBLISHED = 48.0e6         # reference fdm_run fp64, RTX 3070 Ti, 262k aircraft (cuda_fdm/README.md:99)
+METRIC = "decision-steps/sec (FDM frames/s)"
+UNIT = "aircraft-FDM-frames/s"
+WORKLOAD = "configs[1]: FDM+FCS step only, 65,536 envs x 2 F-16s per GPU, 6 frames per decision, fp64"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--e2e-steps", type=int, default=100)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_gpu_index(local_rank):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# --------------------------------------------------------------------------- CPU reference
+def cpu_reference_rate(nsample_per_thread=256, min_seconds=4.0, lineage="root"):
+    """The reference's fdm.cuh (oracle/_ref) on all host threads over a bounded sample of the
+    cfg2 workload; returns (frames/s, threads, sample description, kind)."""
+    from oracle import fdm as ofdm
+    ic = importlib.import_module(PKG + ".ic")
+    kind = "reference"
+    if ofdm.ref_available(lineage):
+        lib = ofdm.ref_lib(lineage)
+        threads = int(lib.f16ref_max_threads())
+        step = lambda s, c: ofdm.ref_step(s, c, SUBSTEPS, lineage, with_obs=True, nthreads=threads)
+    else:                                      # the C restatement, one core
+        kind, threads = "port", 1
+        step = lambda s, c: ofdm.oracle_step(s, c, SUBSTEPS, FCS_DT)
+    n = max(64, min(2 * NENV, nsample_per_thread * threads))
+    rows = ic.baseline_ics(n // 2, 20260102)
+    seeds = ofdm.oracle_seed(rows, FCS_DT)
+    rng = np.random.default_rng(7)
+    import torch
+    grid = ic.action_grid(NUM_BINS).double().numpy()
+    frames, t0, reps = 0, time.perf_counter(), 0
+    s = seeds
+    while True:
+        b = rng.integers(0, NUM_BINS, (n, 4))
+        c = grid[b]
+        c[:, 3] = (0.5 * grid[b[:, 3]].astype(np.float32) + 0.5).astype(np.float64)
+        s, _ = step(s, c)
+        frames += n * SUBSTEPS
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    sample = f"{n} aircraft x {reps} decisions x {SUBSTEPS} frames of the cfg2 workload"
+    return frames / el, threads, sample, kind
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    vals, info = [], None
+    for i in range(args.warmup + args.steps):
+        v, thr, sample, kind = cpu_reference_rate(min_seconds=1.0)
+        if i >= args.warmup:
+            vals.append(v)
+            info = (thr, sample, kind)
+    val = float(np.mean(vals))
+    thr, sample, kind = info
+    line = {"metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * SUBSTEPS * 2 * NENV / val, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": val / REF_PUBLISHED, "dtype": "f64", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD, "parallelism": "host threads (OpenMP over aircraft)"},
+            "cpu_baseline": {"value": val, "unit": UNIT, "cores": thr, "kind": kind, "sample": sample},
+            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- GPU arm
+def profile_traffic():
+    """DRAM bytes per launch of f16_fdm_step from the committed ncu summary (or None)."""
+    p = ROOT / "profiles" / "fdm_step_cfg2.md"
+    if not p.exists():
+        return None
+    for ln in p.read_text().splitlines():
+        if ln.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(ln.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    _lib = importlib.import_module(PKG + "._lib")
+    ge = importlib.import_module(PKG + ".gpu_env")
+    ic = importlib.import_module(PKG + ".ic")
+    L = _lib.load()
+    nac = 2 * NENV
+    K, W = args.steps, max(3, args.warmup)
+
+    sim = ge.GpuDogfight(NENV, substeps=SUBSTEPS, fcs_dt=FCS_DT, device=dev)
+    sim.reset_ic_rows(ic.baseline_ics(NENV, 20260102 + rank))
+    seeds = sim.states_soa.clone()
+    g = torch.Generator(device=dev)
+    g.manual_seed(20260102 + 7919 * rank)
+    grid = ic.action_grid(NUM_BINS).to(dev)
+
+    def commands(n):
+        b = torch.randint(0, NUM_BINS, (n, nac, 4), device=dev, generator=g)
+        c = grid[b]
+        c[..., 3] = 0.5 * c[..., 3] + 0.5
+        return c.double().contiguous()
+
+    cmd = commands(W + K)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)   # 256 MB > 126 MB L2
+    stream = torch.cuda.current_stream(dev)
+    sh = _lib.stream_of(sim.states_soa)
+
+    def launch(c):
+        _lib.check(L.f16_fdm_step(_lib.ptr(sim.states_soa), _lib.LAYOUT_SOA, nac, nac, _lib.ptr(c), SUBSTEPS,
+                                  FCS_DT, _lib.ptr(sim.obs), sh), "f16_fdm_step")
+
+    for i in range(W):
+        launch(cmd[i])
+    torch.cuda.synchronize(dev)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    gpu_index = physical_gpu_index(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    wall0 = time.perf_counter()
+    with ClockSampler(gpu_index) as clk:
+        for k in range(K):
+            flush.zero_()
+            starts[k].record(stream)
+            launch(cmd[W + k])
+            ends[k].record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    wall = time.perf_counter() - wall0
+    times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms_rank = float(np.mean(times))
+    ms = torch.tensor([ms_rank], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms_step = float(ms.item())
+    frames_per_step = nac * SUBSTEPS
+    value = world * frames_per_step / (ms_step * 1e-3)
+
+    # ---- e2e through the reference-facing API: host actions in, obs17 back to the host ----
+    Ke = max(1, args.e2e_steps)
+    host_cmd = cmd[W:W + Ke].cpu().pin_memory()
+    host_obs = torch.empty(nac, 17, dtype=torch.float64).pin_memory()
+    sim.states_soa.copy_(seeds)
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(Ke)]
+    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(Ke)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    for k in range(Ke):
+        flush.zero_()
+        e_starts[k].record(stream)
+        obs = sim.step(host_cmd[k])
+        host_obs.copy_(obs.view(nac, 17), non_blocking=True)
+        e_ends[k].record(stream)
+    torch.cuda.synchronize(dev)
+    e_ms = torch.tensor([float(np.mean([s.elapsed_time(e) for s, e in zip(e_starts, e_ends)]))],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = world * frames_per_step / (float(e_ms.item()) * 1e-3)
+
+    # ---- roofline: FP64 pipe, measured with the DFMA probe on this GPU ----
+    scratch = torch.zeros(148 * 8 * 256, dtype=torch.float64, device=dev)
+    import ctypes
+    flops = ctypes.c_double(0.0)
+    blocks = 148 * 8
+    for _ in range(2):
+        _lib.check(L.f16_probe_fp64(_lib.ptr(scratch), 20000, blocks, ctypes.byref(flops), _lib.stream_of(scratch)),
+                   "probe")
+    pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pe0.record(stream)
+    _lib.check(L.f16_probe_fp64(_lib.ptr(scratch), 200000, blocks, ctypes.byref(flops), _lib.stream_of(scratch)),
+               "probe")
+    pe1.record(stream)
+    torch.cuda.synchronize(dev)
+    peak_tflops = flops.value / (pe0.elapsed_time(pe1) * 1e-3) / 1e12
+    achieved_tflops = FLOP_PER_FRAME * frames_per_step / (ms_rank * 1e-3) / 1e12
+    traffic = profile_traffic()
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            v, thr, sample, kind = cpu_reference_rate()
+            cpu = {"value": v, "unit": UNIT, "cores": thr, "kind": kind, "sample": sample}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / REF_PUBLISHED, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_envs": NENV * world, "aircraft_per_gpu": nac,
+                       "frames_per_step": SUBSTEPS, "fcs_dt": FCS_DT, "parallelism": f"env-shard x{world}",
+                       "l2": "flushed between timed steps (256 MB write, outside the per-step events)",
+                       "timed_region_wall_s": wall},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": nac * 4 * 8,
+                    "d2h_bytes_per_step": nac * 17 * 8, "api": "GpuDogfight.step(host fp64 actions) -> obs17 to host",
+                    "steps": Ke},
+            "roofline": {"bound": "fp64", "achieved": achieved_tflops, "peak": peak_tflops, "unit": "TFLOP/s",
+                         "frac": achieved_tflops / peak_tflops, "traffic": traffic,
+                         "kernel": "k_fdm_step", "flop_per_unit": FLOP_PER_FRAME, "unit_basis": "aircraft-frame",
+                         "peak_source": "measured: FP64 DFMA-chain probe (f16_probe_fp64) on this GPU"},
+            "gpu_launches": K,
+            "clocks": clk.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,131 @@
+/*
+ * f16env.h -- C ABI of the B200-native F-16 parallel-environment hot path.
+ *
+ * One shared library (libf16env.so, built for sm_100a) exports these entry points.  Every
+ * pointer is a DEVICE pointer unless the name says "host"; the caller owns all buffers.
+ * Every entry point returns an f16_status (0 = OK) and never throws.  Kernels are enqueued on
+ * the given stream (NULL = legacy default stream); no entry point synchronises the host,
+ * except where stated.
+ *
+ * Aircraft / environment numbering follows the reference (cuda_fdm/gpu_env.py:1-7 and
+ * cuda_fdm/obs_reward.py:10-11): nac = 2*nenv aircraft, aircraft a = 2e (ownship) and 2e+1
+ * (opponent) belong to environment e, partner(a) = a^1.
+ */
+#ifndef F16ENV_H
+#define F16ENV_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* f16_stream_t;   /* == cudaStream_t */
+
+typedef enum {
+  F16_OK = 0,
+  F16_ERR_ARG = 1,         /* null pointer, negative/zero size, bad enum value */
+  F16_ERR_ALIGN = 2,       /* pointer not aligned as the entry point requires */
+  F16_ERR_LAUNCH = 3,      /* CUDA launch/configuration error (cudaGetLastError) */
+  F16_ERR_NONFINITE = 4,   /* a checked output was non-finite (only when checks are on) */
+  F16_ERR_CUDA = 5,        /* other CUDA runtime error */
+  F16_ERR_TOO_LARGE = 6    /* size above a documented maximum */
+} f16_status;
+
+/* ------------------------------------------------------------------------------------------
+ * FDM state layout: 101 fp64 per aircraft, in the reference's FdmState order
+ * (cuda_fdm/gen/fdm.cuh:519-528; flattening in cuda_fdm/ic.py:92-114).
+ * ---------------------------------------------------------------------------------------- */
+#define F16_STATE_N 101
+#define F16_S_POS 0          /* eci_pos[3] ft */
+#define F16_S_VEL 3          /* eci_vel[3] ft/s */
+#define F16_S_Q 6            /* attitude quaternion ECI->body [4] */
+#define F16_S_PQRI 10        /* inertial body rates [3] rad/s */
+#define F16_S_EPA 13         /* earth position angle rad */
+#define F16_S_FUEL 14        /* total fuel lb */
+#define F16_S_UVWIDOT 15     /* carried ECI acceleration [3] */
+#define F16_S_PQRIDOT 18     /* carried angular acceleration [3] */
+#define F16_S_QDOT 21        /* carried quaternion rate [4] */
+#define F16_S_DEQ_Q 25       /* integrator history, 3 x 4 (newest first) */
+#define F16_S_DEQ_PQRI 37    /* 3 x 3 */
+#define F16_S_DEQ_IVEL 46    /* 3 x 3 */
+#define F16_S_DEQ_UVWIDOT 55 /* 3 x 3 */
+#define F16_S_PREV_BACC 64   /* previous body acceleration [3] */
+#define F16_S_PREV_PQRIDOT 67
+#define F16_S_PREV_PQRI 70
+#define F16_S_PREV_AUX 73    /* alpha, mach, vc_kts, vg_fps, n_pilot_y, n_pilot_z, p, q, r */
+#define F16_S_ENG 82         /* N1, N2, N2norm, FuelFlow_pph */
+#define F16_S_KIN 86         /* kinematic actuators tef, aileron, elevator, rudder, gear, lef */
+#define F16_S_PID 92         /* roll, g-load, yaw PIDs: (input_prev, input_prev2, i_out_total) */
+
+/* obs17 columns of the reference fdm_step_batch (cuda_fdm/gen/fdm_kernel.cu:28-46) */
+#define F16_OBS17_N 17
+
+/* State storage: element (aircraft a, column c) lives at state[c*ld + a] ("SoA", ld >= nac,
+ * coalesced on the GPU) when layout == F16_LAYOUT_SOA, or at state[a*101 + c] ("AoS", the
+ * reference's (nac,101) row-major tensor) when layout == F16_LAYOUT_AOS. */
+#define F16_LAYOUT_SOA 0
+#define F16_LAYOUT_AOS 1
+
+/* ------------------------------------------------------------------------------------------
+ * (1) FDM + FCS integration.
+ * Replaces the NVRTC kernel fdm_step_batch (cuda_fdm/gen/fdm_kernel.cu:32-47) launched by
+ * GpuDogfight.step (cuda_fdm/gpu_env.py:95-106).  Runs `substeps` frames of 1/60 s per
+ * aircraft with the commands held (aileron, elevator, rudder in [-1,1], throttle in [0,1]).
+ *   state   : 101 x nac fp64, layout as above, updated in place
+ *   cmd     : nac x 4 fp64 row-major (the reference's (nac,4) actions tensor)
+ *   fcs_dt  : FCS component dt; 1/120 = cuda_fdm/gen/fdm.cuh:23, 1/60 = the 184-D lineage
+ *   obs17   : nac x 17 fp64 row-major, or NULL
+ * ---------------------------------------------------------------------------------------- */
+int f16_fdm_step(double* state, int layout, int64_t ld, int64_t nac,
+                 const double* cmd, int substeps, double fcs_dt,
+                 double* obs17, f16_stream_t stream);
+
+/* Same, with the commands given as action-bin indices (nac x 4 uint8, bins 0..num_bins-1)
+ * mapped in-kernel as the reference's action_to_env does (R/cuda_fdm/ppo_gpu.py:361-369):
+ * channel value linspace(-1,1,num_bins)[idx], throttle = 0.5*v + 0.5. */
+int f16_fdm_step_bins(double* state, int layout, int64_t ld, int64_t nac,
+                      const uint8_t* bins, int num_bins, int substeps, double fcs_dt,
+                      double* obs17, f16_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * (1b) Initial-condition seeder (replaces the CPU path cuda_fdm/ic.py:117-138 ->
+ * cuda_fdm/ref/jsb_fdm.py:142-210): builds the 101-double seed row of each aircraft from
+ * its IC, including the one throwaway force-path evaluation that seeds the integrators.
+ *   ic : nac x F16_IC_N fp64 row-major, columns below.
+ * ---------------------------------------------------------------------------------------- */
+#define F16_IC_N 12
+#define F16_IC_LAT_DEG 0
+#define F16_IC_LON_DEG 1
+#define F16_IC_ALT_FT 2
+#define F16_IC_VT_FPS 3
+#define F16_IC_PHI_DEG 4
+#define F16_IC_THETA_DEG 5
+#define F16_IC_PSI_DEG 6
+#define F16_IC_ALPHA_DEG 7
+#define F16_IC_BETA_DEG 8
+#define F16_IC_FUEL_LBS 9
+#define F16_IC_FUELFLOW_PPH 10
+#define F16_IC_GEOCENTRIC 11     /* 0 = geodetic latitude (default), 1 = geocentric */
+int f16_seed_ic(const double* ic, int64_t nac, double* state, int layout, int64_t ld,
+                double fcs_dt, f16_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Diagnostics (no counterpart in the reference): FP64 FMA-pipe probe, the measured roofline
+ * denominator of the FDM kernel.  Launches `blocks` x 256 threads running 8 independent FMA
+ * chains for `iters` iterations; *flops receives the FP64 flop count (host pointer).
+ * `scratch` must hold blocks*256 doubles (never written in practice).
+ * ---------------------------------------------------------------------------------------- */
+int f16_probe_fp64(double* scratch, int64_t iters, int blocks, double* flops, f16_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Library information.
+ * ---------------------------------------------------------------------------------------- */
+const char* f16_version(void);
+const char* f16_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* F16ENV_H */

@@ -1,0 +1,65 @@
+#!/usr/bin/env python3
+"""Build the parity checkers (TEST INFRASTRUCTURE ONLY).
+
+* ``oracle/liboracle.so``          -- our C restatement of the reference FDM (fdm_oracle.c).
+* ``oracle/_ref/libf16ref_root.so`` -- the reference's own fdm.cuh (repository root lineage,
+  FCS dt 1/120), host-compiled from where it lies under the reference tree.
+* ``oracle/_ref/libf16ref_r36.so``  -- the same for research/competition_36500/runtime
+  (FCS dt 1/60, the 184-D lineage).
+
+The ``_ref`` builds need the reference tree (``F16_REFERENCE`` or ``/root/reference``); on a
+machine without it they are skipped and the previously built files are used as they are.
+Flags follow the reference's own host validation: ``-O2 -ffp-contract=off``.
+"""
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("F16_REFERENCE", "/root/reference"))
+CFLAGS = ["-O2", "-ffp-contract=off", "-fPIC", "-shared"]
+REF_LINEAGES = {
+    "root": REF / "cuda_fdm" / "gen",
+    "r36": REF / "research" / "competition_36500" / "runtime" / "cuda_fdm" / "gen",
+}
+
+
+def _run(cmd):
+    print(" ".join(str(c) for c in cmd), flush=True)
+    subprocess.run([str(c) for c in cmd], check=True)
+
+
+def build_oracle(force=False):
+    out = HERE / "liboracle.so"
+    src = HERE / "fdm_oracle.c"
+    deps = [src, HERE.parent / "include" / "f16env.h",
+            HERE.parent / "2026_ai_pilot_challenge-1st_solution_b200" / "csrc" / "f16_tables.h"]
+    if force or not out.exists() or any(d.stat().st_mtime > out.stat().st_mtime for d in deps):
+        _run(["gcc", "-std=c99", *CFLAGS, src, "-o", out, "-lm"])
+    return out
+
+
+def build_ref(force=False):
+    outdir = HERE / "_ref"
+    outdir.mkdir(exist_ok=True)
+    built = {}
+    for name, gen in REF_LINEAGES.items():
+        out = outdir / f"libf16ref_{name}.so"
+        if (gen / "fdm.cuh").exists():
+            if force or not out.exists() or (HERE / "ref_driver.cpp").stat().st_mtime > out.stat().st_mtime:
+                _run(["g++", "-std=c++14", *CFLAGS, "-fopenmp", "-I", gen, HERE / "ref_driver.cpp",
+                      "-o", out, "-lm"])
+        if out.exists():
+            built[name] = out
+    return built
+
+
+def main():
+    force = "--force" in sys.argv
+    build_oracle(force)
+    print("reference builds:", build_ref(force))
+
+
+if __name__ == "__main__":
+    main()
