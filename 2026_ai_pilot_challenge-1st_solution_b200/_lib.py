@@ -24,7 +24,7 @@ _I64 = C.c_int64
 # name -> (argtypes, restype); keep in step with include/f16env.h
 _SIGS = {
     "f16_fdm_step": ([_P, C.c_int, _I64, _I64, _P, C.c_int, C.c_double, _P, _P], C.c_int),
-    "f16_fdm_step_bins": ([_P, C.c_int, _I64, _I64, _P, C.c_int, C.c_int, C.c_double, _P, _P], C.c_int),
+    "f16_fdm_step_bins": ([_P, C.c_int, _I64, _I64, _P, _P, C.c_int, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_seed_ic": ([_P, _I64, _P, C.c_int, _I64, C.c_double, _P], C.c_int),
     "f16_probe_fp64": ([_P, _I64, C.c_int, C.POINTER(C.c_double), _P], C.c_int),
     "f16_version": ([], C.c_char_p),

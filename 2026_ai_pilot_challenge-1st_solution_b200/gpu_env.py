@@ -51,6 +51,7 @@ class GpuDogfight:
         self.states = self.states_soa.t()              # (nac, 101) view, stride (1, nac)
         self.obs = torch.zeros(self.nac, OBS_N, dtype=torch.float64, device=self.device)
         self.actions = torch.zeros(self.nac, 4, dtype=torch.float64, device=self.device)
+        self._grid_cache = {}
 
     # ---- reset ----
     def load_seed(self, seed):
@@ -96,13 +97,23 @@ class GpuDogfight:
                                          _lib.stream_of(self.states_soa)), "f16_fdm_step")
         return self.obs.view(self.nenv, self.ppe, OBS_N)
 
-    def step_bins(self, bins, num_bins=21, substeps=None, write_obs=True):
-        """Fused action mapping: bins (nac,4) uint8 -> reference action_to_env grid -> FDM."""
+    def step_bins(self, bins, num_bins=21, substeps=None, write_obs=True, grid=None):
+        """Fused action mapping: bins (nac,4) uint8 -> reference action_to_env grid -> FDM.
+        grid: the float32 action grid (default: torch.linspace(-1, 1, num_bins) evaluated on
+        this device, as the reference trainer builds it, R/cuda_fdm/ppo_gpu.py:1134)."""
         ss = self.substeps if substeps is None else int(substeps)
         _lib.require_cuda_tensor(bins, torch.uint8, (self.nac, 4), "action bins", self.device)
         b = bins.contiguous()
+        if grid is None:
+            grid = self._grid_cache.get(num_bins)
+            if grid is None:
+                grid = torch.linspace(-1.0, 1.0, int(num_bins), device=self.device).cpu().contiguous()
+                self._grid_cache[num_bins] = grid
+        g = torch.as_tensor(grid, dtype=torch.float32).cpu().contiguous()
+        if g.numel() != num_bins:
+            raise ValueError("grid must hold num_bins values")
         _lib.check(self.lib.f16_fdm_step_bins(_lib.ptr(self.states_soa), _lib.LAYOUT_SOA, self.nac, self.nac,
-                                              _lib.ptr(b), int(num_bins), ss, self.fcs_dt,
+                                              _lib.ptr(b), _lib.ptr(g), int(num_bins), ss, self.fcs_dt,
                                               _lib.ptr(self.obs) if write_obs else None,
                                               _lib.stream_of(self.states_soa)), "f16_fdm_step_bins")
         return self.obs.view(self.nenv, self.ppe, OBS_N)

@@ -185,14 +185,16 @@ def hash_bins_np(seed, decision, nac, num_bins=21):
         return (splitmix64_np(key) % np.uint64(num_bins)).astype(np.uint8)
 
 
-def action_grid(num_bins=21):
-    """Reference action grid (R/cuda_fdm/ppo_gpu.py:178-180): float32 linspace(-1, 1, n)."""
-    return torch.linspace(-1.0, 1.0, int(num_bins))
+def action_grid(num_bins=21, device="cpu"):
+    """Reference action grid (R/cuda_fdm/ppo_gpu.py:178-180): float32 linspace(-1, 1, n) on
+    `device` (torch's CPU and CUDA linspace round some interior bins differently)."""
+    return torch.linspace(-1.0, 1.0, int(num_bins), device=device)
 
 
 def bins_to_commands(bins, num_bins=21):
-    """Reference action_to_env (R/cuda_fdm/ppo_gpu.py:361-369) on uint8/int bins -> float32 (N,4)."""
-    grid = action_grid(num_bins).to(bins.device)
+    """Reference action_to_env (R/cuda_fdm/ppo_gpu.py:361-369) on uint8/int bins -> float32 (N,4);
+    the grid is built on the bins' device, as the reference does for grid=None."""
+    grid = action_grid(num_bins, bins.device)
     cont = grid[bins.long()]
     ctrl = cont.clone()
     ctrl[:, 3] = 0.5 * cont[:, 3] + 0.5

@@ -220,7 +220,7 @@ def main():
     seeds = sim.states_soa.clone()
     g = torch.Generator(device=dev)
     g.manual_seed(20260102 + 7919 * rank)
-    grid = ic.action_grid(NUM_BINS).to(dev)
+    grid = ic.action_grid(NUM_BINS, dev)
 
     def commands(n):
         b = torch.randint(0, NUM_BINS, (n, nac, 4), device=dev, generator=g)

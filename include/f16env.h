@@ -84,10 +84,11 @@ int f16_fdm_step(double* state, int layout, int64_t ld, int64_t nac,
 
 /* Same, with the commands given as action-bin indices (nac x 4 uint8, bins 0..num_bins-1)
  * mapped in-kernel as the reference's action_to_env does (R/cuda_fdm/ppo_gpu.py:361-369):
- * channel value linspace(-1,1,num_bins)[idx], throttle = 0.5*v + 0.5. */
+ * channel value = grid_host[idx] (the caller's float32 torch.linspace(-1,1,num_bins), a HOST
+ * pointer, 2 <= num_bins <= 64), throttle = 0.5f*v + 0.5f in float32. */
 int f16_fdm_step_bins(double* state, int layout, int64_t ld, int64_t nac,
-                      const uint8_t* bins, int num_bins, int substeps, double fcs_dt,
-                      double* obs17, f16_stream_t stream);
+                      const uint8_t* bins, const float* grid_host, int num_bins, int substeps,
+                      double fcs_dt, double* obs17, f16_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
  * (1b) Initial-condition seeder (replaces the CPU path cuda_fdm/ic.py:117-138 ->

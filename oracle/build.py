@@ -32,11 +32,11 @@ def _run(cmd):
 
 def build_oracle(force=False):
     out = HERE / "liboracle.so"
-    src = HERE / "fdm_oracle.c"
-    deps = [src, HERE.parent / "include" / "f16env.h",
-            HERE.parent / "2026_ai_pilot_challenge-1st_solution_b200" / "csrc" / "f16_tables.h"]
+    srcs = [HERE / "fdm_oracle.c", HERE / "obs_oracle.c"]
+    deps = srcs + [HERE.parent / "include" / "f16env.h",
+                   HERE.parent / "2026_ai_pilot_challenge-1st_solution_b200" / "csrc" / "f16_tables.h"]
     if force or not out.exists() or any(d.stat().st_mtime > out.stat().st_mtime for d in deps):
-        _run(["gcc", "-std=c99", *CFLAGS, src, "-o", out, "-lm"])
+        _run(["gcc", "-std=c99", *CFLAGS, *srcs, "-o", out, "-lm"])
     return out
 
 

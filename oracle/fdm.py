@@ -100,3 +100,32 @@ def oracle_seed(ic_rows, fcs_dt=1.0 / 120.0):
         assert lib().oracle_seed_ic(_ptr(row), float(fcs_dt), _ptr(o)) == 0
         out[i] = o
     return out
+
+
+# Physical floor (in each column's own unit) below which a state value counts as zero for the
+# relative-error test: 1 ft, 1 ft/s, 1 ft/s^2, 1 lb, 1 kt, 1 % rpm, 1 pph for dimensional
+# columns; 1e-3 for angles, rates, quaternion components, load factors and normalised values.
+def _state_floor():
+    f = np.full(101, 1e-3)
+    f[0:6] = 1.0          # eci_pos ft, eci_vel ft/s
+    f[14] = 1.0           # fuel lb
+    f[15:18] = 1.0        # ECI acceleration ft/s^2
+    f[46:64] = 1.0        # position / acceleration integrator histories
+    f[64:67] = 1.0        # previous body acceleration ft/s^2
+    f[75] = 1.0           # vc kts
+    f[76] = 1.0           # vg ft/s
+    f[82:84] = 1.0        # N1, N2 %
+    f[85] = 1.0           # fuel flow pph
+    return f
+
+
+STATE_FLOOR = _state_floor()
+# obs17: eci_pos ft, eci_vel ft/s, euler rad, uvw ft/s, alpha, beta rad, mach, Vt ft/s, alt ft
+OBS17_FLOOR = np.array([1, 1, 1, 1, 1, 1, 1e-3, 1e-3, 1e-3, 1, 1, 1, 1e-3, 1e-3, 1e-3, 1, 1], dtype=np.float64)
+
+
+def state_rel_err(got, exp, floor=STATE_FLOOR):
+    """|got - exp| / max(|exp|, floor[column]) elementwise (the parity-tolerance metric)."""
+    got = np.asarray(got, dtype=np.float64)
+    exp = np.asarray(exp, dtype=np.float64)
+    return np.abs(got - exp) / np.maximum(np.abs(exp), floor[None, :])

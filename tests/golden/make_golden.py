@@ -91,5 +91,122 @@ def main():
     print("fdm_r36.npz", seeds16.shape)
 
 
+def obs_scenario_ics(nenv, seed):
+    """IC rows (2*nenv, 12) for the observation/reward fixtures: a third 'engaged' pairs (target
+    on the ownship's nose at 150-1300 m, inside the damage cones), a third random cfg3-like
+    pairs (+-20 km, 1-12 km altitude, 150-350 m/s, any attitude), the rest near the 1000 ft hard
+    deck (altitude exits).  Fuel 3000 lb (R/cuda_fdm/rl_env.py:327)."""
+    rng = np.random.default_rng(seed)
+    rows = np.zeros((2 * nenv, 12))
+    d2r = np.pi / 180.0
+    for e in range(nenv):
+        kind = e * 3 // nenv
+        roll, pitch, yaw = rng.uniform(-60, 60), rng.uniform(-20, 20), rng.uniform(0, 360)
+        if kind == 0:
+            n0, e0, alt = rng.uniform(-3000, 3000), rng.uniform(-3000, 3000), rng.uniform(2000, 8000)
+            fwd = np.array([np.cos(pitch * d2r) * np.cos(yaw * d2r), np.cos(pitch * d2r) * np.sin(yaw * d2r),
+                            -np.sin(pitch * d2r)])
+            dist = rng.uniform(150, 1300)
+            side = np.cross(fwd, [0, 0, 1.0])
+            side /= np.linalg.norm(side)
+            p1 = np.array([n0, e0, -alt]) + dist * fwd + side * dist * np.tan(rng.uniform(-0.8, 0.8) * d2r)
+            own = (n0, e0, -alt, roll, pitch, yaw)
+            tgt = (p1[0], p1[1], p1[2], rng.uniform(-60, 60), rng.uniform(-20, 20), rng.uniform(0, 360))
+        elif kind == 1:
+            own = (rng.uniform(-2e4, 2e4), rng.uniform(-2e4, 2e4), -rng.uniform(1000, 12000),
+                   rng.uniform(-180, 180), rng.uniform(-85, 85), rng.uniform(0, 360))
+            tgt = (rng.uniform(-2e4, 2e4), rng.uniform(-2e4, 2e4), -rng.uniform(1000, 12000),
+                   rng.uniform(-180, 180), rng.uniform(-85, 85), rng.uniform(0, 360))
+        else:
+            a0 = rng.choice([200.0, 320.0, 2000.0])
+            own = (rng.uniform(-1000, 1000), 0.0, -a0, roll, pitch, yaw)
+            tgt = (rng.uniform(-1000, 1000), 500.0, -rng.choice([200.0, 2000.0]), 0.0, 0.0, rng.uniform(0, 360))
+        for k, s in enumerate((own, tgt)):
+            lat, lon, alt_ft = ic_mod.official_seed_latlon(np.array([s[0]]), np.array([s[1]]), np.array([s[2]]))
+            r = rows[2 * e + k]
+            r[0], r[1], r[2] = lat[0], lon[0], alt_ft[0]
+            r[3] = rng.uniform(150, 350) / 0.3048
+            r[4], r[5], r[6] = s[3], s[4], s[5] % 360.0
+            r[7], r[8] = rng.uniform(-4, 8), rng.uniform(-3, 3)
+            r[9] = 3000.0
+    return rows
+
+
+def make_obs_golden(nenv=24, steps=8, seed=20260103):
+    """obs_traj.npz: the reference's torch observation / reward path
+    (R/cuda_fdm/obs_reward.py BatchObsReward(enable_kernel=False): push_actions, advance,
+    build_obs, compute_reward; termination by R/cuda_fdm/rl_env.py:481-496) over an FDM
+    trajectory (R/ lineage, FCS dt 1/60) from obs_scenario_ics, with randomised reconstruction
+    buffers (HP, fuel, time incl. 100/150 s cone tiers and the 200 s limit)."""
+    import torch
+    r36 = REF / "research" / "competition_36500" / "runtime"
+    for k in list(sys.modules):
+        if k == "cuda_fdm" or k.startswith("cuda_fdm.") or k in ("my_observation", "my_reward"):
+            del sys.modules[k]
+    sys.path.insert(0, str(r36))
+    sys.path.insert(0, str(REF / "src"))
+    from cuda_fdm import obs_reward as OR
+    from cuda_fdm.rl_env import kinematics_state, ned_from_ecef_altasl, FT2M, R2D
+    from claude_code.my_reward import MY_REWARD_CONFIG
+    from dogfight.envs.termination import time_limit_reached
+
+    rows = obs_scenario_ics(nenv, seed)
+    seeds = ofdm.oracle_seed(rows, 1.0 / 60.0)
+    rng = np.random.default_rng(seed + 1)
+    nac = 2 * nenv
+    ref = OR.BatchObsReward(nenv, device="cpu", enable_kernel=False)
+    hp0 = rng.uniform(0.2, 1.0, nac)
+    hp0[rng.choice(nac, 4, replace=False)] = 0.004          # a hit in the cone ends the match on HP
+    fuel0 = rng.uniform(0.3, 1.0, nac)
+    t0 = rng.choice([0.0, 37.3, 99.95, 120.0, 149.95, 170.0, 199.85, 199.95], nenv)
+    ref.hp.copy_(torch.as_tensor(hp0))
+    ref.fuel.copy_(torch.as_tensor(fuel0))
+    ref.t_sec.copy_(torch.as_tensor(t0))
+
+    def state9(st):
+        ecef_m, euler, vuvw, alt_ft = kinematics_state(torch.as_tensor(st))
+        n, e, d = ned_from_ecef_altasl(ecef_m, alt_ft * FT2M)
+        return torch.cat([torch.stack([n, e, d], 1), euler * R2D, vuvw * FT2M], 1)
+
+    s9 = state9(seeds)
+    ref.initialize_reward_state(s9, cfg=MY_REWARD_CONFIG)
+    init = {k: getattr(ref, k).clone().numpy() for k in ("prev_x", "prev_x_valid", "prev_alt_log")}
+    states = seeds.copy()
+    acts = np.zeros((steps, nac, 4))
+    out = {k: [] for k in ("obs", "reward", "term", "trunc", "hp", "fuel", "t_sec", "pqr", "prev_att", "dealt",
+                           "taken", "hp_loss", "prev_x", "prev_alt_log", "act_hist", "s9")}
+    for k in range(steps):
+        a = np.zeros((nac, 4))
+        a[:, 0:3] = rng.uniform(-0.4, 0.4, (nac, 3))
+        a[:, 3] = rng.uniform(0.5, 0.95, nac)
+        acts[k] = a
+        states, _ = ofdm.oracle_step(states, a, 6, 1.0 / 60.0, with_obs=False)
+        s9 = state9(states)
+        at = torch.as_tensor(a)
+        ref.push_actions(at)
+        ref.advance(s9)
+        obs = ref.build_obs(s9)
+        v = s9.view(nenv, 2, 9)
+        alt = -v[:, :, 2]
+        fin = torch.isfinite(v).all(dim=2)
+        hp = ref.hp.view(nenv, 2)
+        term = (alt < 304.8).any(1) | (hp <= 0.0).any(1) | (~fin).any(1)
+        trunc = time_limit_reached(ref.t_sec, 200.0) & (~term)
+        rew = ref.compute_reward(s9, term, cfg=MY_REWARD_CONFIG, truncated_env=trunc)
+        for key, val in (("obs", obs), ("reward", rew), ("term", term), ("trunc", trunc), ("hp", ref.hp),
+                         ("fuel", ref.fuel), ("t_sec", ref.t_sec), ("pqr", ref.pqr), ("prev_att", ref.prev_att),
+                         ("dealt", ref.last_dmg_dealt), ("taken", ref.last_dmg_taken), ("hp_loss", ref.hp_loss),
+                         ("prev_x", ref.prev_x), ("prev_alt_log", ref.prev_alt_log), ("act_hist", ref.act_hist),
+                         ("s9", s9)):
+            out[key].append(val.clone().numpy())
+    np.savez_compressed(OUT / "obs_traj.npz", ic=rows, seeds=seeds, actions=acts, hp0=hp0, fuel0=fuel0, t0=t0,
+                        init_prev_x=init["prev_x"], init_prev_x_valid=init["prev_x_valid"],
+                        init_prev_alt_log=init["prev_alt_log"],
+                        **{k: np.stack(v) for k, v in out.items()})
+    print("obs_traj.npz", nenv, steps, "terminations per step:", np.stack(out["term"]).sum(1),
+          "truncations:", np.stack(out["trunc"]).sum(1), "nonzero damage:", int((np.stack(out["dealt"]) > 0).sum()))
+
+
 if __name__ == "__main__":
     main()
+    make_obs_golden()

@@ -40,7 +40,7 @@ def test_entry_points_reject_bad_arguments_before_any_launch():
     """Null / negative-size arguments return F16_ERR_ARG without touching a device."""
     lib = pkg_module("_lib").load()
     assert lib.f16_fdm_step(None, 0, 1, 1, None, 6, 1 / 60, None, None) == 1
-    assert lib.f16_fdm_step_bins(None, 0, 1, 1, None, 21, 6, 1 / 60, None, None) == 1
+    assert lib.f16_fdm_step_bins(None, 0, 1, 1, None, None, 21, 6, 1 / 60, None, None) == 1
     buf = (ctypes.c_double * 202)()
     assert lib.f16_fdm_step(ctypes.cast(buf, ctypes.c_void_p), 0, 1, 2, None, 6, 1 / 60, None, None) == 1
     assert lib.f16_fdm_step(ctypes.cast(buf, ctypes.c_void_p), 7, 2, 2, ctypes.cast(buf, ctypes.c_void_p),
