@@ -21,8 +21,35 @@ LAYOUT_AOS = 1
 _P = C.c_void_p
 _I64 = C.c_int64
 
+
+class Recon(C.Structure):
+    """f16_recon: device pointers to the reconstruction buffers (include/f16env.h)."""
+    _fields_ = [(n, C.c_void_p) for n in ("hp", "fuel", "t_sec", "prev_att", "prev_valid", "pqr", "dmg_dealt",
+                                          "dmg_taken", "hp_loss", "act_hist", "prev_x", "prev_x_valid",
+                                          "prev_alt_log")]
+
+
+class RewardCfg(C.Structure):
+    _fields_ = [(n, C.c_double) for n in ("dt", "min_alt", "max_time", "own_damage_weight", "damage_scale",
+                                          "shaping_reward_scale", "win_reward", "loss_reward",
+                                          "timeout_win_reward", "timeout_loss_reward", "timeout_draw_reward",
+                                          "alt_hunt_coef")] + [("reward_mode", C.c_int32), ("reserved", C.c_int32)]
+
+
+class Origin(C.Structure):
+    _fields_ = [(n, C.c_double) for n in ("ox", "oy", "oz", "slat", "clat", "slon", "clon")]
+
+
+_PR = C.POINTER(Recon)
+_PC = C.POINTER(RewardCfg)
+_PO = C.POINTER(Origin)
+
 # name -> (argtypes, restype); keep in step with include/f16env.h
 _SIGS = {
+    "f16_obs_init_reward": ([_P, C.c_int, _I64, _I64, _P, _PR, _PO, _P], C.c_int),
+    "f16_obs_advance": ([_P, C.c_int, _I64, _I64, _P, _PR, _PC, _PO, _P, _P, _P, _P], C.c_int),
+    "f16_obs_build": ([_P, C.c_int, _I64, _I64, _P, _PR, _PO, _P, _P, _P], C.c_int),
+    "f16_obs_step": ([_P, C.c_int, _I64, _I64, _P, _PR, _PC, _PO, _P, _P, _P, _P, _P, _P], C.c_int),
     "f16_fdm_step": ([_P, C.c_int, _I64, _I64, _P, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_fdm_step_bins": ([_P, C.c_int, _I64, _I64, _P, _P, C.c_int, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_seed_ic": ([_P, _I64, _P, C.c_int, _I64, C.c_double, _P], C.c_int),

@@ -1,0 +1,485 @@
+// obs_device.cuh -- fused 184-D observation / final-safe reward / termination, device side.
+//
+// Semantics: the reference's fused kernels research/competition_36500/runtime/cuda_fdm/gen/
+// obs_kernel.cu (kin9 :96-145, geometry :148-330, build_obs_one :336-482, init_reward_kernel
+// :485-501, advance_kernel :504-626, build_obs_kernel :628-649).  Organisation for B200: one
+// thread per ENVIRONMENT handles both aircraft, so the two 9-DoF states are built once and
+// everything the two perspectives share is computed once:
+//   * body matrices R_o, R_p (ned2body of each aircraft) -- 2 instead of 8+ evaluations;
+//   * the line of sight u = (p - o)/|p - o| and its body projections v_o = R_o u,
+//     v_p = R_p (-u): ATA, LOS azimuth/elevation of one side and aspect of the other side are
+//     all read from these two vectors;
+//   * NED velocities, their direction frames (also the bank-angle frames) and the LOS frames.
+// Arithmetic is fp64 throughout (observations are rounded to fp32 at the store, as STORE does).
+#pragma once
+#include <stdint.h>
+#include "../../include/f16env.h"
+
+namespace f16 {
+namespace obs {
+
+constexpr double D2R = 0.017453292519943295;
+constexpr double R2D = 57.29577951308232;
+constexpr double PI2 = 6.283185307179586;
+constexpr double FT2M = 0.3048;
+constexpr double M2FT = 3.28084;
+constexpr double SLR_FT = 20925646.32546;
+constexpr double ROT = 7.292115e-5;
+constexpr double WA = 6378137.0;
+constexpr double WE2 = 0.0066943799901411;
+// observation constants (R/claude_code/my_observation.py:97-149)
+constexpr double MAX_SPEED = 600.0, MAX_RANGE_M = 2500.0, MAX_CLOSURE = 1000.0, VSPEED_SCALE = 100.0;
+constexpr double PQR_SCALE = 4.0, AOA_SCALE = 30.0, SSLIP_SCALE = 15.0, MIN_ALT_M = 304.8, ALT_DANGER = 300.0;
+constexpr double MAX_ALT_M = 15000.0, ENERGY_ADV = 5000.0, PURSUIT_ATA = 30.0, PURSUIT_RANGE = 3000.0;
+constexpr double FUEL_BURN = 8.0e-5, FUEL_REF = 300.0, REL_VEL = 600.0, GACC = 9.80665, EPISODE_MAX = 200.0;
+constexpr double TLIM_TOL = 1.0e-8;
+// damage cones (my_observation.py damage tiers)
+constexpr double MIN_DMG_R_FT = 500.0, T1_MAX = 3000.0, T2_MAX = 3500.0, T3_MAX = 4000.0;
+constexpr double T1_CONE = 1.0, T2_CONE = 2.0, T3_CONE = 3.0, T2_START = 100.0, T3_START = 150.0;
+// final-safe reward (obs_kernel.cu:48-52)
+constexpr double GEOM_BUDGET = 5.0, GEOM_REF_SEC = 200.0, SHAPING_BASE = 0.0001;
+constexpr double ALT_LOG_SCALE_M = 304.8, ALT_LOG_FLOOR = 1.0e-4;
+
+struct M3 {
+  double m[3][3];
+};
+struct V3 {
+  double x, y, z;
+};
+
+__device__ __forceinline__ double clampd(double x, double a, double b) { return x < a ? a : (x > b ? b : x); }
+__device__ __forceinline__ double nrm(const V3& v) { return sqrt(v.x * v.x + v.y * v.y + v.z * v.z); }
+__device__ __forceinline__ V3 mv(const M3& A, const V3& v) {
+  return {A.m[0][0] * v.x + A.m[0][1] * v.y + A.m[0][2] * v.z, A.m[1][0] * v.x + A.m[1][1] * v.y + A.m[1][2] * v.z,
+          A.m[2][0] * v.x + A.m[2][1] * v.y + A.m[2][2] * v.z};
+}
+__device__ __forceinline__ V3 mvT(const M3& A, const V3& v) {
+  return {A.m[0][0] * v.x + A.m[1][0] * v.y + A.m[2][0] * v.z, A.m[0][1] * v.x + A.m[1][1] * v.y + A.m[2][1] * v.z,
+          A.m[0][2] * v.x + A.m[1][2] * v.y + A.m[2][2] * v.z};
+}
+
+// R_ned_to_body = Tx(roll) Ty(pitch) Tz(yaw), angles in degrees (obs_kernel.cu:75-84)
+__device__ __forceinline__ M3 ned2body(double roll, double pitch, double yaw) {
+  double sr, cr, sp, cp, sy, cy;
+  sincos(roll * D2R, &sr, &cr);
+  sincos(pitch * D2R, &sp, &cp);
+  sincos(yaw * D2R, &sy, &cy);
+  M3 R;
+  R.m[0][0] = cp * cy; R.m[0][1] = cp * sy; R.m[0][2] = -sp;
+  R.m[1][0] = sr * sp * cy - cr * sy; R.m[1][1] = sr * sp * sy + cr * cy; R.m[1][2] = sr * cp;
+  R.m[2][0] = cr * sp * cy + sr * sy; R.m[2][1] = cr * sp * sy - sr * cy; R.m[2][2] = cr * cp;
+  return R;
+}
+
+struct Origin {
+  double ox, oy, oz, sl, cl, so, co;
+};
+
+// FDM state row -> official 9-DoF: N, E (tangent plane about the official origin, from the
+// geodetic position at MSL altitude), D = -MSL; roll/pitch/yaw deg; body u, v, w m/s.
+template <typename Row>
+__device__ __forceinline__ void kin9(const Row& st, const Origin& O, double s9[9]) {
+  double px = st(0), py = st(1), pz = st(2), vx = st(3), vy = st(4), vz = st(5);
+  double q0 = st(6), q1 = st(7), q2 = st(8), q3 = st(9), epa = st(13);
+  double se, ce;
+  sincos(epa, &se, &ce);
+  double ex = ce * px + se * py, ey = -se * px + ce * py, ez = pz;
+  double rxy = sqrt(ex * ex + ey * ey);
+  double radius = sqrt(ex * ex + ey * ey + ez * ez);
+  double sLa = ez / radius, cLa = rxy / radius, sLo = ey / rxy, cLo = ex / rxy;
+  // local NED axes in ECI: Tl2i = Tec2i * Tl2ec
+  double N0 = -cLo * sLa, N1 = -sLo * sLa, N2 = cLa;
+  double E0 = -sLo, E1 = cLo;
+  double D0 = -cLo * cLa, D1 = -sLo * cLa, D2 = -sLa;
+  double Ni0 = ce * N0 - se * N1, Ni1 = se * N0 + ce * N1;
+  double Ei0 = ce * E0 - se * E1, Ei1 = se * E0 + ce * E1;
+  double Di0 = ce * D0 - se * D1, Di1 = se * D0 + ce * D1;
+  double a0 = q0 * q0, a1 = q1 * q1, a2 = q2 * q2, a3 = q3 * q3;
+  double b01 = q0 * q1, b02 = q0 * q2, b03 = q0 * q3, b12 = q1 * q2, b13 = q1 * q3, b23 = q2 * q3;
+  double T00 = a0 + a1 - a2 - a3, T01 = 2.0 * (b12 + b03), T02 = 2.0 * (b13 - b02);
+  double T10 = 2.0 * (b12 - b03), T11 = a0 - a1 + a2 - a3, T12 = 2.0 * (b23 + b01);
+  double T20 = 2.0 * (b13 + b02), T21 = 2.0 * (b23 - b01), T22 = a0 - a1 - a2 + a3;
+  double L00 = T00 * Ni0 + T01 * Ni1 + T02 * N2;
+  double L01 = T00 * Ei0 + T01 * Ei1;
+  double L02 = T00 * Di0 + T01 * Di1 + T02 * D2;
+  double L12 = T10 * Di0 + T11 * Di1 + T12 * D2;
+  double L22 = T20 * Di0 + T21 * Di1 + T22 * D2;
+  double theta = asin(-clampd(L02, -1.0, 1.0));
+  double phi = atan2(L12, L22);
+  double psi = atan2(L01, L00);
+  if (psi < 0.0) psi += PI2;
+  double dv0 = vx + ROT * py, dv1 = vy - ROT * px, dv2 = vz;
+  double u = T00 * dv0 + T01 * dv1 + T02 * dv2;
+  double v = T10 * dv0 + T11 * dv1 + T12 * dv2;
+  double w = T20 * dv0 + T21 * dv1 + T22 * dv2;
+  double alt_m = (radius - SLR_FT) * FT2M;
+  // closed-form geodetic latitude (obs_kernel.cu:127-133), then back to ECEF at MSL altitude
+  double exm = ex * FT2M, eym = ey * FT2M, ezm = ez * FT2M;
+  const double b = WA * 0.99664718933525254;        // WA * sqrt(1 - WE2)
+  const double ep2 = (WA * WA - b * b) / (b * b);
+  double pxy = sqrt(exm * exm + eym * eym);
+  double sth, cth;
+  sincos(atan2(ezm * WA, pxy * b), &sth, &cth);
+  double lat = atan2(ezm + ep2 * b * (sth * sth * sth), pxy - WE2 * WA * (cth * cth * cth));
+  double slat, clat;
+  sincos(lat, &slat, &clat);
+  double ir = 1.0 / pxy;
+  double slon = eym * ir, clon = exm * ir;          // sin/cos of atan2(eym, exm)
+  double Nr = WA / sqrt(1.0 - WE2 * slat * slat);
+  double hx = (Nr + alt_m) * clat * clon, hy = (Nr + alt_m) * clat * slon, hz = (Nr * (1.0 - WE2) + alt_m) * slat;
+  double dx = hx - O.ox, dy = hy - O.oy, dz = hz - O.oz;
+  s9[0] = -O.sl * O.co * dx - O.sl * O.so * dy + O.cl * dz;
+  s9[1] = -O.so * dx + O.co * dy;
+  s9[2] = -alt_m;
+  s9[3] = phi * R2D;
+  s9[4] = theta * R2D;
+  s9[5] = psi * R2D;
+  s9[6] = u * FT2M;
+  s9[7] = v * FT2M;
+  s9[8] = w * FT2M;
+}
+
+// frame whose x axis is along x with roll fixed by gravity (obs_kernel.cu:179-203)
+__device__ __forceinline__ M3 dir_frame(const V3& x) {
+  M3 R;
+  double nx = nrm(x);
+  if (nx < 1e-8) {
+    R.m[0][0] = 1; R.m[0][1] = 0; R.m[0][2] = 0;
+    R.m[1][0] = 0; R.m[1][1] = 1; R.m[1][2] = 0;
+    R.m[2][0] = 0; R.m[2][1] = 0; R.m[2][2] = 1;
+    return R;
+  }
+  V3 xn = {x.x / nx, x.y / nx, x.z / nx};
+  // reference order: down (0,0,1), then north (1,0,0), then east (0,1,0)
+  V3 z = {-xn.z * xn.x, -xn.z * xn.y, 1.0 - xn.z * xn.z};
+  if (nrm(z) < 1e-6) {
+    z = {1.0 - xn.x * xn.x, -xn.x * xn.y, -xn.x * xn.z};
+    if (nrm(z) < 1e-6) z = {-xn.y * xn.x, 1.0 - xn.y * xn.y, -xn.y * xn.z};
+  }
+  double nz = nrm(z);
+  z = {z.x / nz, z.y / nz, z.z / nz};
+  V3 y = {z.y * xn.z - z.z * xn.y, z.z * xn.x - z.x * xn.z, z.x * xn.y - z.y * xn.x};
+  double ny = nrm(y);
+  y = {y.x / ny, y.y / ny, y.z / ny};
+  z = {xn.y * y.z - xn.z * y.y, xn.z * y.x - xn.x * y.z, xn.x * y.y - xn.y * y.x};
+  R.m[0][0] = xn.x; R.m[0][1] = xn.y; R.m[0][2] = xn.z;
+  R.m[1][0] = y.x; R.m[1][1] = y.y; R.m[1][2] = y.z;
+  R.m[2][0] = z.x; R.m[2][1] = z.y; R.m[2][2] = z.z;
+  return R;
+}
+
+__device__ __forceinline__ double normz(double x, double lo, double hi) {
+  double mid = (hi + lo) * 0.5, half = (hi - lo) * 0.5;
+  return (clampd(x, lo, hi) - mid) / half;
+}
+__device__ __forceinline__ double damage(double r_ft, double ata_abs, double t) {
+  double a = fabs(ata_abs);
+  if (r_ft >= MIN_DMG_R_FT && r_ft <= T1_MAX && a < T1_CONE) return 1.0 * (T1_MAX - r_ft) / (T1_MAX - MIN_DMG_R_FT);
+  if (t >= T2_START && r_ft >= MIN_DMG_R_FT && r_ft <= T2_MAX && a < T2_CONE)
+    return 0.3 * (T2_MAX - r_ft) / (T2_MAX - MIN_DMG_R_FT);
+  if (t >= T3_START && r_ft >= MIN_DMG_R_FT && r_ft <= T3_MAX && a < T3_CONE)
+    return 0.1 * (T3_MAX - r_ft) / (T3_MAX - MIN_DMG_R_FT);
+  return 0.0;
+}
+__device__ __forceinline__ double smooth3(double x, double a, double b) {
+  double z = clampd((x - a) / (b - a), 0.0, 1.0);
+  return z * z * (3.0 - 2.0 * z);
+}
+__device__ __forceinline__ V3 unit_or(const V3& v, const V3& fb) {
+  double n = nrm(v);
+  V3 s = v;
+  if (!(n >= 1e-9) || !isfinite(n)) {
+    s = fb;
+    n = nrm(fb);
+  }
+  if (!(n >= 1e-9) || !isfinite(n)) return {1.0, 0.0, 0.0};
+  return {s.x / n, s.y / n, s.z / n};
+}
+__device__ __forceinline__ double align3(const V3& a, const V3& b) {
+  V3 au = unit_or(a, {1.0, 0.0, 0.0});
+  V3 bu = unit_or(b, au);
+  double q = 0.5 * (1.0 + clampd(au.x * bu.x + au.y * bu.y + au.z * bu.z, -1.0, 1.0));
+  return clampd(q * q * q, 0.0, 1.0);
+}
+__device__ __forceinline__ double safe_lead(const V3& rel, const V3& ov, const V3& tv, const V3& fwd, double dist_m,
+                                            double dist_ft, double ata) {
+  V3 los = unit_or(rel, fwd);
+  V3 path = unit_or(ov, fwd);
+  double spd = nrm(ov);
+  if (spd < 30.0) spd = 30.0;
+  double tau = clampd(dist_m / spd, 0.30, 1.50);
+  V3 lv = {rel.x + tv.x * tau, rel.y + tv.y * tau, rel.z + tv.z * tau};
+  V3 lead = unit_or(lv, los);
+  double intercept = 0.40 * align3(fwd, lead) + 0.60 * align3(path, lead);
+  double direct = align3(fwd, los);
+  double w = smooth3(dist_ft, 1000.0, 2500.0) * smooth3(fabs(ata), 3.0, 8.0);
+  return clampd(w * intercept + (1.0 - w) * direct, 0.0, 1.0);
+}
+__device__ __forceinline__ double broad(double ata) {
+  ata = clampd(fabs(ata), 0.0, 180.0);
+  return (ata <= 30.0) ? 1.0 : clampd((180.0 - ata) / 150.0, 0.0, 1.0);
+}
+__device__ __forceinline__ double side_score(const V3& rel, const V3& ov, const V3& tv, const V3& fwd, double dist_m,
+                                             double dist_ft, double ata, double t, double rg, double cq) {
+  double lead = safe_lead(rel, ov, tv, fwd, dist_m, dist_ft, ata);
+  double gate = 1.0 - smooth3(fabs(ata), 3.0, 8.0);
+  double control = clampd(gate * rg * cq, 0.0, 1.0);
+  double fine = damage(dist_ft, fabs(ata), t);
+  return clampd(0.50 * broad(ata) + 0.20 * lead + 0.20 * control + 0.10 * fine, 0.0, 1.0);
+}
+__device__ __forceinline__ double alt_log(double alt_m) {
+  double s = alt_m / ALT_LOG_SCALE_M;
+  return log(s < ALT_LOG_FLOOR ? ALT_LOG_FLOOR : s);
+}
+__device__ __forceinline__ void log_so3(const M3& R, double inv_dt, double out[3]) {
+  double tr = R.m[0][0] + R.m[1][1] + R.m[2][2];
+  double theta = acos(clampd((tr - 1.0) * 0.5, -1.0, 1.0));
+  double den = 2.0 * sin(theta), sc = 0.0;
+  if (theta >= 1e-8 && fabs(den) >= 1e-8) sc = theta / den;
+  out[0] = (R.m[2][1] - R.m[1][2]) * sc * inv_dt;
+  out[1] = (R.m[0][2] - R.m[2][0]) * sc * inv_dt;
+  out[2] = (R.m[1][0] - R.m[0][1]) * sc * inv_dt;
+}
+__device__ __forceinline__ float store_val(double v) {
+  if (!isfinite(v)) v = (v > 0.0) ? 10.0 : ((v < 0.0) ? -10.0 : 0.0);
+  return (float)v;
+}
+
+// Everything about one engagement that both perspectives and the reward share.
+struct Pair {
+  double s[2][9];        // 9-DoF of aircraft 0 (even, "o") and 1 (odd, "p")
+  M3 R[2];               // ned2body of each
+  V3 vn[2];              // NED velocity of each
+  V3 vb[2];              // body velocity of each
+  double spd[2];         // |body velocity|
+  V3 delta;              // p - o (m)
+  double dist;           // |delta|
+  V3 los;                // delta / dist (zero if dist <= 1e-6; reference los_u)
+  V3 u;                  // delta / dist when dist > 0 (reference ata/los unit, else zero vector)
+  V3 proj[2];            // R_o u and R_p (-u): body-frame LOS of each aircraft to the other
+  double ata[2];         // ATA of each aircraft at the other (deg, 0..180)
+};
+
+__device__ __forceinline__ void make_pair(Pair& P) {
+  for (int k = 0; k < 2; k++) {
+    P.R[k] = ned2body(P.s[k][3], P.s[k][4], P.s[k][5]);
+    P.vb[k] = {P.s[k][6], P.s[k][7], P.s[k][8]};
+    P.vn[k] = mvT(P.R[k], P.vb[k]);
+    P.spd[k] = nrm(P.vb[k]);
+  }
+  P.delta = {P.s[1][0] - P.s[0][0], P.s[1][1] - P.s[0][1], P.s[1][2] - P.s[0][2]};
+  P.dist = nrm(P.delta);
+  if (P.dist > 0.0) P.u = {P.delta.x / P.dist, P.delta.y / P.dist, P.delta.z / P.dist};
+  else P.u = {0.0, 0.0, 0.0};
+  P.los = (P.dist > 1e-6) ? P.u : V3{0.0, 0.0, 0.0};
+  V3 mu = {-P.u.x, -P.u.y, -P.u.z};
+  P.proj[0] = mv(P.R[0], P.u);
+  P.proj[1] = mv(P.R[1], mu);
+  P.ata[0] = acos(clampd(P.proj[0].x, -1.0, 1.0)) * R2D;
+  P.ata[1] = acos(clampd(P.proj[1].x, -1.0, 1.0)) * R2D;
+}
+
+// Symmetric geometry advantage G = S_own - S_enemy (obs_kernel.cu:305-324), from side 0's view.
+__device__ __forceinline__ double geometry_advantage(const Pair& P, double t) {
+  double dm = P.dist, df = dm / FT2M;
+  V3 los = unit_or(P.delta, {1.0, 0.0, 0.0});
+  const V3& vo = P.vn[0];
+  const V3& vp = P.vn[1];
+  double closing = (vo.x - vp.x) * los.x + (vo.y - vp.y) * los.y + (vo.z - vp.z) * los.z;
+  double ms = 0.5 * (nrm(vo) + nrm(vp));
+  if (ms < 100.0) ms = 100.0;
+  double ratio = closing / ms;
+  double desired = 0.20 * smooth3(df, 2000.0, 4500.0) - 0.12 * (1.0 - smooth3(df, 650.0, 900.0));
+  double dq = (ratio - desired) / 0.15;
+  double cq = exp(-0.5 * dq * dq);
+  double rg = smooth3(df, 600.0, 900.0) * (1.0 - smooth3(df, 3200.0, 4300.0));
+  V3 fo = {P.R[0].m[0][0], P.R[0].m[0][1], P.R[0].m[0][2]};
+  V3 fp = {P.R[1].m[0][0], P.R[1].m[0][1], P.R[1].m[0][2]};
+  V3 mdelta = {-P.delta.x, -P.delta.y, -P.delta.z};
+  double S1 = side_score(P.delta, vo, vp, fo, dm, df, P.ata[0], t, rg, cq);
+  double S2 = side_score(mdelta, vp, vo, fp, dm, df, P.ata[1], t, rg, cq);
+  return clampd(S1 - S2, -1.0, 1.0);
+}
+
+// 16-byte staged writer of one fp32 observation row
+struct RowWriter {
+  float* out;
+  float buf[4];
+  int n;
+  __device__ __forceinline__ void put(double v) {
+    buf[n & 3] = store_val(v);
+    n++;
+    if ((n & 3) == 0) reinterpret_cast<float4*>(out)[(n >> 2) - 1] = make_float4(buf[0], buf[1], buf[2], buf[3]);
+  }
+};
+
+// per-aircraft reconstruction values needed by one perspective
+struct Side {
+  double hp, fuel, dealt, taken;
+  V3 pqr;
+  const double* act_hist;    // 20 values, newest action first
+};
+
+// One perspective's 184 features (obs_kernel.cu:336-482); k = 0 (own = even aircraft) or 1.
+// Fv[k]: dir_frame of aircraft k's NED velocity; Fl[k]: dir_frame of the LOS from aircraft k.
+__device__ __forceinline__ void obs_row(const Pair& P, int k, const Side& me, const Side& th, double t,
+                                       const M3* Fv, const M3& Fl, float* out, double* aux) {
+  const int o = k, p = 1 - k;
+  const double* so = P.s[o];
+  const double* st = P.s[p];
+  const M3& Ro = P.R[o];
+  const M3& Rt = P.R[p];
+  const V3& ovn = P.vn[o];
+  const V3& tvn = P.vn[p];
+  if (aux) {
+    const double* a[3] = {so, st, nullptr};
+    (void)a;
+    aux[0] = so[0]; aux[1] = so[1]; aux[2] = so[2];
+    aux[3] = ovn.x; aux[4] = ovn.y; aux[5] = ovn.z;
+    aux[6] = st[0]; aux[7] = st[1]; aux[8] = st[2];
+    aux[9] = tvn.x; aux[10] = tvn.y; aux[11] = tvn.z;
+    for (int i = 0; i < 3; i++)
+      for (int j = 0; j < 3; j++) aux[12 + 3 * i + j] = Ro.m[i][j];
+  }
+  double sg = (k == 0) ? 1.0 : -1.0;
+  V3 del = {sg * P.delta.x, sg * P.delta.y, sg * P.delta.z};
+  V3 los = {sg * P.los.x, sg * P.los.y, sg * P.los.z};
+  V3 rvn = {tvn.x - ovn.x, tvn.y - ovn.y, tvn.z - ovn.z};
+  double os = P.spd[o], ts = P.spd[p], oalt = -so[2], talt = -st[2];
+  double dist = P.dist;
+  double clos = 0.0;
+  if (dist > 1e-6) clos = (ovn.x - tvn.x) * los.x + (ovn.y - tvn.y) * los.y + (ovn.z - tvn.z) * los.z;
+  double ata = P.ata[o], eata = P.ata[p];
+  // aspect of own seen from the target: target-body projection of the LOS from the target
+  const V3& bt = P.proj[p];
+  double t0 = -bt.x, t1 = -bt.y, t2 = bt.z;
+  double asg = (t1 > 0.0) ? 1.0 : ((t1 < 0.0) ? -1.0 : ((t2 >= 0.0) ? 1.0 : -1.0));
+  double aa = asg * acos(clampd(t0, -1.0, 1.0)) * R2D;
+  const V3& db = P.proj[o];
+  double az = atan2(db.y, db.x) * R2D;
+  double el = -asin(clampd(db.z, -1.0, 1.0)) * R2D;
+  double u = so[6], v = so[7], w = so[8], aoa = 0.0, ss = 0.0;
+  if (os >= 1.0) {
+    aoa = atan2(w, u) * R2D;
+    ss = atan2(v, sqrt(u * u + w * w)) * R2D;
+  }
+  double vs = -ovn.z;
+  double ea = (oalt + os * os / (2.0 * GACC)) - (talt + ts * ts / (2.0 * GACC));
+  double cone = (t >= T3_START) ? T3_CONE : ((t >= T2_START) ? T2_CONE : T1_CONE);
+  double mr = (t >= T3_START) ? T3_MAX : ((t >= T2_START) ? T2_MAX : T1_MAX);
+  double ash = 2.0 * exp(-((ata / 3.0) * (ata / 3.0))) - 1.0;
+  double amg = tanh((cone - fabs(ata)) / cone);
+  double eash = 2.0 * exp(-((eata / 3.0) * (eata / 3.0))) - 1.0;
+  double eamg = tanh((cone - fabs(eata)) / cone);
+  double rmin = MIN_DMG_R_FT * FT2M, rmax = mr * FT2M, span = rmax - rmin;
+  double rn = tanh((dist - rmin) / span), rf = tanh((rmax - dist) / span);
+  // bank about the velocity vector: body y axis (row 1 of R) in the velocity frame
+  double bank[2][2];
+  for (int q = 0; q < 2; q++) {
+    const M3& Rb = P.R[q == 0 ? o : p];
+    const M3& F = Fv[q == 0 ? o : p];
+    V3 by = {Rb.m[1][0], Rb.m[1][1], Rb.m[1][2]};
+    V3 yv = mv(F, by);
+    double mu = atan2(yv.z, yv.y);
+    sincos(mu, &bank[q][0], &bank[q][1]);
+  }
+  double pa = 1.0 - fabs(ata) / PURSUIT_ATA, pr = 1.0 - dist / PURSUIT_RANGE;
+  if (pa < 0.0) pa = 0.0;
+  if (pr < 0.0) pr = 0.0;
+  RowWriter wr{out, {0, 0, 0, 0}, 0};
+  double s_, c_;
+  wr.put(normz(os, 0.0, MAX_SPEED));
+  wr.put(normz(ts, 0.0, MAX_SPEED));
+  wr.put(tanh(aoa / AOA_SCALE));
+  wr.put(tanh(ss / SSLIP_SCALE));
+  wr.put(tanh((oalt - MIN_ALT_M) / ALT_DANGER));
+  wr.put(normz(vs, -VSPEED_SCALE, VSPEED_SCALE));
+  wr.put(normz(me.hp, 0.0, 1.0));
+  wr.put(normz(th.hp, 0.0, 1.0));
+  wr.put(me.hp - th.hp);
+  wr.put(ea / (fabs(ea) + ENERGY_ADV));
+  wr.put(normz(dist, 0.0, MAX_RANGE_M));
+  wr.put(normz(clos, -MAX_CLOSURE, MAX_CLOSURE));
+  sincos(ata * D2R, &s_, &c_); wr.put(s_); wr.put(c_);
+  sincos(aa * D2R, &s_, &c_); wr.put(s_); wr.put(c_);
+  sincos(az * D2R, &s_, &c_); wr.put(s_); wr.put(c_);
+  sincos(el * D2R, &s_, &c_); wr.put(s_); wr.put(c_);
+  wr.put(ash);
+  wr.put(amg);
+  wr.put(eash);
+  wr.put(eamg);
+  wr.put(rn);
+  wr.put(rf);
+  wr.put(normz(t, 0.0, EPISODE_MAX));
+  for (int i = 3; i < 6; i++) { sincos(so[i] * D2R, &s_, &c_); wr.put(s_); wr.put(c_); }
+  for (int i = 3; i < 6; i++) { sincos(st[i] * D2R, &s_, &c_); wr.put(s_); wr.put(c_); }
+  wr.put(bank[0][0]); wr.put(bank[0][1]);
+  wr.put(bank[1][0]); wr.put(bank[1][1]);
+  wr.put(normz(me.fuel, 0.0, 1.0));
+  wr.put(normz(th.fuel, 0.0, 1.0));
+  wr.put(clampd(2.0 * me.dealt - 1.0, -1.0, 1.0));
+  wr.put(clampd(2.0 * me.taken - 1.0, -1.0, 1.0));
+  wr.put(2.0 * (pa * pr) - 1.0);
+  wr.put(normz(oalt, 0.0, MAX_ALT_M));
+  wr.put(normz(talt, 0.0, MAX_ALT_M));
+  // 38 frame-projected vectors in VEC_LAYOUT order (obs_kernel.cu:457-464)
+  V3 oom = mvT(Ro, me.pqr), tom = mvT(Rt, th.pqr);
+  const M3& Fmy = Fv[o];
+  const M3& Fopp = Fv[p];
+  // gravity (0,0,1) in frames mybody, oppbody, myvel, oppvel, los  -> unit
+  {
+    V3 g{0.0, 0.0, 1.0};
+    const M3* F5[5] = {&Ro, &Rt, &Fmy, &Fopp, &Fl};
+    for (int f = 0; f < 5; f++) { V3 c = mv(*F5[f], g); wr.put(c.x); wr.put(c.y); wr.put(c.z); }
+  }
+  // los in frames world, mybody, oppbody, myvel, oppvel -> unit
+  {
+    wr.put(los.x); wr.put(los.y); wr.put(los.z);
+    const M3* F4[4] = {&Ro, &Rt, &Fmy, &Fopp};
+    for (int f = 0; f < 4; f++) { V3 c = mv(*F4[f], los); wr.put(c.x); wr.put(c.y); wr.put(c.z); }
+  }
+  // own_vel in world, mybody, oppbody, oppvel, los -> vel
+  {
+    const M3* F4[4] = {&Ro, &Rt, &Fopp, &Fl};
+    wr.put(normz(ovn.x, -REL_VEL, REL_VEL)); wr.put(normz(ovn.y, -REL_VEL, REL_VEL)); wr.put(normz(ovn.z, -REL_VEL, REL_VEL));
+    for (int f = 0; f < 4; f++) {
+      V3 c = mv(*F4[f], ovn);
+      wr.put(normz(c.x, -REL_VEL, REL_VEL)); wr.put(normz(c.y, -REL_VEL, REL_VEL)); wr.put(normz(c.z, -REL_VEL, REL_VEL));
+    }
+  }
+  // tgt_vel in world, mybody, oppbody, myvel, los -> vel
+  {
+    const M3* F4[4] = {&Ro, &Rt, &Fmy, &Fl};
+    wr.put(normz(tvn.x, -REL_VEL, REL_VEL)); wr.put(normz(tvn.y, -REL_VEL, REL_VEL)); wr.put(normz(tvn.z, -REL_VEL, REL_VEL));
+    for (int f = 0; f < 4; f++) {
+      V3 c = mv(*F4[f], tvn);
+      wr.put(normz(c.x, -REL_VEL, REL_VEL)); wr.put(normz(c.y, -REL_VEL, REL_VEL)); wr.put(normz(c.z, -REL_VEL, REL_VEL));
+    }
+  }
+  // rel_vel in world, mybody, oppbody, myvel, oppvel, los -> vel
+  {
+    const M3* F5[5] = {&Ro, &Rt, &Fmy, &Fopp, &Fl};
+    wr.put(normz(rvn.x, -REL_VEL, REL_VEL)); wr.put(normz(rvn.y, -REL_VEL, REL_VEL)); wr.put(normz(rvn.z, -REL_VEL, REL_VEL));
+    for (int f = 0; f < 5; f++) {
+      V3 c = mv(*F5[f], rvn);
+      wr.put(normz(c.x, -REL_VEL, REL_VEL)); wr.put(normz(c.y, -REL_VEL, REL_VEL)); wr.put(normz(c.z, -REL_VEL, REL_VEL));
+    }
+  }
+  // own_omega and tgt_omega in world, mybody, oppbody, myvel, oppvel, los -> omega
+  {
+    const M3* F5[5] = {&Ro, &Rt, &Fmy, &Fopp, &Fl};
+    const V3* W[2] = {&oom, &tom};
+    for (int q = 0; q < 2; q++) {
+      const V3& om = *W[q];
+      wr.put(tanh(om.x / PQR_SCALE)); wr.put(tanh(om.y / PQR_SCALE)); wr.put(tanh(om.z / PQR_SCALE));
+      for (int f = 0; f < 5; f++) {
+        V3 c = mv(*F5[f], om);
+        wr.put(tanh(c.x / PQR_SCALE)); wr.put(tanh(c.y / PQR_SCALE)); wr.put(tanh(c.z / PQR_SCALE));
+      }
+    }
+  }
+  for (int j = 0; j < 20; j++) wr.put(me.act_hist[j]);
+}
+
+}  // namespace obs
+}  // namespace f16

@@ -113,6 +113,79 @@ int f16_seed_ic(const double* ic, int64_t nac, double* state, int layout, int64_
                 double fcs_dt, f16_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
+ * (2) Fused 184-D observation / final-safe reward / termination.
+ * Replaces the reference's NVRTC kernels init_reward_kernel, advance_kernel and
+ * build_obs_kernel (research/competition_36500/runtime/cuda_fdm/gen/obs_kernel.cu:485,504,628)
+ * launched by BatchObsReward.kernel_init_reward_state / kernel_advance / kernel_build_obs
+ * (R/cuda_fdm/obs_reward.py:410-468).  One GPU thread per environment handles both aircraft.
+ *
+ * f16_recon holds DEVICE pointers to the reference's reconstruction buffers, in its layout
+ * (obs_reward.py:338-353): per aircraft (nac = 2*nenv) hp, fuel, dmg_dealt, dmg_taken, hp_loss,
+ * prev_x, prev_alt_log [nac] fp64; prev_att, pqr [nac][3] fp64; act_hist [nac][5][4] fp64
+ * (newest first, 16-byte aligned); prev_valid, prev_x_valid [nac] uint8 (torch.bool);
+ * per environment t_sec [nenv] fp64.
+ * ---------------------------------------------------------------------------------------- */
+typedef struct {
+  double* hp;
+  double* fuel;
+  double* t_sec;
+  double* prev_att;
+  uint8_t* prev_valid;
+  double* pqr;
+  double* dmg_dealt;
+  double* dmg_taken;
+  double* hp_loss;
+  double* act_hist;
+  double* prev_x;
+  uint8_t* prev_x_valid;
+  double* prev_alt_log;
+} f16_recon;
+
+/* kernel_advance arguments (obs_reward.py:410-438; MY_REWARD_CONFIG, my_reward.py:45-104) */
+typedef struct {
+  double dt;                    /* RL step, 0.1 s */
+  double min_alt;               /* hard deck, m (304.8) */
+  double max_time;              /* episode limit, s (200) */
+  double own_damage_weight;
+  double damage_scale;
+  double shaping_reward_scale;
+  double win_reward, loss_reward;
+  double timeout_win_reward, timeout_loss_reward, timeout_draw_reward;
+  double alt_hunt_coef;
+  int32_t reward_mode;          /* 0 standard, 1 altitude hunt, 2 attack, 3 defense */
+  int32_t reserved;
+} f16_reward_cfg;
+
+/* official N/E origin (ECEF m of BaseLat/BaseLon and its sin/cos; obs_reward.py:376-383) */
+typedef struct {
+  double ox, oy, oz, slat, clat, slon, clon;
+} f16_origin;
+
+/* init_reward_kernel: geometry / log-altitude trackers of the masked environments (mask NULL =
+ * all). */
+int f16_obs_init_reward(const double* state, int layout, int64_t ld, int64_t nenv,
+                        const uint8_t* env_mask, const f16_recon* recon, const f16_origin* origin,
+                        f16_stream_t stream);
+
+/* advance_kernel: action-history push, damage/HP, fuel, SO(3) body rates, time, termination
+ * (term/trunc [nenv] uint8) and reward [nac] fp64. actions [nac][4] fp64, 16-byte aligned. */
+int f16_obs_advance(const double* state, int layout, int64_t ld, int64_t nenv, const double* actions,
+                    const f16_recon* recon, const f16_reward_cfg* cfg, const f16_origin* origin,
+                    double* reward, uint8_t* term, uint8_t* trunc_, f16_stream_t stream);
+
+/* build_obs_kernel: obs [nac][184] fp32 (16-byte aligned) of the masked environments (NULL =
+ * all; unmasked rows are left untouched), aux [nenv][21] fp64 future-position features or NULL. */
+int f16_obs_build(const double* state, int layout, int64_t ld, int64_t nenv, const uint8_t* env_mask,
+                  const f16_recon* recon, const f16_origin* origin, float* obs, double* aux,
+                  f16_stream_t stream);
+
+/* advance + build_obs of every environment in one launch (each FDM row read once). */
+int f16_obs_step(const double* state, int layout, int64_t ld, int64_t nenv, const double* actions,
+                 const f16_recon* recon, const f16_reward_cfg* cfg, const f16_origin* origin,
+                 double* reward, uint8_t* term, uint8_t* trunc_, float* obs, double* aux,
+                 f16_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
  * Diagnostics (no counterpart in the reference): FP64 FMA-pipe probe, the measured roofline
  * denominator of the FDM kernel.  Launches `blocks` x 256 threads running 8 independent FMA
  * chains for `iters` iterations; *flops receives the FP64 flop count (host pointer).

@@ -1,0 +1,163 @@
+"""Fused observation / reward / termination kernels vs the oracle -- needs a B200.
+
+Tolerances: observations and rewards |a - b| <= 1e-5 * max(1, |b|);
+termination / truncation flags bit-exact; HP, fuel, time, damage rates and the geometry /
+log-altitude trackers <= 1e-9 relative (the arccos of a near-aligned ATA amplifies rounding);
+body rates (SO(3) log of an attitude difference) <= 1e-9.  The states fed to both sides are the
+same FDM rows, so these compare the observation kernels alone.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, pkg_module
+from oracle import fdm as ofdm
+from oracle.obs import ObsOracle, origin7
+
+pytestmark = pytest.mark.gpu
+
+
+def within(a, b, tol):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    err = float(np.max(np.abs(a - b) / np.maximum(1.0, np.abs(b))))
+    if err > tol:
+        print(f"max scaled error {err:.3e} > {tol:.1e}")
+    return err <= tol
+
+
+@pytest.fixture(scope="module")
+def g():
+    return np.load(GOLDEN / "obs_traj.npz")
+
+
+@pytest.fixture(scope="module")
+def OR():
+    return pkg_module("obs_reward")
+
+
+def soa(states, cuda):
+    """(nac,101) numpy -> GpuDogfight-style (nac,101) view of a (101,nac) SoA tensor."""
+    return torch.as_tensor(np.ascontiguousarray(states.T)).to(cuda).t()
+
+
+def make_pair(OR, g, cuda):
+    nenv = g["seeds"].shape[0] // 2
+    b = OR.BatchObsReward(nenv, device=cuda)
+    o = ObsOracle(nenv)
+    for t, v in ((b.hp, g["hp0"]), (b.fuel, g["fuel0"]), (b.t_sec, g["t0"])):
+        t.copy_(torch.as_tensor(v))
+    o.hp[:] = g["hp0"]; o.fuel[:] = g["fuel0"]; o.t_sec[:] = g["t0"]
+    return nenv, b, o
+
+
+def test_origin_matches_oracle(OR):
+    o = OR.official_origin()
+    np.testing.assert_array_equal([o.ox, o.oy, o.oz, o.slat, o.clat, o.slon, o.clon], origin7())
+
+
+def test_trajectory_parity_separate_kernels(OR, g, cuda):
+    nenv, b, o = make_pair(OR, g, cuda)
+    b.kernel_init_reward_state(soa(g["seeds"], cuda))
+    o.init_reward(g["seeds"])
+    assert within(b.prev_x.cpu().numpy(), o.prev_x, 1e-9)
+    assert within(b.prev_alt_log.cpu().numpy(), o.prev_alt_log, 1e-9)
+    states = g["seeds"]
+    for k in range(g["actions"].shape[0]):
+        states, _ = ofdm.oracle_step(states, g["actions"][k], 6, 1.0 / 60.0, with_obs=False)
+        st = soa(states, cuda)
+        act = torch.as_tensor(g["actions"][k]).to(cuda)
+        rew, term, trunc = b.kernel_advance(st, act)
+        obs = b.kernel_build_obs(st)
+        er, et, etr = o.advance(states, g["actions"][k])
+        eobs = o.build_obs(states)
+        np.testing.assert_array_equal(term.cpu().numpy(), et)
+        np.testing.assert_array_equal(trunc.cpu().numpy(), etr)
+        assert within(rew.cpu().numpy(), er, 1e-9), f"step {k} reward"
+        assert within(obs.cpu().numpy(), eobs, 1e-5), f"step {k} obs vs oracle"
+        assert within(obs.cpu().numpy(), g["obs"][k], 1e-5), f"step {k} obs vs reference torch path"
+        assert within(rew.cpu().numpy(), g["reward"][k], 1e-5), f"step {k} reward vs reference torch path"
+        for name, mine, exp in (("hp", b.hp, o.hp), ("fuel", b.fuel, o.fuel), ("t_sec", b.t_sec, o.t_sec),
+                                ("dealt", b.last_dmg_dealt, o.last_dmg_dealt), ("hp_loss", b.hp_loss, o.hp_loss),
+                                ("prev_x", b.prev_x, o.prev_x), ("prev_alt_log", b.prev_alt_log, o.prev_alt_log)):
+            assert within(mine.cpu().numpy(), exp, 1e-9), f"step {k} {name}"
+        assert within(b.pqr.cpu().numpy(), o.pqr, 1e-9), f"step {k} pqr"
+        np.testing.assert_array_equal(b.act_hist.cpu().numpy(), o.act_hist)
+        np.testing.assert_array_equal(b.prev_valid.cpu().numpy(), o.prev_valid.astype(bool))
+
+
+def test_fused_step_matches_separate(OR, g, cuda):
+    nenv, a, _ = make_pair(OR, g, cuda)
+    _, b, _ = make_pair(OR, g, cuda)
+    st0 = soa(g["seeds"], cuda)
+    a.kernel_init_reward_state(st0)
+    b.kernel_init_reward_state(st0)
+    states = g["seeds"]
+    for k in range(3):
+        states, _ = ofdm.oracle_step(states, g["actions"][k], 6, 1.0 / 60.0, with_obs=False)
+        st = soa(states, cuda)
+        act = torch.as_tensor(g["actions"][k]).to(cuda)
+        ra, ta, tra = a.kernel_advance(st, act)
+        oa = a.kernel_build_obs(st).clone()
+        ob, rb, tb, trb = b.kernel_step(st, act)
+        assert within(ob.cpu().numpy(), oa.cpu().numpy(), 1e-6)
+        assert within(rb.cpu().numpy(), ra.cpu().numpy(), 1e-12)
+        assert torch.equal(ta, tb) and torch.equal(tra, trb)
+
+
+def test_masked_build_and_aos_layout(OR, g, cuda):
+    nenv, b, o = make_pair(OR, g, cuda)
+    st_soa = soa(g["seeds"], cuda)
+    st_aos = torch.as_tensor(g["seeds"]).to(cuda).contiguous()
+    full = b.kernel_build_obs(st_aos).clone()
+    b.obs_buf.fill_(7.0)
+    mask = torch.zeros(nenv, dtype=torch.bool, device=cuda)
+    mask[::3] = True
+    part = b.kernel_build_obs(st_soa, mask).clone()
+    rows = mask.repeat_interleave(2)
+    assert within(part[rows].cpu().numpy(), full[rows].cpu().numpy(), 1e-6)
+    assert bool((part[~rows] == 7.0).all())
+
+
+def test_aux_features(OR, g, cuda):
+    nenv, b, o = make_pair(OR, g, cuda)
+    b.enable_aux_capture()
+    b.kernel_build_obs(soa(g["seeds"], cuda))
+    _, eaux = o.build_obs(g["seeds"], aux=True)
+    assert within(b.aux_features.cpu().numpy(), eaux, 1e-9)
+
+
+def test_large_random_batch_vs_oracle(OR, cuda):
+    """cfg3-style random pairs at 4,096 envs: fused step vs oracle advance + build."""
+    ic = pkg_module("ic")
+    rng = np.random.default_rng(5)
+    nenv = 4096
+    rows = np.zeros((2 * nenv, 12))
+    lat, lon, alt_ft = ic.official_seed_latlon(rng.uniform(-2e4, 2e4, 2 * nenv), rng.uniform(-2e4, 2e4, 2 * nenv),
+                                               -rng.uniform(1000, 12000, 2 * nenv))
+    rows[:, 0], rows[:, 1], rows[:, 2] = lat, lon, alt_ft
+    rows[:, 3] = rng.uniform(150, 350, 2 * nenv) / 0.3048
+    rows[:, 4] = rng.uniform(-180, 180, 2 * nenv)
+    rows[:, 5] = rng.uniform(-85, 85, 2 * nenv)
+    rows[:, 6] = rng.uniform(0, 360, 2 * nenv)
+    rows[:, 7] = rng.uniform(-5, 10, 2 * nenv)
+    rows[:, 9] = 3000.0
+    states = ofdm.oracle_seed(rows, 1.0 / 60.0)
+    b = OR.BatchObsReward(nenv, device=cuda)
+    o = ObsOracle(nenv)
+    hp = rng.uniform(0.0, 1.0, 2 * nenv)
+    t = rng.uniform(0, 200, nenv)
+    pqr = rng.normal(0, 0.3, (2 * nenv, 3))
+    b.hp.copy_(torch.as_tensor(hp)); o.hp[:] = hp
+    b.t_sec.copy_(torch.as_tensor(t)); o.t_sec[:] = t
+    b.prev_att.copy_(torch.as_tensor(rows[:, 4:7])); o.prev_att[:] = rows[:, 4:7]
+    b.prev_valid.fill_(True); o.prev_valid[:] = 1
+    act = rng.uniform(-1, 1, (2 * nenv, 4))
+    obs, rew, term, trunc = b.kernel_step(soa(states, cuda), torch.as_tensor(act).to(cuda))
+    er, et, etr = o.advance(states, act)
+    eobs = o.build_obs(states)
+    np.testing.assert_array_equal(term.cpu().numpy(), et)
+    np.testing.assert_array_equal(trunc.cpu().numpy(), etr)
+    assert within(rew.cpu().numpy(), er, 1e-9)
+    assert within(obs.cpu().numpy(), eobs, 1e-5)
+    del pqr
