@@ -59,11 +59,15 @@ __device__ __forceinline__ V3 mvT(const M3& A, const V3& v) {
 }
 
 // R_ned_to_body = Tx(roll) Ty(pitch) Tz(yaw), angles in degrees (obs_kernel.cu:75-84)
-__device__ __forceinline__ M3 ned2body(double roll, double pitch, double yaw) {
+// sc (optional) receives sin/cos of roll, pitch, yaw -- the attitude observation features.
+__device__ __forceinline__ M3 ned2body(double roll, double pitch, double yaw, double* sc = nullptr) {
   double sr, cr, sp, cp, sy, cy;
   sincos(roll * D2R, &sr, &cr);
   sincos(pitch * D2R, &sp, &cp);
   sincos(yaw * D2R, &sy, &cy);
+  if (sc) {
+    sc[0] = sr; sc[1] = cr; sc[2] = sp; sc[3] = cp; sc[4] = sy; sc[5] = cy;
+  }
   M3 R;
   R.m[0][0] = cp * cy; R.m[0][1] = cp * sy; R.m[0][2] = -sp;
   R.m[1][0] = sr * sp * cy - cr * sy; R.m[1][1] = sr * sp * sy + cr * cy; R.m[1][2] = sr * cp;
@@ -249,6 +253,7 @@ __device__ __forceinline__ float store_val(double v) {
 struct Pair {
   double s[2][9];        // 9-DoF of aircraft 0 (even, "o") and 1 (odd, "p")
   M3 R[2];               // ned2body of each
+  double att[2][6];      // sin/cos of roll, pitch, yaw of each (from ned2body)
   V3 vn[2];              // NED velocity of each
   V3 vb[2];              // body velocity of each
   double spd[2];         // |body velocity|
@@ -262,7 +267,7 @@ struct Pair {
 
 __device__ __forceinline__ void make_pair(Pair& P) {
   for (int k = 0; k < 2; k++) {
-    P.R[k] = ned2body(P.s[k][3], P.s[k][4], P.s[k][5]);
+    P.R[k] = ned2body(P.s[k][3], P.s[k][4], P.s[k][5], P.att[k]);
     P.vb[k] = {P.s[k][6], P.s[k][7], P.s[k][8]};
     P.vn[k] = mvT(P.R[k], P.vb[k]);
     P.spd[k] = nrm(P.vb[k]);
@@ -306,10 +311,15 @@ struct RowWriter {
   float* out;
   float buf[4];
   int n;
-  __device__ __forceinline__ void put(double v) {
-    buf[n & 3] = store_val(v);
+  __device__ __forceinline__ void putf(float f) {
+    if (!isfinite(f)) f = (f > 0.0f) ? 10.0f : ((f < 0.0f) ? -10.0f : 0.0f);
+    buf[n & 3] = f;
     n++;
     if ((n & 3) == 0) reinterpret_cast<float4*>(out)[(n >> 2) - 1] = make_float4(buf[0], buf[1], buf[2], buf[3]);
+  }
+  __device__ __forceinline__ void put(double v) {
+    if (!isfinite(v)) v = (v > 0.0) ? 10.0 : ((v < 0.0) ? -10.0 : 0.0);
+    putf((float)v);
   }
 };
 
@@ -332,8 +342,6 @@ __device__ __forceinline__ void obs_row(const Pair& P, int k, const Side& me, co
   const V3& ovn = P.vn[o];
   const V3& tvn = P.vn[p];
   if (aux) {
-    const double* a[3] = {so, st, nullptr};
-    (void)a;
     aux[0] = so[0]; aux[1] = so[1]; aux[2] = so[2];
     aux[3] = ovn.x; aux[4] = ovn.y; aux[5] = ovn.z;
     aux[6] = st[0]; aux[7] = st[1]; aux[8] = st[2];
@@ -342,7 +350,6 @@ __device__ __forceinline__ void obs_row(const Pair& P, int k, const Side& me, co
       for (int j = 0; j < 3; j++) aux[12 + 3 * i + j] = Ro.m[i][j];
   }
   double sg = (k == 0) ? 1.0 : -1.0;
-  V3 del = {sg * P.delta.x, sg * P.delta.y, sg * P.delta.z};
   V3 los = {sg * P.los.x, sg * P.los.y, sg * P.los.z};
   V3 rvn = {tvn.x - ovn.x, tvn.y - ovn.y, tvn.z - ovn.z};
   double os = P.spd[o], ts = P.spd[p], oalt = -so[2], talt = -st[2];
@@ -350,49 +357,64 @@ __device__ __forceinline__ void obs_row(const Pair& P, int k, const Side& me, co
   double clos = 0.0;
   if (dist > 1e-6) clos = (ovn.x - tvn.x) * los.x + (ovn.y - tvn.y) * los.y + (ovn.z - tvn.z) * los.z;
   double ata = P.ata[o], eata = P.ata[p];
-  // aspect of own seen from the target: target-body projection of the LOS from the target
-  const V3& bt = P.proj[p];
-  double t0 = -bt.x, t1 = -bt.y, t2 = bt.z;
-  double asg = (t1 > 0.0) ? 1.0 : ((t1 < 0.0) ? -1.0 : ((t2 >= 0.0) ? 1.0 : -1.0));
-  double aa = asg * acos(clampd(t0, -1.0, 1.0)) * R2D;
+  // sin/cos of ATA, aspect, LOS azimuth and elevation straight from the body-frame LOS
+  // projections (the reference takes acos/atan2/asin and then sin/cos of the result):
+  //   ATA = acos(x)            -> cos = x, sin = sqrt(1 - x^2)        (ATA in [0,180])
+  //   aspect = s*acos(-x')     -> cos = -x', sin = s*sqrt(1 - x'^2)   (s: sign rule below)
+  //   az = atan2(y, x)         -> (y, x) / hypot(x, y)
+  //   el = -asin(z)            -> sin = -z, cos = sqrt(1 - z^2)
   const V3& db = P.proj[o];
-  double az = atan2(db.y, db.x) * R2D;
-  double el = -asin(clampd(db.z, -1.0, 1.0)) * R2D;
-  double u = so[6], v = so[7], w = so[8], aoa = 0.0, ss = 0.0;
+  double cx = clampd(db.x, -1.0, 1.0);
+  double s_ata = sqrt(fmax(0.0, (1.0 - cx) * (1.0 + cx))), c_ata = cx;
+  const V3& bt = P.proj[p];
+  double t0 = clampd(-bt.x, -1.0, 1.0), t1 = -bt.y, t2 = bt.z;
+  double asg = (t1 > 0.0) ? 1.0 : ((t1 < 0.0) ? -1.0 : ((t2 >= 0.0) ? 1.0 : -1.0));
+  double c_aa = t0, s_aa = asg * sqrt(fmax(0.0, (1.0 - t0) * (1.0 + t0)));
+  double hxy = sqrt(db.x * db.x + db.y * db.y);
+  double c_az = 1.0, s_az = 0.0;
+  if (hxy > 0.0) { c_az = db.x / hxy; s_az = db.y / hxy; }
+  else if (db.x < 0.0 || (db.x == 0.0 && signbit(db.x))) { c_az = -1.0; }
+  double cz = clampd(db.z, -1.0, 1.0);
+  double s_el = -cz, c_el = sqrt(fmax(0.0, (1.0 - cz) * (1.0 + cz)));
+  double u = so[6], v = so[7], w = so[8];
+  float aoa = 0.0f, ss = 0.0f;
   if (os >= 1.0) {
-    aoa = atan2(w, u) * R2D;
-    ss = atan2(v, sqrt(u * u + w * w)) * R2D;
+    aoa = atan2f((float)w, (float)u) * (float)R2D;
+    ss = atan2f((float)v, (float)sqrt(u * u + w * w)) * (float)R2D;
   }
   double vs = -ovn.z;
   double ea = (oalt + os * os / (2.0 * GACC)) - (talt + ts * ts / (2.0 * GACC));
   double cone = (t >= T3_START) ? T3_CONE : ((t >= T2_START) ? T2_CONE : T1_CONE);
   double mr = (t >= T3_START) ? T3_MAX : ((t >= T2_START) ? T2_MAX : T1_MAX);
-  double ash = 2.0 * exp(-((ata / 3.0) * (ata / 3.0))) - 1.0;
-  double amg = tanh((cone - fabs(ata)) / cone);
-  double eash = 2.0 * exp(-((eata / 3.0) * (eata / 3.0))) - 1.0;
-  double eamg = tanh((cone - fabs(eata)) / cone);
-  double rmin = MIN_DMG_R_FT * FT2M, rmax = mr * FT2M, span = rmax - rmin;
-  double rn = tanh((dist - rmin) / span), rf = tanh((rmax - dist) / span);
-  // bank about the velocity vector: body y axis (row 1 of R) in the velocity frame
+  // bounded output nonlinearities in fp32 (each feature is stored as fp32)
+  float fa = (float)(ata * (1.0 / 3.0)), fe = (float)(eata * (1.0 / 3.0));
+  float ash = 2.0f * expf(-(fa * fa)) - 1.0f;
+  float amg = tanhf((float)((cone - fabs(ata)) / cone));
+  float eash = 2.0f * expf(-(fe * fe)) - 1.0f;
+  float eamg = tanhf((float)((cone - fabs(eata)) / cone));
+  double rmin = MIN_DMG_R_FT * FT2M, rmax = mr * FT2M, ispan = 1.0 / (rmax - rmin);
+  float rn = tanhf((float)((dist - rmin) * ispan)), rf = tanhf((float)((rmax - dist) * ispan));
+  // bank about the velocity vector: mu = atan2(y.z, y.y) of the body y axis (row 1 of R) in
+  // the velocity frame; sin/cos(mu) = (y.z, y.y) / hypot
   double bank[2][2];
   for (int q = 0; q < 2; q++) {
     const M3& Rb = P.R[q == 0 ? o : p];
     const M3& F = Fv[q == 0 ? o : p];
     V3 by = {Rb.m[1][0], Rb.m[1][1], Rb.m[1][2]};
     V3 yv = mv(F, by);
-    double mu = atan2(yv.z, yv.y);
-    sincos(mu, &bank[q][0], &bank[q][1]);
+    double h = sqrt(yv.y * yv.y + yv.z * yv.z);
+    if (h > 0.0) { bank[q][0] = yv.z / h; bank[q][1] = yv.y / h; }
+    else { bank[q][0] = yv.z; bank[q][1] = signbit(yv.y) ? -1.0 : 1.0; }
   }
   double pa = 1.0 - fabs(ata) / PURSUIT_ATA, pr = 1.0 - dist / PURSUIT_RANGE;
   if (pa < 0.0) pa = 0.0;
   if (pr < 0.0) pr = 0.0;
   RowWriter wr{out, {0, 0, 0, 0}, 0};
-  double s_, c_;
   wr.put(normz(os, 0.0, MAX_SPEED));
   wr.put(normz(ts, 0.0, MAX_SPEED));
-  wr.put(tanh(aoa / AOA_SCALE));
-  wr.put(tanh(ss / SSLIP_SCALE));
-  wr.put(tanh((oalt - MIN_ALT_M) / ALT_DANGER));
+  wr.putf(tanhf(aoa * (float)(1.0 / AOA_SCALE)));
+  wr.putf(tanhf(ss * (float)(1.0 / SSLIP_SCALE)));
+  wr.putf(tanhf((float)((oalt - MIN_ALT_M) * (1.0 / ALT_DANGER))));
   wr.put(normz(vs, -VSPEED_SCALE, VSPEED_SCALE));
   wr.put(normz(me.hp, 0.0, 1.0));
   wr.put(normz(th.hp, 0.0, 1.0));
@@ -400,19 +422,19 @@ __device__ __forceinline__ void obs_row(const Pair& P, int k, const Side& me, co
   wr.put(ea / (fabs(ea) + ENERGY_ADV));
   wr.put(normz(dist, 0.0, MAX_RANGE_M));
   wr.put(normz(clos, -MAX_CLOSURE, MAX_CLOSURE));
-  sincos(ata * D2R, &s_, &c_); wr.put(s_); wr.put(c_);
-  sincos(aa * D2R, &s_, &c_); wr.put(s_); wr.put(c_);
-  sincos(az * D2R, &s_, &c_); wr.put(s_); wr.put(c_);
-  sincos(el * D2R, &s_, &c_); wr.put(s_); wr.put(c_);
-  wr.put(ash);
-  wr.put(amg);
-  wr.put(eash);
-  wr.put(eamg);
-  wr.put(rn);
-  wr.put(rf);
+  wr.put(s_ata); wr.put(c_ata);
+  wr.put(s_aa); wr.put(c_aa);
+  wr.put(s_az); wr.put(c_az);
+  wr.put(s_el); wr.put(c_el);
+  wr.putf(ash);
+  wr.putf(amg);
+  wr.putf(eash);
+  wr.putf(eamg);
+  wr.putf(rn);
+  wr.putf(rf);
   wr.put(normz(t, 0.0, EPISODE_MAX));
-  for (int i = 3; i < 6; i++) { sincos(so[i] * D2R, &s_, &c_); wr.put(s_); wr.put(c_); }
-  for (int i = 3; i < 6; i++) { sincos(st[i] * D2R, &s_, &c_); wr.put(s_); wr.put(c_); }
+  for (int i = 0; i < 6; i++) wr.put(P.att[o][i]);     // sin/cos roll, pitch, yaw (own)
+  for (int i = 0; i < 6; i++) wr.put(P.att[p][i]);     // (target)
   wr.put(bank[0][0]); wr.put(bank[0][1]);
   wr.put(bank[1][0]); wr.put(bank[1][1]);
   wr.put(normz(me.fuel, 0.0, 1.0));
@@ -469,12 +491,13 @@ __device__ __forceinline__ void obs_row(const Pair& P, int k, const Side& me, co
   {
     const M3* F5[5] = {&Ro, &Rt, &Fmy, &Fopp, &Fl};
     const V3* W[2] = {&oom, &tom};
+    const float ip = (float)(1.0 / PQR_SCALE);
     for (int q = 0; q < 2; q++) {
       const V3& om = *W[q];
-      wr.put(tanh(om.x / PQR_SCALE)); wr.put(tanh(om.y / PQR_SCALE)); wr.put(tanh(om.z / PQR_SCALE));
+      wr.putf(tanhf((float)om.x * ip)); wr.putf(tanhf((float)om.y * ip)); wr.putf(tanhf((float)om.z * ip));
       for (int f = 0; f < 5; f++) {
         V3 c = mv(*F5[f], om);
-        wr.put(tanh(c.x / PQR_SCALE)); wr.put(tanh(c.y / PQR_SCALE)); wr.put(tanh(c.z / PQR_SCALE));
+        wr.putf(tanhf((float)c.x * ip)); wr.putf(tanhf((float)c.y * ip)); wr.putf(tanhf((float)c.z * ip));
       }
     }
   }
