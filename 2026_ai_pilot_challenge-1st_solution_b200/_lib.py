@@ -50,6 +50,9 @@ _SIGS = {
     "f16_obs_advance": ([_P, C.c_int, _I64, _I64, _P, _PR, _PC, _PO, _P, _P, _P, _P], C.c_int),
     "f16_obs_build": ([_P, C.c_int, _I64, _I64, _P, _PR, _PO, _P, _P, _P], C.c_int),
     "f16_obs_step": ([_P, C.c_int, _I64, _I64, _P, _PR, _PC, _PO, _P, _P, _P, _P, _P, _P], C.c_int),
+    "f16_env_post_step": ([_P, C.c_int, _I64, _I64, _P, _PR, _PC, _PO, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P,
+                           _P, _P, _P], C.c_int),
+    "f16_state9": ([_P, C.c_int, _I64, _I64, _PO, _P, _P], C.c_int),
     "f16_fdm_step": ([_P, C.c_int, _I64, _I64, _P, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_fdm_step_bins": ([_P, C.c_int, _I64, _I64, _P, _P, C.c_int, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_seed_ic": ([_P, _I64, _P, C.c_int, _I64, C.c_double, _P], C.c_int),

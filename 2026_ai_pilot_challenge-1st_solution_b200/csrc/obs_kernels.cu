@@ -228,6 +228,91 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs_init_reward(const double* _
   rc.prev_alt_log[p] = alt_log(-P.s[1][2]);
 }
 
+// Everything GpuDogfightVecEnv.step does after the physics step (R/cuda_fdm/rl_env.py:514-551),
+// in one launch: advance, terminal observations, terminal HP / MSL altitude, and for finished
+// environments the autoreset from the IC pool (state rows, reconstruction reset, reward-tracker
+// anchoring, fresh observations).  pool: (pool_size, 2, 101) AoS rows; pick: pool row per env.
+template <int LAYOUT>
+__global__ void __launch_bounds__(OBS_THREADS) k_env_post(double* __restrict__ st, int64_t ld, int64_t nenv,
+                                                          const double* __restrict__ actions, const f16_recon rc,
+                                                          const f16_reward_cfg cfg, const f16_origin og,
+                                                          const double* __restrict__ pool, int64_t pool_size,
+                                                          const int64_t* __restrict__ pick,
+                                                          double* __restrict__ reward, uint8_t* __restrict__ term,
+                                                          uint8_t* __restrict__ trunc_, uint8_t* __restrict__ done,
+                                                          float* __restrict__ obs, float* __restrict__ terminal_obs,
+                                                          double* __restrict__ terminal_hp,
+                                                          double* __restrict__ terminal_alt, double* __restrict__ aux) {
+  int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= nenv) return;
+  Origin O = origin_of(og);
+  Pair P;
+  load_pair<LAYOUT>(st, ld, e, O, P);
+  AdvanceOut A;
+  advance_env(P, e, rc, cfg, actions, reward, term, trunc_, A);
+  const int64_t o = 2 * e, p = o + 1;
+  bool fin = term[e] || trunc_[e];
+  done[e] = fin;
+  for (int k = 0; k < 2; k++) {
+    int64_t a = o + k;
+    terminal_hp[a] = A.hp[k];
+    RowRef<LAYOUT> R{st, ld, a};
+    double x = R(0), y = R(1), z = R(2);
+    terminal_alt[a] = (sqrt(x * x + y * y + z * z) - SLR_FT) * FT2M;
+  }
+  Side sd[2];
+  for (int k = 0; k < 2; k++) sd[k] = {A.hp[k], A.fuel[k], A.dealt[k], A.taken[k], A.pqr[k], A.hist[k]};
+  if (terminal_obs) obs_env(P, e, sd, A.t, terminal_obs, nullptr);
+  if (!fin) {
+    obs_env(P, e, sd, A.t, obs, aux);
+    return;
+  }
+  // autoreset: new rows from the pool, fresh reconstruction state, anchored trackers
+  int64_t row = pick[e];
+  row = row < 0 ? 0 : (row >= pool_size ? pool_size - 1 : row);
+  const double* src = pool + row * 2 * F16_STATE_N;
+  for (int k = 0; k < 2; k++) {
+    int64_t a = o + k;
+    for (int c = 0; c < F16_STATE_N; c++) {
+      double v = src[k * F16_STATE_N + c];
+      if (LAYOUT == F16_LAYOUT_SOA) st[(int64_t)c * ld + a] = v;
+      else st[a * F16_STATE_N + c] = v;
+    }
+    rc.hp[a] = 1.0; rc.fuel[a] = 1.0;
+    rc.prev_att[a * 3] = 0.0; rc.prev_att[a * 3 + 1] = 0.0; rc.prev_att[a * 3 + 2] = 0.0;
+    rc.prev_valid[a] = 0;
+    rc.pqr[a * 3] = 0.0; rc.pqr[a * 3 + 1] = 0.0; rc.pqr[a * 3 + 2] = 0.0;
+    rc.dmg_dealt[a] = 0.0; rc.dmg_taken[a] = 0.0; rc.hp_loss[a] = 0.0;
+    double2* h = reinterpret_cast<double2*>(rc.act_hist + a * 20);
+    for (int i = 0; i < 10; i++) h[i] = make_double2(0.0, 0.0);
+    A.hist[k][0] = 0.0;
+    for (int i = 0; i < 20; i++) A.hist[k][i] = 0.0;
+  }
+  rc.t_sec[e] = 0.0;
+  Pair Q;
+  load_pair<LAYOUT>(st, ld, e, O, Q);
+  double g = geometry_advantage(Q, 0.0);
+  rc.prev_x[o] = g; rc.prev_x[p] = -g;
+  rc.prev_x_valid[o] = 1; rc.prev_x_valid[p] = 1;
+  rc.prev_alt_log[o] = alt_log(-Q.s[0][2]);
+  rc.prev_alt_log[p] = alt_log(-Q.s[1][2]);
+  Side zs[2];
+  for (int k = 0; k < 2; k++) zs[k] = {1.0, 1.0, 0.0, 0.0, {0.0, 0.0, 0.0}, A.hist[k]};
+  obs_env(Q, e, zs, 0.0, obs, aux);
+}
+
+// 9-DoF export (R/cuda_fdm/rl_env.py:558-566 state9_flat): one thread per aircraft
+template <int LAYOUT>
+__global__ void __launch_bounds__(OBS_THREADS) k_state9(const double* __restrict__ st, int64_t ld, int64_t nac,
+                                                        const f16_origin og, double* __restrict__ s9) {
+  int64_t a = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= nac) return;
+  Origin O = origin_of(og);
+  double v[9];
+  kin9(RowRef<LAYOUT>{st, ld, a}, O, v);
+  for (int i = 0; i < 9; i++) s9[a * 9 + i] = v[i];
+}
+
 inline int grid_for(int64_t n) { return (int)((n + OBS_THREADS - 1) / OBS_THREADS); }
 
 inline int check_recon(const f16_recon* rc, bool need_all) {
@@ -314,5 +399,35 @@ extern "C" int f16_obs_init_reward(const double* state, int layout, int64_t ld, 
   if (!recon || !recon->t_sec || !recon->prev_x || !recon->prev_x_valid || !recon->prev_alt_log) return F16_ERR_ARG;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   F16_DISPATCH_LAYOUT(layout, k_obs_init_reward, grid_for(nenv), state, ld, nenv, env_mask, *recon, *origin);
+  return launch_status();
+}
+
+extern "C" int f16_env_post_step(double* state, int layout, int64_t ld, int64_t nenv, const double* actions,
+                                 const f16_recon* recon, const f16_reward_cfg* cfg, const f16_origin* origin,
+                                 const double* ic_pool, int64_t pool_size, const int64_t* pick, double* reward,
+                                 uint8_t* term, uint8_t* trunc_, uint8_t* done, float* obs, float* terminal_obs,
+                                 double* terminal_hp, double* terminal_alt_m, double* aux, f16_stream_t stream) {
+  int rc = check_common(state, layout, ld, nenv, origin);
+  if (rc) return rc;
+  if ((rc = check_recon(recon, true))) return rc;
+  if (!cfg || !actions || !ic_pool || pool_size <= 0 || !pick || !reward || !term || !trunc_ || !done || !obs ||
+      !terminal_hp || !terminal_alt_m)
+    return F16_ERR_ARG;
+  if (cfg->reward_mode < 0 || cfg->reward_mode > 3) return F16_ERR_ARG;
+  if (!aligned(actions, 16) || !aligned(obs, 16) || (terminal_obs && !aligned(terminal_obs, 16))) return F16_ERR_ALIGN;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  F16_DISPATCH_LAYOUT(layout, k_env_post, grid_for(nenv), state, ld, nenv, actions, *recon, *cfg, *origin, ic_pool,
+                      pool_size, pick, reward, term, trunc_, done, obs, terminal_obs, terminal_hp, terminal_alt_m,
+                      aux);
+  return launch_status();
+}
+
+extern "C" int f16_state9(const double* state, int layout, int64_t ld, int64_t nac, const f16_origin* origin,
+                          double* s9, f16_stream_t stream) {
+  if (!state || nac <= 0 || !origin || !s9) return F16_ERR_ARG;
+  if (layout != F16_LAYOUT_SOA && layout != F16_LAYOUT_AOS) return F16_ERR_ARG;
+  if (layout == F16_LAYOUT_SOA && ld < nac) return F16_ERR_ARG;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  F16_DISPATCH_LAYOUT(layout, k_state9, grid_for(nac), state, ld, nac, *origin, s9);
   return launch_status();
 }

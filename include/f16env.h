@@ -185,6 +185,26 @@ int f16_obs_step(const double* state, int layout, int64_t ld, int64_t nenv, cons
                  double* reward, uint8_t* term, uint8_t* trunc_, float* obs, double* aux,
                  f16_stream_t stream);
 
+/* Everything GpuDogfightVecEnv.step does after the physics step (R/cuda_fdm/rl_env.py:514-551)
+ * in one launch: advance (reward [nac], term/trunc/done [nenv] uint8), terminal observations
+ * (terminal_obs [nac][184] fp32, or NULL to skip), terminal_hp / terminal_alt_m [nac] fp64
+ * (radial MSL altitude of the pre-reset state), then for every finished environment the
+ * autoreset: its two state rows are replaced by ic_pool[pick[e]] (ic_pool: [pool_size][2][101]
+ * fp64 AoS, pick: [nenv] int64), its reconstruction buffers are reset as reset_envs does, the
+ * reward trackers are re-anchored (init_reward_kernel) and obs [nac][184] receives the fresh
+ * observation; live environments get their terminal observation in obs. */
+int f16_env_post_step(double* state, int layout, int64_t ld, int64_t nenv, const double* actions,
+                      const f16_recon* recon, const f16_reward_cfg* cfg, const f16_origin* origin,
+                      const double* ic_pool, int64_t pool_size, const int64_t* pick,
+                      double* reward, uint8_t* term, uint8_t* trunc_, uint8_t* done, float* obs,
+                      float* terminal_obs, double* terminal_hp, double* terminal_alt_m, double* aux,
+                      f16_stream_t stream);
+
+/* Official 9-DoF export of every aircraft (R/cuda_fdm/rl_env.py:558-566 state9_flat):
+ * s9 [nac][9] fp64 = N, E, D m; roll, pitch, yaw deg; body u, v, w m/s. */
+int f16_state9(const double* state, int layout, int64_t ld, int64_t nac, const f16_origin* origin,
+               double* s9, f16_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------
  * Diagnostics (no counterpart in the reference): FP64 FMA-pipe probe, the measured roofline
  * denominator of the FDM kernel.  Launches `blocks` x 256 threads running 8 independent FMA

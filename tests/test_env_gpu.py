@@ -1,0 +1,131 @@
+"""GpuDogfightVecEnv on the fused post-step kernel vs the oracle composition of the reference's
+step (R/cuda_fdm/rl_env.py:499-555) -- needs a B200.
+
+The expected values are built on the CPU from the oracles exactly in the reference's order:
+physics step, advance (reward / termination), terminal observations, terminal HP and radial
+MSL altitude, then for finished environments the IC-pool gather, reset_envs, init_reward and
+the masked observation rebuild.  Tolerances as in test_obs_gpu.py.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, pkg_module
+from oracle import fdm as ofdm
+from oracle.obs import ObsOracle
+
+pytestmark = pytest.mark.gpu
+
+
+def within(a, b, tol):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    err = float(np.max(np.abs(a - b) / np.maximum(1.0, np.abs(b))))
+    if err > tol:
+        print(f"max scaled error {err:.3e} > {tol:.1e}")
+    return err <= tol
+
+
+@pytest.fixture(scope="module")
+def g():
+    return np.load(GOLDEN / "obs_traj.npz")
+
+
+@pytest.fixture(scope="module")
+def RL():
+    return pkg_module("rl_env")
+
+
+def test_env_step_matches_reference_composition(RL, g, cuda):
+    nenv = g["seeds"].shape[0] // 2
+    env = RL.GpuDogfightVecEnv(nenv, seed=3, device=cuda)
+    env._ensure_ic_pool()
+    pool = env.ic_pool.cpu().numpy()
+    env.sim.states.copy_(torch.as_tensor(g["seeds"]))
+    o = ObsOracle(nenv)
+    o.hp[:] = g["hp0"]; o.fuel[:] = g["fuel0"]; o.t_sec[:] = g["t0"]
+    env.obr.hp.copy_(torch.as_tensor(g["hp0"]))
+    env.obr.fuel.copy_(torch.as_tensor(g["fuel0"]))
+    env.obr.t_sec.copy_(torch.as_tensor(g["t0"]))
+    env.obr.kernel_init_reward_state(env.sim.states)
+    o.init_reward(g["seeds"])
+    states = g["seeds"].copy()
+    rng = np.random.default_rng(9)
+    saw_reset = False
+    for k in range(4):
+        act = g["actions"][k]
+        pick = rng.integers(0, env.ic_pool_size, nenv)
+        obs, rew, done, info = env.step(torch.as_tensor(act).to(cuda), reset_indices=torch.as_tensor(pick).to(cuda))
+        # expected, in the reference's order
+        states, _ = ofdm.oracle_step(states, act, 6, 1.0 / 60.0, with_obs=False)
+        er, et, etr = o.advance(states, act)
+        eterm_obs = o.build_obs(states)
+        edone = (et | etr).astype(bool)
+        ehp = o.hp.copy()
+        ealt = (np.linalg.norm(states[:, 0:3], axis=1) - 20925646.32546) * 0.3048
+        eobs = eterm_obs.copy()
+        if edone.any():
+            saw_reset = True
+            rows = np.repeat(edone, 2)
+            states[rows] = pool[pick[edone]].reshape(-1, 101)
+            ac = np.repeat(edone, 2)
+            for key, val in (("hp", 1.0), ("fuel", 1.0), ("last_dmg_dealt", 0.0), ("last_dmg_taken", 0.0),
+                             ("hp_loss", 0.0), ("prev_x", 0.0), ("prev_alt_log", 0.0)):
+                getattr(o, key)[ac] = val
+            o.prev_att[ac] = 0.0; o.pqr[ac] = 0.0; o.act_hist[ac] = 0.0
+            o.prev_valid[ac] = 0; o.prev_x_valid[ac] = 0
+            o.t_sec[edone] = 0.0
+            o.init_reward(states, edone.astype(np.uint8))
+            o.build_obs(states, edone.astype(np.uint8), obs=eobs)
+        np.testing.assert_array_equal(done.cpu().numpy(), edone)
+        np.testing.assert_array_equal(info["terminated"].cpu().numpy(), et.astype(bool))
+        np.testing.assert_array_equal(info["truncated"].cpu().numpy(), etr.astype(bool))
+        assert within(rew.cpu().numpy().ravel(), er, 1e-9), f"step {k} reward"
+        assert within(info["terminal_obs"].cpu().numpy().reshape(-1, 184), eterm_obs, 1e-5), f"step {k} terminal obs"
+        assert within(obs.cpu().numpy().reshape(-1, 184), eobs, 1e-5), f"step {k} obs"
+        assert within(info["terminal_hp"].cpu().numpy().ravel(), ehp, 1e-12)
+        assert within(info["terminal_alt_m"].cpu().numpy().ravel(), ealt, 1e-9)
+        err = ofdm.state_rel_err(env.sim.states.cpu().numpy(), states)
+        assert err.max() <= 1e-8, f"step {k} state err {err.max():.2e}"
+        for key in ("hp", "fuel", "t_sec", "prev_x", "prev_alt_log"):
+            assert within(getattr(env.obr, key).cpu().numpy(), getattr(o, key), 1e-9), f"step {k} {key}"
+        np.testing.assert_array_equal(env.obr.act_hist.cpu().numpy(), o.act_hist)
+        assert bool(info["terminal_state_finite"].all())
+    assert saw_reset, "fixture should trigger autoresets (truncation at t0 ~ 200 s, hard deck)"
+
+
+def test_state9_matches_oracle_kin9(RL, g, cuda):
+    nenv = g["seeds"].shape[0] // 2
+    env = RL.GpuDogfightVecEnv(nenv, device=cuda)
+    env.sim.states.copy_(torch.as_tensor(g["seeds"]))
+    s9 = env.state9_flat().cpu().numpy()
+    e9 = ObsOracle(nenv).kin9(g["seeds"])
+    assert np.abs(s9 - e9).max() < 1e-6
+
+
+def test_reset_with_stagger_and_rollout_smoke(RL, cuda):
+    env = RL.GpuDogfightVecEnv(256, seed=1, device=cuda)
+    obs = env.reset(stagger=True, max_stagger_steps=8)
+    assert obs.shape == (256, 2, 184) and bool(torch.isfinite(obs).all())
+    assert bool((env.obr.t_sec <= 0.8 + 1e-9).all())
+    s9 = env.state9()
+    alt = -s9[:, :, 2]
+    assert bool((alt > 2000 * 0.3048 - 200).all())
+    for _ in range(20):
+        a = torch.rand(256, 2, 4, device=cuda, dtype=torch.float64) * 2 - 1
+        a[..., 3] = a[..., 3].abs()
+        obs, rew, done, info = env.step(a)
+        assert bool(torch.isfinite(obs).all()) and bool(torch.isfinite(rew).all())
+        if bool(done.any()):
+            assert bool((env.obr.t_sec[done] == 0.0).all())
+
+
+def test_evaluation_bank_is_deterministic(RL, cuda):
+    env = RL.GpuDogfightVecEnv(16, seed=7, device=cuda)
+    o1 = env.reset_evaluation(paired=True).clone()
+    env2 = RL.GpuDogfightVecEnv(16, seed=7, device=cuda)
+    o2 = env2.reset_evaluation(paired=True)
+    assert torch.equal(o1, o2)
+    assert torch.equal(o1[:8], o1[8:])
+    meta = env._evaluation_seed_metadata
+    assert meta["base_count"] == 8 and sum(meta["three_nine_distance_counts"].values()) == 8
