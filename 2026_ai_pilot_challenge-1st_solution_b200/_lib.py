@@ -53,6 +53,11 @@ _SIGS = {
     "f16_env_post_step": ([_P, C.c_int, _I64, _I64, _P, _PR, _PC, _PO, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P,
                            _P, _P, _P], C.c_int),
     "f16_state9": ([_P, C.c_int, _I64, _I64, _PO, _P, _P], C.c_int),
+    "f16_gae": ([_P, _P, _P, _P, _P, C.c_int, _I64, _I64, C.c_double, C.c_double, _P, _P, _P], C.c_int),
+    "f16_norm_update": ([_P, _I64, C.c_int, _I64, _P, _P, _P, _P, _I64, _P], C.c_int),
+    "f16_norm_scratch_doubles": ([_I64, C.c_int], _I64),
+    "f16_norm_apply": ([_P, _I64, C.c_int, _I64, _P, _P, C.c_double, C.c_double, _P, _I64, _P, _I64, _P],
+                       C.c_int),
     "f16_fdm_step": ([_P, C.c_int, _I64, _I64, _P, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_fdm_step_bins": ([_P, C.c_int, _I64, _I64, _P, _P, C.c_int, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_seed_ic": ([_P, _I64, _P, C.c_int, _I64, C.c_double, _P], C.c_int),

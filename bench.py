@@ -48,6 +48,8 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--e2e-steps", type=int, default=100)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", default="fdm", choices=["fdm", "obs"],
+                   help="fdm = configs[1] headline (default); obs = configs[2] fused obs/reward kernel")
     return p.parse_args()
 
 
@@ -192,6 +194,125 @@ def profile_traffic():
     return None
 
 
+OBS_NENV = 262_144
+OBS_BYTES_PER_ENV = 2704    # declared C-ABI reads + writes of f16_obs_step per environment
+
+
+def obs_inputs(nenv, seed, dev):
+    """cfg3 synthetic state batch: NED horizontal U(+-20 km), altitude U(1,12) km, speed U(150,350)
+    m/s along the body axis with small alpha, uniformly random attitude quaternions; body-rate
+    buffers N(0,0.3) rad/s, HP/fuel U(0,1), time U(0,200) s, random action histories."""
+    import torch
+    ic = importlib.import_module(PKG + ".ic")
+    nac = 2 * nenv
+    rng = np.random.default_rng(seed)
+    rows = np.zeros((nac, 12))
+    lat, lon, alt_ft = ic.official_seed_latlon(rng.uniform(-2e4, 2e4, nac), rng.uniform(-2e4, 2e4, nac),
+                                               -rng.uniform(1000, 12000, nac))
+    rows[:, 0], rows[:, 1], rows[:, 2] = lat, lon, alt_ft
+    rows[:, 3] = rng.uniform(150, 350, nac) / 0.3048
+    q = rng.normal(size=(nac, 4))
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    w, x, y, z = q.T
+    rows[:, 4] = np.degrees(np.arctan2(2 * (w * x + y * z), 1 - 2 * (x * x + y * y)))
+    rows[:, 5] = np.degrees(np.arcsin(np.clip(2 * (w * y - z * x), -1, 1)))
+    rows[:, 6] = np.degrees(np.arctan2(2 * (w * z + x * y), 1 - 2 * (y * y + z * z))) % 360
+    rows[:, 7] = rng.uniform(-2, 6, nac)
+    rows[:, 9] = 3000.0
+    st = ic.seed_states(rows, 1.0 / 60.0, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    return st, rows, g
+
+
+def run_obs(args, dev, world, rank):
+    """the fused obs184 + reward + termination step (f16_obs_step) on 262,144 envs."""
+    import torch
+    import torch.distributed as dist
+    OR = importlib.import_module(PKG + ".obs_reward")
+    nenv, nac = OBS_NENV, 2 * OBS_NENV
+    st, rows, g = obs_inputs(nenv, 20260103 + rank, dev)
+    states = st.t()
+    b = OR.BatchObsReward(nenv, device=dev)
+    b.hp.uniform_(0, 1, generator=g); b.fuel.uniform_(0, 1, generator=g); b.t_sec.uniform_(0, 200, generator=g)
+    b.pqr.normal_(0, 0.3, generator=g)
+    b.prev_att.copy_(torch.as_tensor(rows[:, 4:7])); b.prev_valid.fill_(True)
+    b.act_hist.uniform_(-1, 1, generator=g)
+    b.kernel_init_reward_state(states)
+    act = torch.empty(nac, 4, dtype=torch.float64, device=dev).uniform_(-1, 1, generator=g)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    K, W = args.steps, max(3, args.warmup)
+    for _ in range(W):
+        b.kernel_step(states, act)
+    torch.cuda.synchronize(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0")))) as clk:
+        for e0, e1 in ev:
+            flush.zero_()
+            e0.record(stream)
+            b.kernel_step(states, act)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = torch.tensor([float(np.mean([a.elapsed_time(c) for a, c in ev]))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    value = world * nenv / (ms * 1e-3)
+    # e2e through the reference-facing API with host buffers: states + actions in, obs + reward out
+    host_st = states.cpu().contiguous().pin_memory()
+    host_act = act.cpu().pin_memory()
+    host_obs = torch.empty(nac, 184, dtype=torch.float32).pin_memory()
+    host_rew = torch.empty(nac, dtype=torch.float64).pin_memory()
+    dev_st = torch.empty(nac, 101, dtype=torch.float64, device=dev)
+    dev_act = torch.empty(nac, 4, dtype=torch.float64, device=dev)
+    Ke = max(1, min(args.e2e_steps, 20))
+    eev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(Ke)]
+    for e0, e1 in eev:
+        flush.zero_()
+        e0.record(stream)
+        dev_st.copy_(host_st, non_blocking=True)
+        dev_act.copy_(host_act, non_blocking=True)
+        o, r, _, _ = b.kernel_step(dev_st, dev_act)
+        host_obs.copy_(o, non_blocking=True)
+        host_rew.copy_(r, non_blocking=True)
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e_ms = torch.tensor([float(np.mean([a.elapsed_time(c) for a, c in eev]))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+    peak = measured_peaks().get("hbm_gbs")
+    achieved = OBS_BYTES_PER_ENV * nenv / (ms * 1e-3) / 1e9
+    if rank == 0:
+        line = {"metric": "fused obs184+reward+termination envs/s", "value": value, "unit": "envs/s",
+                "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+                "config": {"workload": "configs[2]: fused obs184+reward+termination, 262,144 envs x 2 per GPU",
+                           "envs_per_gpu": nenv, "l2": "flushed between timed steps (256 MB write)"},
+                "e2e": {"value": world * nenv / (float(e_ms.item()) * 1e-3), "unit": "envs/s",
+                        "h2d_bytes_per_step": nac * 101 * 8 + nac * 4 * 8, "d2h_bytes_per_step": nac * 184 * 4 + nac * 8,
+                        "api": "BatchObsReward.kernel_step on host state/actions, obs + reward back to host"},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak if peak else None, "traffic": None, "kernel": "k_obs_step",
+                             "bytes_per_unit": OBS_BYTES_PER_ENV, "unit_basis": "environment",
+                             "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)"},
+                "gpu_launches": K, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return json.loads(p.read_text())
+    except (OSError, ValueError):
+        return {}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -207,6 +328,8 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    if args.workload == "obs":
+        return run_obs(args, dev, world, rank)
 
     _lib = importlib.import_module(PKG + "._lib")
     ge = importlib.import_module(PKG + ".gpu_env")

@@ -206,6 +206,29 @@ int f16_state9(const double* state, int layout, int64_t ld, int64_t nac, const f
                double* s9, f16_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
+ * (4) Rollout arithmetic (R/cuda_fdm/ppo_gpu.py).
+ * f16_gae replaces the GAE loop of PPOGPUTrainer.collect_rollout (:1983-1995), bit for bit:
+ * rew, val, done, adv, ret are [T][ld] fp32 (done = the episode-start flags b_done), last_val
+ * and next_done [n] fp32; gamma and lam are the Python floats of the config.
+ * ---------------------------------------------------------------------------------------- */
+int f16_gae(const float* rew, const float* val, const float* done, const float* last_val,
+            const float* next_done, int T, int64_t n, int64_t ld, double gamma, double lam,
+            float* adv, float* ret, f16_stream_t stream);
+
+/* RunningNorm.update (:195-207) over x [B][ldx] fp32 (D features): batch mean / population
+ * variance merged into mean, var [D] and count [1] (fp32, device).  scratch: device buffer of
+ * f16_norm_scratch_doubles(B, D) doubles, 16-byte aligned. */
+int f16_norm_update(const float* x, int64_t B, int D, int64_t ldx, float* mean, float* var, float* count,
+                    double* scratch, int64_t scratch_doubles, f16_stream_t stream);
+int64_t f16_norm_scratch_doubles(int64_t B, int D);
+
+/* RunningNorm.normalize (:209-212): clamp((x - mean) / sqrt(var + eps), +-clip) into y [B][ldy]
+ * fp32 and/or y_bf16 [B][ldb] bf16 (columns D..ldb-1 zero-filled; either output may be NULL). */
+int f16_norm_apply(const float* x, int64_t B, int D, int64_t ldx, const float* mean, const float* var,
+                   double eps, double clip, float* y, int64_t ldy, void* y_bf16, int64_t ldb,
+                   f16_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
  * Diagnostics (no counterpart in the reference): FP64 FMA-pipe probe, the measured roofline
  * denominator of the FDM kernel.  Launches `blocks` x 256 threads running 8 independent FMA
  * chains for `iters` iterations; *flops receives the FP64 flop count (host pointer).

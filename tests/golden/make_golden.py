@@ -207,6 +207,87 @@ def make_obs_golden(nenv=24, steps=8, seed=20260103):
           "truncations:", np.stack(out["trunc"]).sum(1), "nonzero damage:", int((np.stack(out["dealt"]) > 0).sum()))
 
 
+def make_gae_golden(T=24, n=96, seed=20260104):
+    """gae.npz: the trainer's own GAE loop (R/cuda_fdm/ppo_gpu.py:1983-1995, as exercised by
+    cuda_fdm/tests/ppo_gpu_val.py:62-95) run with torch fp32 on CPU, plus that test's independent
+    numpy reference ``_ref_gae`` (fp64), on random rewards / values / done flags, for the
+    reference default (gamma 0.997, lambda 0.95) and BASELINE cfg4's (0.99, 0.95)."""
+    import importlib.util
+    import torch
+    spec = importlib.util.spec_from_file_location("ppo_gpu_val", REF / "cuda_fdm" / "tests" / "ppo_gpu_val.py")
+    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(REF / "src"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    g = torch.Generator().manual_seed(seed)
+    out = {}
+    for tag, gamma, lam in (("ref", 0.997, 0.95), ("cfg4", 0.99, 0.95)):
+        rew = torch.randn(T, n, generator=g) * 3
+        val = torch.randn(T, n, generator=g) * 5
+        done = (torch.rand(T, n, generator=g) < 0.1).float()
+        last_val = torch.randn(n, generator=g) * 5
+        next_done = (torch.rand(n, generator=g) < 0.1).float()
+        adv = torch.zeros_like(rew)
+        lastgae = torch.zeros(n)
+        for t in reversed(range(T)):
+            if t == T - 1:
+                next_nonterminal = 1.0 - next_done
+                next_values = last_val
+            else:
+                next_nonterminal = 1.0 - done[t + 1]
+                next_values = val[t + 1]
+            delta = rew[t] + gamma * next_values * next_nonterminal - val[t]
+            lastgae = delta + gamma * lam * next_nonterminal * lastgae
+            adv[t] = lastgae
+        ret = adv + val
+        ref64 = m._ref_gae(rew.numpy().astype(np.float64), val.numpy().astype(np.float64),
+                           done.numpy().astype(np.float64), last_val.numpy().astype(np.float64),
+                           next_done.numpy().astype(np.float64), gamma, lam)
+        for k, v in (("rew", rew), ("val", val), ("done", done), ("last_val", last_val), ("next_done", next_done),
+                     ("adv", adv), ("ret", ret)):
+            out[f"{tag}_{k}"] = v.numpy()
+        out[f"{tag}_ref64"] = ref64
+        out[f"{tag}_gamma_lam"] = np.array([gamma, lam])
+    np.savez_compressed(OUT / "gae.npz", **out)
+    print("gae.npz", T, n)
+
+
+def make_norm_golden(seed=20260105):
+    """norm.npz: the reference's RunningNorm (R/cuda_fdm/ppo_gpu.py:184-222) on CPU: three
+    batch updates of 184-feature observation-like rows, then normalize of a fourth batch."""
+    import torch
+    r36 = REF / "research" / "competition_36500" / "runtime"
+    for k in list(sys.modules):
+        if k == "cuda_fdm" or k.startswith("cuda_fdm."):
+            del sys.modules[k]
+    sys.path.insert(0, str(r36))
+    sys.path.insert(0, str(REF / "src"))
+    from cuda_fdm.ppo_gpu import RunningNorm
+    rn = RunningNorm(184, "cpu")
+    out = {"seed": np.array(seed)}
+    xs = norm_inputs(seed)
+    for i, x in enumerate(xs[:-1]):
+        rn.update(x)
+        out[f"mean{i}"] = rn.mean.numpy().copy()
+        out[f"var{i}"] = rn.var.numpy().copy()
+        out[f"count{i}"] = rn.count.numpy().copy()
+    out["yt"] = rn.normalize(xs[-1].clone()).numpy()
+    np.savez_compressed(OUT / "norm.npz", **out)
+    print("norm.npz")
+
+
+def norm_inputs(seed):
+    """Deterministic inputs of norm.npz (regenerated by the tests from the stored seed)."""
+    import torch
+    g = torch.Generator().manual_seed(int(seed))
+    xs = [torch.randn(B, 184, generator=g) * torch.linspace(0.1, 3.0, 184) + torch.linspace(-2, 2, 184)
+          for B in (512, 1000, 37)]
+    xs.append(torch.randn(24, 184, generator=g) * 40.0)
+    return xs
+
+
 if __name__ == "__main__":
     main()
     make_obs_golden()
+    make_gae_golden()
+    make_norm_golden()
