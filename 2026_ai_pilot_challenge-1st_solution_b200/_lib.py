@@ -54,6 +54,9 @@ _SIGS = {
                            _P, _P, _P], C.c_int),
     "f16_state9": ([_P, C.c_int, _I64, _I64, _PO, _P, _P], C.c_int),
     "f16_gae": ([_P, _P, _P, _P, _P, C.c_int, _I64, _I64, C.c_double, C.c_double, _P, _P, _P], C.c_int),
+    "f16_mlp_set_create": ([_P, C.c_int, _P], C.c_int),
+    "f16_mlp_set_destroy": ([_P], C.c_int),
+    "f16_policy_forward": ([_P, _P, _P], C.c_int),
     "f16_norm_update": ([_P, _I64, C.c_int, _I64, _P, _P, _P, _P, _I64, _P], C.c_int),
     "f16_norm_scratch_doubles": ([_I64, C.c_int], _I64),
     "f16_norm_apply": ([_P, _I64, C.c_int, _I64, _P, _P, C.c_double, C.c_double, _P, _I64, _P, _I64, _P],

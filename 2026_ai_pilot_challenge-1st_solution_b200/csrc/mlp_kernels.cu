@@ -1,0 +1,610 @@
+// mlp_kernels.cu -- policy / value MLP forward on the 5th-generation tensor cores (sm_100a).
+//
+// Replaces the rollout-time forwards of R/claude_code/model.py MLPDiscreteActorCritic
+// (actor_logits / critic, :162-241) as driven by ppo_gpu.py actor_step / value_step (:273-291)
+// and the frozen-opponent pools (:536-592, :877-898), including the Categorical sample and its
+// summed log-probability (Gumbel-max, fused into the last layer's epilogue).
+//
+// One persistent CTA per SM processes "jobs" = (128-row tile, network).  Per job and layer:
+//   * the A operand (the 128 x K activation tile, bf16) lives in a 128 KB shared-memory region in
+//     the K-major 128-byte-swizzled layout the tensor core reads; layer 0's A is loaded by TMA,
+//     layer l's A is written there by layer l-1's epilogue;
+//   * weight tiles (nn.Linear layout = K-major B) stream through a 3-stage ring of 32 KB TMA
+//     boxes (256 output rows x 64 inputs); no multicast anywhere;
+//   * one thread issues tcgen05.mma (M=128, N<=256, K=16 per instruction) accumulating fp32 in
+//     TMEM (all 512 columns = a full 128 x 512 layer);
+//   * four epilogue warps tcgen05.ld their 32 TMEM lanes, add bias, apply ReLU/tanh, and write the
+//     bf16 activations back to shared memory (or run the output head).
+// Every mbarrier wait is bounded by a clock deadline; a timeout sets an error code and all roles
+// leave their loops, so a malformed launch returns an error instead of hanging.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+#include "common.cuh"
+
+namespace f16 {
+namespace mlp {
+
+constexpr int MAX_LAYERS = 4;
+constexpr int MAX_NETS = 20;
+constexpr int TILE_M = 128;
+constexpr int KCHUNK = 64;                       // bf16 elements per 128-byte swizzle row
+constexpr int NCHUNK = 256;                      // output columns per MMA / weight box
+constexpr int STAGES = 3;
+constexpr int ACT_BYTES = 128 * 1024;            // 8 chunks x (128 rows x 128 B)
+constexpr int STAGE_BYTES = NCHUNK * 128;        // 32 KB
+constexpr int SMEM_BYTES = ACT_BYTES + STAGES * STAGE_BYTES + 256 + 1024;
+constexpr int THREADS = 192;                     // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
+constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
+
+enum Head : int { HEAD_HIDDEN_ONLY = 0, HEAD_CATEGORICAL = 1, HEAD_VALUE = 2 };
+
+struct NetDev {
+  CUtensorMap w[MAX_LAYERS];                     // weight maps (64-byte aligned, in global memory)
+};
+
+struct NetParams {
+  const float* bias[MAX_LAYERS];
+  int n_layers;
+  int in_pad;                                    // K of layer 0 rounded up to 64
+  int width[MAX_LAYERS];                         // true output width of each layer
+  int width_pad[MAX_LAYERS];                     // hidden: multiple of 64; last: multiple of 16
+  int act;                                       // 0 relu, 1 tanh
+  int head;                                      // Head
+  int num_bins, act_dim;                         // categorical head: act_dim groups of num_bins
+};
+
+struct Launch {
+  int64_t rows;                                  // valid rows of X
+  int n_groups;                                  // row groups (frozen-opponent pools); group g owns
+  int64_t group_end[MAX_NETS + 1];               //   rows [group_end[g-1], group_end[g]); starts % 128 == 0
+  int group_net[MAX_NETS][2];                    // networks per group (second = -1 if none)
+  int nets_per_group;
+  int64_t tiles_total;                           // sum over groups of ceil(rows_g / 128)
+  // outputs (row index = X row)
+  uint8_t* bins; int64_t bins_stride; int bins_offset;   // sampled action bins (act_dim bytes per row)
+  int32_t* act_idx;                              // optional int32 [rows][act_dim]
+  float* logp;                                   // summed log-probability per row
+  float* value;                                  // value head output per row
+  float* logits; int64_t logits_ld;              // optional raw logits / value (tests)
+  uint64_t seed, step;
+  int deterministic;                             // argmax instead of sampling
+  int* err;
+};
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false on timeout or when another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > WAIT_CYCLES) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// K-major, 128-byte-swizzled shared-memory matrix descriptor (rows 128 B apart in groups of 8,
+// groups 1024 B apart): start>>4 | LBO 16 B | SBO 1024 B | version 1 | layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M = 128.
+__device__ __forceinline__ uint32_t idesc_bf16(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- job decoding
+struct Job {
+  int64_t row0;
+  int rows;
+  int net;
+};
+__device__ __forceinline__ bool decode_job(const Launch& L, int64_t j, Job& J) {
+  int64_t tile = j / L.nets_per_group;
+  int slot = (int)(j % L.nets_per_group);
+  int64_t start = 0;
+  for (int g = 0; g < L.n_groups; g++) {
+    int64_t end = L.group_end[g];
+    int64_t nt = (end - start + TILE_M - 1) / TILE_M;
+    if (tile < nt) {
+      J.row0 = start + tile * TILE_M;
+      int64_t r = end - J.row0;
+      J.rows = (int)(r < TILE_M ? r : TILE_M);
+      J.net = L.group_net[g][slot];
+      return J.net >= 0;
+    }
+    tile -= nt;
+    start = end;
+  }
+  return false;
+}
+
+__device__ __forceinline__ uint64_t mix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+struct Smem {
+  uint64_t x_full, act_empty, acc_full, act_ready, tmem_empty, drain;
+  uint64_t full[STAGES], empty[STAGES];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ nets_dev,
+         const NetParams* __restrict__ nets, const __grid_constant__ Launch L) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* act = base;
+  uint8_t* stages = base + ACT_BYTES;
+  Smem* S = reinterpret_cast<Smem*>(stages + STAGES * STAGE_BYTES);
+  volatile int* abort_flag = &S->abort_flag;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&S->x_full), 1);
+    mbar_init(smem_u32(&S->act_empty), 1);
+    mbar_init(smem_u32(&S->acc_full), 1);
+    mbar_init(smem_u32(&S->act_ready), 128);
+    mbar_init(smem_u32(&S->tmem_empty), 128);
+    mbar_init(smem_u32(&S->drain), 1);
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(smem_u32(&S->full[s]), 1);
+      mbar_init(smem_u32(&S->empty[s]), 1);
+    }
+    S->abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&S->tmem_base))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S->tmem_base;
+  const int64_t njobs = L.tiles_total * L.nets_per_group;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int64_t jn = 0;
+      for (int64_t j = blockIdx.x; j < njobs; j += gridDim.x) {
+        Job J;
+        if (!decode_job(L, j, J)) continue;
+        const NetParams& P = nets[J.net];
+        const NetDev& D = nets_dev[J.net];
+        if (!mbar_wait(smem_u32(&S->act_empty), (uint32_t)((jn & 1) ^ 1), abort_flag)) break;
+        int kc0 = P.in_pad / KCHUNK;
+        mbar_expect_tx(smem_u32(&S->x_full), (uint32_t)(kc0 * TILE_M * 128));
+        for (int c = 0; c < kc0; c++)
+          tma_load_2d(smem_u32(act + c * TILE_M * 128), &xmap, c * KCHUNK, (int)J.row0, smem_u32(&S->x_full));
+        bool ok = true;
+        for (int l = 0; l < P.n_layers && ok; l++) {
+          int K = (l == 0) ? P.in_pad : P.width_pad[l - 1];
+          int N = P.width_pad[l];
+          // every box of this layer's map moves box_rows x 128 B (rows past N arrive zero-filled)
+          const uint32_t box_bytes = (uint32_t)((N < NCHUNK ? N : NCHUNK) * 128);
+          for (int n0 = 0; n0 < N && ok; n0 += NCHUNK) {
+            for (int k0 = 0; k0 < K; k0 += KCHUNK, it++) {
+              int s = it % STAGES;
+              uint32_t round = it / STAGES;
+              if (!mbar_wait(smem_u32(&S->empty[s]), (round & 1) ^ 1, abort_flag)) { ok = false; break; }
+              mbar_expect_tx(smem_u32(&S->full[s]), box_bytes);
+              tma_load_2d(smem_u32(stages + s * STAGE_BYTES), &D.w[l], k0, n0, smem_u32(&S->full[s]));
+            }
+          }
+        }
+        if (!ok) break;
+        jn++;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, acts = 0;
+      int64_t jn = 0;
+      for (int64_t j = blockIdx.x; j < njobs; j += gridDim.x) {
+        Job J;
+        if (!decode_job(L, j, J)) continue;
+        const NetParams& P = nets[J.net];
+        bool ok = mbar_wait(smem_u32(&S->x_full), (uint32_t)(jn & 1), abort_flag) &&
+                  mbar_wait(smem_u32(&S->tmem_empty), (uint32_t)((jn & 1) ^ 1), abort_flag);
+        for (int l = 0; l < P.n_layers && ok; l++) {
+          if (l > 0) {
+            if (!mbar_wait(smem_u32(&S->act_ready), acts & 1, abort_flag)) { ok = false; break; }
+            acts++;
+          }
+          tc_fence_after();
+          int K = (l == 0) ? P.in_pad : P.width_pad[l - 1];
+          int N = P.width_pad[l];
+          for (int n0 = 0; n0 < N && ok; n0 += NCHUNK) {
+            int nc = (N - n0) < NCHUNK ? (N - n0) : NCHUNK;
+            uint32_t idesc = idesc_bf16(nc);
+            for (int k0 = 0; k0 < K; k0 += KCHUNK, it++) {
+              int s = it % STAGES;
+              uint32_t round = it / STAGES;
+              if (!mbar_wait(smem_u32(&S->full[s]), round & 1, abort_flag)) { ok = false; break; }
+              tc_fence_after();
+              uint32_t a_base = smem_u32(act + (k0 / KCHUNK) * TILE_M * 128);
+              uint32_t b_base = smem_u32(stages + s * STAGE_BYTES);
+#pragma unroll
+              for (int kk = 0; kk < KCHUNK / 16; kk++)
+                tc_mma(tmem + (uint32_t)n0, sdesc(a_base + kk * 32), sdesc(b_base + kk * 32), idesc,
+                       (k0 > 0 || kk > 0) ? 1u : 0u);
+              tc_commit(smem_u32(&S->empty[s]));
+            }
+          }
+          tc_commit(smem_u32(&S->acc_full));
+        }
+        tc_commit(smem_u32(&S->act_empty));
+        if (!ok) break;
+        jn++;
+      }
+      // drain: wait (bounded) until every MMA this thread issued has completed
+      tc_commit(smem_u32(&S->drain));
+      long long t0 = clock64();
+      while (!mbar_try(smem_u32(&S->drain), 0) && clock64() - t0 < WAIT_CYCLES) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2-5)
+    const int q = warp & 3;                       // TMEM lane quarter this warp may access
+    const int m = q * 32 + lane;                  // tile row of this thread
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    uint32_t accs = 0;
+    int64_t jn = 0;
+    for (int64_t j = blockIdx.x; j < njobs; j += gridDim.x) {
+      Job J;
+      if (!decode_job(L, j, J)) continue;
+      const NetParams& P = nets[J.net];
+      bool ok = true;
+      for (int l = 0; l < P.n_layers; l++) {
+        bool got = mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
+        __syncwarp();                               // reconverge before the .sync.aligned TMEM loads
+        if (!got || *abort_flag) { ok = false; break; }
+        accs++;
+        tc_fence_after();
+        const float* bias = P.bias[l];
+        const bool last = (l == P.n_layers - 1);
+        if (!last) {
+          // bias + activation -> bf16 into the swizzled A region of the next layer
+          const int N = P.width_pad[l];
+          for (int c0 = 0; c0 < N; c0 += 32) {
+            float v[32];
+            tmem_ld32(lane_addr + (uint32_t)c0, v);
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+              float x = v[i] + __ldg(bias + c0 + i);
+              v[i] = (P.act == 0) ? fmaxf(x, 0.0f) : tanhf(x);
+            }
+            uint8_t* chunk = act + (c0 / KCHUNK) * TILE_M * 128 + (m >> 3) * 1024 + (m & 7) * 128;
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+              int unit = ((c0 % KCHUNK) / 8) + u;           // 16-byte unit within the 128-byte row
+              __nv_bfloat162 p0 = __floats2bfloat162_rn(v[8 * u + 0], v[8 * u + 1]);
+              __nv_bfloat162 p1 = __floats2bfloat162_rn(v[8 * u + 2], v[8 * u + 3]);
+              __nv_bfloat162 p2 = __floats2bfloat162_rn(v[8 * u + 4], v[8 * u + 5]);
+              __nv_bfloat162 p3 = __floats2bfloat162_rn(v[8 * u + 6], v[8 * u + 7]);
+              uint4 w;
+              w.x = *reinterpret_cast<uint32_t*>(&p0);
+              w.y = *reinterpret_cast<uint32_t*>(&p1);
+              w.z = *reinterpret_cast<uint32_t*>(&p2);
+              w.w = *reinterpret_cast<uint32_t*>(&p3);
+              *reinterpret_cast<uint4*>(chunk + ((unit ^ (m & 7)) * 16)) = w;
+            }
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          tc_fence_before();
+          mbar_arrive(smem_u32(&S->act_ready));
+        } else {
+          const int64_t row = J.row0 + m;
+          const bool valid = m < J.rows;
+          if (P.head == HEAD_VALUE) {
+            float v[32];
+            tmem_ld32(lane_addr, v);
+            float val = v[0] + __ldg(bias);
+            if (valid) {
+              if (L.value) L.value[row] = val;
+              if (L.logits) L.logits[row * L.logits_ld] = val;
+            }
+          } else {
+            // categorical head: act_dim groups of num_bins logits -> Gumbel-max sample + log-prob
+            const int W = P.width[l];
+            float lg[96];
+            for (int c0 = 0; c0 < 96; c0 += 32) tmem_ld32(lane_addr + (uint32_t)c0, lg + c0);
+            for (int i = 0; i < 96; i++) lg[i] += (i < W) ? __ldg(bias + i) : 0.0f;
+            float logp = 0.0f;
+            for (int g = 0; g < P.act_dim; g++) {
+              const float* x = lg + g * P.num_bins;
+              float mx = -INFINITY;
+              for (int b = 0; b < P.num_bins; b++) mx = fmaxf(mx, x[b]);
+              float se = 0.0f;
+              for (int b = 0; b < P.num_bins; b++) se += expf(x[b] - mx);
+              float lse = mx + logf(se);
+              int best = 0;
+              float bestv = -INFINITY;
+              for (int b = 0; b < P.num_bins; b++) {
+                float s = x[b];
+                if (!L.deterministic) {
+                  uint64_t h = mix64(L.seed ^ mix64((L.step << 32) ^ ((uint64_t)row * 131ull + (uint64_t)(g * 64 + b))));
+                  float u = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);   // (0,1)
+                  s += -logf(-logf(u));
+                }
+                if (s > bestv) { bestv = s; best = b; }
+              }
+              logp += x[best] - lse;
+              if (valid) {
+                if (L.bins) L.bins[row * L.bins_stride + L.bins_offset + g] = (uint8_t)best;
+                if (L.act_idx) L.act_idx[row * P.act_dim + g] = best;
+              }
+            }
+            if (valid) {
+              if (L.logp) L.logp[row] = logp;
+              if (L.logits)
+                for (int i = 0; i < W; i++) L.logits[row * L.logits_ld + i] = lg[i];
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(smem_u32(&S->tmem_empty));
+        }
+      }
+      if (!ok) break;
+      jn++;
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  __syncwarp();
+  if (*abort_flag) {
+    // a role gave up waiting: give copies still in flight a bounded time to land before exit
+    for (int i = 0; i < 4; i++) __nanosleep(1000000);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0 && L.err) atomicExch(L.err, F16_ERR_LAUNCH);
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// bf16 row-major [rows][cols] (row stride ld elements) with a 128-byte-swizzled box of 64 x box_rows
+static bool make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)KCHUNK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace mlp
+}  // namespace f16
+
+struct f16_mlp_set_s {
+  int n;
+  f16::mlp::NetDev* dev_maps;      // device [n]
+  f16::mlp::NetParams* dev_params; // device [n]
+  f16::mlp::NetParams host_params[f16::mlp::MAX_NETS];
+};
+
+using namespace f16;
+using namespace f16::mlp;
+
+extern "C" int f16_mlp_set_create(const f16_mlp_desc* descs, int n, f16_mlp_set** out) {
+  if (!descs || n <= 0 || n > MAX_NETS || !out) return F16_ERR_ARG;
+  *out = nullptr;
+  NetDev maps[MAX_NETS];
+  f16_mlp_set_s* s = new f16_mlp_set_s();
+  s->n = n;
+  for (int i = 0; i < n; i++) {
+    const f16_mlp_desc& d = descs[i];
+    NetParams& P = s->host_params[i];
+    memset(&P, 0, sizeof(P));
+    if (d.n_layers < 1 || d.n_layers > MAX_LAYERS || d.in_dim <= 0 || d.in_dim % 8 != 0 || d.in_dim > 512 ||
+        (d.activation != 0 && d.activation != 1) || (d.head != HEAD_CATEGORICAL && d.head != HEAD_VALUE)) {
+      delete s;
+      return F16_ERR_ARG;
+    }
+    P.n_layers = d.n_layers;
+    P.in_pad = (d.in_dim + KCHUNK - 1) / KCHUNK * KCHUNK;
+    P.act = d.activation;
+    P.head = d.head;
+    P.num_bins = d.num_bins;
+    P.act_dim = d.act_dim;
+    int in_l = d.in_dim;
+    for (int l = 0; l < d.n_layers; l++) {
+      int w = d.width[l];
+      bool last = (l == d.n_layers - 1);
+      if (!d.weight[l] || !d.bias[l] || w <= 0) { delete s; return F16_ERR_ARG; }
+      if (!aligned(d.weight[l], 16)) { delete s; return F16_ERR_ALIGN; }
+      if (!last && (w % KCHUNK != 0 || w > 512)) { delete s; return F16_ERR_ARG; }
+      int wp = last ? (w + 15) / 16 * 16 : w;
+      if (last && d.head == HEAD_CATEGORICAL && (wp > 96 || d.act_dim * d.num_bins != w || d.num_bins > 64)) {
+        delete s;
+        return F16_ERR_ARG;
+      }
+      if (last && d.head == HEAD_VALUE && w != 1) { delete s; return F16_ERR_ARG; }
+      P.width[l] = w;
+      P.width_pad[l] = wp;
+      P.bias[l] = d.bias[l];
+      int box_rows = wp < NCHUNK ? wp : NCHUNK;
+      if (!make_map(&maps[i].w[l], d.weight[l], w, in_l, in_l, box_rows)) { delete s; return F16_ERR_CUDA; }
+      in_l = w;
+    }
+  }
+  if (cudaMalloc(&s->dev_maps, sizeof(NetDev) * n) != cudaSuccess ||
+      cudaMalloc(&s->dev_params, sizeof(NetParams) * n) != cudaSuccess) {
+    delete s;
+    return F16_ERR_CUDA;
+  }
+  if (cudaMemcpy(s->dev_maps, maps, sizeof(NetDev) * n, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(s->dev_params, s->host_params, sizeof(NetParams) * n, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(s->dev_maps);
+    cudaFree(s->dev_params);
+    delete s;
+    return F16_ERR_CUDA;
+  }
+  *out = s;
+  return F16_OK;
+}
+
+extern "C" int f16_mlp_set_destroy(f16_mlp_set* s) {
+  if (!s) return F16_ERR_ARG;
+  cudaFree(s->dev_maps);
+  cudaFree(s->dev_params);
+  delete s;
+  return F16_OK;
+}
+
+extern "C" int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args* a, f16_stream_t stream) {
+  if (!set || !a || !a->x || a->rows <= 0 || a->n_groups < 1 || a->n_groups > MAX_NETS || !a->group_end ||
+      !a->group_net || a->nets_per_group < 1 || a->nets_per_group > 2)
+    return F16_ERR_ARG;
+  if (!aligned(a->x, 16) || (a->ldx * 2) % 16 != 0) return F16_ERR_ALIGN;
+  Launch L;
+  memset(&L, 0, sizeof(L));
+  L.rows = a->rows;
+  L.n_groups = a->n_groups;
+  L.nets_per_group = a->nets_per_group;
+  int64_t start = 0, tiles = 0;
+  int in_pad = -1;
+  for (int g = 0; g < a->n_groups; g++) {
+    int64_t end = a->group_end[g];
+    if (end < start || end > a->rows || start % TILE_M != 0) return F16_ERR_ARG;
+    L.group_end[g] = end;
+    tiles += (end - start + TILE_M - 1) / TILE_M;
+    for (int k = 0; k < 2; k++) {
+      int net = k < a->nets_per_group ? a->group_net[g * a->nets_per_group + k] : -1;
+      if (net >= set->n) return F16_ERR_ARG;
+      if (net >= 0) {
+        int ip = set->host_params[net].in_pad;
+        if (in_pad >= 0 && ip != in_pad) return F16_ERR_ARG;
+        in_pad = ip;
+        if (set->host_params[net].head == HEAD_CATEGORICAL && (!a->logp && !a->bins && !a->act_idx && !a->logits))
+          return F16_ERR_ARG;
+      }
+      L.group_net[g][k] = net;
+    }
+    start = end;
+  }
+  if (in_pad < 0 || a->ldx < 8) return F16_ERR_ARG;
+  L.tiles_total = tiles;
+  L.bins = a->bins; L.bins_stride = a->bins_stride; L.bins_offset = a->bins_offset;
+  L.act_idx = a->act_idx; L.logp = a->logp; L.value = a->value;
+  L.logits = a->logits; L.logits_ld = a->logits_ld;
+  L.seed = a->seed; L.step = a->step; L.deterministic = a->deterministic;
+  L.err = a->err;
+  CUtensorMap xmap;
+  if (!make_map(&xmap, a->x, a->rows, a->ldx, a->ldx, TILE_M)) return F16_ERR_CUDA;
+  int64_t njobs = tiles * a->nets_per_group;
+  if (njobs == 0) return F16_OK;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(k_policy, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+      return F16_ERR_LAUNCH;
+    attr[dev] = true;
+  }
+  int grid = (int)(njobs < sm_count() ? njobs : sm_count());
+  k_policy<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(xmap, set->dev_maps,
+                                                                                 set->dev_params, L);
+  return launch_status();
+}

@@ -1,0 +1,122 @@
+"""Rollout-time policy / value forwards on the tcgen05 MLP kernel (csrc/mlp_kernels.cu).
+
+``MlpWeights.from_sequential`` takes the reference's ``nn.Sequential`` stacks
+(R/claude_code/model.py ``_mlp`` :34-44 -> ``actor_logits`` / ``critic``) and keeps bf16 copies of
+the Linear weights and fp32 biases on the device.  ``PolicySet`` registers up to 20 such networks
+once (per weight update / pool refresh) and ``forward`` runs any mix of them over row groups:
+the main actor + critic on the same rows, or the frozen opponents of a league pool on their
+contiguous row blocks, sampling each 21-bin channel with Gumbel-max and summing the log-probs
+(the reference's Categorical(logits).sample() / log_prob(.).sum(-1), ppo_gpu.py:273-285).
+"""
+import ctypes as C
+
+import torch
+
+from . import _lib
+
+HEAD_CATEGORICAL = 1
+HEAD_VALUE = 2
+ACTIVATIONS = {"relu": 0, "tanh": 1}
+
+
+class MlpDesc(C.Structure):
+    _fields_ = [("in_dim", C.c_int), ("n_layers", C.c_int), ("width", C.c_int * 4), ("activation", C.c_int),
+                ("head", C.c_int), ("act_dim", C.c_int), ("num_bins", C.c_int), ("weight", C.c_void_p * 4),
+                ("bias", C.c_void_p * 4)]
+
+
+class PolicyArgs(C.Structure):
+    _fields_ = [("x", C.c_void_p), ("rows", C.c_int64), ("ldx", C.c_int64), ("n_groups", C.c_int),
+                ("group_end", C.POINTER(C.c_int64)), ("group_net", C.POINTER(C.c_int)), ("nets_per_group", C.c_int),
+                ("bins", C.c_void_p), ("bins_stride", C.c_int64), ("bins_offset", C.c_int), ("act_idx", C.c_void_p),
+                ("logp", C.c_void_p), ("value", C.c_void_p), ("logits", C.c_void_p), ("logits_ld", C.c_int64),
+                ("seed", C.c_uint64), ("step", C.c_uint64), ("deterministic", C.c_int), ("err", C.c_void_p)]
+
+
+class MlpWeights:
+    """Device bf16 weights + fp32 biases of one Linear stack."""
+
+    def __init__(self, weights, biases, activation="relu", head=HEAD_CATEGORICAL, act_dim=4, num_bins=21):
+        self.weights = [w.detach().to(torch.bfloat16).contiguous() for w in weights]
+        self.biases = [b.detach().to(torch.float32).contiguous() for b in biases]
+        self.activation = activation
+        self.head = head
+        self.act_dim, self.num_bins = act_dim, num_bins
+        self.in_dim = self.weights[0].shape[1]
+
+    @classmethod
+    def from_sequential(cls, seq, head, device, act_dim=4, num_bins=21):
+        linears = [m for m in seq if isinstance(m, torch.nn.Linear)]
+        acts = {type(m).__name__.lower() for m in seq if not isinstance(m, torch.nn.Linear)}
+        act = "tanh" if "tanh" in acts else "relu"
+        if acts - {"tanh", "relu"}:
+            raise ValueError(f"unsupported activation(s): {acts}")
+        return cls([l.weight.to(device) for l in linears], [l.bias.to(device) for l in linears], act, head,
+                   act_dim, num_bins)
+
+    def desc(self):
+        d = MlpDesc()
+        d.in_dim = self.in_dim
+        d.n_layers = len(self.weights)
+        for i, (w, b) in enumerate(zip(self.weights, self.biases)):
+            d.width[i] = w.shape[0]
+            d.weight[i] = w.data_ptr()
+            d.bias[i] = b.data_ptr()
+        d.activation = ACTIVATIONS[self.activation]
+        d.head = self.head
+        d.act_dim, d.num_bins = self.act_dim, self.num_bins
+        return d
+
+
+class PolicySet:
+    """A registered group of networks (indices are positions in ``nets``)."""
+
+    def __init__(self, nets):
+        self.lib = _lib.load()
+        self.nets = list(nets)           # keeps the device buffers alive
+        arr = (MlpDesc * len(self.nets))(*[n.desc() for n in self.nets])
+        handle = C.c_void_p()
+        _lib.check(self.lib.f16_mlp_set_create(arr, len(self.nets), C.byref(handle)), "f16_mlp_set_create")
+        self.handle = handle
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.nets[0].weights[0].device)
+
+    def close(self):
+        if self.handle:
+            self.lib.f16_mlp_set_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, x_bf16, groups, nets_per_group=1, bins=None, bins_stride=4, bins_offset=0, act_idx=None,
+                logp=None, value=None, logits=None, seed=0, step=0, deterministic=False):
+        """groups: list of (row_end, [net indices]) with every group starting at a multiple of 128."""
+        _lib.require_cuda_tensor(x_bf16, torch.bfloat16, None, "policy input", None)
+        rows, ldx = x_bf16.shape[0], x_bf16.stride(0)
+        ends = (C.c_int64 * len(groups))(*[int(g[0]) for g in groups])
+        flat = []
+        for _, ids in groups:
+            ids = list(ids) + [-1] * (nets_per_group - len(ids))
+            flat.extend(ids[:nets_per_group])
+        netv = (C.c_int * len(flat))(*flat)
+        a = PolicyArgs()
+        a.x = x_bf16.data_ptr(); a.rows = rows; a.ldx = ldx
+        a.n_groups = len(groups); a.group_end = ends; a.group_net = netv; a.nets_per_group = nets_per_group
+        a.bins = bins.data_ptr() if bins is not None else None
+        a.bins_stride = bins_stride; a.bins_offset = bins_offset
+        a.act_idx = act_idx.data_ptr() if act_idx is not None else None
+        a.logp = logp.data_ptr() if logp is not None else None
+        a.value = value.data_ptr() if value is not None else None
+        a.logits = logits.data_ptr() if logits is not None else None
+        a.logits_ld = logits.stride(0) if logits is not None else 0
+        a.seed = seed & (2 ** 64 - 1); a.step = step & (2 ** 64 - 1); a.deterministic = int(bool(deterministic))
+        a.err = self.err.data_ptr()
+        _lib.check(self.lib.f16_policy_forward(self.handle, C.byref(a), _lib.stream_of(x_bf16)), "f16_policy_forward")
+
+    def check_error(self):
+        """Host-synchronising check of the kernel's bounded-wait flag."""
+        if int(self.err.item()) != 0:
+            raise RuntimeError("f16_policy_forward: a bounded pipeline wait timed out")

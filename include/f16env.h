@@ -206,6 +206,59 @@ int f16_state9(const double* state, int layout, int64_t ld, int64_t nac, const f
                double* s9, f16_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
+ * (3) Policy / value MLP forward on the tcgen05 tensor cores (bf16 in, fp32 accumulate).
+ * Replaces the rollout forwards of R/claude_code/model.py MLPDiscreteActorCritic (actor_logits,
+ * critic; :162-241) driven by R/cuda_fdm/ppo_gpu.py actor_step / value_step (:273-291) and the
+ * frozen-opponent pools OpponentPool.act / ActiveLeaguePool.act (:536-592, :877-898), with the
+ * per-channel Categorical sample (Gumbel-max, counter-based RNG) and its summed log-probability
+ * fused into the last layer.
+ *
+ * A network: n_layers <= 4 Linear layers (nn.Linear layout: weight [out][in] bf16 row-major,
+ * device, 16-byte aligned, in a multiple of 8), hidden widths multiples of 64 up to 512, ReLU
+ * (activation 0) or tanh (1) after every hidden layer; head 1 = categorical with
+ * width[last] = act_dim * num_bins <= 96, head 2 = value with width[last] = 1.
+ * ---------------------------------------------------------------------------------------- */
+typedef struct {
+  int in_dim;
+  int n_layers;
+  int width[4];
+  int activation;
+  int head;
+  int act_dim, num_bins;
+  const void* weight[4];
+  const float* bias[4];
+} f16_mlp_desc;
+
+typedef struct f16_mlp_set_s f16_mlp_set;   /* opaque: up to 20 networks with their TMA maps */
+
+/* Build the weight tensor maps of n networks (the weight / bias buffers must outlive the set). */
+int f16_mlp_set_create(const f16_mlp_desc* descs, int n, f16_mlp_set** out);
+int f16_mlp_set_destroy(f16_mlp_set* set);
+
+typedef struct {
+  const void* x;            /* bf16 [rows][ldx] policy input (normalised observations), device */
+  int64_t rows, ldx;
+  int n_groups;             /* row groups; group g owns rows [group_end[g-1], group_end[g]), every
+                               group starting at a multiple of 128 rows */
+  const int64_t* group_end; /* host [n_groups] */
+  const int* group_net;     /* host [n_groups][nets_per_group]: network index in the set, -1 none */
+  int nets_per_group;       /* 1 or 2 (e.g. actor + critic on the same rows) */
+  uint8_t* bins;            /* categorical: sampled bins, row r at bins[r*bins_stride + bins_offset + c] */
+  int64_t bins_stride;
+  int bins_offset;
+  int32_t* act_idx;         /* optional [rows][act_dim] int32 */
+  float* logp;              /* [rows] summed log-probability of the sampled bins */
+  float* value;             /* [rows] value head */
+  float* logits;            /* optional [rows][logits_ld] raw head output (tests) */
+  int64_t logits_ld;
+  uint64_t seed, step;      /* RNG key of this call */
+  int deterministic;        /* 1: argmax (the reference's deterministic=True / sample=False) */
+  int* err;                 /* optional device int: set non-zero if a bounded wait timed out */
+} f16_policy_args;
+
+int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args* args, f16_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------
  * (4) Rollout arithmetic (R/cuda_fdm/ppo_gpu.py).
  * f16_gae replaces the GAE loop of PPOGPUTrainer.collect_rollout (:1983-1995), bit for bit:
  * rew, val, done, adv, ret are [T][ld] fp32 (done = the episode-start flags b_done), last_val
