@@ -11,6 +11,7 @@
 // Chan merge in fp32), and the normalise-clamp that produces the policy input, optionally also
 // as a zero-padded bf16 matrix (the MLP kernel's A operand).
 #include <cuda_bf16.h>
+#include <mutex>
 #include "common.cuh"
 
 namespace f16 {
@@ -163,5 +164,58 @@ extern "C" int f16_norm_apply(const float* x, int64_t B, int D, int64_t ldx, con
             (unsigned)(B < 65535 ? B : 65535));
   ro::k_norm_apply<<<grid, ro::NORM_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy, reinterpret_cast<__nv_bfloat16*>(y_bf16), ldb);
+  return launch_status();
+}
+
+// ---------------------------------------------------------------------------------------------
+// RunningNorm update with library-owned scratch (no counterpart in the reference).
+//
+// For callers that cannot allocate device memory at the point of the update: a fixed-size
+// memory pool or arena that is sealed once training starts, or a host driver that forbids
+// allocation inside its step loop.  The fp64 partial sums live in a file-scope device array of
+// F16_NORM_STATIC_SCRATCH_PAIRS double2 (2 MiB) instead of a caller buffer; its address is read
+// once per device with cudaGetSymbolAddress.  Every scratch slot that the merge kernel reads is
+// written by the partial kernel of the same call first, so nothing needs to start at zero.
+// There is one array per device, so two calls in flight at the same time on one device (two
+// streams, or two host threads) race on it; calls queued on one stream are ordered and safe.
+// ---------------------------------------------------------------------------------------------
+static __device__ __align__(256) double2 g_norm_static_scratch[F16_NORM_STATIC_SCRATCH_PAIRS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_norm_static_mu;
+double2* g_norm_static_addr[kMaxDevices] = {};
+
+// Device address of g_norm_static_scratch on the current device (looked up on first use).
+int norm_static_scratch(double2** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return F16_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_norm_static_mu);
+  if (!g_norm_static_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_norm_static_scratch) != cudaSuccess || !p) {
+      cudaGetLastError();
+      return F16_ERR_CUDA;
+    }
+    g_norm_static_addr[dev] = static_cast<double2*>(p);
+  }
+  *out = g_norm_static_addr[dev];
+  return F16_OK;
+}
+}  // namespace
+
+extern "C" int f16_norm_update_static(const float* x, int64_t B, int D, int64_t ldx, float* mean, float* var,
+                                      float* count, f16_stream_t stream) {
+  if (!x || !mean || !var || !count || B <= 0 || D <= 0 || ldx < D) return F16_ERR_ARG;
+  int64_t nblk = (B + ro::NORM_ROWS_PER_BLOCK - 1) / ro::NORM_ROWS_PER_BLOCK;
+  if (nblk * D > (int64_t)F16_NORM_STATIC_SCRATCH_PAIRS) return F16_ERR_TOO_LARGE;
+  double2* part = nullptr;
+  int rc = norm_static_scratch(&part);
+  if (rc != F16_OK) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  ro::k_norm_partial<<<(unsigned)nblk, ro::NORM_THREADS, 0, s>>>(x, B, D, ldx, part);
+  ro::k_norm_merge<<<(D + ro::NORM_THREADS - 1) / ro::NORM_THREADS, ro::NORM_THREADS, 0, s>>>(
+      part, (int)nblk, B, D, mean, var, count);
+  ro::k_norm_count<<<1, 32, 0, s>>>(count, B);
   return launch_status();
 }

@@ -275,6 +275,19 @@ int f16_norm_update(const float* x, int64_t B, int D, int64_t ldx, float* mean, 
                     double* scratch, int64_t scratch_doubles, f16_stream_t stream);
 int64_t f16_norm_scratch_doubles(int64_t B, int D);
 
+/* f16_norm_update without a caller scratch buffer (no counterpart in the reference).  For hosts
+ * that may not allocate device memory inside their step loop (a sealed memory pool or arena):
+ * the fp64 partial sums go to a library-owned device array of F16_NORM_STATIC_SCRATCH_PAIRS
+ * (sum, sum of squares) pairs, so ceil(B / 512) * D must not exceed it (else
+ * F16_ERR_TOO_LARGE, nothing launched).  No allocation happens in any call.  The first call on
+ * a device looks up that array's address (cudaGetSymbolAddress, with the device current), so
+ * make the first call before any stream capture.  Nothing needs to be zeroed beforehand.  The
+ * array is shared per device: calls that may run at the same time on one device (different
+ * streams or host threads) race; calls on one stream are ordered. */
+#define F16_NORM_STATIC_SCRATCH_PAIRS 131072
+int f16_norm_update_static(const float* x, int64_t B, int D, int64_t ldx, float* mean, float* var,
+                           float* count, f16_stream_t stream);
+
 /* RunningNorm.normalize (:209-212): clamp((x - mean) / sqrt(var + eps), +-clip) into y [B][ldy]
  * fp32 and/or y_bf16 [B][ldb] bf16 (columns D..ldb-1 zero-filled; either output may be NULL). */
 int f16_norm_apply(const float* x, int64_t B, int D, int64_t ldx, const float* mean, const float* var,
