@@ -59,6 +59,8 @@ _SIGS = {
     "f16_policy_forward": ([_P, _P, _P], C.c_int),
     "f16_norm_update": ([_P, _I64, C.c_int, _I64, _P, _P, _P, _P, _I64, _P], C.c_int),
     "f16_norm_scratch_doubles": ([_I64, C.c_int], _I64),
+    "f16_norm_sums": ([_P, _I64, C.c_int, _I64, _P, _P, _I64, _P], C.c_int),
+    "f16_norm_merge_sums": ([_P, _I64, C.c_int, _P, _P, _P, _P], C.c_int),
     "f16_norm_update_static": ([_P, _I64, C.c_int, _I64, _P, _P, _P, _P], C.c_int),
     "f16_norm_apply": ([_P, _I64, C.c_int, _I64, _P, _P, C.c_double, C.c_double, _P, _I64, _P, _I64, _P],
                        C.c_int),

@@ -72,6 +72,8 @@ struct Launch {
   uint64_t seed, step;
   int deterministic;                             // argmax instead of sampling
   int* err;
+  double* cmd; int64_t cmd_stride; int cmd_offset;   // optional env commands of the bins
+  const float* grid;                             //   (fp32 action grid, num_bins values)
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -411,6 +413,12 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
               if (valid) {
                 if (L.bins) L.bins[row * L.bins_stride + L.bins_offset + g] = (uint8_t)best;
                 if (L.act_idx) L.act_idx[row * P.act_dim + g] = best;
+                if (L.cmd) {
+                  // action_to_env in fp32: grid value, throttle (channel 3) 0.5 * v + 0.5
+                  const float gv = __ldg(L.grid + best);
+                  const float cv = g == 3 ? __fadd_rn(__fmul_rn(0.5f, gv), 0.5f) : gv;
+                  L.cmd[row * L.cmd_stride + L.cmd_offset + g] = (double)cv;
+                }
               }
             }
             if (valid) {
@@ -577,7 +585,7 @@ extern "C" int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args*
         int ip = set->host_params[net].in_pad;
         if (in_pad >= 0 && ip != in_pad) return F16_ERR_ARG;
         in_pad = ip;
-        if (set->host_params[net].head == HEAD_CATEGORICAL && (!a->logp && !a->bins && !a->act_idx && !a->logits))
+        if (set->host_params[net].head == HEAD_CATEGORICAL && (!a->logp && !a->bins && !a->act_idx && !a->logits && !a->cmd))
           return F16_ERR_ARG;
       }
       L.group_net[g][k] = net;
@@ -591,6 +599,8 @@ extern "C" int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args*
   L.logits = a->logits; L.logits_ld = a->logits_ld;
   L.seed = a->seed; L.step = a->step; L.deterministic = a->deterministic;
   L.err = a->err;
+  if (a->cmd && (!a->grid || a->cmd_stride < 0 || a->cmd_offset < 0)) return F16_ERR_ARG;
+  L.cmd = a->cmd; L.cmd_stride = a->cmd_stride; L.cmd_offset = a->cmd_offset; L.grid = a->grid;
   CUtensorMap xmap;
   if (!make_map(&xmap, a->x, a->rows, a->ldx, a->ldx, TILE_M)) return F16_ERR_CUDA;
   int64_t njobs = tiles * a->nets_per_group;

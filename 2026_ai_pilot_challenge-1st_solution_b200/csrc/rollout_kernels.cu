@@ -91,6 +91,21 @@ k_norm_merge(const double2* __restrict__ partial, int nblk, int64_t B, int D, fl
   }
 }
 
+// sums[d] = sum over the partial rows (same order as k_norm_merge, so a merge of sums reproduces
+// f16_norm_update bit for bit on one device)
+__global__ void __launch_bounds__(NORM_THREADS)
+k_norm_reduce(const double2* __restrict__ partial, int nblk, int D, double2* __restrict__ sums) {
+  int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  double s = 0.0, q = 0.0;
+  for (int b = 0; b < nblk; b++) {
+    double2 p = partial[(int64_t)b * D + d];
+    s += p.x;
+    q += p.y;
+  }
+  sums[d] = make_double2(s, q);
+}
+
 __global__ void k_norm_count(float* __restrict__ count, int64_t B) {
   if (threadIdx.x == 0 && blockIdx.x == 0) count[0] = __fadd_rn(count[0], (float)B);
 }
@@ -147,6 +162,31 @@ extern "C" int f16_norm_update(const float* x, int64_t B, int D, int64_t ldx, fl
   ro::k_norm_merge<<<(D + ro::NORM_THREADS - 1) / ro::NORM_THREADS, ro::NORM_THREADS, 0, s>>>(part, nblk, B, D,
                                                                                             mean, var, count);
   ro::k_norm_count<<<1, 32, 0, s>>>(count, B);
+  return launch_status();
+}
+
+extern "C" int f16_norm_sums(const float* x, int64_t B, int D, int64_t ldx, double* sums, double* scratch,
+                             int64_t scratch_doubles, f16_stream_t stream) {
+  if (!x || !sums || !scratch || B <= 0 || D <= 0 || ldx < D) return F16_ERR_ARG;
+  int nblk = (int)((B + ro::NORM_ROWS_PER_BLOCK - 1) / ro::NORM_ROWS_PER_BLOCK);
+  if (scratch_doubles < (int64_t)nblk * D * 2) return F16_ERR_TOO_LARGE;
+  if (!aligned(scratch, 16) || !aligned(sums, 16)) return F16_ERR_ALIGN;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  double2* part = reinterpret_cast<double2*>(scratch);
+  ro::k_norm_partial<<<nblk, ro::NORM_THREADS, 0, s>>>(x, B, D, ldx, part);
+  ro::k_norm_reduce<<<(D + ro::NORM_THREADS - 1) / ro::NORM_THREADS, ro::NORM_THREADS, 0, s>>>(
+      part, nblk, D, reinterpret_cast<double2*>(sums));
+  return launch_status();
+}
+
+extern "C" int f16_norm_merge_sums(const double* sums, int64_t B_total, int D, float* mean, float* var,
+                                   float* count, f16_stream_t stream) {
+  if (!sums || !mean || !var || !count || B_total <= 0 || D <= 0) return F16_ERR_ARG;
+  if (!aligned(sums, 16)) return F16_ERR_ALIGN;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  ro::k_norm_merge<<<(D + ro::NORM_THREADS - 1) / ro::NORM_THREADS, ro::NORM_THREADS, 0, s>>>(
+      reinterpret_cast<const double2*>(sums), 1, B_total, D, mean, var, count);
+  ro::k_norm_count<<<1, 32, 0, s>>>(count, B_total);
   return launch_status();
 }
 

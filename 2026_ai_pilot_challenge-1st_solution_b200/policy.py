@@ -30,7 +30,8 @@ class PolicyArgs(C.Structure):
                 ("group_end", C.POINTER(C.c_int64)), ("group_net", C.POINTER(C.c_int)), ("nets_per_group", C.c_int),
                 ("bins", C.c_void_p), ("bins_stride", C.c_int64), ("bins_offset", C.c_int), ("act_idx", C.c_void_p),
                 ("logp", C.c_void_p), ("value", C.c_void_p), ("logits", C.c_void_p), ("logits_ld", C.c_int64),
-                ("seed", C.c_uint64), ("step", C.c_uint64), ("deterministic", C.c_int), ("err", C.c_void_p)]
+                ("seed", C.c_uint64), ("step", C.c_uint64), ("deterministic", C.c_int), ("err", C.c_void_p),
+                ("cmd", C.c_void_p), ("cmd_stride", C.c_int64), ("cmd_offset", C.c_int), ("grid", C.c_void_p)]
 
 
 class MlpWeights:
@@ -53,6 +54,19 @@ class MlpWeights:
             raise ValueError(f"unsupported activation(s): {acts}")
         return cls([l.weight.to(device) for l in linears], [l.bias.to(device) for l in linears], act, head,
                    act_dim, num_bins)
+
+    @torch.no_grad()
+    def load_from(self, seq):
+        """Copy a same-shaped stack's current parameters into these buffers in place (after an
+        optimiser step): the device addresses, hence the registered tensor maps, stay valid."""
+        linears = [m for m in seq if isinstance(m, torch.nn.Linear)]
+        if len(linears) != len(self.weights):
+            raise ValueError("layer count differs from the registered network")
+        for w, b, lin in zip(self.weights, self.biases, linears):
+            if tuple(w.shape) != tuple(lin.weight.shape):
+                raise ValueError("layer shape differs from the registered network")
+            w.copy_(lin.weight)
+            b.copy_(lin.bias)
 
     def desc(self):
         d = MlpDesc()
@@ -92,8 +106,12 @@ class PolicySet:
             pass
 
     def forward(self, x_bf16, groups, nets_per_group=1, bins=None, bins_stride=4, bins_offset=0, act_idx=None,
-                logp=None, value=None, logits=None, seed=0, step=0, deterministic=False):
-        """groups: list of (row_end, [net indices]) with every group starting at a multiple of 128."""
+                logp=None, value=None, logits=None, seed=0, step=0, deterministic=False, cmd=None, cmd_stride=4,
+                cmd_offset=0, grid=None):
+        """groups: list of (row_end, [net indices]) with every group starting at a multiple of 128.
+
+        ``cmd`` (fp64, optional) receives action_to_env of the sampled bins at
+        ``cmd[r * cmd_stride + cmd_offset + c]`` using the fp32 ``grid`` (num_bins values)."""
         _lib.require_cuda_tensor(x_bf16, torch.bfloat16, None, "policy input", None)
         rows, ldx = x_bf16.shape[0], x_bf16.stride(0)
         ends = (C.c_int64 * len(groups))(*[int(g[0]) for g in groups])
@@ -114,6 +132,13 @@ class PolicySet:
         a.logits_ld = logits.stride(0) if logits is not None else 0
         a.seed = seed & (2 ** 64 - 1); a.step = step & (2 ** 64 - 1); a.deterministic = int(bool(deterministic))
         a.err = self.err.data_ptr()
+        if cmd is not None:
+            _lib.require_cuda_tensor(cmd, torch.float64, None, "env commands", x_bf16.device)
+            _lib.require_cuda_tensor(grid, torch.float32, None, "action grid", x_bf16.device)
+            a.cmd = cmd.data_ptr(); a.cmd_stride = cmd_stride; a.cmd_offset = cmd_offset
+            a.grid = grid.contiguous().data_ptr() if grid.is_contiguous() else None
+            if a.grid is None:
+                raise ValueError("action grid must be contiguous")
         _lib.check(self.lib.f16_policy_forward(self.handle, C.byref(a), _lib.stream_of(x_bf16)), "f16_policy_forward")
 
     def check_error(self):

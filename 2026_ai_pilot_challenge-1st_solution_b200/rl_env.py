@@ -256,9 +256,15 @@ class GpuDogfightVecEnv:
         return term, trunc
 
     # ---- step (rl_env.py:499-555) ----
+    @property
+    def action_buffer(self):
+        """The (nac, 4) fp64 command buffer ``step`` reads; a policy may write commands into it
+        directly (f16_policy_forward's cmd output) and pass it back to ``step`` uncopied."""
+        return self._actions
+
     def step(self, actions, *, reset_indices=None):
-        a = self._to_nac4(actions)
-        self._actions.copy_(a)
+        if actions is not self._actions:
+            self._actions.copy_(self._to_nac4(actions))
         if self.ic_pool is None:
             self._ensure_ic_pool()
         sim = self.sim

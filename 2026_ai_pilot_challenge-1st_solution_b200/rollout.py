@@ -47,15 +47,35 @@ class RunningNorm:
         return x if x.stride(1) == 1 else x.contiguous()
 
     @torch.no_grad()
-    def update(self, x):
+    def update(self, x, group=None):
+        """Merge the batch x into the running statistics.  With a torch.distributed ``group`` of
+        more than one rank the batch is the union of every rank's x (per-feature fp64 sums are
+        all-reduced before the merge; every rank must pass the same number of rows), so all ranks
+        keep the same normaliser."""
         x = self._x(x)
         B = x.shape[0]
         need = int(self.lib.f16_norm_scratch_doubles(B, self.dim))
         if self._scratch is None or self._scratch.numel() < need:
             self._scratch = torch.empty(need, dtype=torch.float64, device=self.device)
-        _lib.check(self.lib.f16_norm_update(_lib.ptr(x), B, self.dim, x.stride(0), _lib.ptr(self.mean),
-                                            _lib.ptr(self.var), _lib.ptr(self.count), _lib.ptr(self._scratch),
-                                            self._scratch.numel(), _lib.stream_of(x)), "f16_norm_update")
+        stream = _lib.stream_of(x)
+        world = 1
+        if group is not None:
+            import torch.distributed as dist
+            world = dist.get_world_size(group)
+        if world == 1:
+            _lib.check(self.lib.f16_norm_update(_lib.ptr(x), B, self.dim, x.stride(0), _lib.ptr(self.mean),
+                                                _lib.ptr(self.var), _lib.ptr(self.count), _lib.ptr(self._scratch),
+                                                self._scratch.numel(), stream), "f16_norm_update")
+            return
+        import torch.distributed as dist
+        sums = torch.empty(self.dim * 2, dtype=torch.float64, device=self.device)
+        _lib.check(self.lib.f16_norm_sums(_lib.ptr(x), B, self.dim, x.stride(0), _lib.ptr(sums),
+                                          _lib.ptr(self._scratch), self._scratch.numel(), stream), "f16_norm_sums")
+        dist.all_reduce(sums, group=group)
+        total = B * world                       # every rank holds the same number of environments
+        _lib.check(self.lib.f16_norm_merge_sums(_lib.ptr(sums), total, self.dim, _lib.ptr(self.mean),
+                                                _lib.ptr(self.var), _lib.ptr(self.count), stream),
+                   "f16_norm_merge_sums")
 
     @torch.no_grad()
     def normalize(self, x, out=None):

@@ -48,8 +48,9 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--e2e-steps", type=int, default=100)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", default="fdm", choices=["fdm", "obs"],
-                   help="fdm = configs[1] headline (default); obs = configs[2] fused obs/reward kernel")
+    p.add_argument("--workload", default="fdm", choices=["fdm", "obs", "rollout"],
+                   help="fdm = configs[1] headline (default); obs = configs[2] fused obs/reward kernel; "
+                        "rollout = configs[3] full 64-step rollout (env + obs/reward + actor/critic/opponents + GAE)")
     return p.parse_args()
 
 
@@ -305,6 +306,195 @@ def run_obs(args, dev, world, rank):
     return 0
 
 
+ROLL_NENV = 131_072
+ROLL_T = 64
+ROLL_OPP = 8
+ACTOR_FLOP = 2 * (184 * 512 + 512 * 512 + 512 * 84)      # per row, true layer sizes
+CRITIC_FLOP = 2 * (184 * 512 + 512 * 512 + 512 * 1)
+
+
+def _cpu_rollout_rate(model, nthreads):
+    """Reference CPU composition for one env-decision: host-C fdm.cuh (oracle/_ref, all threads,
+    2 aircraft x 6 frames) + the reference's fp32 torch actor, critic and one opponent actor on
+    all threads.  The obs/reward step is not included (stated in the sample)."""
+    import torch
+    fr, thr, _, kind = cpu_reference_rate(nsample_per_thread=128, min_seconds=3.0, lineage="r36")
+    torch.set_num_threads(nthreads)
+    x = torch.randn(4096, 184)
+    m = model.cpu()
+    with torch.no_grad():
+        m.actor_logits(x); m.critic(x)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 3.0:
+            m.actor_logits(x); m.critic(x); m.actor_logits(x)
+            reps += 1
+        mlp_s = (time.perf_counter() - t0) / (reps * 4096)
+    fdm_s = 12.0 / fr
+    return 1.0 / (fdm_s + mlp_s), thr, kind, (f"fdm.cuh on {thr} threads ({fr:.3g} frames/s, 12 frames per env-decision) "
+                                             f"+ torch fp32 actor+critic+opponent on {nthreads} threads "
+                                             f"({mlp_s * 1e6:.2f} us per env-decision, 4096-row batches); "
+                                             f"obs/reward excluded")
+
+
+def run_rollout(args, dev, world, rank):
+    """the full rollout on 131,072 envs per GPU, T = 64 decisions (384 frames):
+    RunningNorm, tcgen05 actor (sample + log-prob + env commands) and critic in one launch,
+    8 frozen opponents on contiguous env blocks in one grouped launch, FDM + fused post-step,
+    rollout bookkeeping, bootstrap value and GAE.  One bench step = one rollout."""
+    import torch
+    import torch.distributed as dist
+    tr = importlib.import_module(PKG + ".trainer")
+    rl_env = importlib.import_module(PKG + ".rl_env")
+    pg = dist.group.WORLD if world > 1 else None
+    env = rl_env.GpuDogfightVecEnv(ROLL_NENV, substeps=SUBSTEPS, seed=20260104 + rank, device=dev)
+    cfg = tr.PPOConfig(rollout_steps=ROLL_T, gamma=0.99, gae_lambda=0.95, hidden=(512, 512), activation="relu",
+                       seed=20260104)
+    opps = []
+    for i in range(ROLL_OPP):
+        torch.manual_seed(i + 1)
+        opps.append(tr.Opponent(tr.MLPActorCritic(hidden=(512, 512), activation="relu").to(dev)))
+    torch.manual_seed(0)
+    model = tr.MLPActorCritic(hidden=(512, 512), activation="relu")
+    t = tr.PPOTrainer(env, cfg, model=model, opponents=opps, opp_mode="blocks", group=pg)
+    t.reset(stagger=False)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    K, W = args.steps, max(3, args.warmup)
+    for _ in range(W):
+        t.collect_rollout()
+    torch.cuda.synchronize(dev)
+
+    # per-phase device times over one extra (untimed) rollout, events on the launching stream
+    phases = {}
+
+    def timed(name, fn):
+        def wrap(*a, **k):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            r = fn(*a, **k)
+            e1.record(stream)
+            phases.setdefault(name, []).append((e0, e1))
+            return r
+        return wrap
+
+    orig = (t.policy.forward, t.env.step, t.norm.update)
+    main_fwd = timed("policy_forward", orig[0])
+    t.policy.forward = main_fwd
+    t.env.step = timed("env_step", orig[1])
+    t.norm.update = timed("norm_update", orig[2])
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(stream)
+    t.collect_rollout()
+    r1.record(stream)
+    torch.cuda.synchronize(dev)
+    t.policy.forward, t.env.step, t.norm.update = orig
+    fw = phases["policy_forward"]
+    # per decision: [main actor+critic, opponents], then the final bootstrap critic call
+    main_ms = float(np.mean([a.elapsed_time(b) for a, b in fw[0:2 * ROLL_T:2]]))
+    opp_ms = float(np.mean([a.elapsed_time(b) for a, b in fw[1:2 * ROLL_T:2]]))
+    breakdown = {"rollout_ms": r0.elapsed_time(r1),
+                 "per_decision_ms": {"main_actor_critic_mlp": main_ms, "opponents_mlp": opp_ms,
+                                     "env_step": float(np.mean([a.elapsed_time(b) for a, b in phases["env_step"]])),
+                                     "norm_update": float(np.mean([a.elapsed_time(b)
+                                                                   for a, b in phases["norm_update"]]))}}
+    pd = breakdown["per_decision_ms"]
+    pd["other"] = breakdown["rollout_ms"] / ROLL_T - sum(pd.values())
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    wall0 = time.perf_counter()
+    with ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0")))) as clk:
+        for k in range(K):
+            flush.zero_()
+            starts[k].record(stream)
+            t.collect_rollout()
+            ends[k].record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    wall = time.perf_counter() - wall0
+    ms = torch.tensor([float(np.mean([a.elapsed_time(b) for a, b in zip(starts, ends)]))], dtype=torch.float64,
+                      device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    units = ROLL_NENV * ROLL_T
+    value = world * units / (ms * 1e-3)
+
+    # e2e through the public API: learner parameters arrive from host memory (an update's
+    # output), are loaded and refreshed into the kernel, one rollout runs, and its statistics and
+    # advantages / returns go back to host memory.
+    host_params = [p.detach().cpu().pin_memory() for p in t.model.parameters()]
+    host_adv = torch.empty(ROLL_T, ROLL_NENV, dtype=torch.float32).pin_memory()
+    host_ret = torch.empty_like(host_adv).pin_memory()
+    h2d = sum(p.numel() * 4 for p in host_params)
+    d2h = 2 * ROLL_T * ROLL_NENV * 4
+    Ke = max(1, min(args.e2e_steps, 3))
+    es = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(Ke)]
+    for e0, e1 in es:
+        flush.zero_()
+        e0.record(stream)
+        with torch.no_grad():
+            for p, h in zip(t.model.parameters(), host_params):
+                p.copy_(h, non_blocking=True)
+        t.refresh_policy()
+        adv, ret, stats = t.collect_rollout()
+        host_adv.copy_(adv, non_blocking=True)
+        host_ret.copy_(ret, non_blocking=True)
+        _ = {k: float(v.sum()) for k, v in stats.items()}
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e_ms = torch.tensor([float(np.mean([a.elapsed_time(b) for a, b in es]))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+
+    peak = measured_peaks().get("bf16_tflops_sustained")
+    achieved = (ACTOR_FLOP + CRITIC_FLOP) * ROLL_NENV / (main_ms * 1e-3) / 1e12
+    # this library's kernels per rollout: per decision the norm update (3 kernels; 4 when the
+    # statistics are all-reduced), normalise, actor+critic, opponents, FDM, post-step; then
+    # normalise + bootstrap critic + GAE
+    launches_per_rollout = ROLL_T * ((4 if world > 1 else 3) + 5) + 3
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            v, thr, kind, sample = _cpu_rollout_rate(tr.MLPActorCritic(hidden=(512, 512), activation="relu"),
+                                                      os.cpu_count() or 1)
+            cpu = {"value": v, "unit": "decision-steps/s", "cores": thr, "kind": kind, "sample": sample}
+        line = {"metric": "decision-steps/s (env step + obs/reward + actor sample)", "value": value,
+                "unit": "decision-steps/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64+bf16",
+                "data": "synthetic ICs, random-init networks",
+                "config": {"workload": "configs[3]: full rollout, 131,072 envs per GPU, T=64 (384 FDM frames), "
+                                       "actor 184-512-512-84 ReLU bf16 with fused sampling, critic 184-512-512-1, "
+                                       "8 frozen opponents on env blocks, GAE 0.99/0.95",
+                           "envs_per_gpu": ROLL_NENV, "rollout_steps": ROLL_T, "step": "one rollout",
+                           "parallelism": f"env-shard x{world}" + (" + NCCL RunningNorm allreduce" if world > 1 else ""),
+                           "l2": "flushed between rollouts; per-decision working set (212 MB state) > L2",
+                           "breakdown": breakdown, "timed_region_wall_s": wall},
+                "e2e": {"value": world * units / (float(e_ms.item()) * 1e-3), "unit": "decision-steps/s",
+                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "api": "PPOTrainer: host parameters -> refresh_policy -> collect_rollout -> adv/ret to host",
+                        "steps": Ke},
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                             "frac": achieved / peak if peak else None, "traffic": None,
+                             "kernel": "k_policy (main actor + critic, one launch per decision)",
+                             "flop_per_unit": ACTOR_FLOP + CRITIC_FLOP, "unit_basis": "env-decision",
+                             "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (measured)"},
+                "gpu_launches": K * launches_per_rollout, "clocks": clk.summary()}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     try:
@@ -330,6 +520,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     if args.workload == "obs":
         return run_obs(args, dev, world, rank)
+    if args.workload == "rollout":
+        return run_rollout(args, dev, world, rank)
 
     _lib = importlib.import_module(PKG + "._lib")
     ge = importlib.import_module(PKG + ".gpu_env")

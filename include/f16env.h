@@ -254,6 +254,14 @@ typedef struct {
   uint64_t seed, step;      /* RNG key of this call */
   int deterministic;        /* 1: argmax (the reference's deterministic=True / sample=False) */
   int* err;                 /* optional device int: set non-zero if a bounded wait timed out */
+  /* optional env commands of the sampled bins, action_to_env (ppo_gpu.py:361-369) fused:
+   * cmd[r*cmd_stride + cmd_offset + c] = (double)grid[bin] for c < 3 and
+   * (double)(0.5f*grid[bin] + 0.5f) for the throttle channel c = 3 (fp32 arithmetic, as the
+   * reference's float32 action tensor).  grid: device fp32 [num_bins] (torch.linspace). */
+  double* cmd;
+  int64_t cmd_stride;
+  int cmd_offset;
+  const float* grid;
 } f16_policy_args;
 
 int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args* args, f16_stream_t stream);
@@ -274,6 +282,17 @@ int f16_gae(const float* rew, const float* val, const float* done, const float* 
 int f16_norm_update(const float* x, int64_t B, int D, int64_t ldx, float* mean, float* var, float* count,
                     double* scratch, int64_t scratch_doubles, f16_stream_t stream);
 int64_t f16_norm_scratch_doubles(int64_t B, int D);
+
+/* The same update split in two around a cross-rank reduction (no counterpart in the reference,
+ * which is single-GPU): f16_norm_sums writes sums [D][2] fp64 (sum, sum of squares of each
+ * feature over this rank's B rows, 16-byte aligned); after an allreduce-sum of sums over the
+ * ranks, f16_norm_merge_sums merges the global batch of B_total rows into mean / var / count,
+ * so every rank holds the same normaliser.  On one rank the pair equals f16_norm_update bit
+ * for bit. */
+int f16_norm_sums(const float* x, int64_t B, int D, int64_t ldx, double* sums, double* scratch,
+                  int64_t scratch_doubles, f16_stream_t stream);
+int f16_norm_merge_sums(const double* sums, int64_t B_total, int D, float* mean, float* var,
+                        float* count, f16_stream_t stream);
 
 /* f16_norm_update without a caller scratch buffer (no counterpart in the reference).  For hosts
  * that may not allocate device memory inside their step loop (a sealed memory pool or arena):

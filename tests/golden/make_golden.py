@@ -12,6 +12,8 @@ fdm_cfg1.npz  BASELINE configs[0]: 64 envs x 2 F-16s, seeded ICs (altitude U(6,9
               repository-root lineage, FCS dt 1/120).
 fdm_r36.npz   the same ICs (first 16 envs) through the research/competition_36500 lineage
               (FCS dt 1/60) seed builder and fdm.cuh, 60 frames.
+obs_traj.npz, gae.npz, norm.npz, ppo_update.npz: see make_obs_golden, make_gae_golden,
+              make_norm_golden and make_ppo_golden below.
 """
 import importlib
 import os
@@ -24,6 +26,7 @@ ROOT = Path(__file__).resolve().parents[2]
 REF = Path(os.environ.get("F16_REFERENCE", "/root/reference"))
 OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(OUT))
 
 from oracle import fdm as ofdm  # noqa: E402
 
@@ -286,8 +289,42 @@ def norm_inputs(seed):
     return xs
 
 
+def make_ppo_golden(seed=20260106):
+    """ppo_update.npz: the reference's own PPOGPUTrainer.update (R/cuda_fdm/ppo_gpu.py:2020-2144,
+    MLP path, aux_pred off) run on CPU over a seeded 4 x 48 rollout of a (32, 32) tanh
+    MLPActorCritic; stores the parameters after the update and the returned statistics."""
+    import types
+    import torch
+    r36 = REF / "research" / "competition_36500" / "runtime"
+    for k in list(sys.modules):
+        if k == "cuda_fdm" or k.startswith("cuda_fdm.") or k == "claude_code" or k.startswith("claude_code."):
+            del sys.modules[k]
+    sys.path.insert(0, str(r36))
+    import cuda_fdm.ppo_gpu as P
+    from ppo_case import PPO_CFG, PPO_HIDDEN, ppo_inputs
+    torch.manual_seed(seed)
+    model = P.MLPActorCritic(184, 4, 21, hidden=PPO_HIDDEN, activation="tanh")
+    init = torch.cat([p.detach().reshape(-1) for p in model.parameters()]).double()
+    obs, act, old_logp, b_val, adv, ret = ppo_inputs(model, seed)
+    cfg = P.PPOGPUConfig(device="cpu", aux_pred=False, hidden=PPO_HIDDEN, activation="tanh", **PPO_CFG)
+    fake = types.SimpleNamespace(cfg=cfg, model=model, b_obs=obs, b_act=act, b_logp=old_logp, b_val=b_val,
+                                 actor_opt=torch.optim.Adam(model.actor_parameters(), lr=cfg.lr, eps=1e-5),
+                                 critic_opt=torch.optim.Adam(model.critic_parameters(), lr=cfg.lr, eps=1e-5))
+    torch.manual_seed(seed + 1)
+    res = P.PPOGPUTrainer.update(fake, adv, ret)
+    out = {"seed": np.array(seed), "init_sum": np.array([float(init.sum()), float(init.abs().sum())]),
+           "params": torch.cat([p.detach().reshape(-1) for p in model.parameters()]).numpy()}
+    for k in ("pl", "vl", "ent", "kl", "cf", "ev", "actor_grad_norm", "critic_grad_norm"):
+        out[k] = np.array(float(res[k]))
+    out["epochs"] = np.array(res["epochs"]); out["early"] = np.array(bool(res["early"]))
+    out["optimizer_steps"] = np.array(res["optimizer_steps"])
+    np.savez_compressed(OUT / "ppo_update.npz", **out)
+    print("ppo_update.npz", res["epochs"], res["early"], res["optimizer_steps"])
+
+
 if __name__ == "__main__":
     main()
     make_obs_golden()
     make_gae_golden()
     make_norm_golden()
+    make_ppo_golden()
