@@ -40,6 +40,20 @@ class Origin(C.Structure):
     _fields_ = [(n, C.c_double) for n in ("ox", "oy", "oz", "slat", "clat", "slon", "clon")]
 
 
+class FdmIO(C.Structure):
+    """f16_fdm_io (include/f16env.h)."""
+    _fields_ = [("cmd", C.c_void_p), ("bins", C.c_void_p), ("grid_host", C.c_void_p), ("num_bins", C.c_int),
+                ("obs17", C.c_void_p), ("finite", C.c_void_p)]
+
+
+class RecordArgs(C.Structure):
+    """f16_record_args (include/f16env.h)."""
+    _fields_ = [("reward", C.c_void_p), ("done", C.c_void_p), ("terminal_hp", C.c_void_p),
+                ("terminal_alt", C.c_void_p), ("opp_row", C.c_void_p), ("n_opp", C.c_int), ("min_alt", C.c_double),
+                ("finite", C.c_void_p), ("b_rew", C.c_void_p), ("next_done", C.c_void_p), ("ep_ret", C.c_void_p),
+                ("ep_len", C.c_void_p), ("stats", C.c_void_p)]
+
+
 _PR = C.POINTER(Recon)
 _PC = C.POINTER(RewardCfg)
 _PO = C.POINTER(Origin)
@@ -66,6 +80,8 @@ _SIGS = {
                        C.c_int),
     "f16_fdm_step": ([_P, C.c_int, _I64, _I64, _P, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_fdm_step_bins": ([_P, C.c_int, _I64, _I64, _P, _P, C.c_int, C.c_int, C.c_double, _P, _P], C.c_int),
+    "f16_fdm_step_ex": ([_P, C.c_int, _I64, _I64, C.POINTER(FdmIO), C.c_int, C.c_double, _P], C.c_int),
+    "f16_rollout_record": ([_I64, C.POINTER(RecordArgs), _P], C.c_int),
     "f16_seed_ic": ([_P, _I64, _P, C.c_int, _I64, C.c_double, _P], C.c_int),
     "f16_probe_fp64": ([_P, _I64, C.c_int, C.POINTER(C.c_double), _P], C.c_int),
     "f16_version": ([], C.c_char_p),

@@ -63,53 +63,72 @@ __device__ __forceinline__ void load_state(const StateRef<LAYOUT>& R, int64_t a,
   for (int i = 0; i < 6; i++) s.kin[i] = R(a, F16_S_KIN + i);
 }
 
+// Non-finite test on the exponent bits (all-ones exponent = inf or NaN); `bad` ORs it up.
+__device__ __forceinline__ double fin(double v, unsigned& bad) {
+  bad |= (unsigned)((__double2hiint(v) & 0x7ff00000) == 0x7ff00000);
+  return v;
+}
+
 template <int LAYOUT>
-__device__ __forceinline__ void store_state(const StateRef<LAYOUT>& R, int64_t a, const Ac& s) {
+__device__ __forceinline__ void store_state(const StateRef<LAYOUT>& R, int64_t a, const Ac& s, unsigned& bad) {
 #pragma unroll
   for (int i = 0; i < 3; i++) {
-    R(a, F16_S_POS + i) = s.pos[i];
-    R(a, F16_S_VEL + i) = s.vel[i];
-    R(a, F16_S_PQRI + i) = s.pqri[i];
-    R(a, F16_S_UVWIDOT + i) = s.uvwidot[i];
-    R(a, F16_S_PQRIDOT + i) = s.pqridot[i];
-    R(a, F16_S_PREV_BACC + i) = s.pbacc[i];
-    R(a, F16_S_PREV_PQRIDOT + i) = s.ppqridot[i];
-    R(a, F16_S_PREV_PQRI + i) = s.ppqri[i];
+    R(a, F16_S_POS + i) = fin(s.pos[i], bad);
+    R(a, F16_S_VEL + i) = fin(s.vel[i], bad);
+    R(a, F16_S_PQRI + i) = fin(s.pqri[i], bad);
+    R(a, F16_S_UVWIDOT + i) = fin(s.uvwidot[i], bad);
+    R(a, F16_S_PQRIDOT + i) = fin(s.pqridot[i], bad);
+    R(a, F16_S_PREV_BACC + i) = fin(s.pbacc[i], bad);
+    R(a, F16_S_PREV_PQRIDOT + i) = fin(s.ppqridot[i], bad);
+    R(a, F16_S_PREV_PQRI + i) = fin(s.ppqri[i], bad);
   }
 #pragma unroll
   for (int i = 0; i < 4; i++) {
-    R(a, F16_S_Q + i) = s.q[i];
-    R(a, F16_S_QDOT + i) = s.qdot[i];
-    R(a, F16_S_ENG + i) = s.eng[i];
+    R(a, F16_S_Q + i) = fin(s.q[i], bad);
+    R(a, F16_S_QDOT + i) = fin(s.qdot[i], bad);
+    R(a, F16_S_ENG + i) = fin(s.eng[i], bad);
   }
-  R(a, F16_S_EPA) = s.epa;
-  R(a, F16_S_FUEL) = s.fuel;
+  R(a, F16_S_EPA) = fin(s.epa, bad);
+  R(a, F16_S_FUEL) = fin(s.fuel, bad);
 #pragma unroll
   for (int i = 0; i < 9; i++) {
-    R(a, F16_S_PREV_AUX + i) = s.pa[i];
-    R(a, F16_S_PID + i) = s.pid[i];
+    R(a, F16_S_PREV_AUX + i) = fin(s.pa[i], bad);
+    R(a, F16_S_PID + i) = fin(s.pid[i], bad);
   }
 #pragma unroll
-  for (int i = 0; i < 6; i++) R(a, F16_S_KIN + i) = s.kin[i];
+  for (int i = 0; i < 6; i++) R(a, F16_S_KIN + i) = fin(s.kin[i], bad);
+}
+
+template <int LAYOUT>
+__device__ __forceinline__ void store_state(const StateRef<LAYOUT>& R, int64_t a, const Ac& s) {
+  unsigned bad = 0;
+  store_state(R, a, s, bad);
 }
 
 // Store the values pushed into the four integrator histories in frame i into the deque slot
 // j = substeps-1-i they occupy when the launch ends (only slots j <= 2 exist).
 template <int LAYOUT>
-__device__ __forceinline__ void store_history(const StateRef<LAYOUT>& R, int64_t a, int j, const Ac& s) {
+__device__ __forceinline__ void store_history(const StateRef<LAYOUT>& R, int64_t a, int j, const Ac& s,
+                                              unsigned& bad) {
 #pragma unroll
-  for (int i = 0; i < 4; i++) R(a, F16_S_DEQ_Q + 4 * j + i) = s.qdot[i];
+  for (int i = 0; i < 4; i++) R(a, F16_S_DEQ_Q + 4 * j + i) = fin(s.qdot[i], bad);
 #pragma unroll
   for (int i = 0; i < 3; i++) {
-    R(a, F16_S_DEQ_PQRI + 3 * j + i) = s.pqridot[i];
-    R(a, F16_S_DEQ_IVEL + 3 * j + i) = s.vel[i];
-    R(a, F16_S_DEQ_UVWIDOT + 3 * j + i) = s.uvwidot[i];
+    R(a, F16_S_DEQ_PQRI + 3 * j + i) = fin(s.pqridot[i], bad);
+    R(a, F16_S_DEQ_IVEL + 3 * j + i) = fin(s.vel[i], bad);
+    R(a, F16_S_DEQ_UVWIDOT + 3 * j + i) = fin(s.uvwidot[i], bad);
   }
+}
+
+template <int LAYOUT>
+__device__ __forceinline__ void store_history(const StateRef<LAYOUT>& R, int64_t a, int j, const Ac& s) {
+  unsigned bad = 0;
+  store_history(R, a, j, s, bad);
 }
 
 // With fewer than 3 frames per launch the oldest surviving slots are the old ones shifted.
 template <int LAYOUT>
-__device__ __forceinline__ void shift_old_history(const StateRef<LAYOUT>& R, int64_t a, int substeps) {
+__device__ __forceinline__ void shift_old_history(const StateRef<LAYOUT>& R, int64_t a, int substeps, unsigned& bad) {
   if (substeps >= 3) return;
   double q0[4], q1[4], p0[3], p1[3], v0[3], v1[3], u0[3], u1[3];
 #pragma unroll
@@ -124,12 +143,12 @@ __device__ __forceinline__ void shift_old_history(const StateRef<LAYOUT>& R, int
   for (int j = substeps; j <= 2; j++) {
     int o = j - substeps;
 #pragma unroll
-    for (int i = 0; i < 4; i++) R(a, F16_S_DEQ_Q + 4 * j + i) = o == 0 ? q0[i] : q1[i];
+    for (int i = 0; i < 4; i++) R(a, F16_S_DEQ_Q + 4 * j + i) = fin(o == 0 ? q0[i] : q1[i], bad);
 #pragma unroll
     for (int i = 0; i < 3; i++) {
-      R(a, F16_S_DEQ_PQRI + 3 * j + i) = o == 0 ? p0[i] : p1[i];
-      R(a, F16_S_DEQ_IVEL + 3 * j + i) = o == 0 ? v0[i] : v1[i];
-      R(a, F16_S_DEQ_UVWIDOT + 3 * j + i) = o == 0 ? u0[i] : u1[i];
+      R(a, F16_S_DEQ_PQRI + 3 * j + i) = fin(o == 0 ? p0[i] : p1[i], bad);
+      R(a, F16_S_DEQ_IVEL + 3 * j + i) = fin(o == 0 ? v0[i] : v1[i], bad);
+      R(a, F16_S_DEQ_UVWIDOT + 3 * j + i) = fin(o == 0 ? u0[i] : u1[i], bad);
     }
   }
 }
@@ -138,7 +157,7 @@ template <int LAYOUT, bool BINS>
 __global__ void __launch_bounds__(FDM_THREADS, FDM_MIN_BLOCKS)
 k_fdm_step(double* __restrict__ st, int64_t ld, int64_t nac, const double* __restrict__ cmd,
            const uint8_t* __restrict__ bins, const BinGrid grid, int substeps, double fcs_dt,
-           double* __restrict__ obs17) {
+           double* __restrict__ obs17, uint8_t* __restrict__ finite) {
   extern __shared__ double S[];
   stage_tables(S);
   const double inv_fcs_dt = 1.0 / fcs_dt;
@@ -156,19 +175,21 @@ k_fdm_step(double* __restrict__ st, int64_t ld, int64_t nac, const double* __res
       c0 = x.x; c1 = x.y; c2 = y.x; c3 = y.y;
     }
     Ac s;
+    unsigned bad = 0;                       // any stored state value non-finite
     load_state(R, a, s);
-    shift_old_history(R, a, substeps);
+    shift_old_history(R, a, substeps, bad);
     FrameOut out;
     for (int i = 0; i < substeps - 1; i++) {
       int j = substeps - 1 - i;
-      if (j <= 2) store_history(R, a, j, s);
+      if (j <= 2) store_history(R, a, j, s, bad);
       propagate(s);
       dynamics<false>(S, s, c0, c1, c2, c3, fcs_dt, inv_fcs_dt, gear, out);
     }
-    store_history(R, a, 0, s);
+    store_history(R, a, 0, s, bad);
     propagate(s);
     dynamics<true>(S, s, c0, c1, c2, c3, fcs_dt, inv_fcs_dt, gear, out);
-    store_state(R, a, s);
+    store_state(R, a, s, bad);
+    if (finite) finite[a] = bad ? 0 : 1;
     if (obs17) {
       double* o = obs17 + 17 * a;
       o[0] = s.pos[0]; o[1] = s.pos[1]; o[2] = s.pos[2];
@@ -317,7 +338,7 @@ int persistent_grid(K kernel, int64_t nac, size_t smem) {
 
 template <int LAYOUT, bool BINS>
 int launch_step(double* st, int64_t ld, int64_t nac, const double* cmd, const uint8_t* bins, const BinGrid& g,
-                int substeps, double fcs_dt, double* obs17, cudaStream_t stream) {
+                int substeps, double fcs_dt, double* obs17, cudaStream_t stream, uint8_t* finite = nullptr) {
   auto k = k_fdm_step<LAYOUT, BINS>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -327,7 +348,7 @@ int launch_step(double* st, int64_t ld, int64_t nac, const double* cmd, const ui
     attr_set[dev] = true;
   }
   int grid = persistent_grid(k, nac, FDM_SMEM);
-  k<<<grid, FDM_THREADS, FDM_SMEM, stream>>>(st, ld, nac, cmd, bins, g, substeps, fcs_dt, obs17);
+  k<<<grid, FDM_THREADS, FDM_SMEM, stream>>>(st, ld, nac, cmd, bins, g, substeps, fcs_dt, obs17, finite);
   return launch_status();
 }
 
@@ -354,6 +375,37 @@ extern "C" int f16_fdm_step(double* state, int layout, int64_t ld, int64_t nac, 
   if (layout == F16_LAYOUT_SOA)
     return launch_step<F16_LAYOUT_SOA, false>(state, ld, nac, cmd, nullptr, g, substeps, fcs_dt, obs17, s);
   return launch_step<F16_LAYOUT_AOS, false>(state, ld, nac, cmd, nullptr, g, substeps, fcs_dt, obs17, s);
+}
+
+extern "C" int f16_fdm_step_ex(double* state, int layout, int64_t ld, int64_t nac, const f16_fdm_io* io,
+                               int substeps, double fcs_dt, f16_stream_t stream) {
+  int rc = check_state_args(state, layout, ld, nac);
+  if (rc) return rc;
+  if (!io || (!io->cmd == !io->bins) || substeps < 1 || !(fcs_dt > 0.0)) return F16_ERR_ARG;
+  if ((io->obs17 && !aligned(io->obs17, 8))) return F16_ERR_ALIGN;
+  BinGrid g{};
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (io->cmd) {
+    if (!aligned(io->cmd, 16)) return F16_ERR_ALIGN;
+    if (layout == F16_LAYOUT_SOA)
+      return launch_step<F16_LAYOUT_SOA, false>(state, ld, nac, io->cmd, nullptr, g, substeps, fcs_dt, io->obs17, s,
+                                                io->finite);
+    return launch_step<F16_LAYOUT_AOS, false>(state, ld, nac, io->cmd, nullptr, g, substeps, fcs_dt, io->obs17, s,
+                                              io->finite);
+  }
+  if (!io->grid_host || io->num_bins < 2 || io->num_bins > 64) return F16_ERR_ARG;
+  if (!aligned(io->bins, 4)) return F16_ERR_ALIGN;
+  for (int i = 0; i < io->num_bins; i++) {
+    float v = io->grid_host[i];
+    volatile float half_v = 0.5f * v;
+    g.ch[i] = (double)v;
+    g.thr[i] = (double)(half_v + 0.5f);
+  }
+  if (layout == F16_LAYOUT_SOA)
+    return launch_step<F16_LAYOUT_SOA, true>(state, ld, nac, nullptr, io->bins, g, substeps, fcs_dt, io->obs17, s,
+                                             io->finite);
+  return launch_step<F16_LAYOUT_AOS, true>(state, ld, nac, nullptr, io->bins, g, substeps, fcs_dt, io->obs17, s,
+                                           io->finite);
 }
 
 extern "C" int f16_fdm_step_bins(double* state, int layout, int64_t ld, int64_t nac, const uint8_t* bins,

@@ -131,10 +131,98 @@ k_norm_apply(const float* __restrict__ x, int64_t B, int D, int64_t ldx, const f
   }
 }
 
+// ---------------------------------------------------------------- rollout bookkeeping
+// One thread per environment, the per-step statistics of collect_rollout (ppo_gpu.py:1914-1960)
+// in one pass: rollout reward row, next-done flags, running episode return / length, and the
+// sums (episode return / length / count, wins, losses, hard-deck losses, opponent hard-deck
+// wins, per-opponent wins / losses / episodes).  Per-block sums go to fp64 global accumulators
+// with one atomic per block and statistic.
+constexpr int REC_THREADS = 256;
+constexpr int REC_MAX_OPP = 32;
+
+__global__ void __launch_bounds__(REC_THREADS)
+k_rollout_record(int64_t nenv, const double* __restrict__ reward, const uint8_t* __restrict__ done,
+                 const double* __restrict__ thp, const double* __restrict__ talt, const int64_t* __restrict__ opp,
+                 int n_opp, double min_alt, const uint8_t* __restrict__ finite, float* __restrict__ b_rew,
+                 float* __restrict__ next_done, float* __restrict__ ep_ret, float* __restrict__ ep_len,
+                 double* __restrict__ stats) {
+  __shared__ double red[7][REC_THREADS / 32];
+  __shared__ unsigned by_opp[3 * REC_MAX_OPP];
+  __shared__ unsigned any_bad;
+  for (int i = threadIdx.x; i < 3 * n_opp; i += blockDim.x) by_opp[i] = 0;
+  if (threadIdx.x == 0) any_bad = 0;
+  __syncthreads();
+  int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  double v[7] = {0, 0, 0, 0, 0, 0, 0};
+  if (e < nenv) {
+    const float r = (float)reward[2 * e];                 // reward[:, 0].float()
+    const bool d = done[e] != 0;
+    const float df = d ? 1.0f : 0.0f;
+    b_rew[e] = r;
+    next_done[e] = df;
+    const float er = __fadd_rn(ep_ret[e], r);             // ep_ret += raw_reward
+    const float el = __fadd_rn(ep_len[e], 1.0f);          // ep_len += 1.0
+    v[0] = (double)__fmul_rn(er, df);                     // (ep_ret * done_env).sum()
+    v[1] = (double)__fmul_rn(el, df);
+    v[2] = (double)df;
+    const float keep = __fsub_rn(1.0f, df);
+    ep_ret[e] = __fmul_rn(er, keep);
+    ep_len[e] = __fmul_rn(el, keep);
+    const double th0 = thp[2 * e], th1 = thp[2 * e + 1], ta0 = talt[2 * e], ta1 = talt[2 * e + 1];
+    const bool own_alt_dead = ta0 < min_alt;
+    const bool own_dead = (th0 <= 0.0) || own_alt_dead;
+    const bool opp_dead = (th1 <= 0.0) || (ta1 < min_alt);
+    const bool both_alive = !own_dead && !opp_dead;
+    const bool win = (opp_dead && !own_dead) || (both_alive && (th0 > th1 + 1e-9));
+    const bool loss = (own_dead && !opp_dead) || (both_alive && (th0 < th1 - 1e-9));
+    const bool dwin = win && d, dloss = loss && d;
+    v[3] = dwin; v[4] = dloss;
+    v[5] = loss && own_alt_dead && d;
+    v[6] = win && (ta1 < min_alt) && d;
+    if (opp) {
+      const int64_t g = opp[e];
+      if (g >= 0 && g < n_opp) {
+        if (dwin) atomicAdd(&by_opp[g], 1u);
+        if (dloss) atomicAdd(&by_opp[n_opp + g], 1u);
+        if (d) atomicAdd(&by_opp[2 * n_opp + g], 1u);
+      }
+    }
+    if (finite && !finite[e]) atomicOr(&any_bad, 1u);
+  }
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int k = 0; k < 7; k++) {
+    double x = v[k];
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    if (lane == 0) red[k][w] = x;
+  }
+  __syncthreads();
+  if (threadIdx.x < 7) {
+    double x = 0.0;
+    for (int i = 0; i < REC_THREADS / 32; i++) x += red[threadIdx.x][i];
+    if (x != 0.0) atomicAdd(&stats[threadIdx.x], x);
+  }
+  for (int i = threadIdx.x; i < 3 * n_opp; i += blockDim.x)
+    if (by_opp[i]) atomicAdd(&stats[8 + i], (double)by_opp[i]);
+  if (threadIdx.x == 0 && any_bad) stats[7] = 1.0;           // trajectory non-finite
+}
+
 }  // namespace ro
 }  // namespace f16
 
 using namespace f16;
+
+extern "C" int f16_rollout_record(int64_t nenv, const f16_record_args* a, f16_stream_t stream) {
+  if (!a || nenv <= 0 || !a->reward || !a->done || !a->terminal_hp || !a->terminal_alt || !a->b_rew ||
+      !a->next_done || !a->ep_ret || !a->ep_len || !a->stats)
+    return F16_ERR_ARG;
+  if (a->n_opp < 0 || a->n_opp > ro::REC_MAX_OPP || (a->opp_row && a->n_opp == 0)) return F16_ERR_ARG;
+  int grid = (int)((nenv + ro::REC_THREADS - 1) / ro::REC_THREADS);
+  ro::k_rollout_record<<<grid, ro::REC_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      nenv, a->reward, a->done, a->terminal_hp, a->terminal_alt, a->opp_row, a->n_opp, a->min_alt, a->finite,
+      a->b_rew, a->next_done, a->ep_ret, a->ep_len, a->stats);
+  return launch_status();
+}
 
 extern "C" int f16_gae(const float* rew, const float* val, const float* done, const float* last_val,
                        const float* next_done, int T, int64_t n, int64_t ld, double gamma, double lam, float* adv,

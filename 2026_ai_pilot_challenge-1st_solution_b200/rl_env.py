@@ -6,10 +6,12 @@ contract and return values.  Differences in *how*, not *what*:
 
 * IC pairs are drawn vectorised (same distributions as ``_sample_ic_pair``, :224-252) and
   seeded on the GPU (f16_seed_ic) instead of a per-aircraft CPU ``build_seed_vector``;
-* ``step`` runs the FDM kernel (no obs17 output) and then ONE fused kernel
+* ``step`` runs the FDM kernel (no obs17; it also flags non-finite aircraft, replacing a
+  torch.isfinite pass over the whole state) and then ONE fused kernel
   (f16_env_post_step) for advance + terminal observation + autoreset, instead of ~10 torch
   launches and a full clone; like the reference it never synchronises the host.
 """
+import ctypes as C
 import math
 
 import numpy as np
@@ -77,6 +79,7 @@ class GpuDogfightVecEnv:
         self._terminal_alt = torch.zeros(self.nac, dtype=torch.float64, device=dev)
         self._actions = torch.zeros(self.nac, 4, dtype=torch.float64, device=dev)
         self._s9 = torch.zeros(self.nac, 9, dtype=torch.float64, device=dev)
+        self._finite = torch.ones(self.nac, dtype=torch.uint8, device=dev)
         self.terminal_obs_enabled = True
 
     # ---- IC sampling (rl_env.py:224-252), vectorised ----
@@ -269,10 +272,11 @@ class GpuDogfightVecEnv:
             self._ensure_ic_pool()
         sim = self.sim
         sh = _lib.stream_of(sim.states_soa)
-        _lib.check(self.lib.f16_fdm_step(_lib.ptr(sim.states_soa), _lib.LAYOUT_SOA, self.nac, self.nac,
-                                         _lib.ptr(self._actions), self.substeps, sim.fcs_dt, None, sh),
-                   "f16_fdm_step")
-        terminal_state_finite = torch.isfinite(sim.states_soa).all(dim=0).view(self.nenv, 2).all(dim=1)
+        # physics; the same launch flags aircraft whose 101 state values are all finite
+        io = _lib.FdmIO(cmd=self._actions.data_ptr(), finite=self._finite.data_ptr())
+        _lib.check(self.lib.f16_fdm_step_ex(_lib.ptr(sim.states_soa), _lib.LAYOUT_SOA, self.nac, self.nac,
+                                            C.byref(io), self.substeps, sim.fcs_dt, sh), "f16_fdm_step_ex")
+        terminal_state_finite = self._finite.view(torch.bool).view(self.nenv, 2).all(dim=1)
         if reset_indices is None:
             pick = torch.randint(0, self.ic_pool_size, (self.nenv,), device=self.device)
         else:

@@ -21,14 +21,15 @@ benchmark configuration); ``opp_mode="pool"`` keeps a per-environment assignment
 episode ends from ``opp_weights`` (``_sample_opp``, :1306-1309) and regroups the rows each step
 (one small host transfer of the group sizes, as ``ActiveLeaguePool.act`` does, :879-880).
 """
+import ctypes as C
 import dataclasses
-import math
 from typing import Optional
 
 import numpy as np
 import torch
 import torch.nn as nn
 
+from . import _lib
 from .policy import HEAD_CATEGORICAL, HEAD_VALUE, MlpWeights, PolicySet
 from .rollout import RunningNorm, gae, make_action_grid
 
@@ -331,6 +332,8 @@ class PPOTrainer:
         self.last_value = torch.zeros(n, device=dev)
         self.ep_ret = torch.zeros(n, device=dev)
         self.ep_len = torch.zeros(n, device=dev)
+        self._stats = torch.zeros(8 + 3 * P, dtype=torch.float64, device=dev)
+        self._lib = _lib.load()
         self.global_step = 0
         self.decisions = 0
         self._key_main = _mix64((cfg.seed << 8) ^ (self.rank << 1))
@@ -338,6 +341,9 @@ class PPOTrainer:
         self.min_alt = env.min_altitude_m
         self._next_obs = self._next_opp_obs = None
         self._next_done = torch.zeros(n, device=dev)
+        self._rec = _lib.RecordArgs(n_opp=P, min_alt=float(self.min_alt), next_done=self._next_done.data_ptr(),
+                                    ep_ret=self.ep_ret.data_ptr(), ep_len=self.ep_len.data_ptr(),
+                                    stats=self._stats.data_ptr())
 
     # ---- weights ----
     def refresh_policy(self):
@@ -350,7 +356,7 @@ class PPOTrainer:
         obs = self.env.reset(stagger=bool(stagger))
         self._next_obs = obs[:, 0, :]
         self._next_opp_obs = obs[:, 1, :]
-        self._next_done = torch.zeros(self.nenv, device=self.device)
+        self._next_done.zero_()
         self.ep_ret.zero_(); self.ep_len.zero_()
         if self.opp_mode == "pool":
             self.opp_assign = self._sample_opp(self.nenv)
@@ -373,9 +379,18 @@ class PPOTrainer:
         kw = dict(seed=self._key_opp, step=self.decisions, deterministic=not cfg.opp_sample, grid=self.grid)
         if self.opp_mode == "blocks":
             groups = []
+            run = None                                  # consecutive blocks without a normaliser
             for g, (a, b) in enumerate(self._blocks):
-                self._normalize_into(self.opponents[g].norm, opp_obs[a:b], self.x_opp[a:b])
+                if self.opponents[g].norm is None:
+                    run = (run[0] if run else a, b)
+                else:
+                    if run:
+                        self.x_opp[run[0]:run[1], :OBS_DIM].copy_(opp_obs[run[0]:run[1]])
+                        run = None
+                    self._normalize_into(self.opponents[g].norm, opp_obs[a:b], self.x_opp[a:b])
                 groups.append((b, [2 + g]))
+            if run:
+                self.x_opp[run[0]:run[1], :OBS_DIM].copy_(opp_obs[run[0]:run[1]])
             self.policy.forward(self.x_opp[:self.nenv], groups, cmd=cmd, cmd_stride=2 * ACT_DIM, cmd_offset=ACT_DIM,
                                 **kw)
             return
@@ -406,17 +421,8 @@ class PPOTrainer:
         if self._next_obs is None:
             self.reset()
         P = len(self.opponents)
-        ret_sum = torch.zeros((), device=dev)
-        len_sum = torch.zeros((), device=dev)
-        ep_count = torch.zeros((), device=dev)
-        win_sum = torch.zeros((), device=dev)
-        loss_sum = torch.zeros((), device=dev)
-        alt_loss_sum = torch.zeros((), device=dev)
-        opponent_alt_loss_sum = torch.zeros((), device=dev)
-        win_by_opp = torch.zeros(P, device=dev)
-        loss_by_opp = torch.zeros(P, device=dev)
-        ep_by_opp = torch.zeros(P, device=dev)
-        trajectory_finite = torch.ones((), dtype=torch.bool, device=dev)
+        self._stats.zero_()
+        rec = self._rec
         cmd = self.env.action_buffer
 
         for t in range(T):
@@ -436,57 +442,36 @@ class PPOTrainer:
             self._opponents_act(cmd)
             self.decisions += 1
             obs, reward, done, info = self.env.step(cmd)
-            trajectory_finite.logical_and_(info["terminal_state_finite"].all())
-
-            raw_reward = reward[:, 0].float()
-            done_env = done.float()
-            self.b_rew[t] = raw_reward
             self._next_obs = obs[:, 0, :]
             self._next_opp_obs = obs[:, 1, :]
-            self._next_done = done_env
             self.global_step += nenv
-
-            self.ep_ret += raw_reward
-            self.ep_len += 1.0
-            ret_sum += (self.ep_ret * done_env).sum()
-            len_sum += (self.ep_len * done_env).sum()
-            ep_count += done_env.sum()
-            keep = 1.0 - done_env
-            self.ep_ret = self.ep_ret * keep
-            self.ep_len = self.ep_len * keep
-
-            th = info["terminal_hp"]; ta = info["terminal_alt_m"]
-            own_alt_dead = ta[:, 0] < self.min_alt
-            own_dead = (th[:, 0] <= 0.0) | own_alt_dead
-            opp_dead = (th[:, 1] <= 0.0) | (ta[:, 1] < self.min_alt)
-            both_alive = (~own_dead) & (~opp_dead)
-            win = (opp_dead & ~own_dead) | (both_alive & (th[:, 0] > th[:, 1] + 1e-9))
-            loss = (own_dead & ~opp_dead) | (both_alive & (th[:, 0] < th[:, 1] - 1e-9))
-            done_b = done.bool()
-            dwin = (win & done_b).float()
-            dloss = (loss & done_b).float()
-            win_sum += dwin.sum(); loss_sum += dloss.sum()
-            alt_loss_sum += (loss & own_alt_dead & done_b).float().sum()
-            opponent_alt_loss_sum += (win & (ta[:, 1] < self.min_alt) & done_b).float().sum()
-            rows = self.opp_assign
-            win_by_opp.scatter_add_(0, rows, dwin)
-            loss_by_opp.scatter_add_(0, rows, dloss)
-            ep_by_opp.scatter_add_(0, rows, done_b.float())
+            # reward row, next-done, episode return / length and the win / loss statistics of
+            # ppo_gpu.py:1914-1960 in one kernel (f16_rollout_record)
+            th, ta, fin = info["terminal_hp"], info["terminal_alt_m"], info["terminal_state_finite"]
+            rec.reward, rec.done = reward.data_ptr(), done.data_ptr()
+            rec.terminal_hp, rec.terminal_alt, rec.finite = th.data_ptr(), ta.data_ptr(), fin.data_ptr()
+            rec.opp_row = self.opp_assign.data_ptr()
+            rec.b_rew = self.b_rew[t].data_ptr()
+            _lib.check(self._lib.f16_rollout_record(nenv, C.byref(rec), _lib.stream_of(self.b_rew)),
+                       "f16_rollout_record")
 
         self._normalize_into(self.norm, self._next_obs, self.x_main)
         self.policy.forward(self.x_main, [(nenv, [1])], value=self.last_value)
         adv, ret = gae(self.b_rew, self.b_val, self.b_done, self.last_value, self._next_done, cfg.gamma,
                        cfg.gae_lambda)
 
-        finite_checks = [trajectory_finite]
+        st = self._stats.float()
+        finite_checks = [st[7] == 0]
         finite_checks.extend(torch.isfinite(x).all() for x in (self.b_obs, self.b_rew, self.b_val, self.b_logp, adv,
                                                                 ret))
         if not bool(torch.stack(finite_checks).all()):
             raise FloatingPointError("non-finite physical trajectory or PPO rollout; update refused")
         self.policy.check_error()
-        stats = {"ret_sum": ret_sum, "len_sum": len_sum, "ep_count": ep_count, "win_sum": win_sum,
-                 "loss_sum": loss_sum, "alt_loss_sum": alt_loss_sum, "opponent_alt_loss_sum": opponent_alt_loss_sum,
-                 "win_by_opp": win_by_opp, "loss_by_opp": loss_by_opp, "ep_by_opp": ep_by_opp}
+        names = ("ret_sum", "len_sum", "ep_count", "win_sum", "loss_sum", "alt_loss_sum", "opponent_alt_loss_sum")
+        stats = {k: st[i] for i, k in enumerate(names)}
+        stats["win_by_opp"] = st[8:8 + P]
+        stats["loss_by_opp"] = st[8 + P:8 + 2 * P]
+        stats["ep_by_opp"] = st[8 + 2 * P:8 + 3 * P]
         return adv, ret, stats
 
     def reduce_stats(self, stats):

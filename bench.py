@@ -408,12 +408,14 @@ def run_rollout(args, dev, world, rank):
     torch.cuda.synchronize(dev)
     wall0 = time.perf_counter()
     with ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0")))) as clk:
+        torch.cuda.nvtx.range_push("timed")          # lets a profiler select the timed launches
         for k in range(K):
             flush.zero_()
             starts[k].record(stream)
             t.collect_rollout()
             ends[k].record(stream)
         torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_pop()
     if world > 1:
         dist.barrier()
     wall = time.perf_counter() - wall0
@@ -564,12 +566,14 @@ def main():
     torch.cuda.synchronize(dev)
     wall0 = time.perf_counter()
     with ClockSampler(gpu_index) as clk:
+        torch.cuda.nvtx.range_push("timed")
         for k in range(K):
             flush.zero_()
             starts[k].record(stream)
             launch(cmd[W + k])
             ends[k].record(stream)
         torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_pop()
     if world > 1:
         dist.barrier()
     wall = time.perf_counter() - wall0

@@ -90,6 +90,21 @@ int f16_fdm_step_bins(double* state, int layout, int64_t ld, int64_t nac,
                       const uint8_t* bins, const float* grid_host, int num_bins, int substeps,
                       double fcs_dt, double* obs17, f16_stream_t stream);
 
+/* Both forms in one entry point, plus the per-aircraft finite flag the reference's env step
+ * computes after physics (R/cuda_fdm/rl_env.py:517, torch.isfinite(states).all(1)) produced by
+ * the same launch: finite[a] = 1 when every one of the 101 state values of aircraft a is finite
+ * after the step.  Exactly one of cmd / bins is non-NULL; obs17 and finite may be NULL. */
+typedef struct {
+  const double* cmd;        /* nac x 4 fp64, or NULL */
+  const uint8_t* bins;      /* nac x 4 uint8 bins, or NULL */
+  const float* grid_host;   /* with bins: host fp32 grid of num_bins values */
+  int num_bins;
+  double* obs17;            /* nac x 17 fp64, or NULL */
+  uint8_t* finite;          /* nac uint8, or NULL */
+} f16_fdm_io;
+int f16_fdm_step_ex(double* state, int layout, int64_t ld, int64_t nac, const f16_fdm_io* io,
+                    int substeps, double fcs_dt, f16_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------
  * (1b) Initial-condition seeder (replaces the CPU path cuda_fdm/ic.py:117-138 ->
  * cuda_fdm/ref/jsb_fdm.py:142-210): builds the 101-double seed row of each aircraft from
@@ -312,6 +327,32 @@ int f16_norm_update_static(const float* x, int64_t B, int D, int64_t ldx, float*
 int f16_norm_apply(const float* x, int64_t B, int D, int64_t ldx, const float* mean, const float* var,
                    double eps, double clip, float* y, int64_t ldy, void* y_bf16, int64_t ldb,
                    f16_stream_t stream);
+
+/* Per-step bookkeeping of collect_rollout (ppo_gpu.py:1914-1960) in one launch, after the env
+ * step: b_rew[e] = (float)reward[2e]; next_done[e] = done[e]; ep_ret / ep_len updated and
+ * reset on done exactly as the reference's fp32 expressions; and the rollout statistics
+ * accumulated into stats (fp64, zeroed by the caller at rollout start):
+ *   stats[0] ret_sum, [1] len_sum, [2] ep_count, [3] win_sum, [4] loss_sum, [5] alt_loss_sum,
+ *   [6] opponent_alt_loss_sum, [7] set to 1 if any environment's finite flag is 0 (the
+ *   reference's trajectory_finite, negated), [8 + g] win_by_opp[g],
+ *   [8 + n_opp + g] loss_by_opp[g], [8 + 2 n_opp + g] ep_by_opp[g]   (n_opp <= 32).
+ * Win / loss follow the reference (terminal HP and altitude vs min_alt, 1e-9 HP margin). */
+typedef struct {
+  const double* reward;        /* [nac] env reward; the learner is aircraft 2e */
+  const uint8_t* done;         /* [nenv] */
+  const double* terminal_hp;   /* [nac] */
+  const double* terminal_alt;  /* [nac] m */
+  const int64_t* opp_row;      /* [nenv] opponent index of each environment, or NULL */
+  int n_opp;
+  double min_alt;              /* m */
+  const uint8_t* finite;       /* [nenv] terminal_state_finite of this step, or NULL */
+  float* b_rew;                /* [nenv] rollout reward row t */
+  float* next_done;            /* [nenv] */
+  float* ep_ret;               /* [nenv] */
+  float* ep_len;               /* [nenv] */
+  double* stats;               /* [8 + 3 n_opp] */
+} f16_record_args;
+int f16_rollout_record(int64_t nenv, const f16_record_args* args, f16_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
  * Diagnostics (no counterpart in the reference): FP64 FMA-pipe probe, the measured roofline
