@@ -10,7 +10,7 @@
 //     the K-major 128-byte-swizzled layout the tensor core reads; layer 0's A is loaded by TMA,
 //     layer l's A is written there by layer l-1's epilogue;
 //   * weight tiles (nn.Linear layout = K-major B) stream through a 3-stage ring of 32 KB TMA
-//     boxes (256 output rows x 64 inputs); no multicast anywhere;
+//     boxes (256 output rows x 64 inputs), each CTA loading its own copy;
 //   * one thread issues tcgen05.mma (M=128, N<=256, K=16 per instruction) accumulating fp32 in
 //     TMEM (all 512 columns = a full 128 x 512 layer);
 //   * four epilogue warps tcgen05.ld their 32 TMEM lanes, add bias, apply ReLU/tanh, and write the

@@ -206,7 +206,7 @@ def ppo_update(model, actor_opt, critic_opt, cfg, obs, act, old_logp, b_val, adv
             elif cfg.norm_adv:
                 # mean and sample std of the union of the ranks' minibatches (two passes; the
                 # union has at least `world` >= 2 rows, so the sample std is always defined)
-                st = torch.stack([mb_adv.sum(), torch.tensor(float(mb_adv.numel()), device=dev)])
+                st = torch.stack([mb_adv.sum(), mb_adv.new_full((), float(mb_adv.numel()))])
                 dist.all_reduce(st, group=group)
                 mean = st[0] / st[1]
                 sq = ((mb_adv - mean) ** 2).sum()
