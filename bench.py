@@ -33,7 +33,7 @@ NENV = 65_536
 SUBSTEPS = 6
 FCS_DT = 1.0 / 120.0
 NUM_BINS = 21
-FLOP_PER_FRAME = 1493          # FP64 add+mul+div+sqrt per aircraft-frame (op-counting probe)
+FLOP_PER_FRAME = 1493          # FP64 add+mul+div+sqrt per aircraft-frame (op count of the reference frame)
 REF_PUBLISHED = 48.0e6         # reference fdm_run fp64, RTX 3070 Ti, 262k aircraft (cuda_fdm/README.md:99)
 METRIC = "decision-steps/sec (FDM frames/s)"
 UNIT = "aircraft-FDM-frames/s"

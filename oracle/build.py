@@ -7,7 +7,7 @@
 * ``oracle/_ref/libf16ref_r36.so``  -- the same for research/competition_36500/runtime
   (FCS dt 1/60, the 184-D lineage).
 
-The ``_ref`` builds need the reference tree (``F16_REFERENCE`` or ``/root/reference``); on a
+The ``_ref`` builds need the reference tree (the ``F16_REFERENCE`` directory, default: the local reference checkout); on a
 machine without it they are skipped and the previously built files are used as they are.
 Flags follow the reference's own host validation: ``-O2 -ffp-contract=off``.
 """

@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures in tests/golden/ from the reference itself.
 
-Run only where the reference tree is available (``F16_REFERENCE`` or /root/reference); the
+Run only where the reference tree is available (the ``F16_REFERENCE`` directory or the default local checkout); the
 GPU box never runs this.  What each fixture pins:
 
 fdm_cfg1.npz  BASELINE configs[0]: 64 envs x 2 F-16s, seeded ICs (altitude U(6,9) km, Mach
