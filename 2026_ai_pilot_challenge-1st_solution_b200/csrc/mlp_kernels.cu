@@ -35,8 +35,10 @@ constexpr int NCHUNK = 256;                      // output columns per MMA / wei
 constexpr int STAGES = 3;
 constexpr int ACT_BYTES = 128 * 1024;            // 8 chunks x (128 rows x 128 B)
 constexpr int STAGE_BYTES = NCHUNK * 128;        // 32 KB
-constexpr int SMEM_BYTES = ACT_BYTES + STAGES * STAGE_BYTES + 256 + 1024;
-constexpr int THREADS = 192;                     // warp 0 TMA, warp 1 MMA + TMEM, warps 2-5 epilogue
+constexpr int CTRL_BYTES = 1024;                 // barriers, TMEM base, head partial log-probs
+constexpr int SMEM_BYTES = ACT_BYTES + STAGES * STAGE_BYTES + CTRL_BYTES + 1024;
+constexpr int EPI_WARPS = 8;                     // two per TMEM lane quarter, splitting the columns
+constexpr int THREADS = 64 + 32 * EPI_WARPS;     // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 epilogue
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 enum Head : int { HEAD_HIDDEN_ONLY = 0, HEAD_CATEGORICAL = 1, HEAD_VALUE = 2 };
@@ -131,6 +133,20 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
       ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes, without the completion wait
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 // 32 consecutive fp32 columns of this warp's 32 TMEM lanes
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   uint32_t r[32];
@@ -196,13 +212,136 @@ __device__ __forceinline__ uint64_t mix64(uint64_t x) {
   x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
   return x ^ (x >> 31);
 }
+// Sampling noise: a 64-bit key per (call, row) from splitmix64, then per (channel, bin) a
+// 32-bit avalanche mix (Wellons' "lowbias32" constants) of the key and the bin index, giving a
+// 24-bit uniform u in (0,1) and the Gumbel variate -log(-log u).
+__device__ __forceinline__ uint64_t row_key(uint64_t seed, uint64_t step, int64_t row) {
+  return mix64(seed ^ mix64((step << 32) ^ ((uint64_t)row * 0x9E3779B97F4A7C15ull)));
+}
+__device__ __forceinline__ float gumbel(uint64_t key, uint32_t idx) {
+  uint32_t x = ((uint32_t)key ^ (idx * 0x9E3779B9u)) + (uint32_t)(key >> 32);
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  const float u = ((float)(x >> 8) + 0.5f) * (1.0f / 16777216.0f);
+  return -__logf(-__logf(u));
+}
 
 struct Smem {
-  uint64_t x_full, act_empty, acc_full, act_ready, tmem_empty, drain;
+  uint64_t x_full, act_empty, acc_full, act_ready, tmem_empty, drain, logp_bar;
   uint64_t full[STAGES], empty[STAGES];
   uint32_t tmem_base;
   int abort_flag;
+  float logp_part[TILE_M];                       // second-half channels' log-prob per tile row
 };
+static_assert(sizeof(Smem) <= CTRL_BYTES, "control block");
+
+// tanh for hidden activations that are rounded to bf16 right after: the hardware approximation
+// (max relative error about 2^-11) is well below the bf16 rounding step (2^-9).
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Per-row outputs of one sampled channel: bins / int32 index / fp64 env command.
+__device__ __forceinline__ void emit_choice(const Launch& L, int act_dim, int64_t row, int g, int best) {
+  if (L.bins) L.bins[row * L.bins_stride + L.bins_offset + g] = (uint8_t)best;
+  if (L.act_idx) L.act_idx[row * act_dim + g] = best;
+  if (L.cmd) {
+    // action_to_env in fp32: grid value, throttle (channel 3) 0.5 * v + 0.5
+    const float gv = __ldg(L.grid + best);
+    const float cv = g == 3 ? __fadd_rn(__fmul_rn(0.5f, gv), 0.5f) : gv;
+    L.cmd[row * L.cmd_stride + L.cmd_offset + g] = (double)cv;
+  }
+}
+
+// Categorical head with compile-time shape (the reference's 4 channels x 21 bins), split over
+// the two epilogue warps of a lane quarter: half H handles channels [H*A/2, (H+1)*A/2).  Logits
+// stay in registers; per channel max, log-sum-exp, Gumbel-max (or argmax); returns this half's
+// part of the summed log-prob.
+template <int A, int NB, int H>
+__device__ __forceinline__ float cat_head(uint32_t lane_addr, const float* __restrict__ bias, const Launch& L,
+                                          int64_t row, bool valid) {
+  constexpr int GA = A / 2;                      // channels of this half
+  constexpr int W = GA * NB;
+  constexpr int C0 = H * W;                      // first logit column of this half
+  constexpr int LB = C0 / 32 * 32;               // first TMEM column loaded
+  constexpr int NL = (C0 + W - 1) / 32 - C0 / 32 + 1;
+  uint32_t r[NL * 32];
+#pragma unroll
+  for (int c = 0; c < NL; c++) tmem_ld32_nowait(lane_addr + (uint32_t)(LB + 32 * c), r + 32 * c);
+  tmem_wait_ld();
+  float lg[W];
+#pragma unroll
+  for (int i = 0; i < W; i++) lg[i] = __uint_as_float(r[C0 - LB + i]) + __ldg(bias + C0 + i);
+  const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step, row);
+  float logp = 0.0f;
+#pragma unroll
+  for (int gl = 0; gl < GA; gl++) {
+    const int g = H * GA + gl;
+    const float* x = lg + gl * NB;
+    float mx = x[0];
+#pragma unroll
+    for (int b = 1; b < NB; b++) mx = fmaxf(mx, x[b]);
+    float se = 0.0f;
+#pragma unroll
+    for (int b = 0; b < NB; b++) se += __expf(x[b] - mx);
+    const float lse = mx + logf(se);
+    int best = 0;
+    float bestv = -INFINITY;
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+      float sc = x[b];
+      if (!L.deterministic) sc += gumbel(key, (uint32_t)(g * 64 + b));
+      if (sc > bestv) { bestv = sc; best = b; }
+    }
+    float chosen = x[0];
+#pragma unroll
+    for (int b = 1; b < NB; b++) chosen = (b == best) ? x[b] : chosen;
+    logp += chosen - lse;
+    if (valid) emit_choice(L, A, row, g, best);
+  }
+  if (valid && L.logits)
+#pragma unroll
+    for (int i = 0; i < W; i++) L.logits[row * L.logits_ld + C0 + i] = lg[i];
+  return logp;
+}
+
+// Any other categorical shape (act_dim * num_bins <= 96).
+__device__ __noinline__ void cat_head_generic(uint32_t lane_addr, const float* __restrict__ bias, const Launch& L,
+                                              const NetParams& P, int64_t row, bool valid) {
+  const int W = P.width[P.n_layers - 1];
+  float lg[96];
+  for (int c0 = 0; c0 < 96; c0 += 32) tmem_ld32(lane_addr + (uint32_t)c0, lg + c0);
+  for (int i = 0; i < 96; i++) lg[i] += (i < W) ? __ldg(bias + i) : 0.0f;
+  const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step, row);
+  float logp = 0.0f;
+  for (int g = 0; g < P.act_dim; g++) {
+    const float* x = lg + g * P.num_bins;
+    float mx = -INFINITY;
+    for (int b = 0; b < P.num_bins; b++) mx = fmaxf(mx, x[b]);
+    float se = 0.0f;
+    for (int b = 0; b < P.num_bins; b++) se += __expf(x[b] - mx);
+    const float lse = mx + logf(se);
+    int best = 0;
+    float bestv = -INFINITY;
+    for (int b = 0; b < P.num_bins; b++) {
+      float sc = x[b];
+      if (!L.deterministic) sc += gumbel(key, (uint32_t)(g * 64 + b));
+      if (sc > bestv) { bestv = sc; best = b; }
+    }
+    logp += x[best] - lse;
+    if (valid) emit_choice(L, P.act_dim, row, g, best);
+  }
+  if (valid) {
+    if (L.logp) L.logp[row] = logp;
+    if (L.logits)
+      for (int i = 0; i < W; i++) L.logits[row * L.logits_ld + i] = lg[i];
+  }
+}
 
 __global__ void __launch_bounds__(THREADS, 1)
 k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ nets_dev,
@@ -219,8 +358,9 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
     mbar_init(smem_u32(&S->x_full), 1);
     mbar_init(smem_u32(&S->act_empty), 1);
     mbar_init(smem_u32(&S->acc_full), 1);
-    mbar_init(smem_u32(&S->act_ready), 128);
-    mbar_init(smem_u32(&S->tmem_empty), 128);
+    mbar_init(smem_u32(&S->act_ready), 32 * EPI_WARPS);
+    mbar_init(smem_u32(&S->tmem_empty), 32 * EPI_WARPS);
+    mbar_init(smem_u32(&S->logp_bar), TILE_M);
     mbar_init(smem_u32(&S->drain), 1);
     for (int s = 0; s < STAGES; s++) {
       mbar_init(smem_u32(&S->full[s]), 1);
@@ -324,11 +464,14 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2-5)
-    const int q = warp & 3;                       // TMEM lane quarter this warp may access
+    // ------------------------------------------------------------ epilogue (warps 2-9)
+    // Warp w may access TMEM lanes 32*(w%4)..+31 (its quarter of the tile rows); the two warps
+    // of a quarter split the columns: half h takes the 32-column chunks with index % 2 == h.
+    const int q = warp & 3;
+    const int h = (warp - 2) >> 2;
     const int m = q * 32 + lane;                  // tile row of this thread
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    uint32_t accs = 0;
+    uint32_t accs = 0, heads = 0;
     int64_t jn = 0;
     for (int64_t j = blockIdx.x; j < njobs; j += gridDim.x) {
       Job J;
@@ -344,31 +487,57 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
         const float* bias = P.bias[l];
         const bool last = (l == P.n_layers - 1);
         if (!last) {
-          // bias + activation -> bf16 into the swizzled A region of the next layer
+          // bias + activation -> bf16 into the swizzled A region of the next layer.  32-column
+          // chunks, the TMEM load of the next chunk in flight while this one is converted.
           const int N = P.width_pad[l];
-          for (int c0 = 0; c0 < N; c0 += 32) {
-            float v[32];
-            tmem_ld32(lane_addr + (uint32_t)c0, v);
+          const bool relu = P.act == 0;
+          uint8_t* rowbase = act + (m >> 3) * 1024 + (m & 7) * 128;
+          auto convert = [&](const uint32_t* r, int c0) {
+            const float4* b4 = reinterpret_cast<const float4*>(bias + c0);
+            uint8_t* rowp = rowbase + (c0 / KCHUNK) * TILE_M * 128;
+            const int unit0 = (c0 % KCHUNK) / 8;
 #pragma unroll
-            for (int i = 0; i < 32; i++) {
-              float x = v[i] + __ldg(bias + c0 + i);
-              v[i] = (P.act == 0) ? fmaxf(x, 0.0f) : tanhf(x);
-            }
-            uint8_t* chunk = act + (c0 / KCHUNK) * TILE_M * 128 + (m >> 3) * 1024 + (m & 7) * 128;
+            for (int u = 0; u < 4; u++) {                  // 16-byte unit = 8 columns
+              const float4 ba = __ldg(b4 + 2 * u), bb = __ldg(b4 + 2 * u + 1);
+              float x[8] = {__uint_as_float(r[8 * u + 0]) + ba.x, __uint_as_float(r[8 * u + 1]) + ba.y,
+                            __uint_as_float(r[8 * u + 2]) + ba.z, __uint_as_float(r[8 * u + 3]) + ba.w,
+                            __uint_as_float(r[8 * u + 4]) + bb.x, __uint_as_float(r[8 * u + 5]) + bb.y,
+                            __uint_as_float(r[8 * u + 6]) + bb.z, __uint_as_float(r[8 * u + 7]) + bb.w};
+              if (relu) {
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-              int unit = ((c0 % KCHUNK) / 8) + u;           // 16-byte unit within the 128-byte row
-              __nv_bfloat162 p0 = __floats2bfloat162_rn(v[8 * u + 0], v[8 * u + 1]);
-              __nv_bfloat162 p1 = __floats2bfloat162_rn(v[8 * u + 2], v[8 * u + 3]);
-              __nv_bfloat162 p2 = __floats2bfloat162_rn(v[8 * u + 4], v[8 * u + 5]);
-              __nv_bfloat162 p3 = __floats2bfloat162_rn(v[8 * u + 6], v[8 * u + 7]);
+                for (int i = 0; i < 8; i++) x[i] = fmaxf(x[i], 0.0f);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) x[i] = tanh_fast(x[i]);
+              }
+              __nv_bfloat162 p0 = __floats2bfloat162_rn(x[0], x[1]);
+              __nv_bfloat162 p1 = __floats2bfloat162_rn(x[2], x[3]);
+              __nv_bfloat162 p2 = __floats2bfloat162_rn(x[4], x[5]);
+              __nv_bfloat162 p3 = __floats2bfloat162_rn(x[6], x[7]);
               uint4 w;
               w.x = *reinterpret_cast<uint32_t*>(&p0);
               w.y = *reinterpret_cast<uint32_t*>(&p1);
               w.z = *reinterpret_cast<uint32_t*>(&p2);
               w.w = *reinterpret_cast<uint32_t*>(&p3);
-              *reinterpret_cast<uint4*>(chunk + ((unit ^ (m & 7)) * 16)) = w;
+              *reinterpret_cast<uint4*>(rowp + (((unit0 + u) ^ (m & 7)) * 16)) = w;
             }
+          };
+          uint32_t ra[32], rb[32];
+          int c = 32 * h;                                  // this warp's chunks: c, c + 64, ...
+          if (c < N) {
+            tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
+            tmem_wait_ld();
+          }
+          while (c < N) {
+            if (c + 64 < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + 64), rb);
+            convert(ra, c);
+            tmem_wait_ld();
+            c += 64;
+            if (c >= N) break;
+            if (c + 64 < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + 64), ra);
+            convert(rb, c);
+            tmem_wait_ld();
+            c += 64;
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           tc_fence_before();
@@ -377,58 +546,33 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           const int64_t row = J.row0 + m;
           const bool valid = m < J.rows;
           if (P.head == HEAD_VALUE) {
-            float v[32];
-            tmem_ld32(lane_addr, v);
-            float val = v[0] + __ldg(bias);
-            if (valid) {
-              if (L.value) L.value[row] = val;
-              if (L.logits) L.logits[row * L.logits_ld] = val;
-            }
-          } else {
-            // categorical head: act_dim groups of num_bins logits -> Gumbel-max sample + log-prob
-            const int W = P.width[l];
-            float lg[96];
-            for (int c0 = 0; c0 < 96; c0 += 32) tmem_ld32(lane_addr + (uint32_t)c0, lg + c0);
-            for (int i = 0; i < 96; i++) lg[i] += (i < W) ? __ldg(bias + i) : 0.0f;
-            float logp = 0.0f;
-            for (int g = 0; g < P.act_dim; g++) {
-              const float* x = lg + g * P.num_bins;
-              float mx = -INFINITY;
-              for (int b = 0; b < P.num_bins; b++) mx = fmaxf(mx, x[b]);
-              float se = 0.0f;
-              for (int b = 0; b < P.num_bins; b++) se += expf(x[b] - mx);
-              float lse = mx + logf(se);
-              int best = 0;
-              float bestv = -INFINITY;
-              for (int b = 0; b < P.num_bins; b++) {
-                float s = x[b];
-                if (!L.deterministic) {
-                  uint64_t h = mix64(L.seed ^ mix64((L.step << 32) ^ ((uint64_t)row * 131ull + (uint64_t)(g * 64 + b))));
-                  float u = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);   // (0,1)
-                  s += -logf(-logf(u));
-                }
-                if (s > bestv) { bestv = s; best = b; }
-              }
-              logp += x[best] - lse;
+            if (h == 0) {
+              float v[32];
+              tmem_ld32(lane_addr, v);
+              float val = v[0] + __ldg(bias);
               if (valid) {
-                if (L.bins) L.bins[row * L.bins_stride + L.bins_offset + g] = (uint8_t)best;
-                if (L.act_idx) L.act_idx[row * P.act_dim + g] = best;
-                if (L.cmd) {
-                  // action_to_env in fp32: grid value, throttle (channel 3) 0.5 * v + 0.5
-                  const float gv = __ldg(L.grid + best);
-                  const float cv = g == 3 ? __fadd_rn(__fmul_rn(0.5f, gv), 0.5f) : gv;
-                  L.cmd[row * L.cmd_stride + L.cmd_offset + g] = (double)cv;
-                }
+                if (L.value) L.value[row] = val;
+                if (L.logits) L.logits[row * L.logits_ld] = val;
               }
             }
-            if (valid) {
-              if (L.logp) L.logp[row] = logp;
-              if (L.logits)
-                for (int i = 0; i < W; i++) L.logits[row * L.logits_ld + i] = lg[i];
+          } else if (P.act_dim == 4 && P.num_bins == 21) {
+            // channels 0-1 on half 0, 2-3 on half 1; half 1's log-prob joins through shared memory
+            if (h == 1) {
+              float part = cat_head<4, 21, 1>(lane_addr, bias, L, row, valid);
+              S->logp_part[m] = part;
+              mbar_arrive(smem_u32(&S->logp_bar));
+            } else {
+              float part = cat_head<4, 21, 0>(lane_addr, bias, L, row, valid);
+              if (!mbar_wait(smem_u32(&S->logp_bar), heads & 1, abort_flag)) ok = false;
+              else if (valid && L.logp) L.logp[row] = part + S->logp_part[m];
             }
+            heads++;
+          } else if (h == 0) {
+            cat_head_generic(lane_addr, bias, L, P, row, valid);
           }
           tc_fence_before();
           mbar_arrive(smem_u32(&S->tmem_empty));
+          if (!ok) break;
         }
       }
       if (!ok) break;

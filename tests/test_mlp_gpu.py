@@ -181,3 +181,23 @@ def test_sampling_frequencies_chi_square(P, cuda):
         p = chisquare(obs_k, exp_k * obs_k.sum() / exp_k.sum()).pvalue
         print(f"channel {c}: chi-square p = {p:.3f}")
         assert p > 1e-4
+
+
+def test_other_head_shape(P, cuda):
+    """A categorical head other than 4 x 21 (3 channels x 11 bins) takes the generic epilogue."""
+    actor = make_seq(184, (256, 256), 33, "relu", 41, cuda)
+    ps = P.PolicySet([P.MlpWeights.from_sequential(actor, P.HEAD_CATEGORICAL, cuda, act_dim=3, num_bins=11)])
+    rows = 384
+    _, xb = make_x(rows, cuda, seed=9)
+    logits = torch.zeros(rows, 33, device=cuda)
+    act = torch.zeros(rows, 3, dtype=torch.int32, device=cuda)
+    logp = torch.zeros(rows, device=cuda)
+    ps.forward(xb, [(rows, [0])], logits=logits, act_idx=act, logp=logp, seed=3, step=2)
+    torch.cuda.synchronize()
+    check_close(logits, emulate(actor, xb[:, :184]), 1e-2, 1e-2, "3x11 logits")
+    lsm = torch.log_softmax(logits.view(rows, 3, 11), -1)
+    exp_logp = lsm.gather(-1, act.long().unsqueeze(-1)).squeeze(-1).sum(-1)
+    check_close(logp, exp_logp, 1e-4, 1e-5, "3x11 summed log-prob")
+    ps.forward(xb, [(rows, [0])], logits=logits, act_idx=act, deterministic=True)
+    torch.cuda.synchronize()
+    assert torch.equal(act.long(), logits.view(rows, 3, 11).argmax(-1))
