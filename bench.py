@@ -183,9 +183,9 @@ def run_reference_arm(args):
 
 
 # --------------------------------------------------------------------------- GPU arm
-def profile_traffic():
-    """DRAM bytes per launch of f16_fdm_step from the committed ncu summary (or None)."""
-    p = ROOT / "profiles" / "fdm_step_cfg2.md"
+def profile_traffic(name="fdm_step_cfg2.md"):
+    """DRAM bytes per launch of the summarised kernel from a committed ncu summary (or None)."""
+    p = ROOT / "profiles" / name
     if not p.exists():
         return None
     for ln in p.read_text().splitlines():
@@ -298,7 +298,8 @@ def run_obs(args, dev, world, rank):
                         "h2d_bytes_per_step": nac * 101 * 8 + nac * 4 * 8, "d2h_bytes_per_step": nac * 184 * 4 + nac * 8,
                         "api": "BatchObsReward.kernel_step on host state/actions, obs + reward back to host"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                             "frac": achieved / peak if peak else None, "traffic": None, "kernel": "k_obs_step",
+                             "frac": achieved / peak if peak else None,
+                             "traffic": profile_traffic("obs_step_cfg3.md"), "kernel": "k_obs_step",
                              "bytes_per_unit": OBS_BYTES_PER_ENV, "unit_basis": "environment",
                              "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)"},
                 "gpu_launches": K, "clocks": clk.summary()}
@@ -486,7 +487,8 @@ def run_rollout(args, dev, world, rank):
                         "api": "PPOTrainer: host parameters -> refresh_policy -> collect_rollout -> adv/ret to host",
                         "steps": Ke},
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                             "frac": achieved / peak if peak else None, "traffic": None,
+                             "frac": achieved / peak if peak else None,
+                             "traffic": profile_traffic("mlp_policy_cfg4.md"),
                              "kernel": "k_policy (main actor + critic, one launch per decision)",
                              "flop_per_unit": ACTOR_FLOP + CRITIC_FLOP, "unit_basis": "env-decision",
                              "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (measured)"},
