@@ -52,6 +52,7 @@ k_norm_partial(const float* __restrict__ x, int64_t B, int D, int64_t ldx, doubl
   int64_t r1 = r0 + NORM_ROWS_PER_BLOCK < B ? r0 + NORM_ROWS_PER_BLOCK : B;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     double s = 0.0, q = 0.0;
+#pragma unroll 8
     for (int64_t r = r0; r < r1; r++) {
       double v = (double)x[r * ldx + d];
       s += v;
@@ -61,24 +62,50 @@ k_norm_partial(const float* __restrict__ x, int64_t B, int D, int64_t ldx, doubl
   }
 }
 
-// combine the partials and apply the reference's Chan merge (all fp32 ops, reference order):
-//   delta = b_mean - mean; tot = count + b_count; mean += delta * (b_count / tot)
-//   M2 = var*count + b_var*b_count + (delta*delta) * (count*b_count / tot); var = M2 / tot
-__global__ void __launch_bounds__(NORM_THREADS)
-k_norm_merge(const double2* __restrict__ partial, int nblk, int64_t B, int D, float* __restrict__ mean,
-             float* __restrict__ var, float* __restrict__ count) {
-  int d = blockIdx.x * blockDim.x + threadIdx.x;
-  float c = count[0];
-  float bc = (float)B;
-  float tot = __fadd_rn(c, bc);
-  __syncthreads();
+// Sum of the partial rows of 32 features per block: warp w adds rows w, w+8, ... (unrolled, so
+// many loads are in flight), then the 8 warp sums are added in warp order.  Both the merge and
+// the cross-rank sums use it, so one rank reproduces f16_norm_update bit for bit.
+constexpr int MERGE_WARPS = NORM_THREADS / 32;
+__device__ __forceinline__ bool sum_partials(const double2* __restrict__ partial, int nblk, int D, double2& out) {
+  __shared__ double2 acc[MERGE_WARPS][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int d = blockIdx.x * 32 + lane;
+  double s = 0.0, q = 0.0;
   if (d < D) {
-    double s = 0.0, q = 0.0;
-    for (int b = 0; b < nblk; b++) {
+#pragma unroll 4
+    for (int b = w; b < nblk; b += MERGE_WARPS) {
       double2 p = partial[(int64_t)b * D + d];
       s += p.x;
       q += p.y;
     }
+  }
+  acc[w][lane] = make_double2(s, q);
+  __syncthreads();
+  if (w != 0 || d >= D) return false;
+  s = 0.0; q = 0.0;
+#pragma unroll
+  for (int i = 0; i < MERGE_WARPS; i++) {
+    s += acc[i][lane].x;
+    q += acc[i][lane].y;
+  }
+  out = make_double2(s, q);
+  return true;
+}
+
+// combine the partials and apply the reference's Chan merge (all fp32 ops, reference order):
+//   delta = b_mean - mean; tot = count + b_count; mean += delta * (b_count / tot)
+//   M2 = var*count + b_var*b_count + (delta*delta) * (count*b_count / tot); var = M2 / tot
+// grid: ceil(D / 32) blocks of NORM_THREADS
+__global__ void __launch_bounds__(NORM_THREADS)
+k_norm_merge(const double2* __restrict__ partial, int nblk, int64_t B, int D, float* __restrict__ mean,
+             float* __restrict__ var, float* __restrict__ count) {
+  const int d = blockIdx.x * 32 + (threadIdx.x & 31);
+  float c = count[0];
+  float bc = (float)B;
+  float tot = __fadd_rn(c, bc);
+  double2 sq;
+  if (sum_partials(partial, nblk, D, sq)) {
+    const double s = sq.x, q = sq.y;
     double m = s / (double)B;
     double vv = q / (double)B - m * m;
     float bm = (float)m, bv = (float)(vv > 0.0 ? vv : 0.0);
@@ -92,18 +119,11 @@ k_norm_merge(const double2* __restrict__ partial, int nblk, int64_t B, int D, fl
 }
 
 // sums[d] = sum over the partial rows (same order as k_norm_merge, so a merge of sums reproduces
-// f16_norm_update bit for bit on one device)
+// f16_norm_update bit for bit on one device); grid: ceil(D / 32) blocks of NORM_THREADS
 __global__ void __launch_bounds__(NORM_THREADS)
 k_norm_reduce(const double2* __restrict__ partial, int nblk, int D, double2* __restrict__ sums) {
-  int d = blockIdx.x * blockDim.x + threadIdx.x;
-  if (d >= D) return;
-  double s = 0.0, q = 0.0;
-  for (int b = 0; b < nblk; b++) {
-    double2 p = partial[(int64_t)b * D + d];
-    s += p.x;
-    q += p.y;
-  }
-  sums[d] = make_double2(s, q);
+  double2 sq;
+  if (sum_partials(partial, nblk, D, sq)) sums[blockIdx.x * 32 + (threadIdx.x & 31)] = sq;
 }
 
 __global__ void k_norm_count(float* __restrict__ count, int64_t B) {
@@ -111,24 +131,39 @@ __global__ void k_norm_count(float* __restrict__ count, int64_t B) {
 }
 
 // y = clamp((x - mean) / sqrt(var + eps), -clip, clip); fp32 out and/or bf16 out padded to ldb
-// columns (zeros beyond D).
+// columns (zeros beyond D).  With mean == NULL the values pass through unchanged (a cast into
+// the bf16 layout).  One thread per column (den and mean loaded once), APPLY_ROWS rows per
+// block; `nonfinite` (optional) counts warps that produced a non-finite output.
+constexpr int APPLY_ROWS = 32;
 __global__ void __launch_bounds__(NORM_THREADS)
 k_norm_apply(const float* __restrict__ x, int64_t B, int D, int64_t ldx, const float* __restrict__ mean,
              const float* __restrict__ var, float eps, float clip, float* __restrict__ y, int64_t ldy,
-             __nv_bfloat16* __restrict__ yb, int64_t ldb) {
-  int64_t r = blockIdx.y;
-  for (int64_t rr = r; rr < B; rr += gridDim.y) {
-    for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < (yb ? ldb : D); d += gridDim.x * blockDim.x) {
-      float o = 0.0f;
-      if (d < D) {
-        float den = __fsqrt_rn(__fadd_rn(var[d], eps));
-        o = __fdiv_rn(__fsub_rn(x[rr * ldx + d], mean[d]), den);
-        o = o < -clip ? -clip : (o > clip ? clip : o);     // torch.clamp_: NaN stays NaN
+             __nv_bfloat16* __restrict__ yb, int64_t ldb, unsigned* __restrict__ nonfinite) {
+  const int ncol = yb ? (int)ldb : D;
+  const int64_t r0 = (int64_t)blockIdx.x * APPLY_ROWS;
+  const int64_t r1 = r0 + APPLY_ROWS < B ? r0 + APPLY_ROWS : B;
+  bool bad = false;
+  for (int d = threadIdx.x; d < ncol; d += blockDim.x) {
+    if (d < D) {
+      const bool norm = mean != nullptr;
+      const float mu = norm ? mean[d] : 0.0f;
+      const float den = norm ? __fsqrt_rn(__fadd_rn(var[d], eps)) : 1.0f;
+#pragma unroll 4
+      for (int64_t rr = r0; rr < r1; rr++) {
+        float o = x[rr * ldx + d];
+        if (norm) {
+          o = __fdiv_rn(__fsub_rn(o, mu), den);
+          o = o < -clip ? -clip : (o > clip ? clip : o);   // torch.clamp_: NaN stays NaN
+        }
+        bad |= !isfinite(o);
         if (y) y[rr * ldy + d] = o;
+        if (yb) yb[rr * ldb + d] = __float2bfloat16_rn(o);
       }
-      if (yb) yb[rr * ldb + d] = __float2bfloat16_rn(o);
+    } else {
+      for (int64_t rr = r0; rr < r1; rr++) yb[rr * ldb + d] = __float2bfloat16_rn(0.0f);
     }
   }
+  if (nonfinite && __any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicAdd(nonfinite, 1u);
 }
 
 // ---------------------------------------------------------------- rollout bookkeeping
@@ -247,7 +282,7 @@ extern "C" int f16_norm_update(const float* x, int64_t B, int D, int64_t ldx, fl
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   double2* part = reinterpret_cast<double2*>(scratch);
   ro::k_norm_partial<<<nblk, ro::NORM_THREADS, 0, s>>>(x, B, D, ldx, part);
-  ro::k_norm_merge<<<(D + ro::NORM_THREADS - 1) / ro::NORM_THREADS, ro::NORM_THREADS, 0, s>>>(part, nblk, B, D,
+  ro::k_norm_merge<<<(D + 31) / 32, ro::NORM_THREADS, 0, s>>>(part, nblk, B, D,
                                                                                             mean, var, count);
   ro::k_norm_count<<<1, 32, 0, s>>>(count, B);
   return launch_status();
@@ -262,7 +297,7 @@ extern "C" int f16_norm_sums(const float* x, int64_t B, int D, int64_t ldx, doub
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   double2* part = reinterpret_cast<double2*>(scratch);
   ro::k_norm_partial<<<nblk, ro::NORM_THREADS, 0, s>>>(x, B, D, ldx, part);
-  ro::k_norm_reduce<<<(D + ro::NORM_THREADS - 1) / ro::NORM_THREADS, ro::NORM_THREADS, 0, s>>>(
+  ro::k_norm_reduce<<<(D + 31) / 32, ro::NORM_THREADS, 0, s>>>(
       part, nblk, D, reinterpret_cast<double2*>(sums));
   return launch_status();
 }
@@ -272,7 +307,7 @@ extern "C" int f16_norm_merge_sums(const double* sums, int64_t B_total, int D, f
   if (!sums || !mean || !var || !count || B_total <= 0 || D <= 0) return F16_ERR_ARG;
   if (!aligned(sums, 16)) return F16_ERR_ALIGN;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  ro::k_norm_merge<<<(D + ro::NORM_THREADS - 1) / ro::NORM_THREADS, ro::NORM_THREADS, 0, s>>>(
+  ro::k_norm_merge<<<(D + 31) / 32, ro::NORM_THREADS, 0, s>>>(
       reinterpret_cast<const double2*>(sums), 1, B_total, D, mean, var, count);
   ro::k_norm_count<<<1, 32, 0, s>>>(count, B_total);
   return launch_status();
@@ -288,10 +323,22 @@ extern "C" int f16_norm_apply(const float* x, int64_t B, int D, int64_t ldx, con
                               f16_stream_t stream) {
   if (!x || !mean || !var || B <= 0 || D <= 0 || ldx < D || (!y && !y_bf16)) return F16_ERR_ARG;
   if ((y && ldy < D) || (y_bf16 && ldb < D)) return F16_ERR_ARG;
-  dim3 grid((unsigned)(((y_bf16 ? ldb : D) + ro::NORM_THREADS - 1) / ro::NORM_THREADS),
-            (unsigned)(B < 65535 ? B : 65535));
+  unsigned grid = (unsigned)((B + ro::APPLY_ROWS - 1) / ro::APPLY_ROWS);
   ro::k_norm_apply<<<grid, ro::NORM_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy, reinterpret_cast<__nv_bfloat16*>(y_bf16), ldb);
+      x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy, reinterpret_cast<__nv_bfloat16*>(y_bf16), ldb,
+      nullptr);
+  return launch_status();
+}
+
+extern "C" int f16_norm_apply_checked(const float* x, int64_t B, int D, int64_t ldx, const float* mean,
+                                      const float* var, double eps, double clip, float* y, int64_t ldy, void* y_bf16,
+                                      int64_t ldb, uint32_t* nonfinite, f16_stream_t stream) {
+  if (!x || B <= 0 || D <= 0 || ldx < D || (!y && !y_bf16) || (!mean != !var)) return F16_ERR_ARG;
+  if ((y && ldy < D) || (y_bf16 && ldb < D)) return F16_ERR_ARG;
+  unsigned grid = (unsigned)((B + ro::APPLY_ROWS - 1) / ro::APPLY_ROWS);
+  ro::k_norm_apply<<<grid, ro::NORM_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy, reinterpret_cast<__nv_bfloat16*>(y_bf16), ldb,
+      nonfinite);
   return launch_status();
 }
 
@@ -342,7 +389,7 @@ extern "C" int f16_norm_update_static(const float* x, int64_t B, int D, int64_t 
   if (rc != F16_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   ro::k_norm_partial<<<(unsigned)nblk, ro::NORM_THREADS, 0, s>>>(x, B, D, ldx, part);
-  ro::k_norm_merge<<<(D + ro::NORM_THREADS - 1) / ro::NORM_THREADS, ro::NORM_THREADS, 0, s>>>(
+  ro::k_norm_merge<<<(D + 31) / 32, ro::NORM_THREADS, 0, s>>>(
       part, (int)nblk, B, D, mean, var, count);
   ro::k_norm_count<<<1, 32, 0, s>>>(count, B);
   return launch_status();

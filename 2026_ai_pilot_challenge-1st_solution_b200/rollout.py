@@ -87,15 +87,17 @@ class RunningNorm:
         return y
 
     @torch.no_grad()
-    def normalize_bf16(self, x, out_f32=None, out_bf16=None, pad_to=192):
-        """Normalised rows as fp32 (optional) and as a (B, pad_to) zero-padded bf16 matrix."""
+    def normalize_bf16(self, x, out_f32=None, out_bf16=None, pad_to=192, nonfinite=None):
+        """Normalised rows as fp32 (optional) and as a (B, pad_to) zero-padded bf16 matrix;
+        ``nonfinite`` (a device uint32/int32 counter, optional) is incremented when an output
+        value is NaN or infinite."""
         x = self._x(x)
         yb = torch.empty(x.shape[0], pad_to, dtype=torch.bfloat16, device=x.device) if out_bf16 is None else out_bf16
-        _lib.check(self.lib.f16_norm_apply(_lib.ptr(x), x.shape[0], self.dim, x.stride(0), _lib.ptr(self.mean),
-                                           _lib.ptr(self.var), self.eps, self.clip,
-                                           _lib.ptr(out_f32) if out_f32 is not None else None,
-                                           out_f32.stride(0) if out_f32 is not None else 0, _lib.ptr(yb),
-                                           yb.stride(0), _lib.stream_of(x)), "f16_norm_apply")
+        _lib.check(self.lib.f16_norm_apply_checked(
+            _lib.ptr(x), x.shape[0], self.dim, x.stride(0), _lib.ptr(self.mean), _lib.ptr(self.var), self.eps,
+            self.clip, _lib.ptr(out_f32) if out_f32 is not None else None,
+            out_f32.stride(0) if out_f32 is not None else 0, _lib.ptr(yb), yb.stride(0),
+            _lib.ptr(nonfinite) if nonfinite is not None else None, _lib.stream_of(x)), "f16_norm_apply_checked")
         return yb
 
     def state_dict(self):
@@ -108,6 +110,22 @@ class RunningNorm:
         c = RunningNorm(self.dim, self.device, self.clip, self.eps)
         c.load_state_dict(self.state_dict())
         return c
+
+
+@torch.no_grad()
+def cast_bf16(x, out_bf16, out_f32=None, nonfinite=None):
+    """Un-normalised rows (B, D) fp32 into a zero-padded (B, ldb) bf16 policy input (and
+    optionally an fp32 copy) in one kernel: the input of a network without a normaliser."""
+    _lib.require_cuda_tensor(x, torch.float32, None, "observations", None)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("observations must be (B, D) with unit column stride")
+    L = _lib.load()
+    _lib.check(L.f16_norm_apply_checked(_lib.ptr(x), x.shape[0], x.shape[1], x.stride(0), None, None, 0.0, 0.0,
+                                        _lib.ptr(out_f32) if out_f32 is not None else None,
+                                        out_f32.stride(0) if out_f32 is not None else 0, _lib.ptr(out_bf16),
+                                        out_bf16.stride(0), _lib.ptr(nonfinite) if nonfinite is not None else None,
+                                        _lib.stream_of(x)), "f16_norm_apply_checked")
+    return out_bf16
 
 
 def gae(b_rew, b_val, b_done, last_value, next_done, gamma, gae_lambda, adv=None, ret=None):

@@ -328,6 +328,14 @@ int f16_norm_apply(const float* x, int64_t B, int D, int64_t ldx, const float* m
                    double eps, double clip, float* y, int64_t ldy, void* y_bf16, int64_t ldb,
                    f16_stream_t stream);
 
+/* The same, plus: mean == var == NULL passes the values through unchanged (the un-normalised
+ * opponent input, ppo_gpu.py:583, cast into the bf16 layout), and `nonfinite` (device uint32,
+ * optional) is incremented when an output value is NaN or infinite, so the rollout's final
+ * isfinite check of the observation buffer (ppo_gpu.py:2003-2008) needs no extra pass. */
+int f16_norm_apply_checked(const float* x, int64_t B, int D, int64_t ldx, const float* mean,
+                           const float* var, double eps, double clip, float* y, int64_t ldy,
+                           void* y_bf16, int64_t ldb, uint32_t* nonfinite, f16_stream_t stream);
+
 /* Per-step bookkeeping of collect_rollout (ppo_gpu.py:1914-1960) in one launch, after the env
  * step: b_rew[e] = (float)reward[2e]; next_done[e] = done[e]; ep_ret / ep_len updated and
  * reset on done exactly as the reference's fp32 expressions; and the rollout statistics

@@ -60,3 +60,39 @@ def test_running_norm_vs_reference(cuda):
     assert yb.shape == (24, 192)
     assert torch.equal(yb[:, :184], yf.to(torch.bfloat16)) and bool((yb[:, 184:] == 0).all())
     assert torch.equal(yf, y)
+
+
+def test_checked_normalise_cast_and_nonfinite_count(cuda):
+    """f16_norm_apply_checked: normalise equals f16_norm_apply bit for bit (fp32 and bf16 rows,
+    strided input); mean = var = NULL casts the rows unchanged into the zero-padded bf16 layout;
+    the counter stays 0 on finite data and counts a planted NaN row."""
+    ro = pkg_module("rollout")
+    rn = ro.RunningNorm(184, cuda)
+    g = torch.Generator(device=cuda).manual_seed(11)
+    src = torch.randn(3000, 368, device=cuda, generator=g) * 4.0
+    x = src[:, :184]                                      # ldx 368, as the env's (nenv, 2, 184) view
+    rn.update(x)
+    y1, y2 = torch.empty(3000, 184, device=cuda), torch.empty(3000, 184, device=cuda)
+    b1 = torch.full((3000, 192), 7.0, device=cuda).to(torch.bfloat16)
+    b2 = b1.clone()
+    L = pkg_module("_lib")
+    lib = L.load()
+    L.check(lib.f16_norm_apply(L.ptr(x), 3000, 184, 368, L.ptr(rn.mean), L.ptr(rn.var), rn.eps, rn.clip, L.ptr(y1),
+                               184, L.ptr(b1), 192, L.stream_of(x)), "apply")
+    cnt = torch.zeros(1, dtype=torch.int32, device=cuda)
+    rn.normalize_bf16(x, out_f32=y2, out_bf16=b2, nonfinite=cnt)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2) and torch.equal(b1, b2) and int(cnt) == 0
+    assert bool((b2[:, 184:] == 0).all())
+    ref = ((x - rn.mean) / torch.sqrt(rn.var + rn.eps)).clamp(-rn.clip, rn.clip)
+    assert torch.equal(y2, ref)
+    # pass-through cast
+    c = torch.full((3000, 192), 5.0, device=cuda).to(torch.bfloat16)
+    ro.cast_bf16(x, c)
+    torch.cuda.synchronize()
+    assert torch.equal(c[:, :184], x.to(torch.bfloat16)) and bool((c[:, 184:] == 0).all())
+    # a NaN in the input is counted
+    src[17, 5] = float("nan")
+    rn.normalize_bf16(x, out_f32=y2, out_bf16=b2, nonfinite=cnt)
+    torch.cuda.synchronize()
+    assert int(cnt) >= 1 and bool(torch.isnan(y2[17, 5]))
