@@ -246,6 +246,59 @@ __device__ __forceinline__ float tanh_fast(float x) {
   return y;
 }
 
+// two fp32 lanes at once (Blackwell packed f32x2 add, round to nearest like a scalar add)
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// pack two fp32 (lo, hi) into bf16x2 with round-to-nearest, optionally clamping at 0 first
+// (relu(round(x)) == round(relu(x)), so the fused clamp gives the same bits as relu then round)
+__device__ __forceinline__ uint32_t pack_bf16x2(uint64_t v, bool relu) {
+  const float lo = __uint_as_float((uint32_t)v), hi = __uint_as_float((uint32_t)(v >> 32));
+  uint32_t d;
+  if (relu) asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  else asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// bias + activation of 32 accumulator columns [c0, c0+32) of one row, packed to bf16 into the
+// row's 128-byte swizzled line of the next layer's A operand: all bias loads first (one exposed
+// latency per chunk), the bias added two lanes per instruction, one activation branch per chunk,
+// ReLU fused into the conversion
+__device__ __forceinline__ void convert32(const uint32_t (&r)[32], const float* __restrict__ bias, int c0,
+                                          uint8_t* rowbase, int m, bool relu) {
+  const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(bias + c0);
+  ulonglong2 bv[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) bv[i] = __ldg(b2 + i);
+  uint64_t x[16];
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    x[2 * i] = add_f32x2(((uint64_t)r[4 * i + 1] << 32) | r[4 * i], bv[i].x);
+    x[2 * i + 1] = add_f32x2(((uint64_t)r[4 * i + 3] << 32) | r[4 * i + 2], bv[i].y);
+  }
+  if (!relu) {
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const float lo = tanh_fast(__uint_as_float((uint32_t)x[i]));
+      const float hi = tanh_fast(__uint_as_float((uint32_t)(x[i] >> 32)));
+      x[i] = ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+    }
+  }
+  uint8_t* rowp = rowbase + (c0 / KCHUNK) * TILE_M * 128;
+  const int unit0 = (c0 % KCHUNK) / 8;
+#pragma unroll
+  for (int u = 0; u < 4; u++) {                    // 16-byte unit = 8 columns
+    uint4 w;
+    w.x = pack_bf16x2(x[4 * u + 0], relu);
+    w.y = pack_bf16x2(x[4 * u + 1], relu);
+    w.z = pack_bf16x2(x[4 * u + 2], relu);
+    w.w = pack_bf16x2(x[4 * u + 3], relu);
+    *reinterpret_cast<uint4*>(rowp + (((unit0 + u) ^ (m & 7)) * 16)) = w;
+  }
+}
+
 // Per-row outputs of one sampled channel: bins / int32 index / fp64 env command.
 __device__ __forceinline__ void emit_choice(const Launch& L, int act_dim, int64_t row, int g, int best) {
   if (L.bins) L.bins[row * L.bins_stride + L.bins_offset + g] = (uint8_t)best;
@@ -310,37 +363,40 @@ __device__ __forceinline__ float cat_head(uint32_t lane_addr, const float* __res
   return logp;
 }
 
-// Any other categorical shape (act_dim * num_bins <= 96).
+// One fp32 column of this warp's 32 TMEM lanes.
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  return __uint_as_float(r);
+}
+
+// Any other categorical shape (act_dim * num_bins <= 96): the logits are re-read from TMEM one
+// column at a time in each pass, so no per-thread array (and no local memory) is needed.
 __device__ __noinline__ void cat_head_generic(uint32_t lane_addr, const float* __restrict__ bias, const Launch& L,
                                               const NetParams& P, int64_t row, bool valid) {
-  const int W = P.width[P.n_layers - 1];
-  float lg[96];
-  for (int c0 = 0; c0 < 96; c0 += 32) tmem_ld32(lane_addr + (uint32_t)c0, lg + c0);
-  for (int i = 0; i < 96; i++) lg[i] += (i < W) ? __ldg(bias + i) : 0.0f;
+  const int nb = P.num_bins;
   const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step, row);
   float logp = 0.0f;
   for (int g = 0; g < P.act_dim; g++) {
-    const float* x = lg + g * P.num_bins;
+    const int c0 = g * nb;
     float mx = -INFINITY;
-    for (int b = 0; b < P.num_bins; b++) mx = fmaxf(mx, x[b]);
+    for (int b = 0; b < nb; b++) mx = fmaxf(mx, tmem_ld1(lane_addr + (uint32_t)(c0 + b)) + __ldg(bias + c0 + b));
     float se = 0.0f;
-    for (int b = 0; b < P.num_bins; b++) se += __expf(x[b] - mx);
-    const float lse = mx + logf(se);
     int best = 0;
-    float bestv = -INFINITY;
-    for (int b = 0; b < P.num_bins; b++) {
-      float sc = x[b];
+    float bestv = -INFINITY, chosen = 0.0f;
+    for (int b = 0; b < nb; b++) {
+      const float x = tmem_ld1(lane_addr + (uint32_t)(c0 + b)) + __ldg(bias + c0 + b);
+      se += __expf(x - mx);
+      float sc = x;
       if (!L.deterministic) sc += gumbel(key, (uint32_t)(g * 64 + b));
-      if (sc > bestv) { bestv = sc; best = b; }
+      if (sc > bestv) { bestv = sc; best = b; chosen = x; }
+      if (valid && L.logits) L.logits[row * L.logits_ld + c0 + b] = x;
     }
-    logp += x[best] - lse;
+    logp += chosen - (mx + logf(se));
     if (valid) emit_choice(L, P.act_dim, row, g, best);
   }
-  if (valid) {
-    if (L.logp) L.logp[row] = logp;
-    if (L.logits)
-      for (int i = 0; i < W; i++) L.logits[row * L.logits_ld + i] = lg[i];
-  }
+  if (valid && L.logp) L.logp[row] = logp;
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -492,36 +548,6 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           const int N = P.width_pad[l];
           const bool relu = P.act == 0;
           uint8_t* rowbase = act + (m >> 3) * 1024 + (m & 7) * 128;
-          auto convert = [&](const uint32_t* r, int c0) {
-            const float4* b4 = reinterpret_cast<const float4*>(bias + c0);
-            uint8_t* rowp = rowbase + (c0 / KCHUNK) * TILE_M * 128;
-            const int unit0 = (c0 % KCHUNK) / 8;
-#pragma unroll
-            for (int u = 0; u < 4; u++) {                  // 16-byte unit = 8 columns
-              const float4 ba = __ldg(b4 + 2 * u), bb = __ldg(b4 + 2 * u + 1);
-              float x[8] = {__uint_as_float(r[8 * u + 0]) + ba.x, __uint_as_float(r[8 * u + 1]) + ba.y,
-                            __uint_as_float(r[8 * u + 2]) + ba.z, __uint_as_float(r[8 * u + 3]) + ba.w,
-                            __uint_as_float(r[8 * u + 4]) + bb.x, __uint_as_float(r[8 * u + 5]) + bb.y,
-                            __uint_as_float(r[8 * u + 6]) + bb.z, __uint_as_float(r[8 * u + 7]) + bb.w};
-              if (relu) {
-#pragma unroll
-                for (int i = 0; i < 8; i++) x[i] = fmaxf(x[i], 0.0f);
-              } else {
-#pragma unroll
-                for (int i = 0; i < 8; i++) x[i] = tanh_fast(x[i]);
-              }
-              __nv_bfloat162 p0 = __floats2bfloat162_rn(x[0], x[1]);
-              __nv_bfloat162 p1 = __floats2bfloat162_rn(x[2], x[3]);
-              __nv_bfloat162 p2 = __floats2bfloat162_rn(x[4], x[5]);
-              __nv_bfloat162 p3 = __floats2bfloat162_rn(x[6], x[7]);
-              uint4 w;
-              w.x = *reinterpret_cast<uint32_t*>(&p0);
-              w.y = *reinterpret_cast<uint32_t*>(&p1);
-              w.z = *reinterpret_cast<uint32_t*>(&p2);
-              w.w = *reinterpret_cast<uint32_t*>(&p3);
-              *reinterpret_cast<uint4*>(rowp + (((unit0 + u) ^ (m & 7)) * 16)) = w;
-            }
-          };
           uint32_t ra[32], rb[32];
           int c = 32 * h;                                  // this warp's chunks: c, c + 64, ...
           if (c < N) {
@@ -530,12 +556,12 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           }
           while (c < N) {
             if (c + 64 < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + 64), rb);
-            convert(ra, c);
+            convert32(ra, bias, c, rowbase, m, relu);
             tmem_wait_ld();
             c += 64;
             if (c >= N) break;
             if (c + 64 < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + 64), ra);
-            convert(rb, c);
+            convert32(rb, bias, c, rowbase, m, relu);
             tmem_wait_ld();
             c += 64;
           }
