@@ -35,10 +35,15 @@ constexpr int NCHUNK = 256;                      // output columns per MMA / wei
 constexpr int STAGES = 3;
 constexpr int ACT_BYTES = 128 * 1024;            // 8 chunks x (128 rows x 128 B)
 constexpr int STAGE_BYTES = NCHUNK * 128;        // 32 KB
-constexpr int CTRL_BYTES = 1024;                 // barriers, TMEM base, head partial log-probs
+#ifndef F16_MLP_EPI_PER_QUARTER
+#define F16_MLP_EPI_PER_QUARTER 2
+#endif
+constexpr int EPI_PER_Q = F16_MLP_EPI_PER_QUARTER;   // epilogue warps per TMEM lane quarter (2 or 4)
+constexpr int CTRL_BYTES = 2048;                 // barriers, TMEM base, head partial log-probs
 constexpr int SMEM_BYTES = ACT_BYTES + STAGES * STAGE_BYTES + CTRL_BYTES + 1024;
-constexpr int EPI_WARPS = 8;                     // two per TMEM lane quarter, splitting the columns
-constexpr int THREADS = 64 + 32 * EPI_WARPS;     // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 epilogue
+constexpr int EPI_WARPS = 4 * EPI_PER_Q;         // the warps of a quarter split the columns
+constexpr int THREADS = 64 + 32 * EPI_WARPS;     // warp 0 TMA, warp 1 MMA + TMEM, then the epilogue
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 1.9 GHz
 
 enum Head : int { HEAD_HIDDEN_ONLY = 0, HEAD_CATEGORICAL = 1, HEAD_VALUE = 2 };
@@ -234,7 +239,7 @@ struct Smem {
   uint64_t full[STAGES], empty[STAGES];
   uint32_t tmem_base;
   int abort_flag;
-  float logp_part[TILE_M];                       // second-half channels' log-prob per tile row
+  float logp_part[EPI_PER_Q - 1][TILE_M];        // the other parts' channel log-probs per tile row
 };
 static_assert(sizeof(Smem) <= CTRL_BYTES, "control block");
 
@@ -312,13 +317,14 @@ __device__ __forceinline__ void emit_choice(const Launch& L, int act_dim, int64_
 }
 
 // Categorical head with compile-time shape (the reference's 4 channels x 21 bins), split over
-// the two epilogue warps of a lane quarter: half H handles channels [H*A/2, (H+1)*A/2).  Logits
-// stay in registers; per channel max, log-sum-exp, Gumbel-max (or argmax); returns this half's
-// part of the summed log-prob.
-template <int A, int NB, int H>
+// the PARTS epilogue warps of a lane quarter: part H handles channels [H*A/PARTS, (H+1)*A/PARTS).
+// Logits stay in registers; per channel max, log-sum-exp, Gumbel-max (or argmax); returns this
+// part's share of the summed log-prob.
+template <int A, int NB, int H, int PARTS>
 __device__ __forceinline__ float cat_head(uint32_t lane_addr, const float* __restrict__ bias, const Launch& L,
                                           int64_t row, bool valid) {
-  constexpr int GA = A / 2;                      // channels of this half
+  static_assert(A % PARTS == 0, "channels split evenly over the parts");
+  constexpr int GA = A / PARTS;                  // channels of this part
   constexpr int W = GA * NB;
   constexpr int C0 = H * W;                      // first logit column of this half
   constexpr int LB = C0 / 32 * 32;               // first TMEM column loaded
@@ -416,7 +422,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
     mbar_init(smem_u32(&S->acc_full), 1);
     mbar_init(smem_u32(&S->act_ready), 32 * EPI_WARPS);
     mbar_init(smem_u32(&S->tmem_empty), 32 * EPI_WARPS);
-    mbar_init(smem_u32(&S->logp_bar), TILE_M);
+    mbar_init(smem_u32(&S->logp_bar), TILE_M * (EPI_PER_Q - 1));
     mbar_init(smem_u32(&S->drain), 1);
     for (int s = 0; s < STAGES; s++) {
       mbar_init(smem_u32(&S->full[s]), 1);
@@ -520,9 +526,10 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2-9)
-    // Warp w may access TMEM lanes 32*(w%4)..+31 (its quarter of the tile rows); the two warps
-    // of a quarter split the columns: half h takes the 32-column chunks with index % 2 == h.
+    // ------------------------------------------------------------ epilogue (warps 2 and up)
+    // Warp w may access TMEM lanes 32*(w%4)..+31 (its quarter of the tile rows); the EPI_PER_Q
+    // warps of a quarter split the columns: part h takes the 32-column chunks with
+    // index % EPI_PER_Q == h.
     const int q = warp & 3;
     const int h = (warp - 2) >> 2;
     const int m = q * 32 + lane;                  // tile row of this thread
@@ -548,22 +555,34 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           const int N = P.width_pad[l];
           const bool relu = P.act == 0;
           uint8_t* rowbase = act + (m >> 3) * 1024 + (m & 7) * 128;
-          uint32_t ra[32], rb[32];
-          int c = 32 * h;                                  // this warp's chunks: c, c + 64, ...
-          if (c < N) {
-            tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
-            tmem_wait_ld();
-          }
-          while (c < N) {
-            if (c + 64 < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + 64), rb);
-            convert32(ra, bias, c, rowbase, m, relu);
-            tmem_wait_ld();
-            c += 64;
-            if (c >= N) break;
-            if (c + 64 < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + 64), ra);
-            convert32(rb, bias, c, rowbase, m, relu);
-            tmem_wait_ld();
-            c += 64;
+          constexpr int STEP = 32 * EPI_PER_Q;           // this warp's chunks: c, c + STEP, ...
+          if (EPI_PER_Q >= 4) {
+            // enough warps per scheduler to hide the TMEM load latency: one chunk at a time
+            for (int c = 32 * h; c < N; c += STEP) {
+              uint32_t ra[32];
+              tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
+              tmem_wait_ld();
+              convert32(ra, bias, c, rowbase, m, relu);
+            }
+          } else {
+            // the next chunk's TMEM load in flight while this one is converted
+            uint32_t ra[32], rb[32];
+            int c = 32 * h;
+            if (c < N) {
+              tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
+              tmem_wait_ld();
+            }
+            while (c < N) {
+              if (c + STEP < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + STEP), rb);
+              convert32(ra, bias, c, rowbase, m, relu);
+              tmem_wait_ld();
+              c += STEP;
+              if (c >= N) break;
+              if (c + STEP < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + STEP), ra);
+              convert32(rb, bias, c, rowbase, m, relu);
+              tmem_wait_ld();
+              c += STEP;
+            }
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           tc_fence_before();
@@ -582,15 +601,25 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
               }
             }
           } else if (P.act_dim == 4 && P.num_bins == 21) {
-            // channels 0-1 on half 0, 2-3 on half 1; half 1's log-prob joins through shared memory
-            if (h == 1) {
-              float part = cat_head<4, 21, 1>(lane_addr, bias, L, row, valid);
-              S->logp_part[m] = part;
+            // the channels split over the quarter's parts; the other parts' log-probs join part 0
+            // through shared memory
+            if (h != 0) {
+              float part;
+              if (EPI_PER_Q == 2) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr, bias, L, row, valid);
+              else if (h == 1) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr, bias, L, row, valid);
+              else if (h == 2) part = cat_head<4, 21, 2 % EPI_PER_Q, EPI_PER_Q>(lane_addr, bias, L, row, valid);
+              else part = cat_head<4, 21, 3 % EPI_PER_Q, EPI_PER_Q>(lane_addr, bias, L, row, valid);
+              S->logp_part[h - 1][m] = part;
               mbar_arrive(smem_u32(&S->logp_bar));
             } else {
-              float part = cat_head<4, 21, 0>(lane_addr, bias, L, row, valid);
-              if (!mbar_wait(smem_u32(&S->logp_bar), heads & 1, abort_flag)) ok = false;
-              else if (valid && L.logp) L.logp[row] = part + S->logp_part[m];
+              float part = cat_head<4, 21, 0, EPI_PER_Q>(lane_addr, bias, L, row, valid);
+              if (!mbar_wait(smem_u32(&S->logp_bar), heads & 1, abort_flag)) {
+                ok = false;
+              } else if (valid && L.logp) {
+#pragma unroll
+                for (int k = 0; k < EPI_PER_Q - 1; k++) part += S->logp_part[k][m];
+                L.logp[row] = part;
+              }
             }
             heads++;
           } else if (h == 0) {
