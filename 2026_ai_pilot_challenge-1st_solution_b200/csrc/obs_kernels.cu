@@ -12,6 +12,13 @@ namespace f16 {
 namespace obs {
 
 constexpr int OBS_THREADS = 128;
+// Resident blocks per SM the step kernels are compiled for (64 registers per thread): the row
+// builder's live set does not fit in registers at any occupancy, and trading register spills
+// (to L1, which these kernels do not otherwise use) for 32 resident warps measured fastest on a
+// B200 (sweep 1..16: post-step 0.58 -> 0.44 ms, obs step 1.00 -> 0.84 ms).
+#ifndef F16_OBS_MIN_BLOCKS
+#define F16_OBS_MIN_BLOCKS 8
+#endif
 
 template <int LAYOUT>
 struct RowRef {
@@ -193,7 +200,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs_advance(const double* __res
 // Fused: advance (reward, termination, reconstruction update) then both observation rows,
 // reading each FDM row once (the reference launches advance_kernel then build_obs_kernel).
 template <int LAYOUT>
-__global__ void __launch_bounds__(OBS_THREADS) k_obs_step(const double* __restrict__ st, int64_t ld, int64_t nenv,
+__global__ void __launch_bounds__(OBS_THREADS, F16_OBS_MIN_BLOCKS) k_obs_step(const double* __restrict__ st, int64_t ld, int64_t nenv,
                                                           const double* __restrict__ actions, const f16_recon rc,
                                                           const f16_reward_cfg cfg, const f16_origin og,
                                                           double* __restrict__ reward, uint8_t* __restrict__ term,
@@ -233,7 +240,7 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs_init_reward(const double* _
 // environments the autoreset from the IC pool (state rows, reconstruction reset, reward-tracker
 // anchoring, fresh observations).  pool: (pool_size, 2, 101) AoS rows; pick: pool row per env.
 template <int LAYOUT>
-__global__ void __launch_bounds__(OBS_THREADS) k_env_post(double* __restrict__ st, int64_t ld, int64_t nenv,
+__global__ void __launch_bounds__(OBS_THREADS, F16_OBS_MIN_BLOCKS) k_env_post(double* __restrict__ st, int64_t ld, int64_t nenv,
                                                           const double* __restrict__ actions, const f16_recon rc,
                                                           const f16_reward_cfg cfg, const f16_origin og,
                                                           const double* __restrict__ pool, int64_t pool_size,
