@@ -67,6 +67,8 @@ _SIGS = {
     "f16_env_post_step": ([_P, C.c_int, _I64, _I64, _P, _PR, _PC, _PO, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P,
                            _P, _P, _P], C.c_int),
     "f16_state9": ([_P, C.c_int, _I64, _I64, _PO, _P, _P], C.c_int),
+    "f16_external_accel": ([_P, C.c_int, _I64, _I64, _P, _P, _P, _PO, C.c_double, _P], C.c_int),
+    "f16_external_obs": ([_P, C.c_int, _I64, _I64, _P, _P, _P, _PO, _P], C.c_int),
     "f16_gae": ([_P, _P, _P, _P, _P, C.c_int, _I64, _I64, C.c_double, C.c_double, _P, _P, _P], C.c_int),
     "f16_mlp_set_create": ([_P, C.c_int, _P], C.c_int),
     "f16_mlp_set_destroy": ([_P], C.c_int),

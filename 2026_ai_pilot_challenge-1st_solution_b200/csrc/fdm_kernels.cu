@@ -13,7 +13,7 @@ namespace f16 {
 // Launch shape: 256 threads x 2 resident blocks per SM caps the kernel at 128 registers
 // (16 warps/SM).  Measured on B200 for the cfg2 step (131,072 aircraft, 6 frames):
 // 128x3 (168 regs) 0.304 ms, 128x4 0.259 ms, 128x5 (96 regs) 0.286 ms, 256x2 0.253 ms; at higher
-// occupancy the spills win nothing back: 256x3 (85 regs) 3.4e9 -> 1.9e9 frames/s, 256x4 / 128x8
+// occupancy the spills win nothing back: 256x3 (85 regs) 1.9e9 frames/s, 256x4 / 128x8
 // (64 regs) 2.3e9 / 2.2e9 against 3.0e9 for 256x2.
 #ifndef F16_FDM_THREADS
 #define F16_FDM_THREADS 256

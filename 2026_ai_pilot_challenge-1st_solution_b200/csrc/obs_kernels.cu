@@ -320,6 +320,71 @@ __global__ void __launch_bounds__(OBS_THREADS) k_state9(const double* __restrict
   for (int i = 0; i < 9; i++) s9[a * 9 + i] = v[i];
 }
 
+// ---------------- external 214-D observation (R/cuda_fdm/external_observation.cu) ----------------
+// Per aircraft: NED velocity from the 9-DoF state; acceleration = (v - v_prev) / dt where the
+// aircraft's attitude history is valid (0 otherwise); v becomes v_prev.  Launched before the
+// advance (which sets prev_valid), as BatchObsReward.kernel_advance does (obs_reward.py:417-420).
+template <int LAYOUT>
+__global__ void __launch_bounds__(OBS_THREADS) k_external_accel(const double* __restrict__ st, int64_t ld, int64_t nac,
+                                                                const uint8_t* __restrict__ valid,
+                                                                double* __restrict__ previous,
+                                                                double* __restrict__ accel, const f16_origin og,
+                                                                double dt) {
+  int64_t a = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= nac) return;
+  Origin O = origin_of(og);
+  double s[9];
+  kin9(RowRef<LAYOUT>{st, ld, a}, O, s);
+  M3 R = ned2body(s[3], s[4], s[5]);
+  V3 v = mvT(R, V3{s[6], s[7], s[8]});
+  const double vv[3] = {v.x, v.y, v.z};
+  const bool ok = valid[a] != 0;
+  for (int i = 0; i < 3; i++) {
+    accel[a * 3 + i] = ok ? (vv[i] - previous[a * 3 + i]) / dt : 0.0;
+    previous[a * 3 + i] = vv[i];
+  }
+}
+
+// The 214-D row of aircraft a: columns 0-163 of its 184-D row, then 30 acceleration features
+// (own acceleration in the world, own-body, target-body, target-velocity and line-of-sight
+// frames; the target's in the world, own-body, target-body, own-velocity and line-of-sight
+// frames; each clamped to +-150 m/s^2 and scaled to [-1, 1]), then the 20 action-history values.
+template <int LAYOUT>
+__global__ void __launch_bounds__(OBS_THREADS) k_external_obs(const double* __restrict__ st, int64_t ld, int64_t nac,
+                                                              const double* __restrict__ accel,
+                                                              const float* __restrict__ obs184,
+                                                              float* __restrict__ out, const f16_origin og) {
+  int64_t a = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (a >= nac) return;
+  const int64_t b = a ^ 1;
+  Origin O = origin_of(og);
+  double s[9], t[9];
+  kin9(RowRef<LAYOUT>{st, ld, a}, O, s);
+  kin9(RowRef<LAYOUT>{st, ld, b}, O, t);
+  const M3 Ro = ned2body(s[3], s[4], s[5]), Rt = ned2body(t[3], t[4], t[5]);
+  const V3 vo = mvT(Ro, V3{s[6], s[7], s[8]}), vt = mvT(Rt, V3{t[6], t[7], t[8]});
+  const M3 Fo = dir_frame(vo), Ft = dir_frame(vt), Fl = dir_frame(V3{t[0] - s[0], t[1] - s[1], t[2] - s[2]});
+  M3 I;
+  for (int i = 0; i < 3; i++)
+    for (int j = 0; j < 3; j++) I.m[i][j] = i == j ? 1.0 : 0.0;
+  const float* src = obs184 + a * 184;
+  float* row = out + a * 214;
+  for (int i = 0; i < 164; i++) row[i] = src[i];
+  const V3 acc_a = {accel[a * 3], accel[a * 3 + 1], accel[a * 3 + 2]};
+  const V3 acc_b = {accel[b * 3], accel[b * 3 + 1], accel[b * 3 + 2]};
+  // frame order of the ten vectors: I, own body, target body, target velocity, LOS (own
+  // acceleration); I, own body, target body, own velocity, LOS (target acceleration)
+  const M3* frames[10] = {&I, &Ro, &Rt, &Ft, &Fl, &I, &Ro, &Rt, &Fo, &Fl};
+#pragma unroll
+  for (int i = 0; i < 10; i++) {
+    const V3 v = mv(*frames[i], i < 5 ? acc_a : acc_b);
+    row[164 + 3 * i + 0] = store_val(normz(v.x, -150.0, 150.0));
+    row[164 + 3 * i + 1] = store_val(normz(v.y, -150.0, 150.0));
+    row[164 + 3 * i + 2] = store_val(normz(v.z, -150.0, 150.0));
+  }
+  for (int i = 0; i < 20; i++) row[194 + i] = src[164 + i];
+}
+
 inline int grid_for(int64_t n) { return (int)((n + OBS_THREADS - 1) / OBS_THREADS); }
 
 inline int check_recon(const f16_recon* rc, bool need_all) {
@@ -436,5 +501,36 @@ extern "C" int f16_state9(const double* state, int layout, int64_t ld, int64_t n
   if (layout == F16_LAYOUT_SOA && ld < nac) return F16_ERR_ARG;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   F16_DISPATCH_LAYOUT(layout, k_state9, grid_for(nac), state, ld, nac, *origin, s9);
+  return launch_status();
+}
+
+extern "C" int f16_external_accel(const double* state, int layout, int64_t ld, int64_t nac, const uint8_t* valid,
+                                  double* previous, double* accel, const f16_origin* origin, double dt,
+                                  f16_stream_t stream) {
+  if (!state || !valid || !previous || !accel || !origin || nac <= 0 || !(dt > 0.0)) return F16_ERR_ARG;
+  if (layout != F16_LAYOUT_SOA && layout != F16_LAYOUT_AOS) return F16_ERR_ARG;
+  if (layout == F16_LAYOUT_SOA && ld < nac) return F16_ERR_ARG;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (layout == F16_LAYOUT_SOA)
+    obs::k_external_accel<F16_LAYOUT_SOA><<<obs::grid_for(nac), obs::OBS_THREADS, 0, s>>>(state, ld, nac, valid,
+                                                                                          previous, accel, *origin, dt);
+  else
+    obs::k_external_accel<F16_LAYOUT_AOS><<<obs::grid_for(nac), obs::OBS_THREADS, 0, s>>>(state, ld, nac, valid,
+                                                                                          previous, accel, *origin, dt);
+  return launch_status();
+}
+
+extern "C" int f16_external_obs(const double* state, int layout, int64_t ld, int64_t nac, const double* accel,
+                                const float* obs184, float* out214, const f16_origin* origin, f16_stream_t stream) {
+  if (!state || !accel || !obs184 || !out214 || !origin || nac <= 0 || (nac & 1)) return F16_ERR_ARG;
+  if (layout != F16_LAYOUT_SOA && layout != F16_LAYOUT_AOS) return F16_ERR_ARG;
+  if (layout == F16_LAYOUT_SOA && ld < nac) return F16_ERR_ARG;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (layout == F16_LAYOUT_SOA)
+    obs::k_external_obs<F16_LAYOUT_SOA><<<obs::grid_for(nac), obs::OBS_THREADS, 0, s>>>(state, ld, nac, accel, obs184,
+                                                                                        out214, *origin);
+  else
+    obs::k_external_obs<F16_LAYOUT_AOS><<<obs::grid_for(nac), obs::OBS_THREADS, 0, s>>>(state, ld, nac, accel, obs184,
+                                                                                        out214, *origin);
   return launch_status();
 }

@@ -160,6 +160,7 @@ class BatchObsReward:
         sp, lay, ld, keep = self._kernel_states(states)
         ac = self._actions(actions)
         recon = self._recon()
+        self._external_advance(sp, lay, ld)
         _lib.check(self.lib.f16_obs_advance(sp, lay, ld, self.nenv, ac.data_ptr(), recon, rc, self._origin,
                                             self.reward_buf.data_ptr(), self.term_buf.data_ptr(),
                                             self.trunc_buf.data_ptr(), _lib.stream_of(self.hp)), "f16_obs_advance")
@@ -187,11 +188,44 @@ class BatchObsReward:
         sp, lay, ld, keep = self._kernel_states(states)
         ac = self._actions(actions)
         aux = self.aux_features.data_ptr() if self.aux_features is not None else None
+        self._external_advance(sp, lay, ld)
         _lib.check(self.lib.f16_obs_step(sp, lay, ld, self.nenv, ac.data_ptr(), self._recon(), rc, self._origin,
                                          self.reward_buf.data_ptr(), self.term_buf.data_ptr(),
                                          self.trunc_buf.data_ptr(), self.obs_buf.data_ptr(), aux,
                                          _lib.stream_of(self.hp)), "f16_obs_step")
         return self.obs_buf, self.reward_buf, self.term_buf, self.trunc_buf
+
+    # ---- external 214-D observation (obs_reward.py:471-496, external_observation.cu) ----
+    def enable_external_observations(self):
+        """Optional extra state for frozen 214-D opponents; never changes the 184-D rows or the
+        reward."""
+        if hasattr(self, "external_accel"):
+            return
+        n, dev = self.nac, self.device
+        self.external_previous_velocity = torch.zeros(n, 3, device=dev, dtype=self.dtype)
+        self.external_accel = torch.zeros_like(self.external_previous_velocity)
+        self.external_obs = torch.zeros(n, 214, device=dev, dtype=torch.float32)
+        self._AC_KEYS = self._AC_KEYS + ("external_previous_velocity", "external_accel")
+
+    def _external_advance(self, sp, lay, ld):
+        """The acceleration update that precedes the advance when external rows are enabled."""
+        if not hasattr(self, "external_accel"):
+            return
+        _lib.check(self.lib.f16_external_accel(sp, lay, ld, self.nac, self.prev_valid.data_ptr(),
+                                               self.external_previous_velocity.data_ptr(),
+                                               self.external_accel.data_ptr(), self._origin, float(self.dt),
+                                               _lib.stream_of(self.hp)), "f16_external_accel")
+
+    def build_external_obs(self, states):
+        """(nac, 214) rows: the 184-D rows rebuilt from `states` with the 30 acceleration features
+        inserted before the action history."""
+        self.enable_external_observations()
+        self.kernel_build_obs(states)
+        sp, lay, ld, keep = self._kernel_states(states)
+        _lib.check(self.lib.f16_external_obs(sp, lay, ld, self.nac, self.external_accel.data_ptr(),
+                                             self.obs_buf.data_ptr(), self.external_obs.data_ptr(), self._origin,
+                                             _lib.stream_of(self.hp)), "f16_external_obs")
+        return self.external_obs
 
     # ---- state bookkeeping (obs_reward.py:498-562) ----
     def reset_all(self):
@@ -200,11 +234,16 @@ class BatchObsReward:
         self.last_dmg_dealt.zero_(); self.last_dmg_taken.zero_(); self.hp_loss.zero_()
         self.act_hist.zero_(); self.prev_x.zero_(); self.prev_x_valid.zero_()
         self.prev_alt_log.zero_()
+        if hasattr(self, "external_accel"):
+            self.external_accel.zero_(); self.external_previous_velocity.zero_()
 
     def reset_envs(self, env_mask):
         """Reset the reconstruction state of the masked envs in place, without a host sync."""
         ac = env_mask.repeat_interleave(2)
         ac1 = ac.unsqueeze(1)
+        if hasattr(self, "external_accel"):
+            self.external_accel.masked_fill_(ac1, 0.0)
+            self.external_previous_velocity.masked_fill_(ac1, 0.0)
         self.hp.masked_fill_(ac, 1.0)
         self.fuel.masked_fill_(ac, 1.0)
         self.t_sec.masked_fill_(env_mask, 0.0)

@@ -289,6 +289,7 @@ class GpuDogfightVecEnv:
                              self.alt_hunt_coef)
         aux = obr.aux_features.data_ptr() if obr.aux_features is not None else None
         term_obs = self._terminal_obs.data_ptr() if self.terminal_obs_enabled else None
+        obr._external_advance(_lib.ptr(sim.states_soa), _lib.LAYOUT_SOA, self.nac)
         _lib.check(self.lib.f16_env_post_step(
             _lib.ptr(sim.states_soa), _lib.LAYOUT_SOA, self.nac, self.nenv, _lib.ptr(self._actions), obr._recon(), rc,
             obr._origin, _lib.ptr(self.ic_pool), self.ic_pool_size, _lib.ptr(pick), _lib.ptr(obr.reward_buf),
@@ -297,6 +298,10 @@ class GpuDogfightVecEnv:
         term = obr.term_buf.bool()
         trunc = obr.trunc_buf.bool()
         done = self._done.bool()
+        if hasattr(obr, "external_accel"):                  # autoreset clears the external state too
+            d1 = done.repeat_interleave(2).unsqueeze(1)
+            obr.external_accel.masked_fill_(d1, 0.0)
+            obr.external_previous_velocity.masked_fill_(d1, 0.0)
         reward = obr.reward_buf.view(self.nenv, 2).clone()
         obs = obr.obs_buf.view(self.nenv, 2, self.OBS_SIZE)
         info = {"terminated": term, "truncated": trunc,

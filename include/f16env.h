@@ -220,6 +220,19 @@ int f16_env_post_step(double* state, int layout, int64_t ld, int64_t nenv, const
 int f16_state9(const double* state, int layout, int64_t ld, int64_t nac, const f16_origin* origin,
                double* s9, f16_stream_t stream);
 
+/* External 214-D observation for frozen external opponents (no counterpart kernel on the main
+ * path; replaces R/cuda_fdm/external_observation.cu external_acceleration / external_observation
+ * launched by BatchObsReward.kernel_advance / build_external_obs, obs_reward.py:417-420, 487-496).
+ * f16_external_accel: per aircraft NED velocity -> accel = (v - previous) / dt where valid[a]
+ *   (the recon prev_valid BEFORE the advance updates it; 0 otherwise), previous = v.
+ *   previous, accel: [nac][3] fp64.
+ * f16_external_obs: out214 [nac][214] fp32 from the 184-D rows obs184 [nac][184] and accel. */
+int f16_external_accel(const double* state, int layout, int64_t ld, int64_t nac, const uint8_t* valid,
+                       double* previous, double* accel, const f16_origin* origin, double dt,
+                       f16_stream_t stream);
+int f16_external_obs(const double* state, int layout, int64_t ld, int64_t nac, const double* accel,
+                     const float* obs184, float* out214, const f16_origin* origin, f16_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------
  * (3) Policy / value MLP forward on the tcgen05 tensor cores (bf16 in, fp32 accumulate).
  * Replaces the rollout forwards of R/claude_code/model.py MLPDiscreteActorCritic (actor_logits,

@@ -6,6 +6,9 @@
   FCS dt 1/120), host-compiled from where it lies under the reference tree.
 * ``oracle/_ref/libf16ref_r36.so``  -- the same for research/competition_36500/runtime
   (FCS dt 1/60, the 184-D lineage).
+* ``oracle/_ref/libobsref.so``      -- the reference's own observation / reward kernels
+  (research/competition_36500/runtime/cuda_fdm/gen/obs_kernel.cu with external_observation.cu),
+  host-compiled through ref_obs_driver.cpp.
 
 The ``_ref`` builds need the reference tree (the ``F16_REFERENCE`` directory, default: the local reference checkout); on a
 machine without it they are skipped and the previously built files are used as they are.
@@ -52,6 +55,15 @@ def build_ref(force=False):
                       "-o", out, "-lm"])
         if out.exists():
             built[name] = out
+    # the reference's own observation / reward kernels (184-D lineage), host-compiled
+    r36 = REF_LINEAGES["r36"]
+    out = outdir / "libobsref.so"
+    if (r36 / "obs_kernel.cu").exists():
+        drv = HERE / "ref_obs_driver.cpp"
+        if force or not out.exists() or drv.stat().st_mtime > out.stat().st_mtime:
+            _run(["g++", "-std=c++14", *CFLAGS, "-I", r36, "-I", r36.parent, drv, "-o", out, "-lm"])
+    if out.exists():
+        built["obs"] = out
     return built
 
 

@@ -38,7 +38,10 @@ def _lib():
                                           _U8, C.c_long, _D, _D, C.c_int]
         lb.oracle_obs_build.argtypes = [_D, _U8, _D, _D, _D, _D, _D, _D, _D, _F, C.c_long, _D, _D]
         lb.oracle_kin9.argtypes = [_D, C.c_long, _D, _D]
-        for f in ("oracle_obs_init_reward", "oracle_obs_advance", "oracle_obs_build", "oracle_kin9"):
+        lb.oracle_external_accel.argtypes = [_D, _U8, _D, _D, C.c_long, _D, C.c_double]
+        lb.oracle_external_obs.argtypes = [_D, _D, _F, _F, C.c_long, _D]
+        for f in ("oracle_obs_init_reward", "oracle_obs_advance", "oracle_obs_build", "oracle_kin9",
+                  "oracle_external_accel", "oracle_external_obs"):
             getattr(lb, f).restype = None
         _bound = True
     return lb
@@ -123,3 +126,104 @@ class ObsOracle:
         out = np.zeros((st.shape[0], 9))
         _lib().oracle_kin9(_p(st, _D), st.shape[0], _p(self.origin, _D), _p(out, _D))
         return out
+
+
+def external_accel(states, valid, previous, accel, dt=0.1):
+    """oracle_external_accel over (nac,101) states; previous / accel (nac,3) updated in place."""
+    st = np.ascontiguousarray(states, dtype=np.float64)
+    o7 = origin7()
+    _lib().oracle_external_accel(_p(st, _D), _p(np.ascontiguousarray(valid, dtype=np.uint8), _U8),
+                                 _p(previous, _D), _p(accel, _D), st.shape[0], _p(o7, _D), float(dt))
+
+
+def external_obs(states, accel, obs184):
+    """oracle_external_obs: (nac,214) float32 rows from (nac,101) states, (nac,3) accelerations
+    and the (nac,184) observation rows."""
+    st = np.ascontiguousarray(states, dtype=np.float64)
+    acc = np.ascontiguousarray(accel, dtype=np.float64)
+    orig = np.ascontiguousarray(obs184, dtype=np.float32)
+    out = np.zeros((st.shape[0], 214), dtype=np.float32)
+    o7 = origin7()
+    _lib().oracle_external_obs(_p(st, _D), _p(acc, _D), _p(orig, _F), _p(out, _F), st.shape[0], _p(o7, _D))
+    return out
+
+
+_REF = None
+
+
+def ref_available():
+    from pathlib import Path
+    return (Path(__file__).resolve().parent / "_ref" / "libobsref.so").exists()
+
+
+def _ref():
+    """The reference's own obs_kernel.cu + external_observation.cu, host-compiled (oracle/_ref)."""
+    global _REF
+    if _REF is None:
+        from pathlib import Path
+        lb = C.CDLL(str(Path(__file__).resolve().parent / "_ref" / "libobsref.so"))
+        lb.ref_obs_init_reward.argtypes = [_D, _U8, _D, _U8, _D, _D, C.c_int, _D]
+        lb.ref_obs_advance.argtypes = [_D, _D, _D, _D, _D, _D, _U8, _D, _D, _D, _D, _D, _D, _U8, _D, _D, _U8, _U8,
+                                       C.c_int, _D, _D, C.c_int]
+        lb.ref_obs_build.argtypes = [_D, _U8, _D, _D, _D, _D, _D, _D, _D, _F, C.c_int, _D, _D]
+        lb.ref_external_accel.argtypes = [_D, _U8, _D, _D, C.c_int, _D, C.c_double]
+        lb.ref_external_obs.argtypes = [_D, _D, _F, _F, C.c_int, _D]
+        for f in ("ref_obs_init_reward", "ref_obs_advance", "ref_obs_build", "ref_external_accel",
+                  "ref_external_obs"):
+            getattr(lb, f).restype = None
+        _REF = lb
+    return _REF
+
+
+class ObsRef(ObsOracle):
+    """Same buffers and calls as ObsOracle, run through the reference's own kernels."""
+
+    def init_reward(self, states, env_mask=None):
+        st = np.ascontiguousarray(states, np.float64)
+        m = np.ones(self.nenv, np.uint8) if env_mask is None else np.ascontiguousarray(env_mask, np.uint8)
+        _ref().ref_obs_init_reward(_p(st, _D), _p(m, _U8), _p(self.prev_x, _D), _p(self.prev_x_valid, _U8),
+                                   _p(self.prev_alt_log, _D), _p(self.t_sec, _D), self.nenv, _p(self.origin, _D))
+
+    def advance(self, states, actions, mode=0, **cfg):
+        p = dict(DEFAULT_REWARD, **cfg)
+        rp = np.array([p[k] for k in _RP_ORDER], dtype=np.float64)
+        st = np.ascontiguousarray(states, np.float64)
+        ac = np.ascontiguousarray(actions, np.float64)
+        reward = np.zeros(self.nac)
+        term = np.zeros(self.nenv, np.uint8)
+        trunc = np.zeros(self.nenv, np.uint8)
+        _ref().ref_obs_advance(
+            _p(st, _D), _p(ac, _D), _p(self.hp, _D), _p(self.fuel, _D), _p(self.t_sec, _D), _p(self.prev_att, _D),
+            _p(self.prev_valid, _U8), _p(self.pqr, _D), _p(self.last_dmg_dealt, _D), _p(self.last_dmg_taken, _D),
+            _p(self.hp_loss, _D), _p(self.act_hist, _D), _p(self.prev_x, _D), _p(self.prev_x_valid, _U8),
+            _p(self.prev_alt_log, _D), _p(reward, _D), _p(term, _U8), _p(trunc, _U8), self.nenv, _p(self.origin, _D),
+            _p(rp, _D), int(mode))
+        return reward, term, trunc
+
+    def build_obs(self, states, env_mask=None, obs=None, aux=False):
+        st = np.ascontiguousarray(states, np.float64)
+        out = np.zeros((self.nac, 184), np.float32) if obs is None else obs
+        m = np.ones(self.nenv, np.uint8) if env_mask is None else np.ascontiguousarray(env_mask, np.uint8)
+        ax = np.zeros((self.nenv, 21)) if aux else None
+        _ref().ref_obs_build(_p(st, _D), _p(m, _U8), _p(self.hp, _D), _p(self.fuel, _D), _p(self.t_sec, _D),
+                             _p(self.pqr, _D), _p(self.last_dmg_dealt, _D), _p(self.last_dmg_taken, _D),
+                             _p(self.act_hist, _D), out.ctypes.data_as(_F), self.nac, _p(self.origin, _D),
+                             _p(ax, _D))
+        return (out, ax) if aux else out
+
+
+def ref_external_accel(states, valid, previous, accel, dt=0.1):
+    st = np.ascontiguousarray(states, dtype=np.float64)
+    o7 = origin7()
+    _ref().ref_external_accel(_p(st, _D), _p(np.ascontiguousarray(valid, dtype=np.uint8), _U8), _p(previous, _D),
+                              _p(accel, _D), st.shape[0], _p(o7, _D), float(dt))
+
+
+def ref_external_obs(states, accel, obs184):
+    st = np.ascontiguousarray(states, dtype=np.float64)
+    acc = np.ascontiguousarray(accel, dtype=np.float64)
+    orig = np.ascontiguousarray(obs184, dtype=np.float32)
+    out = np.zeros((st.shape[0], 214), dtype=np.float32)
+    o7 = origin7()
+    _ref().ref_external_obs(_p(st, _D), _p(acc, _D), _p(orig, _F), _p(out, _F), st.shape[0], _p(o7, _D))
+    return out

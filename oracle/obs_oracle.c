@@ -539,3 +539,62 @@ void oracle_kin9(const double* states, long nac, const double* origin7, double* 
   Origin O = origin(origin7);
   for (long a = 0; a < nac; a++) kin9(states + a * 101, &O, s9 + a * 9);
 }
+
+/* ---------------------------------------------------------------------------------------------
+ * External 214-D observation for frozen external opponents
+ * (research/competition_36500/runtime/cuda_fdm/external_observation.cu, run by
+ * BatchObsReward.kernel_advance / build_external_obs, obs_reward.py:417-420, 487-496).
+ * ------------------------------------------------------------------------------------------- */
+
+/* external_acceleration (:2-9): NED velocity of each aircraft from its 9-DoF state; the
+   finite-difference acceleration against the stored previous velocity where the aircraft's
+   attitude history is valid (0 otherwise); the velocity becomes the stored previous one. */
+void oracle_external_accel(const double* states, const uint8_t* valid, double* previous, double* accel, long nac,
+                           const double* origin7, double dt) {
+  Origin O = origin(origin7);
+  for (long a = 0; a < nac; a++) {
+    double s[9], R[3][3], v[3];
+    kin9(states + a * 101, &O, s);
+    ned2body(s[3], s[4], s[5], R);
+    mvT(R, s + 6, v);
+    for (int i = 0; i < 3; i++) {
+      accel[a * 3 + i] = valid[a] ? (v[i] - previous[a * 3 + i]) / dt : 0.0;
+      previous[a * 3 + i] = v[i];
+    }
+  }
+}
+
+/* external_observation (:10-28): the 184-D row with 30 acceleration features inserted before
+   the 20-value action history: own acceleration in the world, own-body, target-body,
+   target-velocity and line-of-sight frames, then the target's in the world, own-body,
+   target-body, own-velocity and line-of-sight frames, each clamped to +-150 m/s^2 and scaled
+   to [-1, 1]. */
+void oracle_external_obs(const double* states, const double* accel, const float* original, float* out, long nac,
+                         const double* origin7) {
+  Origin O = origin(origin7);
+  for (long a = 0; a < nac; a++) {
+    long b = a ^ 1;
+    double s[9], t[9], Ro[3][3], Rt[3][3], vo[3], vt[3], delta[3];
+    kin9(states + a * 101, &O, s);
+    kin9(states + b * 101, &O, t);
+    ned2body(s[3], s[4], s[5], Ro);
+    ned2body(t[3], t[4], t[5], Rt);
+    mvT(Ro, s + 6, vo);
+    mvT(Rt, t + 6, vt);
+    for (int i = 0; i < 3; i++) delta[i] = t[i] - s[i];
+    double I[3][3] = {{1, 0, 0}, {0, 1, 0}, {0, 0, 1}}, Fo[3][3], Ft[3][3], Fl[3][3];
+    dir_frame(vo, Fo);
+    dir_frame(vt, Ft);
+    dir_frame(delta, Fl);
+    const double (*F[6])[3] = {I, Ro, Rt, Fo, Ft, Fl};
+    static const int order[10] = {0, 1, 2, 4, 5, 0, 1, 2, 3, 5};
+    float* row = out + a * 214;
+    for (int i = 0; i < 164; i++) row[i] = original[a * 184 + i];
+    for (int i = 0; i < 10; i++) {
+      double v[3];
+      mv(F[order[i]], accel + (i < 5 ? a : b) * 3, v);
+      for (int j = 0; j < 3; j++) row[164 + i * 3 + j] = store(normz(v[j], -150.0, 150.0));
+    }
+    for (int i = 0; i < 20; i++) row[194 + i] = original[a * 184 + 164 + i];
+  }
+}
