@@ -273,6 +273,19 @@ class BatchObsReward:
         if self.aux_features is not None:
             buf["aux_features"][env_mask] = self.aux_features[env_mask]
 
+    def capture_where(self, buf, env_mask):
+        """capture_into without boolean indexing: buf[k] = where(mask, current, buf[k]) for every
+        reconstruction buffer, so no host synchronisation is needed."""
+        ac = env_mask.repeat_interleave(2)
+        for k in self._AC_KEYS:
+            cur = getattr(self, k)
+            m = ac.view(-1, *([1] * (cur.dim() - 1)))
+            buf[k].copy_(torch.where(m, cur, buf[k]))
+        for k in self._ENV_KEYS:
+            buf[k].copy_(torch.where(env_mask, getattr(self, k), buf[k]))
+        if self.aux_features is not None:
+            buf["aux_features"].copy_(torch.where(env_mask.view(-1, 1), self.aux_features, buf["aux_features"]))
+
     def restore(self, buf):
         for k in self._AC_KEYS + self._ENV_KEYS:
             getattr(self, k).copy_(buf[k])

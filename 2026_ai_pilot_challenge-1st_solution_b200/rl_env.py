@@ -163,7 +163,12 @@ class GpuDogfightVecEnv:
         return self.obr.kernel_build_obs(self.sim.states).view(self.nenv, 2, self.OBS_SIZE)
 
     # ---- reset (rl_env.py:368-441) ----
-    def reset(self, stagger=True, max_stagger_steps=256, warmup_action_fn=None):
+    def reset(self, stagger=True, max_stagger_steps=256, warmup_action_fn=None, sync_free=True):
+        """Fresh ICs for every env; with ``stagger`` each env is then advanced a random number of
+        valid steps (rl_env.py:386-441).  ``sync_free`` (default) runs that warm-up entirely on
+        the device (departed envs re-seeded from the IC pool); ``sync_free=False`` follows the
+        reference loop, which checks masks on the host every step and re-seeds departed envs with
+        freshly sampled ICs."""
         seeds = self._build_all_seeds()
         if not bool(torch.isfinite(seeds).all()):
             raise FloatingPointError("non-finite initial physical states")
@@ -171,8 +176,70 @@ class GpuDogfightVecEnv:
         self.obr.reset_all()
         self.obr.kernel_init_reward_state(self.sim.states)
         if stagger and max_stagger_steps > 0:
-            self._staggered_warmup(max_stagger_steps, warmup_action_fn)
+            if sync_free:
+                self._staggered_warmup_device(max_stagger_steps, warmup_action_fn)
+            else:
+                self._staggered_warmup(max_stagger_steps, warmup_action_fn)
         return self.obr.kernel_build_obs(self.sim.states).view(self.nenv, 2, self.OBS_SIZE)
+
+    def _staggered_warmup_device(self, max_steps, action_fn, check_every=0):
+        """The staggered warm-up with every decision on the device: per env a target phase in
+        [0, max_steps); each step the physics kernel, the advance kernel and the departure test
+        run for all envs; departed, not yet captured envs are re-seeded from the IC pool (the
+        autoreset pool, same IC distribution) and restart their count; envs reaching their target
+        are captured with masked copies (torch.where, no boolean indexing).  The only host reads
+        are the final finiteness check and, when ``check_every`` > 0, an all-captured test every
+        that many steps for an early exit."""
+        self._ensure_ic_pool()
+        targ = torch.as_tensor(self.rng.integers(0, max_steps, size=self.nenv), device=self.device)
+        captured, obr_buf, warm_finite = self._warmup_loop_device(max_steps, action_fn, targ, check_every)
+        if not bool(warm_finite):
+            raise FloatingPointError("non-finite physical trajectory during staggered initialization")
+        self.sim.states.copy_(captured)
+        self.obr.restore(obr_buf)
+        self.obr.kernel_init_reward_state(self.sim.states)
+
+    def _warmup_loop_device(self, max_steps, action_fn, targ, check_every=0):
+        """Loop of _staggered_warmup_device; returns (captured states, captured reconstruction
+        buffers, finite flag), all on the device."""
+        dev = self.device
+        age = torch.zeros(self.nenv, dtype=torch.long, device=dev)
+        captured_mask = targ == 0
+        captured = self.sim.states.clone()
+        obr_buf = self.obr.clone_state()
+        warm_finite = torch.ones((), dtype=torch.bool, device=dev)
+        st3 = self.sim.states.view(self.nenv, 2, STATE_N)
+
+        def reseed(mask):
+            pick = torch.randint(0, self.ic_pool_size, (self.nenv,), device=dev)
+            st3.copy_(torch.where(mask.view(-1, 1, 1), self.ic_pool[pick], st3))
+            self.obr.reset_envs(mask)
+            self.obr.kernel_init_reward_state(self.sim.states, mask)
+
+        for i in range(max_steps):
+            if action_fn is None:
+                a = self._random_actions()
+            else:
+                a = action_fn(self.obr.kernel_build_obs(self.sim.states)).to(torch.float64).reshape(self.nac, 4)
+            self.sim.step(a, substeps=self.substeps)
+            fin = torch.isfinite(st3).all(dim=2).all(dim=1)
+            warm_finite.logical_and_((fin | captured_mask).all())
+            self.obr.kernel_advance(self.sim.states, a.contiguous(), cfg=self.reward_cfg,
+                                    min_alt=self.min_altitude_m, max_time=self.max_engage_time_s)
+            dep = self._departed_envs(self.state9_flat()) & (~captured_mask)
+            reseed(dep)
+            age = torch.where(dep, torch.zeros_like(age), age) + (~captured_mask).long()
+            hit = (~captured_mask) & (age == targ)
+            captured.copy_(torch.where(hit.repeat_interleave(2).view(-1, 1), self.sim.states, captured))
+            self.obr.capture_where(obr_buf, hit)
+            captured_mask = captured_mask | hit
+            if check_every > 0 and (i + 1) % check_every == 0 and bool(captured_mask.all()):
+                break
+        rest = ~captured_mask                                   # still short of their phase
+        reseed(rest)
+        captured.copy_(torch.where(rest.repeat_interleave(2).view(-1, 1), self.sim.states, captured))
+        self.obr.capture_where(obr_buf, rest)
+        return captured, obr_buf, warm_finite
 
     def _staggered_warmup(self, max_steps, action_fn):
         """Advance each env a random number of valid steps in [0, max_steps) and capture it there;

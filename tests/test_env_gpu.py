@@ -129,3 +129,30 @@ def test_evaluation_bank_is_deterministic(RL, cuda):
     assert torch.equal(o1[:8], o1[8:])
     meta = env._evaluation_seed_metadata
     assert meta["base_count"] == 8 and sum(meta["three_nine_distance_counts"].values()) == 8
+
+
+def test_staggered_warmup_on_device_is_sync_free(cuda):
+    """The device warm-up loop issues no host synchronisation (torch's sync debug mode would raise
+    on any), and the reset it drives leaves every env at a valid, staggered phase: finite states
+    above the 100 m departure floor, episode clocks spread over the target range."""
+    rl_env = pkg_module("rl_env")
+    env = rl_env.GpuDogfightVecEnv(1024, substeps=6, seed=11)
+    env._ensure_ic_pool()
+    env.sim.states.copy_(env._build_all_seeds())
+    env.obr.reset_all()
+    env.obr.kernel_init_reward_state(env.sim.states)
+    targ = torch.as_tensor(env.rng.integers(0, 32, size=env.nenv), device=env.device)
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        captured, buf, fin = env._warmup_loop_device(32, None, targ)
+    finally:
+        torch.cuda.set_sync_debug_mode("default")
+    assert bool(fin)
+    obs = env.reset(stagger=True, max_stagger_steps=64)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(env.sim.states).all()) and bool(torch.isfinite(obs).all())
+    alt = -env.state9()[:, :, 2]
+    assert float(alt.min()) >= 100.0
+    t = env.obr.t_sec
+    assert 2.0 < float(t.mean()) < 4.5 and int(torch.unique(t).numel()) > 30
