@@ -249,61 +249,130 @@ __device__ __forceinline__ float store_val(double v) {
   return (float)v;
 }
 
-// Everything about one engagement that both perspectives and the reward share.
-struct Pair {
-  double s[2][9];        // 9-DoF of aircraft 0 (even, "o") and 1 (odd, "p")
-  M3 R[2];               // ned2body of each
-  double att[2][6];      // sin/cos of roll, pitch, yaw of each (from ned2body)
-  V3 vn[2];              // NED velocity of each
-  V3 vb[2];              // body velocity of each
-  double spd[2];         // |body velocity|
-  V3 delta;              // p - o (m)
-  double dist;           // |delta|
-  V3 los;                // delta / dist (zero if dist <= 1e-6; reference los_u)
-  V3 u;                  // delta / dist when dist > 0 (reference ata/los unit, else zero vector)
-  V3 proj[2];            // R_o u and R_p (-u): body-frame LOS of each aircraft to the other
-  double ata[2];         // ATA of each aircraft at the other (deg, 0..180)
+// ---------------- lane-pair organisation ----------------
+// One thread per AIRCRAFT: the two aircraft of environment e are the adjacent lanes a = 2e and
+// a = 2e + 1 (k = a & 1) of one warp.  Each lane builds its own aircraft's geometry once and
+// stages it in shared memory, field-major [field][thread], where the partner lane reads it (a
+// warp reads 32 consecutive doubles of one field: no bank conflicts); the per-lane register
+// set is then one aircraft's working values, not an engagement's.  Values the reference
+// computes once per environment from side 0's view (LOS delta, range, geometry-advantage
+// quality terms) are computed by both lanes from the same operands in the same order, and side
+// 1 takes the exact negations the reference takes (md = -delta, mu = -u), so both lanes hold
+// the reference's bits.  Partner values that are read before they are overwritten (old HP,
+// tracker validity, previous altitude log) travel by shuffle, never through memory.
+enum StageField : int {
+  F_S = 0,       // 9-DoF: N, E, D (m), roll, pitch, yaw (deg), u, v, w (m/s)
+  F_R = 9,       // ned2body, row-major
+  F_ATT = 18,    // sin/cos of roll, pitch, yaw
+  F_VN = 24,     // NED velocity
+  F_SPD = 27,    // |body velocity|
+  F_FV = 28,     // dir_frame(NED velocity), row-major
+  F_FL = 37,     // dir_frame(line of sight from this aircraft to the other)
+  F_PROJ = 46,   // body-frame unit line of sight to the other aircraft
+  F_ATA = 49,    // ATA at the other aircraft (deg)
+  F_HP = 50,     // reconstruction values of the row: HP, fuel, damage dealt / taken rates
+  F_FUEL = 51,
+  F_DEALT = 52,
+  F_TAKEN = 53,
+  F_PQR = 54,    // body rates from the attitude change
+  NFIELD = 57
 };
 
-__device__ __forceinline__ void make_pair(Pair& P) {
-  for (int k = 0; k < 2; k++) {
-    P.R[k] = ned2body(P.s[k][3], P.s[k][4], P.s[k][5], P.att[k]);
-    P.vb[k] = {P.s[k][6], P.s[k][7], P.s[k][8]};
-    P.vn[k] = mvT(P.R[k], P.vb[k]);
-    P.spd[k] = nrm(P.vb[k]);
+template <int T>
+struct Lanes {
+  double* sm;     // the block's staging array, NFIELD x T
+  int i;          // threadIdx.x
+  unsigned pm;    // the pair's lane mask
+  __device__ __forceinline__ double& own(int f) const { return sm[f * T + i]; }
+  __device__ __forceinline__ double par(int f) const { return sm[f * T + (i ^ 1)]; }
+  // aircraft c (0: even, 1: odd) of the pair
+  __device__ __forceinline__ double col(int f, int c) const { return sm[f * T + ((i & ~1) | c)]; }
+  __device__ __forceinline__ V3 vec(int f, int c) const { return {col(f, c), col(f + 1, c), col(f + 2, c)}; }
+  __device__ __forceinline__ M3 mat(int f, int c) const {
+    M3 M;
+#pragma unroll
+    for (int r = 0; r < 3; r++)
+#pragma unroll
+      for (int q = 0; q < 3; q++) M.m[r][q] = col(f + 3 * r + q, c);
+    return M;
   }
-  P.delta = {P.s[1][0] - P.s[0][0], P.s[1][1] - P.s[0][1], P.s[1][2] - P.s[0][2]};
-  P.dist = nrm(P.delta);
-  if (P.dist > 0.0) P.u = {P.delta.x / P.dist, P.delta.y / P.dist, P.delta.z / P.dist};
-  else P.u = {0.0, 0.0, 0.0};
-  P.los = (P.dist > 1e-6) ? P.u : V3{0.0, 0.0, 0.0};
-  V3 mu = {-P.u.x, -P.u.y, -P.u.z};
-  P.proj[0] = mv(P.R[0], P.u);
-  P.proj[1] = mv(P.R[1], mu);
-  P.ata[0] = acos(clampd(P.proj[0].x, -1.0, 1.0)) * R2D;
-  P.ata[1] = acos(clampd(P.proj[1].x, -1.0, 1.0)) * R2D;
+  __device__ __forceinline__ void put_vec(int f, const V3& v) const { own(f) = v.x; own(f + 1) = v.y; own(f + 2) = v.z; }
+  __device__ __forceinline__ void put_mat(int f, const M3& M) const {
+#pragma unroll
+    for (int r = 0; r < 3; r++)
+#pragma unroll
+      for (int q = 0; q < 3; q++) own(f + 3 * r + q) = M.m[r][q];
+  }
+  __device__ __forceinline__ void sync() const { __syncwarp(pm); }
+  __device__ __forceinline__ double xchg(double v) const { return __shfl_xor_sync(pm, v, 1); }
+  __device__ __forceinline__ int xchg(int v) const { return __shfl_xor_sync(pm, v, 1); }
+};
+
+// Own aircraft: 9-DoF, body matrix and attitude sin/cos, NED velocity, speed, velocity frame.
+template <int T, typename Row>
+__device__ __forceinline__ void stage_aircraft(const Lanes<T>& L, const Row& row, const Origin& O) {
+  double s[9];
+  kin9(row, O, s);
+  double att[6];
+  const M3 R = ned2body(s[3], s[4], s[5], att);
+  const V3 vb = {s[6], s[7], s[8]};
+  const V3 vn = mvT(R, vb);
+#pragma unroll
+  for (int j = 0; j < 9; j++) L.own(F_S + j) = s[j];
+#pragma unroll
+  for (int j = 0; j < 6; j++) L.own(F_ATT + j) = att[j];
+  L.put_mat(F_R, R);
+  L.put_vec(F_VN, vn);
+  L.own(F_SPD) = nrm(vb);
+  L.put_mat(F_FV, dir_frame(vn));
 }
 
-// Symmetric geometry advantage G = S_own - S_enemy (obs_kernel.cu:305-324), from side 0's view.
-__device__ __forceinline__ double geometry_advantage(const Pair& P, double t) {
-  double dm = P.dist, df = dm / FT2M;
-  V3 los = unit_or(P.delta, {1.0, 0.0, 0.0});
-  const V3& vo = P.vn[0];
-  const V3& vp = P.vn[1];
-  double closing = (vo.x - vp.x) * los.x + (vo.y - vp.y) * los.y + (vo.z - vp.z) * los.z;
+// The pair's line of sight from side 0 (reference P.delta, P.dist, P.u): identical on both lanes.
+struct Los {
+  V3 d0;          // aircraft 1 - aircraft 0 (m)
+  double dist;
+  V3 u0;          // d0 / dist, zero when dist == 0
+};
+
+// After stage_aircraft on both lanes: the pair's LOS, and this aircraft's body-frame LOS, ATA
+// and LOS frame staged (reference make_pair and the Fl frames of build_obs).
+template <int T>
+__device__ __forceinline__ Los stage_los(const Lanes<T>& L, int k) {
+  Los g;
+  g.d0 = {L.col(F_S, 1) - L.col(F_S, 0), L.col(F_S + 1, 1) - L.col(F_S + 1, 0), L.col(F_S + 2, 1) - L.col(F_S + 2, 0)};
+  g.dist = nrm(g.d0);
+  if (g.dist > 0.0) g.u0 = {g.d0.x / g.dist, g.d0.y / g.dist, g.d0.z / g.dist};
+  else g.u0 = {0.0, 0.0, 0.0};
+  const V3 d = k ? V3{-g.d0.x, -g.d0.y, -g.d0.z} : g.d0;
+  const V3 u = k ? V3{-g.u0.x, -g.u0.y, -g.u0.z} : g.u0;
+  const V3 pj = mv(L.mat(F_R, k), u);
+  L.put_vec(F_PROJ, pj);
+  L.own(F_ATA) = acos(clampd(pj.x, -1.0, 1.0)) * R2D;
+  L.put_mat(F_FL, dir_frame(d));
+  return g;
+}
+
+// Symmetric geometry advantage (obs_kernel.cu:305-324) from this lane's side: G for side 0,
+// -G for side 1.  Each lane scores its own side; the two scores meet by shuffle.
+template <int T>
+__device__ __forceinline__ double geometry_advantage(const Lanes<T>& L, int k, const Los& g, double t) {
+  const double dm = g.dist, df = dm / FT2M;
+  const V3 los = unit_or(g.d0, {1.0, 0.0, 0.0});
+  const V3 vo = L.vec(F_VN, 0), vp = L.vec(F_VN, 1);
+  const double closing = (vo.x - vp.x) * los.x + (vo.y - vp.y) * los.y + (vo.z - vp.z) * los.z;
   double ms = 0.5 * (nrm(vo) + nrm(vp));
   if (ms < 100.0) ms = 100.0;
-  double ratio = closing / ms;
-  double desired = 0.20 * smooth3(df, 2000.0, 4500.0) - 0.12 * (1.0 - smooth3(df, 650.0, 900.0));
-  double dq = (ratio - desired) / 0.15;
-  double cq = exp(-0.5 * dq * dq);
-  double rg = smooth3(df, 600.0, 900.0) * (1.0 - smooth3(df, 3200.0, 4300.0));
-  V3 fo = {P.R[0].m[0][0], P.R[0].m[0][1], P.R[0].m[0][2]};
-  V3 fp = {P.R[1].m[0][0], P.R[1].m[0][1], P.R[1].m[0][2]};
-  V3 mdelta = {-P.delta.x, -P.delta.y, -P.delta.z};
-  double S1 = side_score(P.delta, vo, vp, fo, dm, df, P.ata[0], t, rg, cq);
-  double S2 = side_score(mdelta, vp, vo, fp, dm, df, P.ata[1], t, rg, cq);
-  return clampd(S1 - S2, -1.0, 1.0);
+  const double ratio = closing / ms;
+  const double desired = 0.20 * smooth3(df, 2000.0, 4500.0) - 0.12 * (1.0 - smooth3(df, 650.0, 900.0));
+  const double dq = (ratio - desired) / 0.15;
+  const double cq = exp(-0.5 * dq * dq);
+  const double rg = smooth3(df, 600.0, 900.0) * (1.0 - smooth3(df, 3200.0, 4300.0));
+  const V3 rel = k ? V3{-g.d0.x, -g.d0.y, -g.d0.z} : g.d0;
+  const V3 fwd = {L.col(F_R + 0, k), L.col(F_R + 1, k), L.col(F_R + 2, k)};
+  const double S = side_score(rel, k ? vp : vo, k ? vo : vp, fwd, dm, df, L.own(F_ATA), t, rg, cq);
+  const double Sp = L.xchg(S);
+  const double go = clampd((k ? Sp : S) - (k ? S : Sp), -1.0, 1.0);
+  return k ? -go : go;
 }
 
 // 16-byte staged writer of one fp32 observation row
@@ -323,105 +392,92 @@ struct RowWriter {
   }
 };
 
-// per-aircraft reconstruction values needed by one perspective
-struct Side {
-  double hp, fuel, dealt, taken;
-  V3 pqr;
-  const double* act_hist;    // 20 values, newest action first
-};
+// normz with the constant half-range folded into a reciprocal: (clamp(x) - mid) / half as one
+// multiply (1 ulp of fp64 at most; every feature is stored as fp32)
+__device__ __forceinline__ double normz_k(double x, double lo, double hi) {
+  return (clampd(x, lo, hi) - (hi + lo) * 0.5) * (2.0 / (hi - lo));
+}
 
-// One perspective's 184 features (obs_kernel.cu:336-482); k = 0 (own = even aircraft) or 1.
-// Fv[k]: dir_frame of aircraft k's NED velocity; Fl[k]: dir_frame of the LOS from aircraft k.
-__device__ __forceinline__ void obs_row(const Pair& P, int k, const Side& me, const Side& th, double t,
-                                       const M3* Fv, const M3& Fl, float* out, double* aux) {
+// This lane's 184 features (obs_kernel.cu:336-482) after stage_aircraft, stage_los and the
+// reconstruction fields are staged on both lanes.  hist: the aircraft's 20 action-history
+// values (newest first) or NULL for zeros; aux: the 21 future-position features or NULL.
+template <int T>
+__device__ __forceinline__ void obs_row(const Lanes<T>& L, int k, const Los& g, double t, const double* hist,
+                                       float* __restrict__ out, double* __restrict__ aux) {
   const int o = k, p = 1 - k;
-  const double* so = P.s[o];
-  const double* st = P.s[p];
-  const M3& Ro = P.R[o];
-  const M3& Rt = P.R[p];
-  const V3& ovn = P.vn[o];
-  const V3& tvn = P.vn[p];
+  const M3 Ro = L.mat(F_R, o);
+  const V3 ovn = L.vec(F_VN, o), tvn = L.vec(F_VN, p);
   if (aux) {
-    aux[0] = so[0]; aux[1] = so[1]; aux[2] = so[2];
+    aux[0] = L.col(F_S, o); aux[1] = L.col(F_S + 1, o); aux[2] = L.col(F_S + 2, o);
     aux[3] = ovn.x; aux[4] = ovn.y; aux[5] = ovn.z;
-    aux[6] = st[0]; aux[7] = st[1]; aux[8] = st[2];
+    aux[6] = L.col(F_S, p); aux[7] = L.col(F_S + 1, p); aux[8] = L.col(F_S + 2, p);
     aux[9] = tvn.x; aux[10] = tvn.y; aux[11] = tvn.z;
     for (int i = 0; i < 3; i++)
       for (int j = 0; j < 3; j++) aux[12 + 3 * i + j] = Ro.m[i][j];
   }
-  double sg = (k == 0) ? 1.0 : -1.0;
-  V3 los = {sg * P.los.x, sg * P.los.y, sg * P.los.z};
-  V3 rvn = {tvn.x - ovn.x, tvn.y - ovn.y, tvn.z - ovn.z};
-  double os = P.spd[o], ts = P.spd[p], oalt = -so[2], talt = -st[2];
-  double dist = P.dist;
+  const double sg = (k == 0) ? 1.0 : -1.0;
+  const V3 pl = (g.dist > 1e-6) ? g.u0 : V3{0.0, 0.0, 0.0};
+  const V3 los = {sg * pl.x, sg * pl.y, sg * pl.z};
+  const V3 rvn = {tvn.x - ovn.x, tvn.y - ovn.y, tvn.z - ovn.z};
+  const double os = L.col(F_SPD, o), ts = L.col(F_SPD, p), oalt = -L.col(F_S + 2, o), talt = -L.col(F_S + 2, p);
+  const double dist = g.dist;
   double clos = 0.0;
   if (dist > 1e-6) clos = (ovn.x - tvn.x) * los.x + (ovn.y - tvn.y) * los.y + (ovn.z - tvn.z) * los.z;
-  double ata = P.ata[o], eata = P.ata[p];
+  const double ata = L.col(F_ATA, o), eata = L.col(F_ATA, p);
   // sin/cos of ATA, aspect, LOS azimuth and elevation straight from the body-frame LOS
   // projections (the reference takes acos/atan2/asin and then sin/cos of the result):
   //   ATA = acos(x)            -> cos = x, sin = sqrt(1 - x^2)        (ATA in [0,180])
   //   aspect = s*acos(-x')     -> cos = -x', sin = s*sqrt(1 - x'^2)   (s: sign rule below)
   //   az = atan2(y, x)         -> (y, x) / hypot(x, y)
   //   el = -asin(z)            -> sin = -z, cos = sqrt(1 - z^2)
-  const V3& db = P.proj[o];
-  double cx = clampd(db.x, -1.0, 1.0);
-  double s_ata = sqrt(fmax(0.0, (1.0 - cx) * (1.0 + cx))), c_ata = cx;
-  const V3& bt = P.proj[p];
-  double t0 = clampd(-bt.x, -1.0, 1.0), t1 = -bt.y, t2 = bt.z;
-  double asg = (t1 > 0.0) ? 1.0 : ((t1 < 0.0) ? -1.0 : ((t2 >= 0.0) ? 1.0 : -1.0));
-  double c_aa = t0, s_aa = asg * sqrt(fmax(0.0, (1.0 - t0) * (1.0 + t0)));
-  double hxy = sqrt(db.x * db.x + db.y * db.y);
+  const V3 db = L.vec(F_PROJ, o);
+  const double cx = clampd(db.x, -1.0, 1.0);
+  const double s_ata = sqrt(fmax(0.0, (1.0 - cx) * (1.0 + cx))), c_ata = cx;
+  const V3 bt = L.vec(F_PROJ, p);
+  const double t0 = clampd(-bt.x, -1.0, 1.0), t1 = -bt.y, t2 = bt.z;
+  const double asg = (t1 > 0.0) ? 1.0 : ((t1 < 0.0) ? -1.0 : ((t2 >= 0.0) ? 1.0 : -1.0));
+  const double c_aa = t0, s_aa = asg * sqrt(fmax(0.0, (1.0 - t0) * (1.0 + t0)));
+  const double hxy = sqrt(db.x * db.x + db.y * db.y);
   double c_az = 1.0, s_az = 0.0;
   if (hxy > 0.0) { c_az = db.x / hxy; s_az = db.y / hxy; }
   else if (db.x < 0.0 || (db.x == 0.0 && signbit(db.x))) { c_az = -1.0; }
-  double cz = clampd(db.z, -1.0, 1.0);
-  double s_el = -cz, c_el = sqrt(fmax(0.0, (1.0 - cz) * (1.0 + cz)));
-  double u = so[6], v = so[7], w = so[8];
+  const double cz = clampd(db.z, -1.0, 1.0);
+  const double s_el = -cz, c_el = sqrt(fmax(0.0, (1.0 - cz) * (1.0 + cz)));
+  const double u = L.col(F_S + 6, o), v = L.col(F_S + 7, o), w = L.col(F_S + 8, o);
   float aoa = 0.0f, ss = 0.0f;
   if (os >= 1.0) {
     aoa = atan2f((float)w, (float)u) * (float)R2D;
     ss = atan2f((float)v, (float)sqrt(u * u + w * w)) * (float)R2D;
   }
-  double vs = -ovn.z;
-  double ea = (oalt + os * os / (2.0 * GACC)) - (talt + ts * ts / (2.0 * GACC));
-  double cone = (t >= T3_START) ? T3_CONE : ((t >= T2_START) ? T2_CONE : T1_CONE);
-  double mr = (t >= T3_START) ? T3_MAX : ((t >= T2_START) ? T2_MAX : T1_MAX);
+  const double vs = -ovn.z;
+  const double ea = (oalt + os * os / (2.0 * GACC)) - (talt + ts * ts / (2.0 * GACC));
+  const double cone = (t >= T3_START) ? T3_CONE : ((t >= T2_START) ? T2_CONE : T1_CONE);
+  const double mr = (t >= T3_START) ? T3_MAX : ((t >= T2_START) ? T2_MAX : T1_MAX);
   // bounded output nonlinearities in fp32 (each feature is stored as fp32)
-  float fa = (float)(ata * (1.0 / 3.0)), fe = (float)(eata * (1.0 / 3.0));
-  float ash = 2.0f * expf(-(fa * fa)) - 1.0f;
-  float amg = tanhf((float)((cone - fabs(ata)) / cone));
-  float eash = 2.0f * expf(-(fe * fe)) - 1.0f;
-  float eamg = tanhf((float)((cone - fabs(eata)) / cone));
-  double rmin = MIN_DMG_R_FT * FT2M, rmax = mr * FT2M, ispan = 1.0 / (rmax - rmin);
-  float rn = tanhf((float)((dist - rmin) * ispan)), rf = tanhf((float)((rmax - dist) * ispan));
-  // bank about the velocity vector: mu = atan2(y.z, y.y) of the body y axis (row 1 of R) in
-  // the velocity frame; sin/cos(mu) = (y.z, y.y) / hypot
-  double bank[2][2];
-  for (int q = 0; q < 2; q++) {
-    const M3& Rb = P.R[q == 0 ? o : p];
-    const M3& F = Fv[q == 0 ? o : p];
-    V3 by = {Rb.m[1][0], Rb.m[1][1], Rb.m[1][2]};
-    V3 yv = mv(F, by);
-    double h = sqrt(yv.y * yv.y + yv.z * yv.z);
-    if (h > 0.0) { bank[q][0] = yv.z / h; bank[q][1] = yv.y / h; }
-    else { bank[q][0] = yv.z; bank[q][1] = signbit(yv.y) ? -1.0 : 1.0; }
-  }
+  const float fa = (float)(ata * (1.0 / 3.0)), fe = (float)(eata * (1.0 / 3.0));
+  const float ash = 2.0f * expf(-(fa * fa)) - 1.0f;
+  const float amg = tanhf((float)((cone - fabs(ata)) / cone));
+  const float eash = 2.0f * expf(-(fe * fe)) - 1.0f;
+  const float eamg = tanhf((float)((cone - fabs(eata)) / cone));
+  const double rmin = MIN_DMG_R_FT * FT2M, rmax = mr * FT2M, ispan = 1.0 / (rmax - rmin);
+  const float rn = tanhf((float)((dist - rmin) * ispan)), rf = tanhf((float)((rmax - dist) * ispan));
   double pa = 1.0 - fabs(ata) / PURSUIT_ATA, pr = 1.0 - dist / PURSUIT_RANGE;
   if (pa < 0.0) pa = 0.0;
   if (pr < 0.0) pr = 0.0;
+  const double me_hp = L.col(F_HP, o), th_hp = L.col(F_HP, p);
   RowWriter wr{out, {0, 0, 0, 0}, 0};
-  wr.put(normz(os, 0.0, MAX_SPEED));
-  wr.put(normz(ts, 0.0, MAX_SPEED));
+  wr.put(normz_k(os, 0.0, MAX_SPEED));
+  wr.put(normz_k(ts, 0.0, MAX_SPEED));
   wr.putf(tanhf(aoa * (float)(1.0 / AOA_SCALE)));
   wr.putf(tanhf(ss * (float)(1.0 / SSLIP_SCALE)));
   wr.putf(tanhf((float)((oalt - MIN_ALT_M) * (1.0 / ALT_DANGER))));
-  wr.put(normz(vs, -VSPEED_SCALE, VSPEED_SCALE));
-  wr.put(normz(me.hp, 0.0, 1.0));
-  wr.put(normz(th.hp, 0.0, 1.0));
-  wr.put(me.hp - th.hp);
+  wr.put(normz_k(vs, -VSPEED_SCALE, VSPEED_SCALE));
+  wr.put(normz_k(me_hp, 0.0, 1.0));
+  wr.put(normz_k(th_hp, 0.0, 1.0));
+  wr.put(me_hp - th_hp);
   wr.put(ea / (fabs(ea) + ENERGY_ADV));
-  wr.put(normz(dist, 0.0, MAX_RANGE_M));
-  wr.put(normz(clos, -MAX_CLOSURE, MAX_CLOSURE));
+  wr.put(normz_k(dist, 0.0, MAX_RANGE_M));
+  wr.put(normz_k(clos, -MAX_CLOSURE, MAX_CLOSURE));
   wr.put(s_ata); wr.put(c_ata);
   wr.put(s_aa); wr.put(c_aa);
   wr.put(s_az); wr.put(c_az);
@@ -432,76 +488,85 @@ __device__ __forceinline__ void obs_row(const Pair& P, int k, const Side& me, co
   wr.putf(eamg);
   wr.putf(rn);
   wr.putf(rf);
-  wr.put(normz(t, 0.0, EPISODE_MAX));
-  for (int i = 0; i < 6; i++) wr.put(P.att[o][i]);     // sin/cos roll, pitch, yaw (own)
-  for (int i = 0; i < 6; i++) wr.put(P.att[p][i]);     // (target)
-  wr.put(bank[0][0]); wr.put(bank[0][1]);
-  wr.put(bank[1][0]); wr.put(bank[1][1]);
-  wr.put(normz(me.fuel, 0.0, 1.0));
-  wr.put(normz(th.fuel, 0.0, 1.0));
-  wr.put(clampd(2.0 * me.dealt - 1.0, -1.0, 1.0));
-  wr.put(clampd(2.0 * me.taken - 1.0, -1.0, 1.0));
+  wr.put(normz_k(t, 0.0, EPISODE_MAX));
+  for (int i = 0; i < 6; i++) wr.put(L.col(F_ATT + i, o));     // sin/cos roll, pitch, yaw (own)
+  for (int i = 0; i < 6; i++) wr.put(L.col(F_ATT + i, p));     // (target)
+  // bank about the velocity vector: mu = atan2(y.z, y.y) of the body y axis (row 1 of R) in
+  // the velocity frame; sin/cos(mu) = (y.z, y.y) / hypot
+  for (int q = 0; q < 2; q++) {
+    const int c = q == 0 ? o : p;
+    const V3 by = {L.col(F_R + 3, c), L.col(F_R + 4, c), L.col(F_R + 5, c)};
+    const V3 yv = mv(L.mat(F_FV, c), by);
+    const double h = sqrt(yv.y * yv.y + yv.z * yv.z);
+    if (h > 0.0) { wr.put(yv.z / h); wr.put(yv.y / h); }
+    else { wr.put(yv.z); wr.put(signbit(yv.y) ? -1.0 : 1.0); }
+  }
+  wr.put(normz_k(L.col(F_FUEL, o), 0.0, 1.0));
+  wr.put(normz_k(L.col(F_FUEL, p), 0.0, 1.0));
+  wr.put(clampd(2.0 * L.col(F_DEALT, o) - 1.0, -1.0, 1.0));
+  wr.put(clampd(2.0 * L.col(F_TAKEN, o) - 1.0, -1.0, 1.0));
   wr.put(2.0 * (pa * pr) - 1.0);
-  wr.put(normz(oalt, 0.0, MAX_ALT_M));
-  wr.put(normz(talt, 0.0, MAX_ALT_M));
-  // 38 frame-projected vectors in VEC_LAYOUT order (obs_kernel.cu:457-464)
-  V3 oom = mvT(Ro, me.pqr), tom = mvT(Rt, th.pqr);
-  const M3& Fmy = Fv[o];
-  const M3& Fopp = Fv[p];
+  wr.put(normz_k(oalt, 0.0, MAX_ALT_M));
+  wr.put(normz_k(talt, 0.0, MAX_ALT_M));
+  // 38 frame-projected vectors in VEC_LAYOUT order (obs_kernel.cu:457-464); frames by index:
+  // 0 own body, 1 target body, 2 own velocity, 3 target velocity, 4 LOS
+  auto frame = [&](int f) -> M3 {
+    if (f == 0) return Ro;
+    if (f == 1) return L.mat(F_R, p);
+    if (f == 2) return L.mat(F_FV, o);
+    if (f == 3) return L.mat(F_FV, p);
+    return L.mat(F_FL, o);
+  };
   // gravity (0,0,1) in frames mybody, oppbody, myvel, oppvel, los  -> unit
-  {
-    V3 g{0.0, 0.0, 1.0};
-    const M3* F5[5] = {&Ro, &Rt, &Fmy, &Fopp, &Fl};
-    for (int f = 0; f < 5; f++) { V3 c = mv(*F5[f], g); wr.put(c.x); wr.put(c.y); wr.put(c.z); }
-  }
+#pragma unroll
+  for (int f = 0; f < 5; f++) { V3 c = mv(frame(f), V3{0.0, 0.0, 1.0}); wr.put(c.x); wr.put(c.y); wr.put(c.z); }
   // los in frames world, mybody, oppbody, myvel, oppvel -> unit
-  {
-    wr.put(los.x); wr.put(los.y); wr.put(los.z);
-    const M3* F4[4] = {&Ro, &Rt, &Fmy, &Fopp};
-    for (int f = 0; f < 4; f++) { V3 c = mv(*F4[f], los); wr.put(c.x); wr.put(c.y); wr.put(c.z); }
-  }
+  wr.put(los.x); wr.put(los.y); wr.put(los.z);
+#pragma unroll
+  for (int f = 0; f < 4; f++) { V3 c = mv(frame(f), los); wr.put(c.x); wr.put(c.y); wr.put(c.z); }
+  const double kv = 1.0 / REL_VEL;
+  auto putv = [&](const V3& c) {
+    wr.put(clampd(c.x, -REL_VEL, REL_VEL) * kv);
+    wr.put(clampd(c.y, -REL_VEL, REL_VEL) * kv);
+    wr.put(clampd(c.z, -REL_VEL, REL_VEL) * kv);
+  };
   // own_vel in world, mybody, oppbody, oppvel, los -> vel
+  putv(ovn);
   {
-    const M3* F4[4] = {&Ro, &Rt, &Fopp, &Fl};
-    wr.put(normz(ovn.x, -REL_VEL, REL_VEL)); wr.put(normz(ovn.y, -REL_VEL, REL_VEL)); wr.put(normz(ovn.z, -REL_VEL, REL_VEL));
-    for (int f = 0; f < 4; f++) {
-      V3 c = mv(*F4[f], ovn);
-      wr.put(normz(c.x, -REL_VEL, REL_VEL)); wr.put(normz(c.y, -REL_VEL, REL_VEL)); wr.put(normz(c.z, -REL_VEL, REL_VEL));
-    }
+    const int F4[4] = {0, 1, 3, 4};
+#pragma unroll
+    for (int f = 0; f < 4; f++) putv(mv(frame(F4[f]), ovn));
   }
   // tgt_vel in world, mybody, oppbody, myvel, los -> vel
+  putv(tvn);
   {
-    const M3* F4[4] = {&Ro, &Rt, &Fmy, &Fl};
-    wr.put(normz(tvn.x, -REL_VEL, REL_VEL)); wr.put(normz(tvn.y, -REL_VEL, REL_VEL)); wr.put(normz(tvn.z, -REL_VEL, REL_VEL));
-    for (int f = 0; f < 4; f++) {
-      V3 c = mv(*F4[f], tvn);
-      wr.put(normz(c.x, -REL_VEL, REL_VEL)); wr.put(normz(c.y, -REL_VEL, REL_VEL)); wr.put(normz(c.z, -REL_VEL, REL_VEL));
-    }
+    const int F4[4] = {0, 1, 2, 4};
+#pragma unroll
+    for (int f = 0; f < 4; f++) putv(mv(frame(F4[f]), tvn));
   }
   // rel_vel in world, mybody, oppbody, myvel, oppvel, los -> vel
-  {
-    const M3* F5[5] = {&Ro, &Rt, &Fmy, &Fopp, &Fl};
-    wr.put(normz(rvn.x, -REL_VEL, REL_VEL)); wr.put(normz(rvn.y, -REL_VEL, REL_VEL)); wr.put(normz(rvn.z, -REL_VEL, REL_VEL));
-    for (int f = 0; f < 5; f++) {
-      V3 c = mv(*F5[f], rvn);
-      wr.put(normz(c.x, -REL_VEL, REL_VEL)); wr.put(normz(c.y, -REL_VEL, REL_VEL)); wr.put(normz(c.z, -REL_VEL, REL_VEL));
-    }
-  }
+  putv(rvn);
+#pragma unroll
+  for (int f = 0; f < 5; f++) putv(mv(frame(f), rvn));
   // own_omega and tgt_omega in world, mybody, oppbody, myvel, oppvel, los -> omega
   {
-    const M3* F5[5] = {&Ro, &Rt, &Fmy, &Fopp, &Fl};
-    const V3* W[2] = {&oom, &tom};
     const float ip = (float)(1.0 / PQR_SCALE);
+#pragma unroll
     for (int q = 0; q < 2; q++) {
-      const V3& om = *W[q];
+      const V3 om = mvT(L.mat(F_R, q == 0 ? o : p), L.vec(F_PQR, q == 0 ? o : p));
       wr.putf(tanhf((float)om.x * ip)); wr.putf(tanhf((float)om.y * ip)); wr.putf(tanhf((float)om.z * ip));
+#pragma unroll
       for (int f = 0; f < 5; f++) {
-        V3 c = mv(*F5[f], om);
+        V3 c = mv(frame(f), om);
         wr.putf(tanhf((float)c.x * ip)); wr.putf(tanhf((float)c.y * ip)); wr.putf(tanhf((float)c.z * ip));
       }
     }
   }
-  for (int j = 0; j < 20; j++) wr.put(me.act_hist[j]);
+  if (hist) {
+    for (int j = 0; j < 20; j++) wr.put(hist[j]);
+  } else {
+    for (int j = 0; j < 20; j++) wr.put(0.0);
+  }
 }
 
 }  // namespace obs

@@ -1,24 +1,30 @@
 // obs_kernels.cu -- observation / reward / termination kernels and their C-ABI entry points.
 //
-// All kernels run one thread per environment (both aircraft): the two 9-DoF states are built
-// from the FDM rows once (14 state columns each, coalesced in the SoA layout), the shared
-// geometry once (obs_device.cuh Pair), and each aircraft's 184-float row is written with 16-byte
-// vector stores.  Reconstruction buffers keep the reference's per-aircraft layout
-// (R/cuda_fdm/obs_reward.py:338-353) so the reference's tensors can be passed as they are.
+// The per-environment kernels run one thread per AIRCRAFT, the two aircraft of an environment
+// on adjacent lanes (obs_device.cuh, lane-pair organisation): each lane reads its own FDM row
+// (14 state columns, consecutive lanes on consecutive addresses in the SoA layout), stages its
+// aircraft's geometry in shared memory for the partner, updates its own reconstruction values
+// and writes its own 184-float row with 16-byte vector stores.  Reconstruction buffers keep
+// the reference's per-aircraft layout (R/cuda_fdm/obs_reward.py:338-353) so the reference's
+// tensors can be passed as they are.
 #include "common.cuh"
 #include "obs_device.cuh"
 
 namespace f16 {
 namespace obs {
 
-constexpr int OBS_THREADS = 128;
-// Resident blocks per SM the step kernels are compiled for (64 registers per thread): the row
-// builder's live set does not fit in registers at any occupancy, and trading register spills
-// (to L1, which these kernels do not otherwise use) for 32 resident warps measured fastest on a
-// B200 (sweep 1..16: post-step 0.58 -> 0.44 ms, obs step 1.00 -> 0.84 ms).
-#ifndef F16_OBS_MIN_BLOCKS
-#define F16_OBS_MIN_BLOCKS 8
+constexpr int OBS_THREADS = 128;        // per-aircraft kernels without staging (state9, external)
+// Lane-pair kernels: 64 threads (32 environments) per block and 29 KB of staging, so 7 blocks
+// fit per SM with up to 144 registers per thread -- the row builder's working set then stays in
+// registers (one thread per environment needed more than 255 and spilled at every occupancy).
+#ifndef F16_OBS_PAIR_THREADS
+#define F16_OBS_PAIR_THREADS 64
 #endif
+#ifndef F16_OBS_PAIR_MIN_BLOCKS
+#define F16_OBS_PAIR_MIN_BLOCKS 7
+#endif
+constexpr int PT = F16_OBS_PAIR_THREADS;
+static_assert(PT % 32 == 0, "pairs must not straddle warps");
 
 template <int LAYOUT>
 struct RowRef {
@@ -31,208 +37,221 @@ struct RowRef {
 
 __device__ __forceinline__ Origin origin_of(const f16_origin& o) { return {o.ox, o.oy, o.oz, o.slat, o.clat, o.slon, o.clon}; }
 
+// Lane setup of a lane-pair kernel; false for lanes past the last aircraft (whole pairs, since
+// the aircraft count is even).
+struct PairLane {
+  int64_t a, e;
+  int k;
+};
+__device__ __forceinline__ bool pair_lane(int64_t nenv, PairLane& pl) {
+  pl.a = (int64_t)blockIdx.x * PT + threadIdx.x;
+  pl.e = pl.a >> 1;
+  pl.k = (int)(pl.a & 1);
+  return pl.a < 2 * nenv;
+}
+__device__ __forceinline__ Lanes<PT> lanes_of(double* sm) {
+  return {sm, (int)threadIdx.x, 3u << (threadIdx.x & 30)};
+}
+
+// Both staging passes for the pair (stage_aircraft, then stage_los once both are staged).
 template <int LAYOUT>
-__device__ __forceinline__ void load_pair(const double* st, int64_t ld, int64_t e, const Origin& O, Pair& P) {
-  kin9(RowRef<LAYOUT>{st, ld, 2 * e}, O, P.s[0]);
-  kin9(RowRef<LAYOUT>{st, ld, 2 * e + 1}, O, P.s[1]);
-  make_pair(P);
+__device__ __forceinline__ Los stage_pair(const Lanes<PT>& L, const double* st, int64_t ld, int64_t a, int k,
+                                          const Origin& O) {
+  stage_aircraft(L, RowRef<LAYOUT>{st, ld, a}, O);
+  L.sync();
+  Los g = stage_los(L, k);
+  L.sync();
+  return g;
 }
 
 // action-history push of one aircraft (roll by one, newest first): hist[0..19] <- (a, hist[0..15])
-__device__ __forceinline__ void push_hist(double* __restrict__ h, const double* __restrict__ act, double out[20]) {
+__device__ __forceinline__ void push_hist(double* h, const double* __restrict__ act) {
   const double2* h2 = reinterpret_cast<const double2*>(h);
   double2 o[8];
 #pragma unroll
   for (int i = 0; i < 8; i++) o[i] = h2[i];
   const double2* a2 = reinterpret_cast<const double2*>(act);
-  double2 x = a2[0], y = a2[1];
-  out[0] = x.x; out[1] = x.y; out[2] = y.x; out[3] = y.y;
-#pragma unroll
-  for (int i = 0; i < 8; i++) { out[4 + 2 * i] = o[i].x; out[5 + 2 * i] = o[i].y; }
+  const double2 x = a2[0], y = a2[1];
   double2* w = reinterpret_cast<double2*>(h);
+  w[0] = x;
+  w[1] = y;
 #pragma unroll
-  for (int i = 0; i < 10; i++) w[i] = make_double2(out[2 * i], out[2 * i + 1]);
+  for (int i = 0; i < 8; i++) w[2 + i] = o[i];
 }
 
-struct AdvanceOut {
-  double hp[2], fuel[2], dealt[2], taken[2], t;
-  V3 pqr[2];
-  double hist[2][20];
+// Reconstruction values of a fresh episode staged for the observation row.
+template <int T>
+__device__ __forceinline__ void stage_fresh(const Lanes<T>& L) {
+  L.own(F_HP) = 1.0; L.own(F_FUEL) = 1.0; L.own(F_DEALT) = 0.0; L.own(F_TAKEN) = 0.0;
+  L.own(F_PQR) = 0.0; L.own(F_PQR + 1) = 0.0; L.own(F_PQR + 2) = 0.0;
+}
+
+struct Advanced {
+  double hp, t;        // this aircraft's HP after the step; the environment's new clock
+  bool te, tr;         // the environment's termination / truncation
 };
 
-// advance_kernel semantics (obs_kernel.cu:504-626) for environment e on a built Pair.
-__device__ __forceinline__ void advance_env(const Pair& P, int64_t e, const f16_recon& rc, const f16_reward_cfg& cfg,
-                                            const double* __restrict__ actions, double* __restrict__ reward,
-                                            uint8_t* __restrict__ term, uint8_t* __restrict__ trunc_,
-                                            AdvanceOut& A) {
-  const int64_t o = 2 * e, p = o + 1;
+// advance_kernel semantics (obs_kernel.cu:504-626) for this lane's aircraft after stage_pair:
+// damage / HP / fuel / body rates / attitude history of the aircraft, the environment's clock
+// and flags (written by the even lane), the aircraft's final-safe reward and reward trackers;
+// the row's reconstruction values are staged.
+template <int T>
+__device__ __forceinline__ Advanced advance_lane(const Lanes<T>& L, const PairLane& pl, const Los& g,
+                                                 const f16_recon& rc, const f16_reward_cfg& cfg,
+                                                 const double* __restrict__ actions, double* __restrict__ reward,
+                                                 uint8_t* __restrict__ term, uint8_t* __restrict__ trunc_) {
+  const int64_t a = pl.a, e = pl.e;
+  const int k = pl.k;
   const double dt = cfg.dt;
-  push_hist(rc.act_hist + o * 20, actions + o * 4, A.hist[0]);
-  push_hist(rc.act_hist + p * 20, actions + p * 4, A.hist[1]);
-  double r_ft = P.dist * M2FT;
-  double t_old = rc.t_sec[e];
-  double rate_o = damage(r_ft, P.ata[0], t_old), rate_p = damage(r_ft, P.ata[1], t_old);
-  double ho0 = rc.hp[o], hp0 = rc.hp[p];
-  double ho = ho0 - rate_p * dt, hpn = hp0 - rate_o * dt;
-  if (ho < 0.0) ho = 0.0;
-  if (hpn < 0.0) hpn = 0.0;
-  double lo = ho0 - ho, lp = hp0 - hpn;
-  rc.hp[o] = ho; rc.hp[p] = hpn;
-  rc.hp_loss[o] = lo; rc.hp_loss[p] = lp;
-  rc.dmg_dealt[o] = rate_o; rc.dmg_taken[o] = rate_p;
-  rc.dmg_dealt[p] = rate_p; rc.dmg_taken[p] = rate_o;
-  A.hp[0] = ho; A.hp[1] = hpn;
-  A.dealt[0] = rate_o; A.taken[0] = rate_p; A.dealt[1] = rate_p; A.taken[1] = rate_o;
-  double fo = rc.fuel[o] - FUEL_BURN * (P.spd[0] / FUEL_REF) * dt;
-  double fp = rc.fuel[p] - FUEL_BURN * (P.spd[1] / FUEL_REF) * dt;
-  A.fuel[0] = fo < 0.0 ? 0.0 : fo;
-  A.fuel[1] = fp < 0.0 ? 0.0 : fp;
-  rc.fuel[o] = A.fuel[0]; rc.fuel[p] = A.fuel[1];
+  push_hist(rc.act_hist + a * 20, actions + a * 4);
+  const double r_ft = g.dist * M2FT;
+  const double t_old = rc.t_sec[e];
+  const double ata = L.own(F_ATA), ata_p = L.par(F_ATA);
+  const double rate = damage(r_ft, ata, t_old), rate_p = damage(r_ft, ata_p, t_old);
+  const double h0 = rc.hp[a];
+  const double h0_p = L.xchg(h0);
+  double h = h0 - rate_p * dt, h_p = h0_p - rate * dt;
+  if (h < 0.0) h = 0.0;
+  if (h_p < 0.0) h_p = 0.0;
+  const double lo = h0 - h, lp = h0_p - h_p;
+  rc.hp[a] = h;
+  rc.hp_loss[a] = lo;
+  rc.dmg_dealt[a] = rate;
+  rc.dmg_taken[a] = rate_p;
+  double f = rc.fuel[a] - FUEL_BURN * (L.own(F_SPD) / FUEL_REF) * dt;
+  if (f < 0.0) f = 0.0;
+  rc.fuel[a] = f;
   // body rates from the attitude change: log_SO3(R_prev R_curr^T) / dt
   const double inv_dt = 1.0 / (dt > 1e-8 ? dt : 1e-8);
-  for (int k = 0; k < 2; k++) {
-    int64_t a = o + k;
-    double lg[3] = {0.0, 0.0, 0.0};
-    if (rc.prev_valid[a]) {
-      M3 Np = ned2body(rc.prev_att[a * 3], rc.prev_att[a * 3 + 1], rc.prev_att[a * 3 + 2]);
-      const M3& Nc = P.R[k];
-      M3 rd;
-      for (int i = 0; i < 3; i++)
-        for (int j = 0; j < 3; j++)
-          rd.m[i][j] = Np.m[i][0] * Nc.m[j][0] + Np.m[i][1] * Nc.m[j][1] + Np.m[i][2] * Nc.m[j][2];
-      log_so3(rd, inv_dt, lg);
-    }
-    rc.pqr[a * 3] = lg[0]; rc.pqr[a * 3 + 1] = lg[1]; rc.pqr[a * 3 + 2] = lg[2];
-    A.pqr[k] = {lg[0], lg[1], lg[2]};
-    rc.prev_att[a * 3] = P.s[k][3]; rc.prev_att[a * 3 + 1] = P.s[k][4]; rc.prev_att[a * 3 + 2] = P.s[k][5];
-    rc.prev_valid[a] = 1;
+  double lg[3] = {0.0, 0.0, 0.0};
+  if (rc.prev_valid[a]) {
+    const M3 Np = ned2body(rc.prev_att[a * 3], rc.prev_att[a * 3 + 1], rc.prev_att[a * 3 + 2]);
+    const M3 Nc = L.mat(F_R, k);
+    M3 rd;
+    for (int i = 0; i < 3; i++)
+      for (int j = 0; j < 3; j++)
+        rd.m[i][j] = Np.m[i][0] * Nc.m[j][0] + Np.m[i][1] * Nc.m[j][1] + Np.m[i][2] * Nc.m[j][2];
+    log_so3(rd, inv_dt, lg);
   }
-  double t_new = t_old + dt;
-  rc.t_sec[e] = t_new;
-  A.t = t_new;
-  double ao = -P.s[0][2], ap = -P.s[1][2];
+  rc.pqr[a * 3] = lg[0]; rc.pqr[a * 3 + 1] = lg[1]; rc.pqr[a * 3 + 2] = lg[2];
+  rc.prev_att[a * 3] = L.own(F_S + 3); rc.prev_att[a * 3 + 1] = L.own(F_S + 4); rc.prev_att[a * 3 + 2] = L.own(F_S + 5);
+  rc.prev_valid[a] = 1;
+  const double t_new = t_old + dt;
+  const double alt = -L.own(F_S + 2), alt_p = -L.par(F_S + 2);
   bool fin = true;
-  for (int k = 0; k < 9; k++)
-    if (!isfinite(P.s[0][k]) || !isfinite(P.s[1][k])) fin = false;
-  uint8_t te = (ao < cfg.min_alt) || (ap < cfg.min_alt) || (ho <= 0.0) || (hpn <= 0.0) || (!fin);
-  uint8_t tr = (!te) && (t_new >= cfg.max_time - TLIM_TOL);
-  term[e] = te;
-  trunc_[e] = tr;
-  double go = geometry_advantage(P, t_new), gp = -go;
-  double lgo = alt_log(ao), lgp = alt_log(ap);
-  uint8_t vo = rc.prev_x_valid[o], vp = rc.prev_x_valid[p];
-  double pgo = vo ? rc.prev_x[o] : go, pgp = vp ? rc.prev_x[p] : gp;
-  double gm = cfg.shaping_reward_scale / SHAPING_BASE;
-  double rgo = gm * (GEOM_BUDGET / GEOM_REF_SEC) * 0.5 * (pgo + go) * dt;
-  double rgp = gm * (GEOM_BUDGET / GEOM_REF_SEC) * 0.5 * (pgp + gp) * dt;
-  if (cfg.reward_mode == 1) {
-    rgo = vp ? cfg.alt_hunt_coef * (rc.prev_alt_log[p] - lgp) : 0.0;
-    rgp = vo ? cfg.alt_hunt_coef * (rc.prev_alt_log[o] - lgo) : 0.0;
+  for (int j = 0; j < 9; j++)
+    if (!isfinite(L.col(F_S + j, 0)) || !isfinite(L.col(F_S + j, 1))) fin = false;
+  const bool te = (alt < cfg.min_alt) || (alt_p < cfg.min_alt) || (h <= 0.0) || (h_p <= 0.0) || (!fin);
+  const bool tr = (!te) && (t_new >= cfg.max_time - TLIM_TOL);
+  if (k == 0) {
+    rc.t_sec[e] = t_new;
+    term[e] = te;
+    trunc_[e] = tr;
   }
-  rc.prev_x[o] = go; rc.prev_x[p] = gp;
-  rc.prev_x_valid[o] = 1; rc.prev_x_valid[p] = 1;
-  rc.prev_alt_log[o] = lgo; rc.prev_alt_log[p] = lgp;
+  const double gx = geometry_advantage(L, k, g, t_new);
+  const double lga = alt_log(alt), lga_p = alt_log(alt_p);
+  const int valid = rc.prev_x_valid[a];
+  const int valid_p = L.xchg(valid);
+  const double alt_log_prev_p = L.xchg(rc.prev_alt_log[a]);
+  const double pg = valid ? rc.prev_x[a] : gx;
+  const double gm = cfg.shaping_reward_scale / SHAPING_BASE;
+  double rgx = gm * (GEOM_BUDGET / GEOM_REF_SEC) * 0.5 * (pg + gx) * dt;
+  if (cfg.reward_mode == 1) rgx = valid_p ? cfg.alt_hunt_coef * (alt_log_prev_p - lga_p) : 0.0;
+  rc.prev_x[a] = gx;
+  rc.prev_x_valid[a] = 1;
+  rc.prev_alt_log[a] = lga;
   const double dsc = cfg.damage_scale, ow = cfg.own_damage_weight;
-  double rdo = (lp - lo * ow) * dsc, rdp = (lo - lp * ow) * dsc;
-  if (cfg.reward_mode == 2) { rdo = lp * dsc; rdp = lo * dsc; }
-  else if (cfg.reward_mode == 3) { rdo = -(lo * ow) * dsc; rdp = -(lp * ow) * dsc; }
-  double rto = 0.0, rtp = 0.0;
+  double rd = (lp - lo * ow) * dsc;
+  if (cfg.reward_mode == 2) rd = lp * dsc;
+  else if (cfg.reward_mode == 3) rd = -(lo * ow) * dsc;
+  double rt = 0.0;
   if (te) {
-    if (ao < cfg.min_alt) rto = -ho * dsc;
-    else if (ap < cfg.min_alt) rto = hpn * dsc;
-    else { if (hpn <= 0.0) rto += cfg.win_reward; if (ho <= 0.0) rto += cfg.loss_reward; }
-    if (ap < cfg.min_alt) rtp = -hpn * dsc;
-    else if (ao < cfg.min_alt) rtp = ho * dsc;
-    else { if (ho <= 0.0) rtp += cfg.win_reward; if (hpn <= 0.0) rtp += cfg.loss_reward; }
+    if (alt < cfg.min_alt) rt = -h * dsc;
+    else if (alt_p < cfg.min_alt) rt = h_p * dsc;
+    else { if (h_p <= 0.0) rt += cfg.win_reward; if (h <= 0.0) rt += cfg.loss_reward; }
   } else if (tr) {
-    rto = (ho > hpn) ? cfg.timeout_win_reward : ((ho < hpn) ? cfg.timeout_loss_reward : cfg.timeout_draw_reward);
-    rtp = (hpn > ho) ? cfg.timeout_win_reward : ((hpn < ho) ? cfg.timeout_loss_reward : cfg.timeout_draw_reward);
+    rt = (h > h_p) ? cfg.timeout_win_reward : ((h < h_p) ? cfg.timeout_loss_reward : cfg.timeout_draw_reward);
   }
-  reward[o] = rdo + rgo + rto;
-  reward[p] = rdp + rgp + rtp;
-}
-
-// Both observation rows of environment e from a built Pair and the two aircraft's recon values.
-__device__ __forceinline__ void obs_env(const Pair& P, int64_t e, const Side* sd, double t, float* __restrict__ obs,
-                                        double* __restrict__ aux) {
-  M3 Fv[2] = {dir_frame(P.vn[0]), dir_frame(P.vn[1])};
-  V3 md = {-P.delta.x, -P.delta.y, -P.delta.z};
-  M3 Fl0 = dir_frame(P.delta);
-  obs_row(P, 0, sd[0], sd[1], t, Fv, Fl0, obs + (2 * e) * 184, aux ? aux + e * 21 : nullptr);
-  M3 Fl1 = dir_frame(md);
-  obs_row(P, 1, sd[1], sd[0], t, Fv, Fl1, obs + (2 * e + 1) * 184, nullptr);
+  reward[a] = rd + rgx + rt;
+  L.own(F_HP) = h; L.own(F_FUEL) = f; L.own(F_DEALT) = rate; L.own(F_TAKEN) = rate_p;
+  L.own(F_PQR) = lg[0]; L.own(F_PQR + 1) = lg[1]; L.own(F_PQR + 2) = lg[2];
+  return {h, t_new, te, tr};
 }
 
 template <int LAYOUT>
-__global__ void __launch_bounds__(OBS_THREADS) k_obs_build(const double* __restrict__ st, int64_t ld, int64_t nenv,
-                                                           const uint8_t* __restrict__ mask, const f16_recon rc,
-                                                           const f16_origin og, float* __restrict__ obs,
-                                                           double* __restrict__ aux) {
-  int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= nenv || (mask && !mask[e])) return;
-  Origin O = origin_of(og);
-  Pair P;
-  load_pair<LAYOUT>(st, ld, e, O, P);
-  Side sd[2];
-  for (int k = 0; k < 2; k++) {
-    int64_t a = 2 * e + k;
-    sd[k] = {rc.hp[a], rc.fuel[a], rc.dmg_dealt[a], rc.dmg_taken[a],
-             {rc.pqr[a * 3], rc.pqr[a * 3 + 1], rc.pqr[a * 3 + 2]}, rc.act_hist + a * 20};
-  }
-  obs_env(P, e, sd, rc.t_sec[e], obs, aux);
+__global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_obs_build(const double* __restrict__ st, int64_t ld,
+                                                                           int64_t nenv, const uint8_t* __restrict__ mask,
+                                                                           const f16_recon rc, const f16_origin og,
+                                                                           float* __restrict__ obs,
+                                                                           double* __restrict__ aux) {
+  __shared__ double sm[NFIELD * PT];
+  PairLane pl;
+  if (!pair_lane(nenv, pl) || (mask && !mask[pl.e])) return;
+  const Lanes<PT> L = lanes_of(sm);
+  const Los g = stage_pair<LAYOUT>(L, st, ld, pl.a, pl.k, origin_of(og));
+  const int64_t a = pl.a;
+  L.own(F_HP) = rc.hp[a]; L.own(F_FUEL) = rc.fuel[a]; L.own(F_DEALT) = rc.dmg_dealt[a]; L.own(F_TAKEN) = rc.dmg_taken[a];
+  L.own(F_PQR) = rc.pqr[a * 3]; L.own(F_PQR + 1) = rc.pqr[a * 3 + 1]; L.own(F_PQR + 2) = rc.pqr[a * 3 + 2];
+  L.sync();
+  obs_row(L, pl.k, g, rc.t_sec[pl.e], rc.act_hist + a * 20, obs + a * 184, (aux && pl.k == 0) ? aux + pl.e * 21 : nullptr);
 }
 
 template <int LAYOUT>
-__global__ void __launch_bounds__(OBS_THREADS) k_obs_advance(const double* __restrict__ st, int64_t ld, int64_t nenv,
-                                                             const double* __restrict__ actions, const f16_recon rc,
-                                                             const f16_reward_cfg cfg, const f16_origin og,
-                                                             double* __restrict__ reward, uint8_t* __restrict__ term,
-                                                             uint8_t* __restrict__ trunc_) {
-  int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= nenv) return;
-  Origin O = origin_of(og);
-  Pair P;
-  load_pair<LAYOUT>(st, ld, e, O, P);
-  AdvanceOut A;
-  advance_env(P, e, rc, cfg, actions, reward, term, trunc_, A);
+__global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_obs_advance(const double* __restrict__ st, int64_t ld,
+                                                                             int64_t nenv,
+                                                                             const double* __restrict__ actions,
+                                                                             const f16_recon rc, const f16_reward_cfg cfg,
+                                                                             const f16_origin og,
+                                                                             double* __restrict__ reward,
+                                                                             uint8_t* __restrict__ term,
+                                                                             uint8_t* __restrict__ trunc_) {
+  __shared__ double sm[NFIELD * PT];
+  PairLane pl;
+  if (!pair_lane(nenv, pl)) return;
+  const Lanes<PT> L = lanes_of(sm);
+  const Los g = stage_pair<LAYOUT>(L, st, ld, pl.a, pl.k, origin_of(og));
+  advance_lane(L, pl, g, rc, cfg, actions, reward, term, trunc_);
 }
 
-// Fused: advance (reward, termination, reconstruction update) then both observation rows,
+// Fused: advance (reward, termination, reconstruction update) then the observation rows,
 // reading each FDM row once (the reference launches advance_kernel then build_obs_kernel).
 template <int LAYOUT>
-__global__ void __launch_bounds__(OBS_THREADS, F16_OBS_MIN_BLOCKS) k_obs_step(const double* __restrict__ st, int64_t ld, int64_t nenv,
-                                                          const double* __restrict__ actions, const f16_recon rc,
-                                                          const f16_reward_cfg cfg, const f16_origin og,
-                                                          double* __restrict__ reward, uint8_t* __restrict__ term,
-                                                          uint8_t* __restrict__ trunc_, float* __restrict__ obs,
-                                                          double* __restrict__ aux) {
-  int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= nenv) return;
-  Origin O = origin_of(og);
-  Pair P;
-  load_pair<LAYOUT>(st, ld, e, O, P);
-  AdvanceOut A;
-  advance_env(P, e, rc, cfg, actions, reward, term, trunc_, A);
-  Side sd[2];
-  for (int k = 0; k < 2; k++) sd[k] = {A.hp[k], A.fuel[k], A.dealt[k], A.taken[k], A.pqr[k], A.hist[k]};
-  obs_env(P, e, sd, A.t, obs, aux);
+__global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_obs_step(const double* __restrict__ st, int64_t ld,
+                                                                          int64_t nenv,
+                                                                          const double* __restrict__ actions,
+                                                                          const f16_recon rc, const f16_reward_cfg cfg,
+                                                                          const f16_origin og,
+                                                                          double* __restrict__ reward,
+                                                                          uint8_t* __restrict__ term,
+                                                                          uint8_t* __restrict__ trunc_,
+                                                                          float* __restrict__ obs,
+                                                                          double* __restrict__ aux) {
+  __shared__ double sm[NFIELD * PT];
+  PairLane pl;
+  if (!pair_lane(nenv, pl)) return;
+  const Lanes<PT> L = lanes_of(sm);
+  const Los g = stage_pair<LAYOUT>(L, st, ld, pl.a, pl.k, origin_of(og));
+  const Advanced A = advance_lane(L, pl, g, rc, cfg, actions, reward, term, trunc_);
+  L.sync();
+  obs_row(L, pl.k, g, A.t, rc.act_hist + pl.a * 20, obs + pl.a * 184,
+          (aux && pl.k == 0) ? aux + pl.e * 21 : nullptr);
 }
 
 template <int LAYOUT>
-__global__ void __launch_bounds__(OBS_THREADS) k_obs_init_reward(const double* __restrict__ st, int64_t ld,
-                                                                 int64_t nenv, const uint8_t* __restrict__ mask,
-                                                                 const f16_recon rc, const f16_origin og) {
-  int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= nenv || (mask && !mask[e])) return;
-  Origin O = origin_of(og);
-  Pair P;
-  load_pair<LAYOUT>(st, ld, e, O, P);
-  double g = geometry_advantage(P, rc.t_sec[e]);
-  int64_t o = 2 * e, p = o + 1;
-  rc.prev_x[o] = g; rc.prev_x[p] = -g;
-  rc.prev_x_valid[o] = 1; rc.prev_x_valid[p] = 1;
-  rc.prev_alt_log[o] = alt_log(-P.s[0][2]);
-  rc.prev_alt_log[p] = alt_log(-P.s[1][2]);
+__global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_obs_init_reward(const double* __restrict__ st,
+                                                                                 int64_t ld, int64_t nenv,
+                                                                                 const uint8_t* __restrict__ mask,
+                                                                                 const f16_recon rc,
+                                                                                 const f16_origin og) {
+  __shared__ double sm[NFIELD * PT];
+  PairLane pl;
+  if (!pair_lane(nenv, pl) || (mask && !mask[pl.e])) return;
+  const Lanes<PT> L = lanes_of(sm);
+  const Los g = stage_pair<LAYOUT>(L, st, ld, pl.a, pl.k, origin_of(og));
+  const double gx = geometry_advantage(L, pl.k, g, rc.t_sec[pl.e]);
+  rc.prev_x[pl.a] = gx;
+  rc.prev_x_valid[pl.a] = 1;
+  rc.prev_alt_log[pl.a] = alt_log(-L.own(F_S + 2));
 }
 
 // Everything GpuDogfightVecEnv.step does after the physics step (R/cuda_fdm/rl_env.py:514-551),
@@ -240,72 +259,72 @@ __global__ void __launch_bounds__(OBS_THREADS) k_obs_init_reward(const double* _
 // environments the autoreset from the IC pool (state rows, reconstruction reset, reward-tracker
 // anchoring, fresh observations).  pool: (pool_size, 2, 101) AoS rows; pick: pool row per env.
 template <int LAYOUT>
-__global__ void __launch_bounds__(OBS_THREADS, F16_OBS_MIN_BLOCKS) k_env_post(double* __restrict__ st, int64_t ld, int64_t nenv,
-                                                          const double* __restrict__ actions, const f16_recon rc,
-                                                          const f16_reward_cfg cfg, const f16_origin og,
-                                                          const double* __restrict__ pool, int64_t pool_size,
-                                                          const int64_t* __restrict__ pick,
-                                                          double* __restrict__ reward, uint8_t* __restrict__ term,
-                                                          uint8_t* __restrict__ trunc_, uint8_t* __restrict__ done,
-                                                          float* __restrict__ obs, float* __restrict__ terminal_obs,
-                                                          double* __restrict__ terminal_hp,
-                                                          double* __restrict__ terminal_alt, double* __restrict__ aux) {
-  int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= nenv) return;
-  Origin O = origin_of(og);
-  Pair P;
-  load_pair<LAYOUT>(st, ld, e, O, P);
-  AdvanceOut A;
-  advance_env(P, e, rc, cfg, actions, reward, term, trunc_, A);
-  const int64_t o = 2 * e, p = o + 1;
-  bool fin = term[e] || trunc_[e];
-  done[e] = fin;
-  for (int k = 0; k < 2; k++) {
-    int64_t a = o + k;
-    terminal_hp[a] = A.hp[k];
+__global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_env_post(double* __restrict__ st, int64_t ld,
+                                                                          int64_t nenv,
+                                                                          const double* __restrict__ actions,
+                                                                          const f16_recon rc, const f16_reward_cfg cfg,
+                                                                          const f16_origin og,
+                                                                          const double* __restrict__ pool,
+                                                                          int64_t pool_size,
+                                                                          const int64_t* __restrict__ pick,
+                                                                          double* __restrict__ reward,
+                                                                          uint8_t* __restrict__ term,
+                                                                          uint8_t* __restrict__ trunc_,
+                                                                          uint8_t* __restrict__ done,
+                                                                          float* __restrict__ obs,
+                                                                          float* __restrict__ terminal_obs,
+                                                                          double* __restrict__ terminal_hp,
+                                                                          double* __restrict__ terminal_alt,
+                                                                          double* __restrict__ aux) {
+  __shared__ double sm[NFIELD * PT];
+  PairLane pl;
+  if (!pair_lane(nenv, pl)) return;
+  const Lanes<PT> L = lanes_of(sm);
+  const Origin O = origin_of(og);
+  const int64_t a = pl.a, e = pl.e;
+  Los g = stage_pair<LAYOUT>(L, st, ld, a, pl.k, O);
+  const Advanced A = advance_lane(L, pl, g, rc, cfg, actions, reward, term, trunc_);
+  const bool fin = A.te || A.tr;
+  if (pl.k == 0) done[e] = fin;
+  terminal_hp[a] = A.hp;
+  {
     RowRef<LAYOUT> R{st, ld, a};
-    double x = R(0), y = R(1), z = R(2);
+    const double x = R(0), y = R(1), z = R(2);
     terminal_alt[a] = (sqrt(x * x + y * y + z * z) - SLR_FT) * FT2M;
   }
-  Side sd[2];
-  for (int k = 0; k < 2; k++) sd[k] = {A.hp[k], A.fuel[k], A.dealt[k], A.taken[k], A.pqr[k], A.hist[k]};
-  if (terminal_obs) obs_env(P, e, sd, A.t, terminal_obs, nullptr);
+  L.sync();
+  double* ax = (aux && pl.k == 0) ? aux + e * 21 : nullptr;
+  if (terminal_obs) obs_row(L, pl.k, g, A.t, rc.act_hist + a * 20, terminal_obs + a * 184, nullptr);
   if (!fin) {
-    obs_env(P, e, sd, A.t, obs, aux);
+    obs_row(L, pl.k, g, A.t, rc.act_hist + a * 20, obs + a * 184, ax);
     return;
   }
-  // autoreset: new rows from the pool, fresh reconstruction state, anchored trackers
+  // autoreset: this aircraft's row from the pool, fresh reconstruction state, anchored trackers
   int64_t row = pick[e];
   row = row < 0 ? 0 : (row >= pool_size ? pool_size - 1 : row);
-  const double* src = pool + row * 2 * F16_STATE_N;
-  for (int k = 0; k < 2; k++) {
-    int64_t a = o + k;
-    for (int c = 0; c < F16_STATE_N; c++) {
-      double v = src[k * F16_STATE_N + c];
-      if (LAYOUT == F16_LAYOUT_SOA) st[(int64_t)c * ld + a] = v;
-      else st[a * F16_STATE_N + c] = v;
-    }
-    rc.hp[a] = 1.0; rc.fuel[a] = 1.0;
-    rc.prev_att[a * 3] = 0.0; rc.prev_att[a * 3 + 1] = 0.0; rc.prev_att[a * 3 + 2] = 0.0;
-    rc.prev_valid[a] = 0;
-    rc.pqr[a * 3] = 0.0; rc.pqr[a * 3 + 1] = 0.0; rc.pqr[a * 3 + 2] = 0.0;
-    rc.dmg_dealt[a] = 0.0; rc.dmg_taken[a] = 0.0; rc.hp_loss[a] = 0.0;
-    double2* h = reinterpret_cast<double2*>(rc.act_hist + a * 20);
-    for (int i = 0; i < 10; i++) h[i] = make_double2(0.0, 0.0);
-    A.hist[k][0] = 0.0;
-    for (int i = 0; i < 20; i++) A.hist[k][i] = 0.0;
+  const double* src = pool + (row * 2 + pl.k) * F16_STATE_N;
+  for (int c = 0; c < F16_STATE_N; c++) {
+    const double v = src[c];
+    if (LAYOUT == F16_LAYOUT_SOA) st[(int64_t)c * ld + a] = v;
+    else st[a * F16_STATE_N + c] = v;
   }
-  rc.t_sec[e] = 0.0;
-  Pair Q;
-  load_pair<LAYOUT>(st, ld, e, O, Q);
-  double g = geometry_advantage(Q, 0.0);
-  rc.prev_x[o] = g; rc.prev_x[p] = -g;
-  rc.prev_x_valid[o] = 1; rc.prev_x_valid[p] = 1;
-  rc.prev_alt_log[o] = alt_log(-Q.s[0][2]);
-  rc.prev_alt_log[p] = alt_log(-Q.s[1][2]);
-  Side zs[2];
-  for (int k = 0; k < 2; k++) zs[k] = {1.0, 1.0, 0.0, 0.0, {0.0, 0.0, 0.0}, A.hist[k]};
-  obs_env(Q, e, zs, 0.0, obs, aux);
+  rc.hp[a] = 1.0; rc.fuel[a] = 1.0;
+  rc.prev_att[a * 3] = 0.0; rc.prev_att[a * 3 + 1] = 0.0; rc.prev_att[a * 3 + 2] = 0.0;
+  rc.prev_valid[a] = 0;
+  rc.pqr[a * 3] = 0.0; rc.pqr[a * 3 + 1] = 0.0; rc.pqr[a * 3 + 2] = 0.0;
+  rc.dmg_dealt[a] = 0.0; rc.dmg_taken[a] = 0.0; rc.hp_loss[a] = 0.0;
+  double2* h = reinterpret_cast<double2*>(rc.act_hist + a * 20);
+  for (int i = 0; i < 10; i++) h[i] = make_double2(0.0, 0.0);
+  if (pl.k == 0) rc.t_sec[e] = 0.0;
+  L.sync();                                     // the partner's rows are written: restage
+  g = stage_pair<LAYOUT>(L, st, ld, a, pl.k, O);
+  const double gx = geometry_advantage(L, pl.k, g, 0.0);
+  rc.prev_x[a] = gx;
+  rc.prev_x_valid[a] = 1;
+  rc.prev_alt_log[a] = alt_log(-L.own(F_S + 2));
+  stage_fresh(L);
+  L.sync();
+  obs_row(L, pl.k, g, 0.0, nullptr, obs + a * 184, ax);
 }
 
 // 9-DoF export (R/cuda_fdm/rl_env.py:558-566 state9_flat): one thread per aircraft
@@ -386,6 +405,8 @@ __global__ void __launch_bounds__(OBS_THREADS) k_external_obs(const double* __re
 }
 
 inline int grid_for(int64_t n) { return (int)((n + OBS_THREADS - 1) / OBS_THREADS); }
+// lane-pair kernels: one thread per aircraft
+inline int pair_grid(int64_t nenv) { return (int)((2 * nenv + PT - 1) / PT); }
 
 inline int check_recon(const f16_recon* rc, bool need_all) {
   if (!rc) return F16_ERR_ARG;
@@ -411,12 +432,12 @@ inline int check_common(const double* st, int layout, int64_t ld, int64_t nenv, 
 using namespace f16;
 using namespace f16::obs;
 
-#define F16_DISPATCH_LAYOUT(layout, KERNEL, GRID, ...)                                      \
+#define F16_DISPATCH_LAYOUT(layout, KERNEL, GRID, BLOCK, ...)                               \
   do {                                                                                      \
     if ((layout) == F16_LAYOUT_SOA)                                                         \
-      KERNEL<F16_LAYOUT_SOA><<<(GRID), OBS_THREADS, 0, s>>>(__VA_ARGS__);                   \
+      KERNEL<F16_LAYOUT_SOA><<<(GRID), (BLOCK), 0, s>>>(__VA_ARGS__);                       \
     else                                                                                    \
-      KERNEL<F16_LAYOUT_AOS><<<(GRID), OBS_THREADS, 0, s>>>(__VA_ARGS__);                   \
+      KERNEL<F16_LAYOUT_AOS><<<(GRID), (BLOCK), 0, s>>>(__VA_ARGS__);                       \
   } while (0)
 
 extern "C" int f16_obs_build(const double* state, int layout, int64_t ld, int64_t nenv, const uint8_t* env_mask,
@@ -428,7 +449,7 @@ extern "C" int f16_obs_build(const double* state, int layout, int64_t ld, int64_
   if (!obs) return F16_ERR_ARG;
   if (!aligned(obs, 16)) return F16_ERR_ALIGN;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  F16_DISPATCH_LAYOUT(layout, k_obs_build, grid_for(nenv), state, ld, nenv, env_mask, *recon, *origin, obs, aux);
+  F16_DISPATCH_LAYOUT(layout, k_obs_build, pair_grid(nenv), PT, state, ld, nenv, env_mask, *recon, *origin, obs, aux);
   return launch_status();
 }
 
@@ -442,7 +463,7 @@ extern "C" int f16_obs_advance(const double* state, int layout, int64_t ld, int6
   if (cfg->reward_mode < 0 || cfg->reward_mode > 3) return F16_ERR_ARG;
   if (!aligned(actions, 16)) return F16_ERR_ALIGN;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  F16_DISPATCH_LAYOUT(layout, k_obs_advance, grid_for(nenv), state, ld, nenv, actions, *recon, *cfg, *origin, reward,
+  F16_DISPATCH_LAYOUT(layout, k_obs_advance, pair_grid(nenv), PT, state, ld, nenv, actions, *recon, *cfg, *origin, reward,
                       term, trunc_);
   return launch_status();
 }
@@ -458,7 +479,7 @@ extern "C" int f16_obs_step(const double* state, int layout, int64_t ld, int64_t
   if (cfg->reward_mode < 0 || cfg->reward_mode > 3) return F16_ERR_ARG;
   if (!aligned(actions, 16) || !aligned(obs, 16)) return F16_ERR_ALIGN;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  F16_DISPATCH_LAYOUT(layout, k_obs_step, grid_for(nenv), state, ld, nenv, actions, *recon, *cfg, *origin, reward,
+  F16_DISPATCH_LAYOUT(layout, k_obs_step, pair_grid(nenv), PT, state, ld, nenv, actions, *recon, *cfg, *origin, reward,
                       term, trunc_, obs, aux);
   return launch_status();
 }
@@ -470,7 +491,7 @@ extern "C" int f16_obs_init_reward(const double* state, int layout, int64_t ld, 
   if (rc) return rc;
   if (!recon || !recon->t_sec || !recon->prev_x || !recon->prev_x_valid || !recon->prev_alt_log) return F16_ERR_ARG;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  F16_DISPATCH_LAYOUT(layout, k_obs_init_reward, grid_for(nenv), state, ld, nenv, env_mask, *recon, *origin);
+  F16_DISPATCH_LAYOUT(layout, k_obs_init_reward, pair_grid(nenv), PT, state, ld, nenv, env_mask, *recon, *origin);
   return launch_status();
 }
 
@@ -488,7 +509,7 @@ extern "C" int f16_env_post_step(double* state, int layout, int64_t ld, int64_t 
   if (cfg->reward_mode < 0 || cfg->reward_mode > 3) return F16_ERR_ARG;
   if (!aligned(actions, 16) || !aligned(obs, 16) || (terminal_obs && !aligned(terminal_obs, 16))) return F16_ERR_ALIGN;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  F16_DISPATCH_LAYOUT(layout, k_env_post, grid_for(nenv), state, ld, nenv, actions, *recon, *cfg, *origin, ic_pool,
+  F16_DISPATCH_LAYOUT(layout, k_env_post, pair_grid(nenv), PT, state, ld, nenv, actions, *recon, *cfg, *origin, ic_pool,
                       pool_size, pick, reward, term, trunc_, done, obs, terminal_obs, terminal_hp, terminal_alt_m,
                       aux);
   return launch_status();
@@ -500,7 +521,7 @@ extern "C" int f16_state9(const double* state, int layout, int64_t ld, int64_t n
   if (layout != F16_LAYOUT_SOA && layout != F16_LAYOUT_AOS) return F16_ERR_ARG;
   if (layout == F16_LAYOUT_SOA && ld < nac) return F16_ERR_ARG;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  F16_DISPATCH_LAYOUT(layout, k_state9, grid_for(nac), state, ld, nac, *origin, s9);
+  F16_DISPATCH_LAYOUT(layout, k_state9, grid_for(nac), OBS_THREADS, state, ld, nac, *origin, s9);
   return launch_status();
 }
 
