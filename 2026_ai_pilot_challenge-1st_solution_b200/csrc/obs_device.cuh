@@ -248,6 +248,9 @@ __device__ __forceinline__ float store_val(double v) {
   if (!isfinite(v)) v = (v > 0.0) ? 10.0 : ((v < 0.0) ? -10.0 : 0.0);
   return (float)v;
 }
+__device__ __forceinline__ float store_f(float f) {
+  return isfinite(f) ? f : ((f > 0.0f) ? 10.0f : ((f < 0.0f) ? -10.0f : 0.0f));
+}
 
 // ---------------- lane-pair organisation ----------------
 // One thread per AIRCRAFT: the two aircraft of environment e are the adjacent lanes a = 2e and
@@ -309,22 +312,43 @@ struct Lanes {
 };
 
 // Own aircraft: 9-DoF, body matrix and attitude sin/cos, NED velocity, speed, velocity frame.
+// prev: the aircraft's previous attitude (deg) when its attitude history is valid, else NULL;
+// with it the body rates log_SO3(R_prev R^T) / dt of advance_kernel are staged in F_PQR (zero
+// without).  Both body matrices come out of one rolled loop, so the three sincos are inlined
+// once; the previous matrix passes through the F_FL slots, which stage_los fills afterwards.
 template <int T, typename Row>
-__device__ __forceinline__ void stage_aircraft(const Lanes<T>& L, const Row& row, const Origin& O) {
+__device__ __forceinline__ void stage_aircraft(const Lanes<T>& L, const Row& row, const Origin& O,
+                                               const double* prev = nullptr, double inv_dt = 0.0) {
   double s[9];
   kin9(row, O, s);
-  double att[6];
-  const M3 R = ned2body(s[3], s[4], s[5], att);
-  const V3 vb = {s[6], s[7], s[8]};
-  const V3 vn = mvT(R, vb);
 #pragma unroll
   for (int j = 0; j < 9; j++) L.own(F_S + j) = s[j];
+  const int passes = prev ? 2 : 1;
+#pragma unroll 1
+  for (int q = 0; q < passes; q++) {
+    double att[6];
+    const M3 R = ned2body(q ? prev[0] : s[3], q ? prev[1] : s[4], q ? prev[2] : s[5], att);
+    L.put_mat(q ? F_FL : F_R, R);
+    if (q == 0) {
 #pragma unroll
-  for (int j = 0; j < 6; j++) L.own(F_ATT + j) = att[j];
-  L.put_mat(F_R, R);
-  L.put_vec(F_VN, vn);
-  L.own(F_SPD) = nrm(vb);
-  L.put_mat(F_FV, dir_frame(vn));
+      for (int j = 0; j < 6; j++) L.own(F_ATT + j) = att[j];
+      const V3 vb = {s[6], s[7], s[8]};
+      const V3 vn = mvT(R, vb);
+      L.put_vec(F_VN, vn);
+      L.own(F_SPD) = nrm(vb);
+      L.put_mat(F_FV, dir_frame(vn));
+    }
+  }
+  double lg[3] = {0.0, 0.0, 0.0};
+  if (prev) {
+    const M3 Np = L.mat(F_FL, L.i & 1), Nc = L.mat(F_R, L.i & 1);
+    M3 rd;
+    for (int i = 0; i < 3; i++)
+      for (int j = 0; j < 3; j++)
+        rd.m[i][j] = Np.m[i][0] * Nc.m[j][0] + Np.m[i][1] * Nc.m[j][1] + Np.m[i][2] * Nc.m[j][2];
+    log_so3(rd, inv_dt, lg);
+  }
+  L.put_vec(F_PQR, V3{lg[0], lg[1], lg[2]});
 }
 
 // The pair's line of sight from side 0 (reference P.delta, P.dist, P.u): identical on both lanes.
@@ -510,12 +534,10 @@ __device__ __forceinline__ void obs_row(const Lanes<T>& L, int k, const Los& g, 
   wr.put(normz_k(talt, 0.0, MAX_ALT_M));
   // 38 frame-projected vectors in VEC_LAYOUT order (obs_kernel.cu:457-464); frames by index:
   // 0 own body, 1 target body, 2 own velocity, 3 target velocity, 4 LOS
+  const int cols = o | (p << 1) | (o << 2) | (p << 3) | (o << 4);      // staging column of frame f
   auto frame = [&](int f) -> M3 {
-    if (f == 0) return Ro;
-    if (f == 1) return L.mat(F_R, p);
-    if (f == 2) return L.mat(F_FV, o);
-    if (f == 3) return L.mat(F_FV, p);
-    return L.mat(F_FL, o);
+    const int base = f < 2 ? F_R : (f < 4 ? F_FV : F_FL);
+    return L.mat(base, (cols >> f) & 1);
   };
   // gravity (0,0,1) in frames mybody, oppbody, myvel, oppvel, los  -> unit
 #pragma unroll
@@ -524,44 +546,55 @@ __device__ __forceinline__ void obs_row(const Lanes<T>& L, int k, const Los& g, 
   wr.put(los.x); wr.put(los.y); wr.put(los.z);
 #pragma unroll
   for (int f = 0; f < 4; f++) { V3 c = mv(frame(f), los); wr.put(c.x); wr.put(c.y); wr.put(c.z); }
+  // The remaining 84 features (80..163) start on a 16-byte boundary and come in items of one
+  // vector in one frame (3 features); four items are 12 features = three float4 stores, so the
+  // items run as a rolled loop over groups of four (compact code: this kernel is otherwise
+  // bound by instruction fetch), with the source vector and frame of each item decoded from
+  // its index.
+  //   velocity items (features 80-127): own_vel in world, mybody, oppbody, oppvel, los;
+  //   tgt_vel in world, mybody, oppbody, myvel, los; rel_vel in world and all five frames.
+  //   Frame code 0 = world, f + 1 = frame f; 3 bits per item.
+  //   omega items (features 128-163): own_omega then tgt_omega, each in world and frames 0-4.
+  const V3 oom = mvT(Ro, L.vec(F_PQR, o)), tom = mvT(L.mat(F_R, p), L.vec(F_PQR, p));
+  constexpr unsigned long long VEL_FRAMES =
+      (0ull << 0) | (1ull << 3) | (2ull << 6) | (4ull << 9) | (5ull << 12) |
+      (0ull << 15) | (1ull << 18) | (2ull << 21) | (3ull << 24) | (5ull << 27) |
+      (0ull << 30) | (1ull << 33) | (2ull << 36) | (3ull << 39) | (4ull << 42) | (5ull << 45);
+  float4* out4 = reinterpret_cast<float4*>(out);
   const double kv = 1.0 / REL_VEL;
-  auto putv = [&](const V3& c) {
-    wr.put(clampd(c.x, -REL_VEL, REL_VEL) * kv);
-    wr.put(clampd(c.y, -REL_VEL, REL_VEL) * kv);
-    wr.put(clampd(c.z, -REL_VEL, REL_VEL) * kv);
-  };
-  // own_vel in world, mybody, oppbody, oppvel, los -> vel
-  putv(ovn);
-  {
-    const int F4[4] = {0, 1, 3, 4};
+  const float ip = (float)(1.0 / PQR_SCALE);
+#pragma unroll 1
+  for (int it = 0; it < 28; it += 4) {
+    float v[12];
 #pragma unroll
-    for (int f = 0; f < 4; f++) putv(mv(frame(F4[f]), ovn));
-  }
-  // tgt_vel in world, mybody, oppbody, myvel, los -> vel
-  putv(tvn);
-  {
-    const int F4[4] = {0, 1, 2, 4};
-#pragma unroll
-    for (int f = 0; f < 4; f++) putv(mv(frame(F4[f]), tvn));
-  }
-  // rel_vel in world, mybody, oppbody, myvel, oppvel, los -> vel
-  putv(rvn);
-#pragma unroll
-  for (int f = 0; f < 5; f++) putv(mv(frame(f), rvn));
-  // own_omega and tgt_omega in world, mybody, oppbody, myvel, oppvel, los -> omega
-  {
-    const float ip = (float)(1.0 / PQR_SCALE);
-#pragma unroll
-    for (int q = 0; q < 2; q++) {
-      const V3 om = mvT(L.mat(F_R, q == 0 ? o : p), L.vec(F_PQR, q == 0 ? o : p));
-      wr.putf(tanhf((float)om.x * ip)); wr.putf(tanhf((float)om.y * ip)); wr.putf(tanhf((float)om.z * ip));
-#pragma unroll
-      for (int f = 0; f < 5; f++) {
-        V3 c = mv(frame(f), om);
-        wr.putf(tanhf((float)c.x * ip)); wr.putf(tanhf((float)c.y * ip)); wr.putf(tanhf((float)c.z * ip));
+    for (int j = 0; j < 4; j++) {
+      const int item = it + j;
+      const bool omega = item >= 16;
+      int fc;
+      V3 x;
+      if (!omega) {
+        fc = (int)((VEL_FRAMES >> (3 * item)) & 7);
+        x = item < 5 ? ovn : (item < 10 ? tvn : rvn);
+      } else {
+        fc = (item - 16) % 6;
+        x = item < 22 ? oom : tom;
+      }
+      const V3 c = fc == 0 ? x : mv(frame(fc - 1), x);
+      if (!omega) {
+        v[3 * j + 0] = store_val(clampd(c.x, -REL_VEL, REL_VEL) * kv);
+        v[3 * j + 1] = store_val(clampd(c.y, -REL_VEL, REL_VEL) * kv);
+        v[3 * j + 2] = store_val(clampd(c.z, -REL_VEL, REL_VEL) * kv);
+      } else {
+        v[3 * j + 0] = store_f(tanhf((float)c.x * ip));
+        v[3 * j + 1] = store_f(tanhf((float)c.y * ip));
+        v[3 * j + 2] = store_f(tanhf((float)c.z * ip));
       }
     }
+    const int q = (80 + 3 * it) >> 2;
+#pragma unroll
+    for (int j = 0; j < 3; j++) out4[q + j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
+  wr.n = 164;
   if (hist) {
     for (int j = 0; j < 20; j++) wr.put(hist[j]);
   } else {

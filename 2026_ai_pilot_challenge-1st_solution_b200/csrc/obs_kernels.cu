@@ -53,11 +53,12 @@ __device__ __forceinline__ Lanes<PT> lanes_of(double* sm) {
   return {sm, (int)threadIdx.x, 3u << (threadIdx.x & 30)};
 }
 
-// Both staging passes for the pair (stage_aircraft, then stage_los once both are staged).
+// Both staging passes for the pair (stage_aircraft, then stage_los once both are staged);
+// prev / inv_dt as in stage_aircraft.
 template <int LAYOUT>
 __device__ __forceinline__ Los stage_pair(const Lanes<PT>& L, const double* st, int64_t ld, int64_t a, int k,
-                                          const Origin& O) {
-  stage_aircraft(L, RowRef<LAYOUT>{st, ld, a}, O);
+                                          const Origin& O, const double* prev = nullptr, double inv_dt = 0.0) {
+  stage_aircraft(L, RowRef<LAYOUT>{st, ld, a}, O, prev, inv_dt);
   L.sync();
   Los g = stage_los(L, k);
   L.sync();
@@ -85,6 +86,12 @@ __device__ __forceinline__ void stage_fresh(const Lanes<T>& L) {
   L.own(F_HP) = 1.0; L.own(F_FUEL) = 1.0; L.own(F_DEALT) = 0.0; L.own(F_TAKEN) = 0.0;
   L.own(F_PQR) = 0.0; L.own(F_PQR + 1) = 0.0; L.own(F_PQR + 2) = 0.0;
 }
+
+// The aircraft's previous attitude when its history is valid (body rates), else NULL.
+__device__ __forceinline__ const double* prev_attitude(const f16_recon& rc, int64_t a) {
+  return rc.prev_valid[a] ? rc.prev_att + a * 3 : nullptr;
+}
+__device__ __forceinline__ double inv_dt_of(const f16_reward_cfg& cfg) { return 1.0 / (cfg.dt > 1e-8 ? cfg.dt : 1e-8); }
 
 struct Advanced {
   double hp, t;        // this aircraft's HP after the step; the environment's new clock
@@ -121,19 +128,8 @@ __device__ __forceinline__ Advanced advance_lane(const Lanes<T>& L, const PairLa
   double f = rc.fuel[a] - FUEL_BURN * (L.own(F_SPD) / FUEL_REF) * dt;
   if (f < 0.0) f = 0.0;
   rc.fuel[a] = f;
-  // body rates from the attitude change: log_SO3(R_prev R_curr^T) / dt
-  const double inv_dt = 1.0 / (dt > 1e-8 ? dt : 1e-8);
-  double lg[3] = {0.0, 0.0, 0.0};
-  if (rc.prev_valid[a]) {
-    const M3 Np = ned2body(rc.prev_att[a * 3], rc.prev_att[a * 3 + 1], rc.prev_att[a * 3 + 2]);
-    const M3 Nc = L.mat(F_R, k);
-    M3 rd;
-    for (int i = 0; i < 3; i++)
-      for (int j = 0; j < 3; j++)
-        rd.m[i][j] = Np.m[i][0] * Nc.m[j][0] + Np.m[i][1] * Nc.m[j][1] + Np.m[i][2] * Nc.m[j][2];
-    log_so3(rd, inv_dt, lg);
-  }
-  rc.pqr[a * 3] = lg[0]; rc.pqr[a * 3 + 1] = lg[1]; rc.pqr[a * 3 + 2] = lg[2];
+  // body rates from the attitude change (staged by stage_aircraft from the previous attitude)
+  rc.pqr[a * 3] = L.own(F_PQR); rc.pqr[a * 3 + 1] = L.own(F_PQR + 1); rc.pqr[a * 3 + 2] = L.own(F_PQR + 2);
   rc.prev_att[a * 3] = L.own(F_S + 3); rc.prev_att[a * 3 + 1] = L.own(F_S + 4); rc.prev_att[a * 3 + 2] = L.own(F_S + 5);
   rc.prev_valid[a] = 1;
   const double t_new = t_old + dt;
@@ -174,7 +170,6 @@ __device__ __forceinline__ Advanced advance_lane(const Lanes<T>& L, const PairLa
   }
   reward[a] = rd + rgx + rt;
   L.own(F_HP) = h; L.own(F_FUEL) = f; L.own(F_DEALT) = rate; L.own(F_TAKEN) = rate_p;
-  L.own(F_PQR) = lg[0]; L.own(F_PQR + 1) = lg[1]; L.own(F_PQR + 2) = lg[2];
   return {h, t_new, te, tr};
 }
 
@@ -209,7 +204,7 @@ __global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_obs_advance(con
   PairLane pl;
   if (!pair_lane(nenv, pl)) return;
   const Lanes<PT> L = lanes_of(sm);
-  const Los g = stage_pair<LAYOUT>(L, st, ld, pl.a, pl.k, origin_of(og));
+  const Los g = stage_pair<LAYOUT>(L, st, ld, pl.a, pl.k, origin_of(og), prev_attitude(rc, pl.a), inv_dt_of(cfg));
   advance_lane(L, pl, g, rc, cfg, actions, reward, term, trunc_);
 }
 
@@ -230,7 +225,7 @@ __global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_obs_step(const 
   PairLane pl;
   if (!pair_lane(nenv, pl)) return;
   const Lanes<PT> L = lanes_of(sm);
-  const Los g = stage_pair<LAYOUT>(L, st, ld, pl.a, pl.k, origin_of(og));
+  const Los g = stage_pair<LAYOUT>(L, st, ld, pl.a, pl.k, origin_of(og), prev_attitude(rc, pl.a), inv_dt_of(cfg));
   const Advanced A = advance_lane(L, pl, g, rc, cfg, actions, reward, term, trunc_);
   L.sync();
   obs_row(L, pl.k, g, A.t, rc.act_hist + pl.a * 20, obs + pl.a * 184,
@@ -282,7 +277,7 @@ __global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_env_post(double
   const Lanes<PT> L = lanes_of(sm);
   const Origin O = origin_of(og);
   const int64_t a = pl.a, e = pl.e;
-  Los g = stage_pair<LAYOUT>(L, st, ld, a, pl.k, O);
+  Los g = stage_pair<LAYOUT>(L, st, ld, a, pl.k, O, prev_attitude(rc, a), inv_dt_of(cfg));
   const Advanced A = advance_lane(L, pl, g, rc, cfg, actions, reward, term, trunc_);
   const bool fin = A.te || A.tr;
   if (pl.k == 0) done[e] = fin;
