@@ -54,6 +54,15 @@ class RecordArgs(C.Structure):
                 ("ep_len", C.c_void_p), ("stats", C.c_void_p)]
 
 
+class PayoffArgs(C.Structure):
+    """f16_payoff_args (include/f16env.h)."""
+    _fields_ = [("done", C.c_void_p), ("terminal_hp", C.c_void_p), ("terminal_alt", C.c_void_p),
+                ("finite", C.c_void_p), ("reward", C.c_void_p), ("left_slot", C.c_void_p), ("lanes", C.c_int64),
+                ("min_alt", C.c_double), ("step", C.c_int32), ("finished", C.c_void_p), ("scores", C.c_void_p),
+                ("own_crash", C.c_void_p), ("opp_crash", C.c_void_p), ("finished_count", C.c_void_p),
+                ("final_step", C.c_void_p), ("nonfinite", C.c_void_p)]
+
+
 _PR = C.POINTER(Recon)
 _PC = C.POINTER(RewardCfg)
 _PO = C.POINTER(Origin)
@@ -86,6 +95,7 @@ _SIGS = {
     "f16_fdm_step_bins": ([_P, C.c_int, _I64, _I64, _P, _P, C.c_int, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_fdm_step_ex": ([_P, C.c_int, _I64, _I64, C.POINTER(FdmIO), C.c_int, C.c_double, _P], C.c_int),
     "f16_rollout_record": ([_I64, C.POINTER(RecordArgs), _P], C.c_int),
+    "f16_payoff_record": ([_I64, C.POINTER(PayoffArgs), _P], C.c_int),
     "f16_seed_ic": ([_P, _I64, _P, C.c_int, _I64, C.c_double, _P], C.c_int),
     "f16_probe_fp64": ([_P, _I64, C.c_int, C.POINTER(C.c_double), _P], C.c_int),
     "f16_version": ([], C.c_char_p),

@@ -259,6 +259,44 @@ extern "C" int f16_rollout_record(int64_t nenv, const f16_record_args* a, f16_st
   return launch_status();
 }
 
+namespace f16 {
+namespace ro {
+// One thread per environment (batched_payoff.py:131-156): first-game scoring of the left policy.
+__global__ void __launch_bounds__(256) k_payoff_record(int64_t nenv, const f16_payoff_args a) {
+  const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= nenv || a.finished[e]) return;
+  const int ls = a.left_slot[e] ? 1 : 0;
+  const double lhp = a.terminal_hp[2 * e + ls], rhp = a.terminal_hp[2 * e + 1 - ls];
+  const double lalt = a.terminal_alt[2 * e + ls], ralt = a.terminal_alt[2 * e + 1 - ls];
+  const bool ok = a.finite[e] && isfinite(lhp) && isfinite(rhp) && isfinite(lalt) && isfinite(ralt) &&
+                  isfinite(a.reward[2 * e]) && isfinite(a.reward[2 * e + 1]);
+  if (!ok) atomicAdd(a.nonfinite, 1);
+  if (!a.done[e]) return;
+  const bool ld = (lhp <= 0.0) || (lalt < a.min_alt);
+  const bool rd = (rhp <= 0.0) || (ralt < a.min_alt);
+  const bool alive = !ld && !rd;
+  const bool win = (rd && !ld) || (alive && (lhp > rhp + 1e-9));
+  const bool loss = (ld && !rd) || (alive && (lhp < rhp - 1e-9));
+  a.scores[e] = win ? 1.0f : (loss ? 0.0f : 0.5f);
+  a.own_crash[e] = lalt < a.min_alt;
+  a.opp_crash[e] = ralt < a.min_alt;
+  a.finished[e] = 1;
+  const int64_t m = e / a.lanes;
+  if ((int64_t)atomicAdd(&a.finished_count[m], 1) + 1 == a.lanes) a.final_step[m] = a.step;
+}
+}  // namespace ro
+}  // namespace f16
+
+extern "C" int f16_payoff_record(int64_t nenv, const f16_payoff_args* a, f16_stream_t stream) {
+  if (!a || nenv <= 0 || a->lanes <= 0 || !a->done || !a->terminal_hp || !a->terminal_alt || !a->finite ||
+      !a->reward || !a->left_slot || !a->finished || !a->scores || !a->own_crash || !a->opp_crash ||
+      !a->finished_count || !a->final_step || !a->nonfinite)
+    return F16_ERR_ARG;
+  const int grid = (int)((nenv + 255) / 256);
+  ro::k_payoff_record<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(nenv, *a);
+  return launch_status();
+}
+
 extern "C" int f16_gae(const float* rew, const float* val, const float* done, const float* last_val,
                        const float* next_done, int T, int64_t n, int64_t ld, double gamma, double lam, float* adv,
                        float* ret, f16_stream_t stream) {

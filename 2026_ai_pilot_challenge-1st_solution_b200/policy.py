@@ -37,23 +37,37 @@ class PolicyArgs(C.Structure):
 class MlpWeights:
     """Device bf16 weights + fp32 biases of one Linear stack."""
 
-    def __init__(self, weights, biases, activation="relu", head=HEAD_CATEGORICAL, act_dim=4, num_bins=21):
+    def __init__(self, weights, biases, activation="relu", head=HEAD_CATEGORICAL, act_dim=4, num_bins=21,
+                 in_width=None):
         self.weights = [w.detach().to(torch.bfloat16).contiguous() for w in weights]
         self.biases = [b.detach().to(torch.float32).contiguous() for b in biases]
+        # the kernel reads the input in 16-byte units, and all networks of one launch share the
+        # input row layout: the first layer gets zero columns up to in_width (default: the next
+        # multiple of 8, e.g. 216 for the 214-D external observation), which meet the zero
+        # padding of the input rows
+        self.obs_dim = self.weights[0].shape[1]
+        width = -(-self.obs_dim // 8) * 8 if in_width is None else int(in_width)
+        if width < self.obs_dim or width % 8:
+            raise ValueError("in_width must be a multiple of 8 not below the network's input width")
+        if width != self.obs_dim:
+            w0 = self.weights[0]
+            pad = torch.zeros(w0.shape[0], width, dtype=w0.dtype, device=w0.device)
+            pad[:, :self.obs_dim] = w0
+            self.weights[0] = pad
         self.activation = activation
         self.head = head
         self.act_dim, self.num_bins = act_dim, num_bins
         self.in_dim = self.weights[0].shape[1]
 
     @classmethod
-    def from_sequential(cls, seq, head, device, act_dim=4, num_bins=21):
+    def from_sequential(cls, seq, head, device, act_dim=4, num_bins=21, in_width=None):
         linears = [m for m in seq if isinstance(m, torch.nn.Linear)]
         acts = {type(m).__name__.lower() for m in seq if not isinstance(m, torch.nn.Linear)}
         act = "tanh" if "tanh" in acts else "relu"
         if acts - {"tanh", "relu"}:
             raise ValueError(f"unsupported activation(s): {acts}")
         return cls([l.weight.to(device) for l in linears], [l.bias.to(device) for l in linears], act, head,
-                   act_dim, num_bins)
+                   act_dim, num_bins, in_width)
 
     @torch.no_grad()
     def load_from(self, seq):
@@ -63,9 +77,10 @@ class MlpWeights:
         if len(linears) != len(self.weights):
             raise ValueError("layer count differs from the registered network")
         for w, b, lin in zip(self.weights, self.biases, linears):
-            if tuple(w.shape) != tuple(lin.weight.shape):
+            rows, cols = lin.weight.shape
+            if w.shape[0] != rows or not (w.shape[1] == cols or (w is self.weights[0] and cols == self.obs_dim)):
                 raise ValueError("layer shape differs from the registered network")
-            w.copy_(lin.weight)
+            w[:, :cols].copy_(lin.weight)
             b.copy_(lin.bias)
 
     def desc(self):

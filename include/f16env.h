@@ -375,6 +375,36 @@ typedef struct {
 } f16_record_args;
 int f16_rollout_record(int64_t nenv, const f16_record_args* args, f16_stream_t stream);
 
+/* Per-step scoring of batched payoff evaluation (R/cuda_fdm/batched_payoff.py:131-156; the
+ * single-matchup form ppo_gpu.py:1467-1500), after the env step.  Environments still playing
+ * their first game (finished[e] == 0) are active: an active environment whose terminal state
+ * flag, terminal HP, terminal altitude or reward is not finite increments nonfinite.  An active
+ * environment that is done is scored for the left policy, which flies aircraft left_slot[e]:
+ * dead = HP <= 0 or altitude below min_alt; win = only the other side dead, or both alive and
+ * left HP > right HP + 1e-9; loss symmetric; score 1 / 0.5 / 0 (win / draw / loss, fp32);
+ * own_crash / opp_crash = the left / right aircraft's altitude below min_alt; finished[e] = 1;
+ * and the finish count of its matchup (lanes consecutive environments per matchup) is
+ * incremented -- the increment that completes the matchup writes final_step = step. */
+typedef struct {
+  const uint8_t* done;          /* [nenv] */
+  const double* terminal_hp;    /* [nac] */
+  const double* terminal_alt;   /* [nac] m */
+  const uint8_t* finite;        /* [nenv] the step's terminal_state_finite */
+  const double* reward;         /* [nac] */
+  const uint8_t* left_slot;     /* [nenv] aircraft (0 / 1) flown by the left policy */
+  int64_t lanes;                /* environments per matchup (> 0) */
+  double min_alt;               /* m */
+  int32_t step;                 /* 1-based step index */
+  uint8_t* finished;            /* [nenv] */
+  float* scores;                /* [nenv] */
+  uint8_t* own_crash;           /* [nenv] */
+  uint8_t* opp_crash;           /* [nenv] */
+  int32_t* finished_count;      /* [nenv / lanes], zeroed by the caller */
+  int32_t* final_step;          /* [nenv / lanes] */
+  int32_t* nonfinite;           /* [1], zeroed by the caller */
+} f16_payoff_args;
+int f16_payoff_record(int64_t nenv, const f16_payoff_args* args, f16_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------
  * Diagnostics (no counterpart in the reference): FP64 FMA-pipe probe, the measured roofline
  * denominator of the FDM kernel.  Launches `blocks` x 256 threads running 8 independent FMA
