@@ -97,6 +97,48 @@ class GpuDogfight:
                                          _lib.stream_of(self.states_soa)), "f16_fdm_step")
         return self.obs.view(self.nenv, self.ppe, OBS_N)
 
+    def step_host(self, actions, obs_out=None, substeps=None, chunks=4):
+        """step() driven from host memory: ``actions`` (nac, 4) fp64 on the host (pinned, so the
+        copies are asynchronous) and obs17 written into ``obs_out`` (nac, 17) fp64 host memory
+        (pinned; allocated once when omitted).  The aircraft are split into ``chunks`` slices
+        whose host-to-device copy, FDM launch and device-to-host copy run on two alternating
+        streams, so the copies of one slice overlap the physics of the next; the caller's
+        current stream waits for all of it.  Results are step()'s bit for bit (aircraft are
+        independent).  Returns ``obs_out`` viewed (nenv, ppe, 17)."""
+        ss = self.substeps if substeps is None else int(substeps)
+        a = torch.as_tensor(actions, dtype=torch.float64)
+        if a.device.type != "cpu":
+            raise ValueError("step_host takes host actions; use step() for device tensors")
+        a = a.reshape(self.nac, 4).contiguous()
+        if obs_out is None:
+            if getattr(self, "_host_obs", None) is None:
+                self._host_obs = torch.empty(self.nac, OBS_N, dtype=torch.float64).pin_memory()
+            obs_out = self._host_obs
+        if obs_out.device.type != "cpu" or obs_out.dtype != torch.float64 or obs_out.numel() != self.nac * OBS_N:
+            raise ValueError("obs_out must be a (nac, 17) float64 host tensor")
+        out = obs_out.view(self.nac, OBS_N)
+        if getattr(self, "_side_streams", None) is None:
+            self._side_streams = [torch.cuda.Stream(self.device) for _ in range(2)]
+        cur = torch.cuda.current_stream(self.device)
+        start = torch.cuda.Event()
+        start.record(cur)
+        n, chunks = self.nac, max(1, min(int(chunks), self.nac))
+        st, act, obs = self.states_soa.data_ptr(), self.actions.data_ptr(), self.obs.data_ptr()
+        for i in range(chunks):
+            lo, hi = n * i // chunks, n * (i + 1) // chunks
+            if hi == lo:
+                continue
+            s = self._side_streams[i % 2]
+            s.wait_event(start)
+            with torch.cuda.stream(s):
+                self.actions[lo:hi].copy_(a[lo:hi], non_blocking=True)
+                _lib.check(self.lib.f16_fdm_step(st + 8 * lo, _lib.LAYOUT_SOA, self.nac, hi - lo, act + 32 * lo, ss,
+                                                 self.fcs_dt, obs + 8 * OBS_N * lo, s.cuda_stream), "f16_fdm_step")
+                out[lo:hi].copy_(self.obs[lo:hi], non_blocking=True)
+        for s in self._side_streams:
+            cur.wait_stream(s)
+        return out.view(self.nenv, self.ppe, OBS_N)
+
     def step_bins(self, bins, num_bins=21, substeps=None, write_obs=True, grid=None):
         """Fused action mapping: bins (nac,4) uint8 -> reference action_to_env grid -> FDM.
         grid: the float32 action grid (default: torch.linspace(-1, 1, num_bins) evaluated on

@@ -135,3 +135,19 @@ def test_reset_ic_dicts(cfg1, mods, cuda):
     sim.reset_ic(dicts)
     exp = ofdm.oracle_seed(rows, float(cfg1["fcs_dt"]))
     assert scaled_err(sim.states.cpu().numpy(), exp).max() <= 1e-9
+
+
+def test_step_host_matches_step(cfg1, mods, cuda):
+    """The host-driven, slice-pipelined step gives step()'s states and obs17 bit for bit."""
+    ge, ic = mods
+    fcs_dt = float(cfg1["fcs_dt"])
+    a = make_sim(mods, 64, cfg1["seeds"], fcs_dt, cuda)
+    b = make_sim(mods, 64, cfg1["seeds"], fcs_dt, cuda)
+    out = torch.empty(128, 17, dtype=torch.float64).pin_memory()
+    for k in range(3):
+        c = ic.bins_to_commands(torch.as_tensor(cfg1["bins"][k]).to(cuda)).double().contiguous()
+        oa = a.step(c).reshape(128, 17).clone()
+        ob = b.step_host(c.cpu().pin_memory(), out, chunks=3)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(a.states, b.states, rtol=0, atol=0)
+        torch.testing.assert_close(oa.cpu(), ob.reshape(128, 17), rtol=0, atol=0)
