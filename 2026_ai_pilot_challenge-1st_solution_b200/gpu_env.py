@@ -97,7 +97,7 @@ class GpuDogfight:
                                          _lib.stream_of(self.states_soa)), "f16_fdm_step")
         return self.obs.view(self.nenv, self.ppe, OBS_N)
 
-    def step_host(self, actions, obs_out=None, substeps=None, chunks=4):
+    def step_host(self, actions, obs_out=None, substeps=None, chunks=2):
         """step() driven from host memory: ``actions`` (nac, 4) fp64 on the host (pinned, so the
         copies are asynchronous) and obs17 written into ``obs_out`` (nac, 17) fp64 host memory
         (pinned; allocated once when omitted).  The aircraft are split into ``chunks`` slices

@@ -48,11 +48,14 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--e2e-steps", type=int, default=100)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", default="fdm", choices=["fdm", "obs", "rollout", "ppo"],
+    p.add_argument("--workload", default="fdm",
+                   choices=["fdm", "obs", "rollout", "ppo", "seed", "external", "warmup", "payoff"],
                    help="fdm = configs[1] headline (default); obs = configs[2] fused obs/reward kernel; "
                         "rollout = configs[3] full 64-step rollout (env + obs/reward + actor/critic/opponents + GAE); "
                         "ppo = configs[4] PPO league iteration (rollout + 4x16 minibatch update, NCCL gradient "
-                        "allreduce across ranks)")
+                        "allreduce across ranks); seed / external / warmup / payoff = the next rows: GPU IC "
+                        "seeder, 214-D external observation, device-side staggered warm-up, batched payoff "
+                        "evaluation")
     return p.parse_args()
 
 
@@ -604,6 +607,126 @@ def run_ppo(args, dev, world, rank):
     return 0
 
 
+def run_aux(args, dev, world, rank):
+    """The rows beside the hot path, each timed with CUDA events on the launching stream:
+    seed      f16_seed_ic on 131,072 aircraft (BASELINE's IC distribution); aircraft seeded/s,
+              with the reference's seeding restated in C (oracle) on one host core beside it;
+    external  the 214-D external rows of 262,144 envs (f16_external_accel before the advance
+              + f16_external_obs after it); aircraft rows/s;
+    warmup    GpuDogfightVecEnv.reset(stagger=True) of 131,072 envs: seeding, the device-side
+              staggered warm-up (up to 256 random-action decisions, no host sync) and the first
+              observations; environments reset/s;
+    payoff    BatchedPayoff: one left policy against 16 right policies (184-512-512-84 ReLU),
+              32 games per ordering each (1,024 environments), sampled actions, to completion;
+              games/s."""
+    import torch
+    K, W = max(1, args.steps), max(3, args.warmup)
+    stream = torch.cuda.current_stream(dev)
+    ic = importlib.import_module(PKG + ".ic")
+    _lib = importlib.import_module(PKG + "._lib")
+    L = _lib.load()
+    clk_idx = physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0")))
+    cpu = None
+    extra = {}
+
+    def timed(fn, k):
+        es = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k)]
+        for a, b in es:
+            a.record(stream)
+            fn()
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+        return float(np.mean([a.elapsed_time(b) for a, b in es]))
+
+    if args.workload == "seed":
+        n = 2 * NENV
+        rows = torch.as_tensor(ic.baseline_ics(NENV, 20260102 + rank), dtype=torch.float64, device=dev).contiguous()
+        out = torch.empty(101, n, dtype=torch.float64, device=dev)
+        go = lambda: _lib.check(L.f16_seed_ic(_lib.ptr(rows), n, _lib.ptr(out), _lib.LAYOUT_SOA, n, FCS_DT,
+                                              _lib.stream_of(out)), "f16_seed_ic")
+        for _ in range(W):
+            go()
+        with ClockSampler(clk_idx) as clk:
+            ms = timed(go, K)
+        units, metric, unit, launches = n, "aircraft seeded/s (GPU IC seeder)", "aircraft/s", K
+        config = {"workload": "next row f1: f16_seed_ic, 131,072 aircraft, BASELINE IC distribution"}
+        if not args.no_cpu_baseline and world == 1:
+            from oracle import fdm as ofdm
+            sample = ic.baseline_ics(1024, 5)
+            t0 = time.perf_counter()
+            reps = 0
+            while time.perf_counter() - t0 < 2.0:
+                ofdm.oracle_seed(sample, FCS_DT)
+                reps += 1
+            cpu = {"value": reps * 2048 / (time.perf_counter() - t0), "unit": unit, "cores": 1, "kind": "port",
+                   "sample": f"{reps} x 2,048 aircraft through the C restatement of the reference seeding"}
+    elif args.workload == "external":
+        ob = importlib.import_module(PKG + ".obs_reward")
+        nenv = 262_144
+        st, _, g = obs_inputs(nenv, 20260103 + rank, dev)
+        obr = ob.BatchObsReward(nenv, device=dev)
+        obr.enable_external_observations()
+        obr.prev_valid.fill_(1)
+        obr.kernel_build_obs(st.t())
+        sp, lay, ld, _keep = obr._kernel_states(st.t())
+
+        def go():
+            obr._external_advance(sp, lay, ld)
+            obr.build_external_obs(st.t())
+        for _ in range(W):
+            go()
+        with ClockSampler(clk_idx) as clk:
+            ms = timed(go, K)
+        units, metric, unit, launches = 2 * nenv, "external 214-D rows/s", "aircraft-rows/s", 3 * K
+        config = {"workload": "next row f2: acceleration update + 214-D rows (incl. the 184-D rebuild they "
+                              "extend) for 262,144 envs x 2"}
+    elif args.workload == "warmup":
+        rl_env = importlib.import_module(PKG + ".rl_env")
+        env = rl_env.GpuDogfightVecEnv(ROLL_NENV, substeps=SUBSTEPS, seed=20260105 + rank, device=dev)
+        go = lambda: env.reset(stagger=True, sync_free=True)
+        go()
+        torch.cuda.synchronize(dev)
+        with ClockSampler(clk_idx) as clk:
+            ms = timed(go, max(1, min(K, 3)))
+        units, metric, unit, launches = ROLL_NENV, "staggered resets/s (device-side warm-up)", "envs/s", None
+        config = {"workload": "next row f3: reset(stagger=True) of 131,072 envs, warm-up up to 256 decisions"}
+    else:
+        tr = importlib.import_module(PKG + ".trainer")
+        payoff = importlib.import_module(PKG + ".payoff")
+        mk = lambda s: (torch.manual_seed(s), tr.MLPActorCritic(hidden=(512, 512), activation="relu").to(dev))[1]
+        left = payoff.EvalPolicy(mk(100))
+        rights = [payoff.EvalPolicy(mk(200 + i)) for i in range(16)]
+        bp = payoff.BatchedPayoff(per_order=32, capacity=16, seed=11 + rank, device=dev)
+        bp.evaluate(left, rights[:2], seed_block=0)
+        torch.cuda.synchronize(dev)
+        steps = []
+
+        def go():
+            steps.append(max(r["steps"] for r in bp.evaluate(left, rights, seed_block=len(steps) + 1)))
+        with ClockSampler(clk_idx) as clk:
+            ms = timed(go, max(1, min(K, 3)))
+        units, metric, unit, launches = 16 * 64, "payoff games/s (batched evaluation to completion)", "games/s", None
+        config = {"workload": "next row f4: 1 left vs 16 right policies, 32 games per ordering each",
+                  "decisions_per_evaluation": steps}
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank == 0:
+        line = {"metric": metric, "value": world * units / (ms * 1e-3), "unit": unit, "n_gpus": world, "steps": K,
+                "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f64" if args.workload != "payoff" else "f64+bf16", "data": "synthetic",
+                "config": config, "clocks": clk.summary()}
+        if launches is not None:
+            line["gpu_launches"] = launches
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     try:
@@ -647,6 +770,8 @@ def main():
         return run_rollout(args, dev, world, rank)
     if args.workload == "ppo":
         return run_ppo(args, dev, world, rank)
+    if args.workload in ("seed", "external", "warmup", "payoff"):
+        return run_aux(args, dev, world, rank)
 
     _lib = importlib.import_module(PKG + "._lib")
     ge = importlib.import_module(PKG + ".gpu_env")
@@ -714,6 +839,9 @@ def main():
     host_cmd = cmd[W:W + Ke].cpu().pin_memory()
     host_obs = torch.empty(nac, 17, dtype=torch.float64).pin_memory()
     sim.states_soa.copy_(seeds)
+    for k in range(2):                      # untimed: the API's side streams and first launches
+        sim.step_host(host_cmd[k % Ke], host_obs)
+    sim.states_soa.copy_(seeds)
     e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(Ke)]
     e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(Ke)]
     if world > 1:
@@ -766,7 +894,7 @@ def main():
                        "timed_region_wall_s": wall},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": nac * 4 * 8,
                     "d2h_bytes_per_step": nac * 17 * 8, "api": "GpuDogfight.step_host(pinned host fp64 actions) -> obs17 into pinned host memory "
-                           "(4 aircraft slices: copies overlap the physics of the next slice)",
+                           "(2 aircraft slices on two streams: copies overlap the physics of the other slice)",
                     "steps": Ke},
             "roofline": {"bound": "fp64", "achieved": achieved_tflops, "peak": peak_tflops, "unit": "TFLOP/s",
                          "frac": achieved_tflops / peak_tflops, "traffic": traffic,
