@@ -60,7 +60,7 @@ class PayoffArgs(C.Structure):
                 ("finite", C.c_void_p), ("reward", C.c_void_p), ("left_slot", C.c_void_p), ("lanes", C.c_int64),
                 ("min_alt", C.c_double), ("step", C.c_int32), ("finished", C.c_void_p), ("scores", C.c_void_p),
                 ("own_crash", C.c_void_p), ("opp_crash", C.c_void_p), ("finished_count", C.c_void_p),
-                ("final_step", C.c_void_p), ("nonfinite", C.c_void_p)]
+                ("final_step", C.c_void_p), ("nonfinite", C.c_void_p), ("step_dev", C.c_void_p)]
 
 
 _PR = C.POINTER(Recon)

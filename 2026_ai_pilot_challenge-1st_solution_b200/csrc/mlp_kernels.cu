@@ -77,6 +77,7 @@ struct Launch {
   float* value;                                  // value head output per row
   float* logits; int64_t logits_ld;              // optional raw logits / value (tests)
   uint64_t seed, step;
+  const uint64_t* step_dev;                      // optional device counter added to step
   int deterministic;                             // argmax instead of sampling
   int* err;
   double* cmd; int64_t cmd_stride; int cmd_offset;   // optional env commands of the bins
@@ -336,7 +337,7 @@ __device__ __forceinline__ float cat_head(uint32_t lane_addr, const float* __res
   float lg[W];
 #pragma unroll
   for (int i = 0; i < W; i++) lg[i] = __uint_as_float(r[C0 - LB + i]) + __ldg(bias + C0 + i);
-  const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step, row);
+  const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step + (L.step_dev ? *L.step_dev : 0ull), row);
   float logp = 0.0f;
 #pragma unroll
   for (int gl = 0; gl < GA; gl++) {
@@ -382,7 +383,7 @@ __device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
 __device__ __noinline__ void cat_head_generic(uint32_t lane_addr, const float* __restrict__ bias, const Launch& L,
                                               const NetParams& P, int64_t row, bool valid) {
   const int nb = P.num_bins;
-  const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step, row);
+  const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step + (L.step_dev ? *L.step_dev : 0ull), row);
   float logp = 0.0f;
   for (int g = 0; g < P.act_dim; g++) {
     const int c0 = g * nb;
@@ -796,7 +797,7 @@ extern "C" int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args*
   L.bins = a->bins; L.bins_stride = a->bins_stride; L.bins_offset = a->bins_offset;
   L.act_idx = a->act_idx; L.logp = a->logp; L.value = a->value;
   L.logits = a->logits; L.logits_ld = a->logits_ld;
-  L.seed = a->seed; L.step = a->step; L.deterministic = a->deterministic;
+  L.seed = a->seed; L.step = a->step; L.step_dev = a->step_dev; L.deterministic = a->deterministic;
   L.err = a->err;
   if (a->cmd && (!a->grid || a->cmd_stride < 0 || a->cmd_offset < 0)) return F16_ERR_ARG;
   L.cmd = a->cmd; L.cmd_stride = a->cmd_stride; L.cmd_offset = a->cmd_offset; L.grid = a->grid;

@@ -282,7 +282,8 @@ __global__ void __launch_bounds__(256) k_payoff_record(int64_t nenv, const f16_p
   a.opp_crash[e] = ralt < a.min_alt;
   a.finished[e] = 1;
   const int64_t m = e / a.lanes;
-  if ((int64_t)atomicAdd(&a.finished_count[m], 1) + 1 == a.lanes) a.final_step[m] = a.step;
+  if ((int64_t)atomicAdd(&a.finished_count[m], 1) + 1 == a.lanes)
+    a.final_step[m] = a.step + (a.step_dev ? (int32_t)*a.step_dev : 0);
 }
 }  // namespace ro
 }  // namespace f16

@@ -17,8 +17,11 @@ Per step, on the device and without a host synchronisation:
   * one scatter of the commands into the env's command buffer, the fused env step, and
     ``f16_payoff_record`` (per-lane first-game scoring, matchup completion step, non-finite
     count).
-The host reads completion and the non-finite count every ``check_every`` steps (the reference
-reads them every step); finished lanes are frozen, so the extra steps change no result.
+The whole decision is captured once as a CUDA graph and replayed (the reference replays a
+graph of its 128-row forwards); the RNG step and the scoring step come from a device counter
+the graph advances.  The host reads completion and the non-finite count every ``check_every``
+decisions (the reference reads them every decision); finished lanes are frozen, so the extra
+decisions change no result.
 
 Sampling is the kernel's counter-based Gumbel-max stream keyed by the evaluation seed, the
 step and the row: replayable for a given seed, not torch.multinomial's stream (the
@@ -153,8 +156,10 @@ class BatchedPayoff:
         return src, groups, spans, valid, src[valid].clone()
 
     @torch.no_grad()
-    def evaluate(self, left, rights, *, seed_block=0, sample=True, check_every=8):
-        """One summary dict per right policy (the reference's evaluate_chunk)."""
+    def evaluate(self, left, rights, *, seed_block=0, sample=True, check_every=8, use_graph=True):
+        """One summary dict per right policy (the reference's evaluate_chunk).  With ``use_graph``
+        the per-decision launches (gather, normalise, policy, scatter, env step, scoring) are
+        one CUDA graph replayed every decision, like the reference's captured forwards."""
         rights = list(rights)
         if not 1 <= len(rights) <= self.capacity:
             raise ValueError("matchup count must be between one and batch capacity")
@@ -199,31 +204,48 @@ class BatchedPayoff:
                                own_crash=self.own_crash.data_ptr(), opp_crash=self.opp_crash.data_ptr(),
                                finished_count=self.counts[1:].data_ptr(), final_step=self.final_step.data_ptr(),
                                nonfinite=self.counts[:1].data_ptr())
-        stream = _lib.stream_of(self.scores)
-        complete = False
-        for step in range(1, max_steps + 1):
+        counter = torch.zeros(1, dtype=torch.int64, device=dev)     # decisions taken before this one
+        args.step, args.step_dev = 1, counter.data_ptr()
+        keep = {}
+
+        def decision():
             obs = env.obr.obs_buf.view(env.nac, 184)
             torch.index_select(obs, 0, src, out=x184)
             if external:
-                full = env.obr.build_external_obs(env.sim.states)
-                torch.index_select(full, 0, src, out=x214)
+                torch.index_select(env.obr.build_external_obs(env.sim.states), 0, src, out=x214)
             for p, (a, b) in zip(pols, spans):
                 x = (x214 if p.obs_dim == 214 else x184)[a:b]
                 if p.norm is not None:
                     p.norm.normalize_bf16(x, out_bf16=xb[a:b], pad_to=in_pad)
                 else:
                     cast_bf16(x, xb[a:b])
-            pset.forward(xb, groups, seed=eval_seed, step=step, deterministic=not sample, cmd=cmd_rows,
-                         cmd_stride=4, cmd_offset=0, grid=self.grid)
+            pset.forward(xb, groups, seed=eval_seed, step=1, step_dev=counter, deterministic=not sample,
+                         cmd=cmd_rows, cmd_stride=4, cmd_offset=0, grid=self.grid)
             cmd.index_copy_(0, dst, cmd_rows.index_select(0, valid))
-            _, reward, done, info = env.step(cmd)
+            _, _, _, info = env.step(cmd)
+            keep["finite"] = info["terminal_state_finite"].to(torch.uint8)
             args.done = env._done.data_ptr()
             args.terminal_hp, args.terminal_alt = env._terminal_hp.data_ptr(), env._terminal_alt.data_ptr()
-            fin = info["terminal_state_finite"].to(torch.uint8)
-            args.finite = fin.data_ptr()
+            args.finite = keep["finite"].data_ptr()
             args.reward = env.obr.reward_buf.data_ptr()
-            args.step = step
-            _lib.check(self.lib.f16_payoff_record(env.nenv, args, stream), "f16_payoff_record")
+            _lib.check(self.lib.f16_payoff_record(env.nenv, args, _lib.stream_of(self.scores)), "f16_payoff_record")
+            counter.add_(1)
+
+        # the first decision runs eagerly (it also initialises every lazily built buffer); the
+        # rest replay one captured CUDA graph of it, the step counter advancing on the device
+        decision()
+        graph = None
+        if use_graph:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                decision()
+        complete = False
+        for step in range(1, max_steps + 1):
+            if step > 1:
+                if graph is not None:
+                    graph.replay()
+                else:
+                    decision()
             if step % int(check_every) == 0 or step == max_steps:
                 c = self.counts[:1 + n_match].tolist()
                 if c[0]:
@@ -231,6 +253,7 @@ class BatchedPayoff:
                 if all(v == lanes for v in c[1:]):
                     complete = True
                     break
+        del graph
         pset.check_error()
         s = self.scores[:used].view(n_match, lanes).cpu().numpy()
         oc = self.own_crash[:used].view(n_match, lanes).cpu().numpy().astype(bool)

@@ -31,7 +31,8 @@ class PolicyArgs(C.Structure):
                 ("bins", C.c_void_p), ("bins_stride", C.c_int64), ("bins_offset", C.c_int), ("act_idx", C.c_void_p),
                 ("logp", C.c_void_p), ("value", C.c_void_p), ("logits", C.c_void_p), ("logits_ld", C.c_int64),
                 ("seed", C.c_uint64), ("step", C.c_uint64), ("deterministic", C.c_int), ("err", C.c_void_p),
-                ("cmd", C.c_void_p), ("cmd_stride", C.c_int64), ("cmd_offset", C.c_int), ("grid", C.c_void_p)]
+                ("cmd", C.c_void_p), ("cmd_stride", C.c_int64), ("cmd_offset", C.c_int), ("grid", C.c_void_p),
+                ("step_dev", C.c_void_p)]
 
 
 class MlpWeights:
@@ -122,11 +123,13 @@ class PolicySet:
 
     def forward(self, x_bf16, groups, nets_per_group=1, bins=None, bins_stride=4, bins_offset=0, act_idx=None,
                 logp=None, value=None, logits=None, seed=0, step=0, deterministic=False, cmd=None, cmd_stride=4,
-                cmd_offset=0, grid=None):
+                cmd_offset=0, grid=None, step_dev=None):
         """groups: list of (row_end, [net indices]) with every group starting at a multiple of 128.
 
         ``cmd`` (fp64, optional) receives action_to_env of the sampled bins at
-        ``cmd[r * cmd_stride + cmd_offset + c]`` using the fp32 ``grid`` (num_bins values)."""
+        ``cmd[r * cmd_stride + cmd_offset + c]`` using the fp32 ``grid`` (num_bins values).
+        ``step_dev`` (device int64 [1], optional) is added to ``step`` when the kernel runs, so a
+        captured CUDA graph draws fresh samples on every replay."""
         _lib.require_cuda_tensor(x_bf16, torch.bfloat16, None, "policy input", None)
         rows, ldx = x_bf16.shape[0], x_bf16.stride(0)
         ends = (C.c_int64 * len(groups))(*[int(g[0]) for g in groups])
@@ -147,6 +150,9 @@ class PolicySet:
         a.logits_ld = logits.stride(0) if logits is not None else 0
         a.seed = seed & (2 ** 64 - 1); a.step = step & (2 ** 64 - 1); a.deterministic = int(bool(deterministic))
         a.err = self.err.data_ptr()
+        if step_dev is not None:
+            _lib.require_cuda_tensor(step_dev, torch.int64, (1,), "step counter", x_bf16.device)
+            a.step_dev = step_dev.data_ptr()
         if cmd is not None:
             _lib.require_cuda_tensor(cmd, torch.float64, None, "env commands", x_bf16.device)
             _lib.require_cuda_tensor(grid, torch.float32, None, "action grid", x_bf16.device)

@@ -290,6 +290,9 @@ typedef struct {
   int64_t cmd_stride;
   int cmd_offset;
   const float* grid;
+  /* optional device counter added to `step` when the kernel runs (NULL: none), so one captured
+   * CUDA graph can be replayed with a fresh RNG step each time */
+  const uint64_t* step_dev;
 } f16_policy_args;
 
 int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args* args, f16_stream_t stream);
@@ -402,6 +405,7 @@ typedef struct {
   int32_t* finished_count;      /* [nenv / lanes], zeroed by the caller */
   int32_t* final_step;          /* [nenv / lanes] */
   int32_t* nonfinite;           /* [1], zeroed by the caller */
+  const int64_t* step_dev;      /* optional device counter added to `step` (graph replays), or NULL */
 } f16_payoff_args;
 int f16_payoff_record(int64_t nenv, const f16_payoff_args* args, f16_stream_t stream);
 

@@ -106,3 +106,13 @@ def test_sampled_evaluation_replays(cuda):
     for r in r1:
         assert set(np.unique(np.asarray(r["paired_scores"]) * 2).tolist()) <= {0.0, 0.5, 1.0, 1.5, 2.0}
         assert r["stochastic"] and r["policy_rng_seed"] == r2[0]["policy_rng_seed"]
+
+
+def test_graph_replay_equals_eager(cuda):
+    """The captured decision graph (device step counter) reproduces the eager loop exactly."""
+    payoff = pkg_module("payoff")
+    A, B, C, _ = _policies(cuda)
+    bp = payoff.BatchedPayoff(per_order=4, capacity=2, seed=21, device=cuda)
+    g = bp.evaluate(A, [B, C], seed_block=3, use_graph=True)
+    e = bp.evaluate(A, [B, C], seed_block=3, use_graph=False, check_every=1)
+    assert [_key(x) for x in g] == [_key(x) for x in e]
