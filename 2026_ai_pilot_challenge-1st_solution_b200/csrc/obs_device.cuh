@@ -244,9 +244,13 @@ __device__ __forceinline__ void log_so3(const M3& R, double inv_dt, double out[3
   out[1] = (R.m[0][2] - R.m[2][0]) * sc * inv_dt;
   out[2] = (R.m[1][0] - R.m[0][1]) * sc * inv_dt;
 }
+// The reference's STORE (obs_kernel.cu:331-333): a non-finite double becomes +-10 / 0, then the
+// value is rounded to fp32 (a finite double past the float range stays infinite).  The rounded
+// value is tested first, so the double is only inspected on the rare non-finite path.
 __device__ __forceinline__ float store_val(double v) {
-  if (!isfinite(v)) v = (v > 0.0) ? 10.0 : ((v < 0.0) ? -10.0 : 0.0);
-  return (float)v;
+  float f = (float)v;
+  if (!isfinite(f) && !isfinite(v)) f = (v > 0.0) ? 10.0f : ((v < 0.0) ? -10.0f : 0.0f);
+  return f;
 }
 __device__ __forceinline__ float store_f(float f) {
   return isfinite(f) ? f : ((f > 0.0f) ? 10.0f : ((f < 0.0f) ? -10.0f : 0.0f));
@@ -404,16 +408,18 @@ struct RowWriter {
   float* out;
   float buf[4];
   int n;
-  __device__ __forceinline__ void putf(float f) {
-    if (!isfinite(f)) f = (f > 0.0f) ? 10.0f : ((f < 0.0f) ? -10.0f : 0.0f);
+  __device__ __forceinline__ void push(float f) {
     buf[n & 3] = f;
     n++;
     if ((n & 3) == 0) reinterpret_cast<float4*>(out)[(n >> 2) - 1] = make_float4(buf[0], buf[1], buf[2], buf[3]);
   }
-  __device__ __forceinline__ void put(double v) {
-    if (!isfinite(v)) v = (v > 0.0) ? 10.0 : ((v < 0.0) ? -10.0 : 0.0);
-    putf((float)v);
+  // a feature computed in fp32: NaN -> 0, +-inf -> +-10
+  __device__ __forceinline__ void putf(float f) {
+    if (!isfinite(f)) f = (f > 0.0f) ? 10.0f : ((f < 0.0f) ? -10.0f : 0.0f);
+    push(f);
   }
+  // a feature computed in fp64, stored as the reference's STORE does
+  __device__ __forceinline__ void put(double v) { push(store_val(v)); }
 };
 
 // normz with the constant half-range folded into a reciprocal: (clamp(x) - mid) / half as one

@@ -48,6 +48,8 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--e2e-steps", type=int, default=100)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--tf32", action="store_true", help="ppo workload: TF32 matmuls in the update (below the "
+                                                         "reference's fp32; reported in dtype)")
     p.add_argument("--workload", default="fdm",
                    choices=["fdm", "obs", "rollout", "ppo", "seed", "external", "warmup", "payoff"],
                    help="fdm = configs[1] headline (default); obs = configs[2] fused obs/reward kernel; "
@@ -512,11 +514,12 @@ def run_ppo(args, dev, world, rank):
     envs against 16 frozen opponents (env blocks), then 4 epochs x 16 minibatches of clipped PPO
     (clip 0.2) with gradients, advantage statistics and approx-KL all-reduced over NCCL, so all
     ranks apply identical optimiser steps (weak scaling: 131,072 envs per GPU).  The update runs
-    in torch with TF32 matmuls."""
+    in torch at the reference's precision: fp32 matmuls (PyTorch's default, which the reference
+    keeps); --tf32 opts into TF32 matmuls and says so in the line's dtype."""
     import torch
     import torch.distributed as dist
-    torch.backends.cuda.matmul.allow_tf32 = True
-    torch.backends.cudnn.allow_tf32 = True
+    torch.backends.cuda.matmul.allow_tf32 = bool(args.tf32)
+    torch.backends.cudnn.allow_tf32 = bool(args.tf32)
     tr = importlib.import_module(PKG + ".trainer")
     rl_env = importlib.import_module(PKG + ".rl_env")
     pg = dist.group.WORLD if world > 1 else None
@@ -585,7 +588,7 @@ def run_ppo(args, dev, world, rank):
         nparams = sum(p.numel() for p in t.model.parameters())
         line = {"metric": "decision-steps/s over full PPO iterations (rollout + update)", "value": value,
                 "unit": "decision-steps/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_it,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64+bf16 (update tf32)",
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64+bf16 (update " + ("tf32" if args.tf32 else "fp32") + ")",
                 "data": "synthetic ICs, random-init networks",
                 "config": {"workload": "configs[4]: PPO league iteration, 131,072 envs per GPU, T=64, 4 epochs x 16 "
                                        "minibatches, clip 0.2, 16 frozen opponents, NCCL gradient allreduce",
