@@ -75,14 +75,41 @@ __device__ __forceinline__ M3 ned2body(double roll, double pitch, double yaw, do
   return R;
 }
 
+// ned2body from the sin/cos of roll, pitch, yaw (sc as ned2body writes them)
+__device__ __forceinline__ M3 ned2body_sc(const double* sc) {
+  const double sr = sc[0], cr = sc[1], sp = sc[2], cp = sc[3], sy = sc[4], cy = sc[5];
+  M3 R;
+  R.m[0][0] = cp * cy; R.m[0][1] = cp * sy; R.m[0][2] = -sp;
+  R.m[1][0] = sr * sp * cy - cr * sy; R.m[1][1] = sr * sp * sy + cr * cy; R.m[1][2] = sr * cp;
+  R.m[2][0] = cr * sp * cy + sr * sy; R.m[2][1] = cr * sp * sy - sr * cy; R.m[2][2] = cr * cp;
+  return R;
+}
+
 struct Origin {
   double ox, oy, oz, sl, cl, so, co;
 };
 
 // FDM state row -> official 9-DoF: N, E (tangent plane about the official origin, from the
 // geodetic position at MSL altitude), D = -MSL; roll/pitch/yaw deg; body u, v, w m/s.
+// sin/cos of atan2(y, x) without the angle: (y, x) / hypot(x, y); at the origin the angle is
+// atan2's signed-zero result, taken the long way (never on a real state).
+__device__ __forceinline__ void sincos_atan2(double y, double x, double* s, double* c) {
+  const double h = sqrt(x * x + y * y);
+  if (h > 0.0) {
+    const double ih = 1.0 / h;
+    *s = y * ih;
+    *c = x * ih;
+  } else {
+    sincos(atan2(y, x), s, c);
+  }
+}
+
+// sc (optional) receives sin/cos of roll, pitch, yaw (the attitude features and the inputs of
+// ned2body_sc), from the same matrix elements the angles come from: sin/cos(atan2(y, x)) =
+// (y, x) / hypot and cos(asin(-z)) = sqrt(1 - z^2) -- identities, rounding-level differences
+// from the reference's sin/cos of the degree values.
 template <typename Row>
-__device__ __forceinline__ void kin9(const Row& st, const Origin& O, double s9[9]) {
+__device__ __forceinline__ void kin9(const Row& st, const Origin& O, double s9[9], double* sc = nullptr) {
   double px = st(0), py = st(1), pz = st(2), vx = st(3), vy = st(4), vz = st(5);
   double q0 = st(6), q1 = st(7), q2 = st(8), q3 = st(9), epa = st(13);
   double se, ce;
@@ -111,6 +138,13 @@ __device__ __forceinline__ void kin9(const Row& st, const Origin& O, double s9[9
   double theta = asin(-clampd(L02, -1.0, 1.0));
   double phi = atan2(L12, L22);
   double psi = atan2(L01, L00);
+  if (sc) {
+    sincos_atan2(L12, L22, &sc[0], &sc[1]);
+    const double sp = -clampd(L02, -1.0, 1.0);
+    sc[2] = sp;
+    sc[3] = sqrt(fmax(0.0, (1.0 - sp) * (1.0 + sp)));
+    sincos_atan2(L01, L00, &sc[4], &sc[5]);
+  }
   if (psi < 0.0) psi += PI2;
   double dv0 = vx + ROT * py, dv1 = vy - ROT * px, dv2 = vz;
   double u = T00 * dv0 + T01 * dv1 + T02 * dv2;
@@ -123,10 +157,9 @@ __device__ __forceinline__ void kin9(const Row& st, const Origin& O, double s9[9
   const double ep2 = (WA * WA - b * b) / (b * b);
   double pxy = sqrt(exm * exm + eym * eym);
   double sth, cth;
-  sincos(atan2(ezm * WA, pxy * b), &sth, &cth);
-  double lat = atan2(ezm + ep2 * b * (sth * sth * sth), pxy - WE2 * WA * (cth * cth * cth));
-  double slat, clat;
-  sincos(lat, &slat, &clat);
+  sincos_atan2(ezm * WA, pxy * b, &sth, &cth);
+  double slat, clat;                                // of lat = atan2(num, den)
+  sincos_atan2(ezm + ep2 * b * (sth * sth * sth), pxy - WE2 * WA * (cth * cth * cth), &slat, &clat);
   double ir = 1.0 / pxy;
   double slon = eym * ir, clon = exm * ir;          // sin/cos of atan2(eym, exm)
   double Nr = WA / sqrt(1.0 - WE2 * slat * slat);
@@ -153,18 +186,19 @@ __device__ __forceinline__ M3 dir_frame(const V3& x) {
     R.m[2][0] = 0; R.m[2][1] = 0; R.m[2][2] = 1;
     return R;
   }
-  V3 xn = {x.x / nx, x.y / nx, x.z / nx};
+  const double ix = 1.0 / nx;
+  V3 xn = {x.x * ix, x.y * ix, x.z * ix};
   // reference order: down (0,0,1), then north (1,0,0), then east (0,1,0)
   V3 z = {-xn.z * xn.x, -xn.z * xn.y, 1.0 - xn.z * xn.z};
   if (nrm(z) < 1e-6) {
     z = {1.0 - xn.x * xn.x, -xn.x * xn.y, -xn.x * xn.z};
     if (nrm(z) < 1e-6) z = {-xn.y * xn.x, 1.0 - xn.y * xn.y, -xn.y * xn.z};
   }
-  double nz = nrm(z);
-  z = {z.x / nz, z.y / nz, z.z / nz};
+  const double iz = 1.0 / nrm(z);
+  z = {z.x * iz, z.y * iz, z.z * iz};
   V3 y = {z.y * xn.z - z.z * xn.y, z.z * xn.x - z.x * xn.z, z.x * xn.y - z.y * xn.x};
-  double ny = nrm(y);
-  y = {y.x / ny, y.y / ny, y.z / ny};
+  const double iy = 1.0 / nrm(y);
+  y = {y.x * iy, y.y * iy, y.z * iy};
   z = {xn.y * y.z - xn.z * y.y, xn.z * y.x - xn.x * y.z, xn.x * y.y - xn.y * y.x};
   R.m[0][0] = xn.x; R.m[0][1] = xn.y; R.m[0][2] = xn.z;
   R.m[1][0] = y.x; R.m[1][1] = y.y; R.m[1][2] = y.z;
@@ -197,7 +231,8 @@ __device__ __forceinline__ V3 unit_or(const V3& v, const V3& fb) {
     n = nrm(fb);
   }
   if (!(n >= 1e-9) || !isfinite(n)) return {1.0, 0.0, 0.0};
-  return {s.x / n, s.y / n, s.z / n};
+  const double in = 1.0 / n;
+  return {s.x * in, s.y * in, s.z * in};
 }
 __device__ __forceinline__ double align3(const V3& a, const V3& b) {
   V3 au = unit_or(a, {1.0, 0.0, 0.0});
@@ -237,8 +272,9 @@ __device__ __forceinline__ double alt_log(double alt_m) {
 }
 __device__ __forceinline__ void log_so3(const M3& R, double inv_dt, double out[3]) {
   double tr = R.m[0][0] + R.m[1][1] + R.m[2][2];
-  double theta = acos(clampd((tr - 1.0) * 0.5, -1.0, 1.0));
-  double den = 2.0 * sin(theta), sc = 0.0;
+  const double c = clampd((tr - 1.0) * 0.5, -1.0, 1.0);
+  double theta = acos(c);
+  double den = 2.0 * sqrt((1.0 - c) * (1.0 + c)), sc = 0.0;     // 2 sin(acos c)
   if (theta >= 1e-8 && fabs(den) >= 1e-8) sc = theta / den;
   out[0] = (R.m[2][1] - R.m[1][2]) * sc * inv_dt;
   out[1] = (R.m[0][2] - R.m[2][0]) * sc * inv_dt;
@@ -316,40 +352,34 @@ struct Lanes {
 };
 
 // Own aircraft: 9-DoF, body matrix and attitude sin/cos, NED velocity, speed, velocity frame.
-// prev: the aircraft's previous attitude (deg) when its attitude history is valid, else NULL;
-// with it the body rates log_SO3(R_prev R^T) / dt of advance_kernel are staged in F_PQR (zero
-// without).  Both body matrices come out of one rolled loop, so the three sincos are inlined
-// once; the previous matrix passes through the F_FL slots, which stage_los fills afterwards.
+// The current body matrix is built from the attitude sin/cos kin9 derives from the matrix
+// elements (no sincos); the previous one (ned2body of the stored degrees, as the reference)
+// only when prev is given: the aircraft's previous attitude when its history is valid, else
+// NULL; with it the body rates log_SO3(R_prev R^T) / dt of advance_kernel are staged in F_PQR
+// (zero without).
 template <int T, typename Row>
 __device__ __forceinline__ void stage_aircraft(const Lanes<T>& L, const Row& row, const Origin& O,
                                                const double* prev = nullptr, double inv_dt = 0.0) {
-  double s[9];
-  kin9(row, O, s);
+  double s[9], att[6];
+  kin9(row, O, s, att);
 #pragma unroll
   for (int j = 0; j < 9; j++) L.own(F_S + j) = s[j];
-  const int passes = prev ? 2 : 1;
-#pragma unroll 1
-  for (int q = 0; q < passes; q++) {
-    double att[6];
-    const M3 R = ned2body(q ? prev[0] : s[3], q ? prev[1] : s[4], q ? prev[2] : s[5], att);
-    L.put_mat(q ? F_FL : F_R, R);
-    if (q == 0) {
 #pragma unroll
-      for (int j = 0; j < 6; j++) L.own(F_ATT + j) = att[j];
-      const V3 vb = {s[6], s[7], s[8]};
-      const V3 vn = mvT(R, vb);
-      L.put_vec(F_VN, vn);
-      L.own(F_SPD) = nrm(vb);
-      L.put_mat(F_FV, dir_frame(vn));
-    }
-  }
+  for (int j = 0; j < 6; j++) L.own(F_ATT + j) = att[j];
+  const M3 R = ned2body_sc(att);
+  L.put_mat(F_R, R);
+  const V3 vb = {s[6], s[7], s[8]};
+  const V3 vn = mvT(R, vb);
+  L.put_vec(F_VN, vn);
+  L.own(F_SPD) = nrm(vb);
+  L.put_mat(F_FV, dir_frame(vn));
   double lg[3] = {0.0, 0.0, 0.0};
   if (prev) {
-    const M3 Np = L.mat(F_FL, L.i & 1), Nc = L.mat(F_R, L.i & 1);
+    const M3 Np = ned2body(prev[0], prev[1], prev[2]);
     M3 rd;
     for (int i = 0; i < 3; i++)
       for (int j = 0; j < 3; j++)
-        rd.m[i][j] = Np.m[i][0] * Nc.m[j][0] + Np.m[i][1] * Nc.m[j][1] + Np.m[i][2] * Nc.m[j][2];
+        rd.m[i][j] = Np.m[i][0] * R.m[j][0] + Np.m[i][1] * R.m[j][1] + Np.m[i][2] * R.m[j][2];
     log_so3(rd, inv_dt, lg);
   }
   L.put_vec(F_PQR, V3{lg[0], lg[1], lg[2]});
