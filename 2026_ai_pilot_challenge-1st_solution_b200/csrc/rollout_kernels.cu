@@ -62,6 +62,49 @@ k_norm_partial(const float* __restrict__ x, int64_t B, int D, int64_t ldx, doubl
   }
 }
 
+// The same partial sums with 16-byte loads, for D % 4 == 0 and a 16-byte aligned, 4-float
+// strided x: thread t sums columns 4c..4c+3 (c = t mod D/4) of the rows r0 + j, r0 + j + S, ...
+// (stripe j = t div D/4, S = PART4_THREADS div D/4 stripes), so two resident blocks per SM keep
+// ~64 KB of loads in flight instead of one 4-byte load per column; the stripes' fp64 sums meet
+// in shared memory and are added in stripe order (deterministic).
+constexpr int PART4_THREADS = 512;
+__global__ void __launch_bounds__(PART4_THREADS)
+k_norm_partial4(const float4* __restrict__ x, int64_t B, int D, int64_t ldx4, double2* __restrict__ partial) {
+  extern __shared__ double2 stripes[];              // [S][D]
+  const int ncg = D >> 2;
+  const int S = PART4_THREADS / ncg;
+  const int cg = threadIdx.x % ncg, st = threadIdx.x / ncg;
+  const int64_t r0 = (int64_t)blockIdx.x * NORM_ROWS_PER_BLOCK;
+  const int64_t r1 = r0 + NORM_ROWS_PER_BLOCK < B ? r0 + NORM_ROWS_PER_BLOCK : B;
+  if (st < S) {
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0, q0 = 0.0, q1 = 0.0, q2 = 0.0, q3 = 0.0;
+#pragma unroll 4
+    for (int64_t r = r0 + st; r < r1; r += S) {
+      const float4 v = x[r * ldx4 + cg];
+      const double a = v.x, b = v.y, c = v.z, d = v.w;
+      s0 += a; q0 += a * a;
+      s1 += b; q1 += b * b;
+      s2 += c; q2 += c * c;
+      s3 += d; q3 += d * d;
+    }
+    double2* o = stripes + (int64_t)st * D + 4 * cg;
+    o[0] = make_double2(s0, q0);
+    o[1] = make_double2(s1, q1);
+    o[2] = make_double2(s2, q2);
+    o[3] = make_double2(s3, q3);
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    double s = 0.0, q = 0.0;
+    for (int i = 0; i < S; i++) {
+      const double2 p = stripes[(int64_t)i * D + d];
+      s += p.x;
+      q += p.y;
+    }
+    partial[(int64_t)blockIdx.x * D + d] = make_double2(s, q);
+  }
+}
+
 // Sum of the partial rows of 32 features per block: warp w adds rows w, w+8, ... (unrolled, so
 // many loads are in flight), then the 8 warp sums are added in warp order.  Both the merge and
 // the cross-rank sums use it, so one rank reproduces f16_norm_update bit for bit.
@@ -312,6 +355,31 @@ extern "C" int f16_gae(const float* rew, const float* val, const float* done, co
   return launch_status();
 }
 
+namespace f16 {
+namespace ro {
+// The partial-sum pass of the norm update: the 16-byte kernel when the layout allows it.
+inline void launch_partial(const float* x, int64_t B, int D, int64_t ldx, double2* part, int64_t nblk,
+                           cudaStream_t s) {
+  const bool vec = (D % 4 == 0) && (ldx % 4 == 0) && aligned(x, 16) && D / 4 <= PART4_THREADS && D >= 4;
+  if (!vec) {
+    k_norm_partial<<<(unsigned)nblk, NORM_THREADS, 0, s>>>(x, B, D, ldx, part);
+    return;
+  }
+  const int S = PART4_THREADS / (D / 4);
+  const size_t smem = (size_t)S * D * sizeof(double2);
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    cudaFuncSetAttribute(k_norm_partial4, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    attr[dev] = true;
+  }
+  k_norm_partial4<<<(unsigned)nblk, PART4_THREADS, smem, s>>>(reinterpret_cast<const float4*>(x), B, D, ldx / 4,
+                                                               part);
+}
+}  // namespace ro
+}  // namespace f16
+
 extern "C" int f16_norm_update(const float* x, int64_t B, int D, int64_t ldx, float* mean, float* var, float* count,
                                double* scratch, int64_t scratch_doubles, f16_stream_t stream) {
   if (!x || !mean || !var || !count || !scratch || B <= 0 || D <= 0 || ldx < D) return F16_ERR_ARG;
@@ -320,7 +388,7 @@ extern "C" int f16_norm_update(const float* x, int64_t B, int D, int64_t ldx, fl
   if (!aligned(scratch, 16)) return F16_ERR_ALIGN;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   double2* part = reinterpret_cast<double2*>(scratch);
-  ro::k_norm_partial<<<nblk, ro::NORM_THREADS, 0, s>>>(x, B, D, ldx, part);
+  ro::launch_partial(x, B, D, ldx, part, nblk, s);
   ro::k_norm_merge<<<(D + 31) / 32, ro::NORM_THREADS, 0, s>>>(part, nblk, B, D,
                                                                                             mean, var, count);
   ro::k_norm_count<<<1, 32, 0, s>>>(count, B);
@@ -335,7 +403,7 @@ extern "C" int f16_norm_sums(const float* x, int64_t B, int D, int64_t ldx, doub
   if (!aligned(scratch, 16) || !aligned(sums, 16)) return F16_ERR_ALIGN;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   double2* part = reinterpret_cast<double2*>(scratch);
-  ro::k_norm_partial<<<nblk, ro::NORM_THREADS, 0, s>>>(x, B, D, ldx, part);
+  ro::launch_partial(x, B, D, ldx, part, nblk, s);
   ro::k_norm_reduce<<<(D + 31) / 32, ro::NORM_THREADS, 0, s>>>(
       part, nblk, D, reinterpret_cast<double2*>(sums));
   return launch_status();
@@ -427,7 +495,7 @@ extern "C" int f16_norm_update_static(const float* x, int64_t B, int D, int64_t 
   int rc = norm_static_scratch(&part);
   if (rc != F16_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  ro::k_norm_partial<<<(unsigned)nblk, ro::NORM_THREADS, 0, s>>>(x, B, D, ldx, part);
+  ro::launch_partial(x, B, D, ldx, part, nblk, s);
   ro::k_norm_merge<<<(D + 31) / 32, ro::NORM_THREADS, 0, s>>>(
       part, (int)nblk, B, D, mean, var, count);
   ro::k_norm_count<<<1, 32, 0, s>>>(count, B);
