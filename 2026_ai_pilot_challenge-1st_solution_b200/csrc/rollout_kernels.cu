@@ -209,6 +209,80 @@ k_norm_apply(const float* __restrict__ x, int64_t B, int D, int64_t ldx, const f
   if (nonfinite && __any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicAdd(nonfinite, 1u);
 }
 
+// The same transform with 16-byte accesses, when D, the row strides and the pointers allow it:
+// thread t handles columns 4c..4c+3 (c = t mod G, G = the written column groups: D/4, or ldb/4
+// with the bf16 padding) of rows r0 + j, r0 + j + S, ... (stripe j = t div G, S = 256 div G);
+// the per-element arithmetic is k_norm_apply's, so the outputs are identical.
+constexpr int APPLY4_ROWS = 64;
+__device__ __forceinline__ float norm_elem(float v, float mu, float den, bool norm, float clip) {
+  if (!norm) return v;
+  float o = __fdiv_rn(__fsub_rn(v, mu), den);
+  return o < -clip ? -clip : (o > clip ? clip : o);
+}
+__global__ void __launch_bounds__(NORM_THREADS)
+k_norm_apply4(const float4* __restrict__ x, int64_t B, int D, int64_t ldx4, const float* __restrict__ mean,
+              const float* __restrict__ var, float eps, float clip, float4* __restrict__ y, int64_t ldy4,
+              uint2* __restrict__ yb, int64_t ldb4, unsigned* __restrict__ nonfinite) {
+  const int dg = D >> 2;
+  const int G = yb ? (int)ldb4 : dg;
+  const int S = NORM_THREADS / G;
+  const int cg = threadIdx.x % G, st = threadIdx.x / G;
+  const int64_t r0 = (int64_t)blockIdx.x * APPLY4_ROWS;
+  const int64_t r1 = r0 + APPLY4_ROWS < B ? r0 + APPLY4_ROWS : B;
+  const bool norm = mean != nullptr;
+  bool bad = false;
+  if (st < S) {
+    if (cg < dg) {
+      float mu[4] = {0.0f, 0.0f, 0.0f, 0.0f}, den[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+      if (norm) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          mu[i] = mean[4 * cg + i];
+          den[i] = __fsqrt_rn(__fadd_rn(var[4 * cg + i], eps));
+        }
+      }
+#pragma unroll 4
+      for (int64_t r = r0 + st; r < r1; r += S) {
+        const float4 v = x[r * ldx4 + cg];
+        float4 o;
+        o.x = norm_elem(v.x, mu[0], den[0], norm, clip);
+        o.y = norm_elem(v.y, mu[1], den[1], norm, clip);
+        o.z = norm_elem(v.z, mu[2], den[2], norm, clip);
+        o.w = norm_elem(v.w, mu[3], den[3], norm, clip);
+        bad |= !isfinite(o.x) || !isfinite(o.y) || !isfinite(o.z) || !isfinite(o.w);
+        if (y) y[r * ldy4 + cg] = o;
+        if (yb) {
+          __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y), hi = __floats2bfloat162_rn(o.z, o.w);
+          uint2 packed;
+          packed.x = *reinterpret_cast<unsigned*>(&lo);
+          packed.y = *reinterpret_cast<unsigned*>(&hi);
+          yb[r * ldb4 + cg] = packed;
+        }
+      }
+    } else {
+      for (int64_t r = r0 + st; r < r1; r += S) yb[r * ldb4 + cg] = make_uint2(0u, 0u);
+    }
+  }
+  if (nonfinite && __any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicAdd(nonfinite, 1u);
+}
+
+// Launch of the normalise / cast: the 16-byte kernel when the layout allows it.
+inline void launch_apply(const float* x, int64_t B, int D, int64_t ldx, const float* mean, const float* var,
+                         float eps, float clip, float* y, int64_t ldy, __nv_bfloat16* yb, int64_t ldb,
+                         unsigned* nonfinite, cudaStream_t s) {
+  const bool vec = D % 4 == 0 && ldx % 4 == 0 && aligned(x, 16) && (!y || (ldy % 4 == 0 && aligned(y, 16))) &&
+                   (!yb || (ldb % 4 == 0 && aligned(yb, 8))) && (yb ? ldb / 4 : D / 4) <= NORM_THREADS;
+  if (!vec) {
+    const unsigned grid = (unsigned)((B + APPLY_ROWS - 1) / APPLY_ROWS);
+    k_norm_apply<<<grid, NORM_THREADS, 0, s>>>(x, B, D, ldx, mean, var, eps, clip, y, ldy, yb, ldb, nonfinite);
+    return;
+  }
+  const unsigned grid = (unsigned)((B + APPLY4_ROWS - 1) / APPLY4_ROWS);
+  k_norm_apply4<<<grid, NORM_THREADS, 0, s>>>(reinterpret_cast<const float4*>(x), B, D, ldx / 4, mean, var, eps,
+                                              clip, reinterpret_cast<float4*>(y), ldy / 4,
+                                              reinterpret_cast<uint2*>(yb), ldb / 4, nonfinite);
+}
+
 // ---------------------------------------------------------------- rollout bookkeeping
 // One thread per environment, the per-step statistics of collect_rollout (ppo_gpu.py:1914-1960)
 // in one pass: rollout reward row, next-done flags, running episode return / length, and the
@@ -430,10 +504,8 @@ extern "C" int f16_norm_apply(const float* x, int64_t B, int D, int64_t ldx, con
                               f16_stream_t stream) {
   if (!x || !mean || !var || B <= 0 || D <= 0 || ldx < D || (!y && !y_bf16)) return F16_ERR_ARG;
   if ((y && ldy < D) || (y_bf16 && ldb < D)) return F16_ERR_ARG;
-  unsigned grid = (unsigned)((B + ro::APPLY_ROWS - 1) / ro::APPLY_ROWS);
-  ro::k_norm_apply<<<grid, ro::NORM_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy, reinterpret_cast<__nv_bfloat16*>(y_bf16), ldb,
-      nullptr);
+  ro::launch_apply(x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy,
+                   reinterpret_cast<__nv_bfloat16*>(y_bf16), ldb, nullptr, reinterpret_cast<cudaStream_t>(stream));
   return launch_status();
 }
 
@@ -442,10 +514,8 @@ extern "C" int f16_norm_apply_checked(const float* x, int64_t B, int D, int64_t 
                                       int64_t ldb, uint32_t* nonfinite, f16_stream_t stream) {
   if (!x || B <= 0 || D <= 0 || ldx < D || (!y && !y_bf16) || (!mean != !var)) return F16_ERR_ARG;
   if ((y && ldy < D) || (y_bf16 && ldb < D)) return F16_ERR_ARG;
-  unsigned grid = (unsigned)((B + ro::APPLY_ROWS - 1) / ro::APPLY_ROWS);
-  ro::k_norm_apply<<<grid, ro::NORM_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy, reinterpret_cast<__nv_bfloat16*>(y_bf16), ldb,
-      nonfinite);
+  ro::launch_apply(x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy,
+                   reinterpret_cast<__nv_bfloat16*>(y_bf16), ldb, nonfinite, reinterpret_cast<cudaStream_t>(stream));
   return launch_status();
 }
 
