@@ -51,11 +51,12 @@ def parse():
     p.add_argument("--tf32", action="store_true", help="ppo workload: TF32 matmuls in the update (below the "
                                                          "reference's fp32; reported in dtype)")
     p.add_argument("--workload", default="fdm",
-                   choices=["fdm", "obs", "rollout", "ppo", "seed", "external", "warmup", "payoff"],
+                   choices=["fdm", "obs", "rollout", "ppo", "mlp", "seed", "external", "warmup", "payoff"],
                    help="fdm = configs[1] headline (default); obs = configs[2] fused obs/reward kernel; "
                         "rollout = configs[3] full 64-step rollout (env + obs/reward + actor/critic/opponents + GAE); "
                         "ppo = configs[4] PPO league iteration (rollout + 4x16 minibatch update, NCCL gradient "
-                        "allreduce across ranks); seed / external / warmup / payoff = the next rows: GPU IC "
+                        "allreduce across ranks); mlp = the rollout's actor+critic launch alone (k_policy, "
+                        "131,072 rows); seed / external / warmup / payoff = the next rows: GPU IC "
                         "seeder, 214-D external observation, device-side staggered warm-up, batched payoff "
                         "evaluation")
     return p.parse_args()
@@ -730,6 +731,71 @@ def run_aux(args, dev, world, rank):
     return 0
 
 
+def run_mlp(args, dev, world, rank):
+    """The rollout's main policy launch alone: actor 184-512-512-84 ReLU with Gumbel-max sampling,
+    log-prob and env commands, and critic 184-512-512-1, on 131,072 bf16 rows (k_policy, one
+    launch per step), with the input rows rewritten between steps so every launch reads them
+    from HBM.  The kernel-level figure behind the rollout's roofline line."""
+    import torch
+    tr = importlib.import_module(PKG + ".trainer")
+    pol = importlib.import_module(PKG + ".policy")
+    ro = importlib.import_module(PKG + ".rollout")
+    torch.manual_seed(0)
+    model = tr.MLPActorCritic(hidden=(512, 512), activation="relu").to(dev)
+    nets = [pol.MlpWeights.from_sequential(model.actor_logits, pol.HEAD_CATEGORICAL, dev),
+            pol.MlpWeights.from_sequential(model.critic, pol.HEAD_VALUE, dev)]
+    ps = pol.PolicySet(nets)
+    n = ROLL_NENV
+    g = torch.Generator(device=dev).manual_seed(3)
+    src = torch.randn(2, n, 192, device=dev, generator=g).to(torch.bfloat16)
+    src[:, :, 184:] = 0
+    x = torch.empty(n, 192, dtype=torch.bfloat16, device=dev)
+    bins = torch.empty(n, 4, dtype=torch.uint8, device=dev)
+    logp = torch.empty(n, device=dev)
+    val = torch.empty(n, device=dev)
+    cmd = torch.empty(n, 8, dtype=torch.float64, device=dev)
+    grid = ro.make_action_grid(21, dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    K, W = max(1, args.steps), max(3, args.warmup)
+
+    def launch(k):
+        ps.forward(x, [(n, [0, 1])], nets_per_group=2, bins=bins, logp=logp, value=val, seed=7, step=k, cmd=cmd,
+                   cmd_stride=8, cmd_offset=0, grid=grid)
+    for k in range(W):
+        x.copy_(src[k % 2])
+        launch(k)
+    torch.cuda.synchronize(dev)
+    es = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    with ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0")))) as clk:
+        for k, (a, b) in enumerate(es):
+            flush.zero_()
+            x.copy_(src[k % 2])
+            a.record(stream)
+            launch(W + k)
+            b.record(stream)
+        torch.cuda.synchronize(dev)
+    ps.check_error()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in es]))
+    peak, peak_src = peak_of("bf16_tflops")
+    achieved = (ACTOR_FLOP + CRITIC_FLOP) * n / (ms * 1e-3) / 1e12
+    if rank == 0:
+        line = {"metric": "actor+critic rows/s (k_policy alone)", "value": world * n / (ms * 1e-3), "unit": "rows/s",
+                "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
+                "config": {"workload": "the rollout's main policy launch: 131,072 rows, actor 184-512-512-84 ReLU "
+                                       "(sampled bins, log-prob, env commands) + critic 184-512-512-1",
+                           "l2": "256 MB flush and a fresh input copy before each timed launch"},
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                             "frac": achieved / peak, "traffic": profile_traffic("mlp_policy_cfg4.md"),
+                             "kernel": "k_policy", "flop_per_unit": ACTOR_FLOP + CRITIC_FLOP, "unit_basis": "row",
+                             "peak_source": peak_src + " (burst: one launch timed alone)"},
+                "gpu_launches": K, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    ps.close()
+    return 0
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     try:
@@ -773,6 +839,8 @@ def main():
         return run_rollout(args, dev, world, rank)
     if args.workload == "ppo":
         return run_ppo(args, dev, world, rank)
+    if args.workload == "mlp":
+        return run_mlp(args, dev, world, rank)
     if args.workload in ("seed", "external", "warmup", "payoff"):
         return run_aux(args, dev, world, rank)
 
