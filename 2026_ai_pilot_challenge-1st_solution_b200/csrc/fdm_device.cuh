@@ -596,8 +596,11 @@ __device__ __forceinline__ void dynamics(const double* __restrict__ S, Ac& s, do
   Seg sb13 = seg_find(S, F16T_GRID_BETA13, F16N_GRID_BETA13, be);
   Seg sb7 = seg_find(S, F16T_GRID_BETA7, F16N_GRID_BETA7, be);
   const double kge = S[F16T_KCLGE_Y + F16N_KCLGE_Y - 1];      // KCLGE(765 ft) is past the table end
+  // the nine Mach tables share one search on the union of their grids (resampled copies,
+  // F16T_MU_*: the same piecewise-linear functions)
+  Seg sm = seg_find(S, F16T_MACHU, F16N_MACHU, mach);
 #define A1(nm) lut1s(S, F16T_##nm, 12, sa)
-#define M1(nm, n) lut1(S, F16T_##nm##_X, F16T_##nm##_Y, n, mach)
+#define M1(nm, n) lut1s(S, F16T_MU_##nm, F16N_MACHU, sm)
   double k = qbar * 300.0;
   double ssum;
   ssum = 0.0;

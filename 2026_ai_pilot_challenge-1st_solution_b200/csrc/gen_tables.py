@@ -71,6 +71,21 @@ ENGINE_2D = [("ENG_IDLE", "T2r_34", "T2c_34", "T2d_34"),
              ("ENG_AUG", "T2r_36", "T2c_36", "T2d_36")]
 ATMOS = [("ATM_ALT", "ATM_ALT"), ("ATM_TMP", "ATM_TMP"), ("ATM_LAPSE", "ATM_LAPSE"),
          ("ATM_PBRK", "ATM_PBRK"), ("ATM_DBRK", "ATM_DBRK")]
+# the nine Mach-indexed aerodynamic tables, also stored resampled on the union of their grids
+MACH_1D = ["CDMACH", "CYB_M", "CLB_M", "CLDA_M", "CLDR_M", "CMA_M", "CNB_M", "CNDA_M", "CNDR_M"]
+
+
+def table1d(x, y, k):
+    """The reference's table1d (end clamps, linear inside) evaluated in double."""
+    if k <= x[0]:
+        return y[0]
+    if k >= x[-1]:
+        return y[-1]
+    r = 1
+    while r < len(x) - 1 and x[r] < k:
+        r += 1
+    f = min((k - x[r - 1]) / (x[r] - x[r - 1]), 1.0)
+    return f * (y[r] - y[r - 1]) + y[r - 1]
 
 
 def build(arrays, scalars):
@@ -113,6 +128,16 @@ def build(arrays, scalars):
         put(name, arrays[d])
     for name, src in ATMOS:
         put(name, arrays[src])
+    # Resampled Mach tables: a piecewise-linear table evaluated at a superset of its breakpoints
+    # and interpolated linearly again is the same function (end clamps included, since every
+    # grid lies inside the union's range), so the nine lookups can share one segment search.
+    srcs = {name: (x, y) for name, x, y in OTHER_1D}
+    union = sorted({v for name in MACH_1D for v in arrays[srcs[name][0]]})
+    put("MACHU", union)
+    for name in MACH_1D:
+        x, y = arrays[srcs[name][0]], arrays[srcs[name][1]]
+        assert x == sorted(x) and x[0] >= union[0] and x[-1] <= union[-1], name
+        put("MU_" + name, [table1d(x, y, u) for u in union])
     used = set(ALPHA_1D_X) | {y for _, y in ALPHA_1D} | {"T1x_2"}
     for _, r, c, d, _ in ALPHA_2D:
         used |= {r, c, d}
