@@ -241,26 +241,24 @@ __device__ __forceinline__ bool near_eq(double a, double b) {
 }
 constexpr int ACT_MAX_PASSES = 16;   // hard bound on actuator passes per FCS step
 
-// two-detent actuator [-d, d] with equal times (aileron/elevator/rudder/lef); rate = 2d/t
+// two-detent actuator [-d, d] with equal times (aileron/elevator/rudder/lef); rate = 2d/t.
+// The reference's pass loop (fdm.cuh:264-290 with two detents) moves at most once: a pass either
+// reaches the target (y = x, after which the loop test finds them equal, or for a NaN target
+// finds the remaining time NaN) or spends all of dt.  So it is one conditional step here,
+// straight-line code the compiler can interleave across the three control channels.
 __device__ __forceinline__ double act2(double& out, double in, double dlo, double dhi, double t, double inv_rate,
                                        double dt, bool seeded, double seed) {
-  double x = in * dhi;
+  const double x = clampd(in * dhi, dlo, dhi);
   double y = seeded ? seed : out;
-  x = clampd(x, dlo, dhi);
-  double rem = dt;
   const double rate = (dhi - dlo) / t;
-  // The reference loop ends after at most two passes for any finite input (each pass either
-  // reaches the target or spends the remaining dt); the cap only bounds non-finite inputs.
-  for (int it = 0; it < ACT_MAX_PASSES && rem > 0.0 && !near_eq(x, y); it++) {
-    if (t <= 0.0) { y = x; break; }
-    double need = fabs((x - y) * inv_rate);
-    if (rem < need) {
-      need = rem;
-      if (y < x) y += need * rate; else y -= need * rate;
-    } else {
+  if (dt > 0.0 && !near_eq(x, y)) {
+    if (t <= 0.0) {
       y = x;
+    } else {
+      const double need = fabs((x - y) * inv_rate);
+      if (dt < need) y = (y < x) ? y + dt * rate : y - dt * rate;
+      else y = x;
     }
-    rem -= need;
   }
   out = y;
   return y;
@@ -403,8 +401,13 @@ __device__ __forceinline__ double turbine(const double* __restrict__ S, double* 
   eng[0] = approach(eng[0], F16C_IDLEN1 + tp * n1f, up, n1dn, dt);
   eng[2] = (eng[1] - F16C_IDLEN2) * (1.0 / n2f);
   Seg rs = seg_find(S, F16T_GRID_DENSALT, 8, densalt);
-  Seg mi = seg_find(S, F16T_ENG_IDLE_MACH, 6, mach);
-  Seg mm = seg_find(S, F16T_ENG_MIL_MACH, 8, mach);
+  // The idle (0..1.0) and military (0..1.4) Mach grids are the first 6 / 8 points of the
+  // afterburner grid (0..2.6, same values): one search on it gives all three segments exactly
+  // (past a shorter grid's end the segment is its last with fraction 1, as table2d clamps).
+  Seg ma = seg_find(S, F16T_ENG_AUG_MACH, 14, mach);
+  Seg mi = ma, mm = ma;
+  if (ma.r > 5) { mi.r = 5; mi.f = 1.0; }
+  if (ma.r > 7) { mm.r = 7; mm.f = 1.0; }
   double idle = F16C_MILTHRUST * lut2s(S, F16T_ENG_IDLE, 8, mi, rs);
   double mil = (F16C_MILTHRUST - idle) * lut2s(S, F16T_ENG_MIL, 8, mm, rs);
   double thrust = idle + mil * eng[2] * eng[2];
@@ -413,7 +416,6 @@ __device__ __forceinline__ double turbine(const double* __restrict__ S, double* 
   eng[3] = approach(eng[3], thrust * tsfc, 1000.0, 10000.0, dt);
   if (eng[3] < F16C_IdleFF) eng[3] = F16C_IdleFF;
   if (aug > 0.0) {
-    Seg ma = seg_find(S, F16T_ENG_AUG_MACH, 14, mach);
     double td = (F16C_MAXTHRUST * lut2s(S, F16T_ENG_AUG, 8, ma, rs)) - thrust;
     thrust += td * aug;
     eng[3] = approach(eng[3], thrust * F16C_ATSFC, 5000.0, 10000.0, dt);
