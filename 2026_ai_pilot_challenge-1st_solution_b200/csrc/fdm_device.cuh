@@ -143,7 +143,7 @@ __device__ __forceinline__ void stage_tables(double* __restrict__ S) {
 
 // ---------------- ISA atmosphere (fdm.cuh:174-224) ----------------
 struct Air {
-  double T, P, rho, a, sigma, densalt;
+  double T, P, rho, ia, sigma, densalt;   // ia: 1 / speed of sound
 };
 __device__ __forceinline__ double geopot(double h) { return (h * F16C_EarthRadius) / (F16C_EarthRadius + h); }
 __device__ __forceinline__ double geomet(double g) { return (g * F16C_EarthRadius) / (F16C_EarthRadius - g); }
@@ -171,7 +171,7 @@ __device__ __forceinline__ void isa(const double* __restrict__ S, double h, Air&
   o.T = T;
   o.P = P;
   o.rho = rho;
-  o.a = sqrt(F16C_SHRatio * F16C_Reng * T);
+  o.ia = rsqrt(F16C_SHRatio * F16C_Reng * T);
   o.sigma = rho * (1.0 / (F16C_StdDaySLpressure / (F16C_Reng * F16C_StdDaySLtemperature)));
   // density altitude (fdm.cuh:195-206)
   int d = 7;
@@ -474,9 +474,9 @@ __device__ __forceinline__ void propagate(Ac& s) {
   #pragma unroll
   for (int i = 0; i < 4; i++) s.q[i] = s.q[i] + dt * s.qdot[i];
   {
-    double m = sqrt(s.q[0] * s.q[0] + s.q[1] * s.q[1] + s.q[2] * s.q[2] + s.q[3] * s.q[3]);
-    if (m != 0.0) {
-      double k = 1.0 / m;
+    const double qq = s.q[0] * s.q[0] + s.q[1] * s.q[1] + s.q[2] * s.q[2] + s.q[3] * s.q[3];
+    if (qq != 0.0) {
+      const double k = rsqrt(qq);                 // 1 / |q|
       s.q[0] *= k; s.q[1] *= k; s.q[2] *= k; s.q[3] *= k;
     }
   }
@@ -503,10 +503,11 @@ __device__ __forceinline__ void dynamics(const double* __restrict__ S, Ac& s, do
                                          double gear_pos, FrameOut& out) {
   // ---- kinematics (fdm.cuh:544-563) in ECI ----
   const double px = s.pos[0], py = s.pos[1], pz = s.pos[2];
-  double rxy2 = px * px + py * py;
-  double rxy = sqrt(rxy2);
-  double rad = sqrt(rxy2 + pz * pz);
-  double irxy = 1.0 / rxy, irad = 1.0 / rad;
+  // reciprocal square roots, the lengths as products (rounding-level differences from
+  // sqrt and a division)
+  double rxy2 = px * px + py * py, rad2 = rxy2 + pz * pz;
+  double irxy = rsqrt(rxy2), irad = rsqrt(rad2);
+  double rxy = rxy2 * irxy, rad = rad2 * irad;
   double slo = py * irxy, clo = px * irxy;     // inertial longitude
   double sla = pz * irad, cla = rxy * irad;    // geocentric latitude
   // Tl2i columns = local N, E, D axes in ECI
@@ -566,15 +567,16 @@ __device__ __forceinline__ void dynamics(const double* __restrict__ S, Ac& s, do
   Surf sf;
   fcs(S, s.kin, s.pid, c_ail, c_ele, c_rud, s.pa, L22, fcs_dt, inv_fcs_dt, gear_pos, sf);
   // air data (fdm.cuh:471-497)
-  double uw = u * u + w * w, vt2 = uw + v * v, vt = sqrt(vt2);
+  double uw = u * u + w * w, vt2 = uw + v * v;
+  const double ivt = vt2 > 0.0 ? rsqrt(vt2) : 0.0, isuw = uw > 0.0 ? rsqrt(uw) : 0.0;
+  const double vt = vt2 * ivt, suw = uw * isuw;
   double al = 0.0, be = 0.0;
-  double suw = sqrt(uw);
   if (vt > 0.001) {
     be = atan2(v, suw);
     if (uw >= 1e-6) al = atan2(w, u);
   }
   double qbar = 0.5 * at.rho * vt2;
-  double mach = vt / at.a;
+  double mach = vt * at.ia;
   double vg = sqrt(vn * vn + ve * ve);
   // pilot-station load factor from the previous frame's accelerations
   double ex = F16C_INCHTOFT * (mp.cgx - -336.2), ez = F16C_INCHTOFT * (mp.cgz - 29.5);   // eye point (y = 0)
@@ -590,8 +592,7 @@ __device__ __forceinline__ void dynamics(const double* __restrict__ S, Ac& s, do
   double burn;
   double thrust = turbine(S, s.eng, 2.0 * c_thr, mach, at.densalt, at.T, at.sigma, burn);
   // aerodynamics: one segment search per shared grid
-  double two = 2.0 * vt;
-  double i2v = (two != 0.0) ? 1.0 / two : 0.0;
+  double i2v = 0.5 * ivt;                       // 1 / (2 vt), 0 at rest
   double b2v = 30.0 * i2v, c2v = 11.32 * i2v;
   Seg sa = seg_find(S, F16T_ALPHA, 12, al);
   Seg se = seg_find(S, F16T_GRID_ELEV, F16N_GRID_ELEV, sf.ele);
@@ -658,8 +659,8 @@ __device__ __forceinline__ void dynamics(const double* __restrict__ S, Ac& s, do
 #undef M1
   // wind -> body (fdm.cuh:592-598); sin/cos of alpha and beta from the body velocity
   double ca, sa_, cb, sb;
-  if (al == 0.0) { ca = 1.0; sa_ = 0.0; } else { double ir = 1.0 / suw; ca = u * ir; sa_ = w * ir; }
-  if (be == 0.0) { cb = 1.0; sb = 0.0; } else { double iv = 1.0 / vt; cb = suw * iv; sb = v * iv; }
+  if (al == 0.0) { ca = 1.0; sa_ = 0.0; } else { ca = u * isuw; sa_ = w * isuw; }
+  if (be == 0.0) { cb = 1.0; sb = 0.0; } else { cb = suw * ivt; sb = v * ivt; }
   double drag = -DR, side = SI, lift = -LI;
   double Fx = ca * cb * drag + (-ca * sb) * side + (-sa_) * lift;
   double Fy = sb * drag + cb * side;

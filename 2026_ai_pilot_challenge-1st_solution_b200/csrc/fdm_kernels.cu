@@ -303,7 +303,7 @@ k_seed_ic(const double* __restrict__ ic, int64_t nac, double* __restrict__ st, i
     // prev_aux from the IC (ic.py:127-132)
     Air at;
     isa(S, alt, at);
-    double mach = vt / at.a;
+    double mach = vt * at.ia;
     s.pa[0] = al; s.pa[1] = mach; s.pa[2] = vcas_kts(mach, at.P); s.pa[3] = vt; s.pa[4] = 0.0;
     s.pa[5] = -1.0; s.pa[6] = 0.0; s.pa[7] = 0.0; s.pa[8] = 0.0;
     double pa_ic[9];
