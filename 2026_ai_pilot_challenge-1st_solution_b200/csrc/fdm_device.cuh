@@ -457,9 +457,30 @@ struct Ac {
   double uvwidot[3], pqridot[3], qdot[4];
   double ivel1[3], ivel2[3];       // integrator history of eci_vel: deq_ivel[0], deq_ivel[1]
   double uvd1[3];                  // integrator history of the ECI acceleration: deq_uvwidot[0]
-  double pbacc[3], ppqridot[3], ppqri[3];
+  double pbacc[3], ppqridot[3], ppqri[3];   // previous-frame accelerations: state fields, set
+                                            // only by the frame whose state is stored
+  double nld[2];                            // pilot load factor (y, z) of the coming frame
   double pa[9], eng[4], kin[6], pid[9];
 };
+
+// Pilot-station load factor (y, z) a frame computes from the previous frame's body
+// accelerations (reference air data, fdm.cuh:471-497), with the eye point of the cg at `fuel`
+// (mass_props' own expressions).  Evaluated when the accelerations are produced, for the frame
+// that uses them, so the nine values need not stay live across the frame boundary.
+__device__ __forceinline__ void load_factor(double fuel, const double* ba, const double* pd, const double* pr,
+                                            double* nld) {
+  const double empty = 17400.0, pw = 230.0;
+  const double f0 = fuel * 0.5;
+  const double iw = 1.0 / (empty + (f0 + f0) + pw);
+  const double cgx = (empty * -193.0 + pw * -336.2 + f0 * -174.4 + f0 * -174.4) * iw;
+  const double cgz = (empty * -5.1 + pw * 0.0 + f0 * 5.0 + f0 * 5.0) * iw;
+  const double ex = F16C_INCHTOFT * (cgx - -336.2), ez = F16C_INCHTOFT * (cgz - 29.5);   // eye point (y = 0)
+  const double c1y = pd[2] * ex - pd[0] * ez, c1z = -pd[1] * ex;
+  const double c2x = pr[1] * ez, c2y = pr[2] * ex - pr[0] * ez, c2z = -pr[1] * ex;
+  const double c3y = pr[2] * c2x - pr[0] * c2z, c3z = pr[0] * c2y - pr[1] * c2x;
+  nld[0] = (ba[1] + c1y + c3y) * (1.0 / F16C_SLGRAVITY);
+  nld[1] = (ba[2] + c1z + c3z) * (1.0 / F16C_SLGRAVITY);
+}
 
 struct FrameOut {
   double euler[3], uvw[3], alpha, beta, mach, vt, alt;
@@ -578,15 +599,8 @@ __device__ __forceinline__ void dynamics(const double* __restrict__ S, Ac& s, do
   double qbar = 0.5 * at.rho * vt2;
   double mach = vt * at.ia;
   double vg = sqrt(vn * vn + ve * ve);
-  // pilot-station load factor from the previous frame's accelerations
-  double ex = F16C_INCHTOFT * (mp.cgx - -336.2), ez = F16C_INCHTOFT * (mp.cgz - 29.5);   // eye point (y = 0)
-  const double* pr = s.ppqri;
-  const double* pd = s.ppqridot;
-  double c1y = pd[2] * ex - pd[0] * ez, c1z = -pd[1] * ex;
-  double c2x = pr[1] * ez, c2y = pr[2] * ex - pr[0] * ez, c2z = -pr[1] * ex;
-  double c3y = pr[2] * c2x - pr[0] * c2z, c3z = pr[0] * c2y - pr[1] * c2x;
-  double npy = (s.pbacc[1] + c1y + c3y) * (1.0 / F16C_SLGRAVITY);
-  double npz = (s.pbacc[2] + c1z + c3z) * (1.0 / F16C_SLGRAVITY);
+  // pilot-station load factor from the previous frame's accelerations (load_factor)
+  const double npy = s.nld[0], npz = s.nld[1];
   double vc = vcas_kts(mach, at.P);
   // engine (thr_pos = 2*cmd, fdm.cuh:586-587)
   double burn;
@@ -693,10 +707,15 @@ __device__ __forceinline__ void dynamics(const double* __restrict__ S, Ac& s, do
   s.uvwidot[1] = T01 * ba0 + T11 * ba1 + T21 * ba2 + gy;
   s.uvwidot[2] = T02 * ba0 + T12 * ba1 + T22 * ba2 + gz;
   s.pqridot[0] = pdd0; s.pqridot[1] = pdd1; s.pqridot[2] = pdd2;
-  s.ppqridot[0] = pdd0; s.ppqridot[1] = pdd1; s.ppqridot[2] = pdd2;
-  s.pbacc[0] = ba0; s.pbacc[1] = ba1; s.pbacc[2] = ba2;
-  s.ppqri[0] = wi0; s.ppqri[1] = wi1; s.ppqri[2] = wi2;
   s.fuel -= burn;
+  {
+    const double ba[3] = {ba0, ba1, ba2}, pdd[3] = {pdd0, pdd1, pdd2}, wi[3] = {wi0, wi1, wi2};
+    load_factor(s.fuel, ba, pdd, wi, s.nld);
+    if (WANT_OUT) {
+#pragma unroll
+      for (int i = 0; i < 3; i++) { s.pbacc[i] = ba[i]; s.ppqridot[i] = pdd[i]; s.ppqri[i] = wi[i]; }
+    }
+  }
   s.pa[0] = al; s.pa[1] = mach; s.pa[2] = vc; s.pa[3] = vg;
   s.pa[4] = npy; s.pa[5] = npz; s.pa[6] = p; s.pa[7] = q; s.pa[8] = r;
   if (WANT_OUT) {

@@ -63,6 +63,7 @@ __device__ __forceinline__ void load_state(const StateRef<LAYOUT>& R, int64_t a,
   }
 #pragma unroll
   for (int i = 0; i < 6; i++) s.kin[i] = R(a, F16_S_KIN + i);
+  load_factor(s.fuel, s.pbacc, s.ppqridot, s.ppqri, s.nld);
 }
 
 // Non-finite test on the exponent bits (all-ones exponent = inf or NaN); `bad` ORs it up.
@@ -313,8 +314,9 @@ k_seed_ic(const double* __restrict__ ic, int64_t nac, double* __restrict__ st, i
     for (int i = 0; i < 9; i++) s.pid[i] = 0.0;
     s.eng[0] = 100.0; s.eng[1] = 100.0; s.eng[2] = (100.0 - F16C_IDLEN2) / (F16C_MAXN2 - F16C_IDLEN2); s.eng[3] = ff;
     for (int i = 0; i < 3; i++) { s.pbacc[i] = 0.0; s.ppqridot[i] = 0.0; s.ppqri[i] = s.pqri[i]; }
+    load_factor(s.fuel, s.pbacc, s.ppqridot, s.ppqri, s.nld);
     FrameOut out;
-    dynamics<false>(S, s, 0.0, 0.0, 0.0, 0.8, fcs_dt, 1.0 / fcs_dt, gear, out);
+    dynamics<true>(S, s, 0.0, 0.0, 0.0, 0.8, fcs_dt, 1.0 / fcs_dt, gear, out);
     // outputs: the derivatives; everything else returns to the fresh / IC values
     s.fuel = fuel;
     for (int i = 0; i < 9; i++) s.pa[i] = pa_ic[i];
