@@ -458,12 +458,15 @@ __device__ __forceinline__ double normz_k(double x, double lo, double hi) {
   return (clampd(x, lo, hi) - (hi + lo) * 0.5) * (2.0 / (hi - lo));
 }
 
+// The last 20 features (the action history, newest first): read from `hist`, zeros (a fresh
+// episode), or already written by the history push.
+enum HistMode : int { HIST_READ = 0, HIST_ZERO = 1, HIST_DONE = 2 };
+
 // This lane's 184 features (obs_kernel.cu:336-482) after stage_aircraft, stage_los and the
-// reconstruction fields are staged on both lanes.  hist: the aircraft's 20 action-history
-// values (newest first) or NULL for zeros; aux: the 21 future-position features or NULL.
+// reconstruction fields are staged on both lanes; aux: the 21 future-position features or NULL.
 template <int T>
-__device__ __forceinline__ void obs_row(const Lanes<T>& L, int k, const Los& g, double t, const double* hist,
-                                       float* __restrict__ out, double* __restrict__ aux) {
+__device__ __forceinline__ void obs_row(const Lanes<T>& L, int k, const Los& g, double t, int hist_mode,
+                                       const double* hist, float* __restrict__ out, double* __restrict__ aux) {
   const int o = k, p = 1 - k;
   const M3 Ro = L.mat(F_R, o);
   const V3 ovn = L.vec(F_VN, o), tvn = L.vec(F_VN, p);
@@ -631,9 +634,9 @@ __device__ __forceinline__ void obs_row(const Lanes<T>& L, int k, const Los& g, 
     for (int j = 0; j < 3; j++) out4[q + j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
   wr.n = 164;
-  if (hist) {
+  if (hist_mode == HIST_READ) {
     for (int j = 0; j < 20; j++) wr.put(hist[j]);
-  } else {
+  } else if (hist_mode == HIST_ZERO) {
     for (int j = 0; j < 20; j++) wr.put(0.0);
   }
 }

@@ -65,19 +65,31 @@ __device__ __forceinline__ Los stage_pair(const Lanes<PT>& L, const double* st, 
   return g;
 }
 
-// action-history push of one aircraft (roll by one, newest first): hist[0..19] <- (a, hist[0..15])
-__device__ __forceinline__ void push_hist(double* h, const double* __restrict__ act) {
+// action-history push of one aircraft (roll by one, newest first): hist[0..19] <- (a, hist[0..15]).
+// The new history is also the last 20 features of the aircraft's observation row (columns
+// 164-183, stored as the reference's STORE does): written here into each row given (rows may
+// be NULL), while the values are in registers, instead of being read back for the row.
+__device__ __forceinline__ void push_hist(double* h, const double* __restrict__ act, float* row_a, float* row_b) {
   const double2* h2 = reinterpret_cast<const double2*>(h);
-  double2 o[8];
+  double2 o[10];
 #pragma unroll
-  for (int i = 0; i < 8; i++) o[i] = h2[i];
+  for (int i = 0; i < 8; i++) o[2 + i] = h2[i];
   const double2* a2 = reinterpret_cast<const double2*>(act);
-  const double2 x = a2[0], y = a2[1];
+  o[0] = a2[0];
+  o[1] = a2[1];
   double2* w = reinterpret_cast<double2*>(h);
-  w[0] = x;
-  w[1] = y;
 #pragma unroll
-  for (int i = 0; i < 8; i++) w[2 + i] = o[i];
+  for (int i = 0; i < 10; i++) w[i] = o[i];
+  float* rows[2] = {row_a, row_b};
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    if (!rows[r]) continue;
+    float4* d = reinterpret_cast<float4*>(rows[r] + 164);
+#pragma unroll
+    for (int i = 0; i < 5; i++)
+      d[i] = make_float4(store_val(o[2 * i].x), store_val(o[2 * i].y), store_val(o[2 * i + 1].x),
+                         store_val(o[2 * i + 1].y));
+  }
 }
 
 // Reconstruction values of a fresh episode staged for the observation row.
@@ -106,11 +118,12 @@ template <int T>
 __device__ __forceinline__ Advanced advance_lane(const Lanes<T>& L, const PairLane& pl, const Los& g,
                                                  const f16_recon& rc, const f16_reward_cfg& cfg,
                                                  const double* __restrict__ actions, double* __restrict__ reward,
-                                                 uint8_t* __restrict__ term, uint8_t* __restrict__ trunc_) {
+                                                 uint8_t* __restrict__ term, uint8_t* __restrict__ trunc_,
+                                                 float* hist_row_a = nullptr, float* hist_row_b = nullptr) {
   const int64_t a = pl.a, e = pl.e;
   const int k = pl.k;
   const double dt = cfg.dt;
-  push_hist(rc.act_hist + a * 20, actions + a * 4);
+  push_hist(rc.act_hist + a * 20, actions + a * 4, hist_row_a, hist_row_b);
   const double r_ft = g.dist * M2FT;
   const double t_old = rc.t_sec[e];
   const double ata = L.own(F_ATA), ata_p = L.par(F_ATA);
@@ -188,7 +201,8 @@ __global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_obs_build(const
   L.own(F_HP) = rc.hp[a]; L.own(F_FUEL) = rc.fuel[a]; L.own(F_DEALT) = rc.dmg_dealt[a]; L.own(F_TAKEN) = rc.dmg_taken[a];
   L.own(F_PQR) = rc.pqr[a * 3]; L.own(F_PQR + 1) = rc.pqr[a * 3 + 1]; L.own(F_PQR + 2) = rc.pqr[a * 3 + 2];
   L.sync();
-  obs_row(L, pl.k, g, rc.t_sec[pl.e], rc.act_hist + a * 20, obs + a * 184, (aux && pl.k == 0) ? aux + pl.e * 21 : nullptr);
+  obs_row(L, pl.k, g, rc.t_sec[pl.e], HIST_READ, rc.act_hist + a * 20, obs + a * 184,
+          (aux && pl.k == 0) ? aux + pl.e * 21 : nullptr);
 }
 
 template <int LAYOUT>
@@ -226,10 +240,9 @@ __global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_obs_step(const 
   if (!pair_lane(nenv, pl)) return;
   const Lanes<PT> L = lanes_of(sm);
   const Los g = stage_pair<LAYOUT>(L, st, ld, pl.a, pl.k, origin_of(og), prev_attitude(rc, pl.a), inv_dt_of(cfg));
-  const Advanced A = advance_lane(L, pl, g, rc, cfg, actions, reward, term, trunc_);
+  const Advanced A = advance_lane(L, pl, g, rc, cfg, actions, reward, term, trunc_, obs + pl.a * 184);
   L.sync();
-  obs_row(L, pl.k, g, A.t, rc.act_hist + pl.a * 20, obs + pl.a * 184,
-          (aux && pl.k == 0) ? aux + pl.e * 21 : nullptr);
+  obs_row(L, pl.k, g, A.t, HIST_DONE, nullptr, obs + pl.a * 184, (aux && pl.k == 0) ? aux + pl.e * 21 : nullptr);
 }
 
 template <int LAYOUT>
@@ -278,7 +291,8 @@ __global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_env_post(double
   const Origin O = origin_of(og);
   const int64_t a = pl.a, e = pl.e;
   Los g = stage_pair<LAYOUT>(L, st, ld, a, pl.k, O, prev_attitude(rc, a), inv_dt_of(cfg));
-  const Advanced A = advance_lane(L, pl, g, rc, cfg, actions, reward, term, trunc_);
+  const Advanced A = advance_lane(L, pl, g, rc, cfg, actions, reward, term, trunc_, obs + a * 184,
+                                  terminal_obs ? terminal_obs + a * 184 : nullptr);
   const bool fin = A.te || A.tr;
   if (pl.k == 0) done[e] = fin;
   terminal_hp[a] = A.hp;
@@ -289,9 +303,9 @@ __global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_env_post(double
   }
   L.sync();
   double* ax = (aux && pl.k == 0) ? aux + e * 21 : nullptr;
-  if (terminal_obs) obs_row(L, pl.k, g, A.t, rc.act_hist + a * 20, terminal_obs + a * 184, nullptr);
+  if (terminal_obs) obs_row(L, pl.k, g, A.t, HIST_DONE, nullptr, terminal_obs + a * 184, nullptr);
   if (!fin) {
-    obs_row(L, pl.k, g, A.t, rc.act_hist + a * 20, obs + a * 184, ax);
+    obs_row(L, pl.k, g, A.t, HIST_DONE, nullptr, obs + a * 184, ax);
     return;
   }
   // autoreset: this aircraft's row from the pool, fresh reconstruction state, anchored trackers
@@ -319,7 +333,7 @@ __global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_env_post(double
   rc.prev_alt_log[a] = alt_log(-L.own(F_S + 2));
   stage_fresh(L);
   L.sync();
-  obs_row(L, pl.k, g, 0.0, nullptr, obs + a * 184, ax);
+  obs_row(L, pl.k, g, 0.0, HIST_ZERO, nullptr, obs + a * 184, ax);
 }
 
 // 9-DoF export (R/cuda_fdm/rl_env.py:558-566 state9_flat): one thread per aircraft
