@@ -35,8 +35,12 @@ constexpr int NCHUNK = 256;                      // output columns per MMA / wei
 constexpr int STAGES = 3;
 constexpr int ACT_BYTES = 128 * 1024;            // 8 chunks x (128 rows x 128 B)
 constexpr int STAGE_BYTES = NCHUNK * 128;        // 32 KB
+// Four epilogue warps per quarter (18 warps, 96 registers): with the split hidden layers each
+// thread holds two packed chunks of the first half; measured 0.326 ms for the rollout's actor +
+// critic launch against 0.335 ms for two warps without the split and 0.367 ms for two warps
+// with it (register spills).
 #ifndef F16_MLP_EPI_PER_QUARTER
-#define F16_MLP_EPI_PER_QUARTER 2
+#define F16_MLP_EPI_PER_QUARTER 4
 #endif
 constexpr int EPI_PER_Q = F16_MLP_EPI_PER_QUARTER;   // epilogue warps per TMEM lane quarter (2 or 4)
 constexpr int CTRL_BYTES = 2048;                 // barriers, TMEM base, head partial log-probs
@@ -192,6 +196,14 @@ struct Job {
   int rows;
   int net;
 };
+// A hidden layer two weight boxes wide (512 outputs): the MMA issuer signals its first 256
+// accumulator columns (acc_h0) before issuing the second half, and the epilogue converts that
+// half into registers while the second half's MMAs run; it stores them once the layer's MMAs
+// are done reading the activations they replace (acc_full).
+__device__ __forceinline__ bool split_layer(const NetParams& P, int l) {
+  return l < P.n_layers - 1 && P.width_pad[l] == 2 * NCHUNK;
+}
+
 __device__ __forceinline__ bool decode_job(const Launch& L, int64_t j, Job& J) {
   int64_t tile = j / L.nets_per_group;
   int slot = (int)(j % L.nets_per_group);
@@ -237,6 +249,7 @@ __device__ __forceinline__ float gumbel(uint64_t key, uint32_t idx) {
 
 struct Smem {
   uint64_t x_full, act_empty, acc_full, act_ready, tmem_empty, drain, logp_bar;
+  uint64_t acc_h0;                               // a 512-wide hidden layer's first 256 columns done
   uint64_t full[STAGES], empty[STAGES];
   uint32_t tmem_base;
   int abort_flag;
@@ -272,6 +285,43 @@ __device__ __forceinline__ uint32_t pack_bf16x2(uint64_t v, bool relu) {
 // row's 128-byte swizzled line of the next layer's A operand: all bias loads first (one exposed
 // latency per chunk), the bias added two lanes per instruction, one activation branch per chunk,
 // ReLU fused into the conversion
+// bias + activation of one 32-column chunk packed as the four 16-byte bf16 units it stores
+__device__ __forceinline__ void pack32(const uint32_t (&r)[32], const float* __restrict__ bias, int c0, bool relu,
+                                       uint4 (&w)[4]) {
+  const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(bias + c0);
+  ulonglong2 bv[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) bv[i] = __ldg(b2 + i);
+  uint64_t x[16];
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    x[2 * i] = add_f32x2(((uint64_t)r[4 * i + 1] << 32) | r[4 * i], bv[i].x);
+    x[2 * i + 1] = add_f32x2(((uint64_t)r[4 * i + 3] << 32) | r[4 * i + 2], bv[i].y);
+  }
+  if (!relu) {
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const float lo = tanh_fast(__uint_as_float((uint32_t)x[i]));
+      const float hi = tanh_fast(__uint_as_float((uint32_t)(x[i] >> 32)));
+      x[i] = ((uint64_t)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 4; u++) {
+    w[u].x = pack_bf16x2(x[4 * u + 0], relu);
+    w[u].y = pack_bf16x2(x[4 * u + 1], relu);
+    w[u].z = pack_bf16x2(x[4 * u + 2], relu);
+    w[u].w = pack_bf16x2(x[4 * u + 3], relu);
+  }
+}
+// the packed chunk into the swizzled A region of the next layer (row m, columns c0..c0+31)
+__device__ __forceinline__ void store32(const uint4 (&w)[4], uint8_t* rowbase, int c0, int m) {
+  uint8_t* rowp = rowbase + (c0 / KCHUNK) * TILE_M * 128;
+  const int unit0 = (c0 % KCHUNK) / 8;
+#pragma unroll
+  for (int u = 0; u < 4; u++) *reinterpret_cast<uint4*>(rowp + (((unit0 + u) ^ (m & 7)) * 16)) = w[u];
+}
+
 __device__ __forceinline__ void convert32(const uint32_t (&r)[32], const float* __restrict__ bias, int c0,
                                           uint8_t* rowbase, int m, bool relu) {
   const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(bias + c0);
@@ -421,6 +471,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
     mbar_init(smem_u32(&S->x_full), 1);
     mbar_init(smem_u32(&S->act_empty), 1);
     mbar_init(smem_u32(&S->acc_full), 1);
+    mbar_init(smem_u32(&S->acc_h0), 1);
     mbar_init(smem_u32(&S->act_ready), 32 * EPI_WARPS);
     mbar_init(smem_u32(&S->tmem_empty), 32 * EPI_WARPS);
     mbar_init(smem_u32(&S->logp_bar), TILE_M * (EPI_PER_Q - 1));
@@ -497,6 +548,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           tc_fence_after();
           int K = (l == 0) ? P.in_pad : P.width_pad[l - 1];
           int N = P.width_pad[l];
+          const bool split = split_layer(P, l);
           for (int n0 = 0; n0 < N && ok; n0 += NCHUNK) {
             int nc = (N - n0) < NCHUNK ? (N - n0) : NCHUNK;
             uint32_t idesc = idesc_bf16(nc);
@@ -513,6 +565,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
                        (k0 > 0 || kk > 0) ? 1u : 0u);
               tc_commit(smem_u32(&S->empty[s]));
             }
+            if (split && n0 == 0) tc_commit(smem_u32(&S->acc_h0));
           }
           tc_commit(smem_u32(&S->acc_full));
         }
@@ -535,7 +588,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
     const int h = (warp - 2) >> 2;
     const int m = q * 32 + lane;                  // tile row of this thread
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    uint32_t accs = 0, heads = 0;
+    uint32_t accs = 0, heads = 0, h0s = 0;
     int64_t jn = 0;
     for (int64_t j = blockIdx.x; j < njobs; j += gridDim.x) {
       Job J;
@@ -543,10 +596,13 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
       const NetParams& P = nets[J.net];
       bool ok = true;
       for (int l = 0; l < P.n_layers; l++) {
-        bool got = mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
+        const bool split = split_layer(P, l);
+        bool got = split ? mbar_wait(smem_u32(&S->acc_h0), h0s & 1, abort_flag)
+                         : mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
         __syncwarp();                               // reconverge before the .sync.aligned TMEM loads
         if (!got || *abort_flag) { ok = false; break; }
-        accs++;
+        if (split) h0s++;
+        else accs++;
         tc_fence_after();
         const float* bias = P.bias[l];
         const bool last = (l == P.n_layers - 1);
@@ -557,9 +613,33 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           const bool relu = P.act == 0;
           uint8_t* rowbase = act + (m >> 3) * 1024 + (m & 7) * 128;
           constexpr int STEP = 32 * EPI_PER_Q;           // this warp's chunks: c, c + STEP, ...
+          int cstart = 32 * h;
+          if (split) {
+            // first half: packed into registers (one chunk loaded at a time: the held half
+            // takes the registers a second load buffer would)
+            constexpr int NH = NCHUNK / STEP;
+            uint4 held[NH][4];
+#pragma unroll
+            for (int i = 0; i < NH; i++) {
+              const int c = cstart + i * STEP;
+              uint32_t ra[32];
+              tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
+              tmem_wait_ld();
+              pack32(ra, bias, c, relu, held[i]);
+            }
+            // the layer's second-half MMAs are done with the activations being replaced
+            bool got2 = mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
+            __syncwarp();
+            if (!got2 || *abort_flag) { ok = false; break; }
+            accs++;
+            tc_fence_after();
+#pragma unroll
+            for (int i = 0; i < NH; i++) store32(held[i], rowbase, cstart + i * STEP, m);
+            cstart += NCHUNK;
+          }
           if (EPI_PER_Q >= 4) {
             // enough warps per scheduler to hide the TMEM load latency: one chunk at a time
-            for (int c = 32 * h; c < N; c += STEP) {
+            for (int c = cstart; c < N; c += STEP) {
               uint32_t ra[32];
               tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
               tmem_wait_ld();
@@ -568,7 +648,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           } else {
             // the next chunk's TMEM load in flight while this one is converted
             uint32_t ra[32], rb[32];
-            int c = 32 * h;
+            int c = cstart;
             if (c < N) {
               tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
               tmem_wait_ld();
