@@ -36,7 +36,8 @@ constexpr int ATM_EXPD = ATM_KISO + 8;           // -1/(1+g0*Mair/(Rstar*L_b))  
 constexpr int ATM_KDISO = ATM_EXPD + 8;          // -(Rstar*T_b)/(g0*Mair)        (8)
 constexpr int ATM_TOL = ATM_KDISO + 8;           // T_b / L_b                      (8)
 constexpr int ATM_RDB = ATM_TOL + 8;             // 1/rho_b                        (9)
-constexpr int SMEM_DOUBLES = ATM_RDB + 9;
+constexpr int ATM_LTB = ATM_RDB + 9;             // log(T_b)                       (8)
+constexpr int SMEM_DOUBLES = ATM_LTB + 8;
 
 __device__ const double g_tab[F16_TAB_LEN] = {F16_TAB_VALUES};
 
@@ -135,6 +136,7 @@ __device__ __forceinline__ void stage_tables(double* __restrict__ S) {
       double Tt = S[F16T_ATM_TMP + b];
       S[ATM_KDISO + b] = -(F16C_Rstar * Tt) / gm;
       S[ATM_TOL + b] = (L != 0.0) ? Tt / L : 0.0;
+      S[ATM_LTB + b] = log(Tb);
     }
     for (int b = 0; b < 9; b++) S[ATM_RDB + b] = 1.0 / S[F16T_ATM_DBRK + b];
   }
@@ -162,16 +164,17 @@ __device__ __forceinline__ void isa(const double* __restrict__ S, double h, Air&
   double L = S[F16T_ATM_LAPSE + b];
   double P;
   if (L != 0.0) {
-    double fac = Tb / (Tb + L * dh);
-    P = S[F16T_ATM_PBRK + b] * exp(S[ATM_EXPP + b] * log(fac));
+    // (Tb / (Tb + L dh))^e as exp(e (log Tb - log(Tb + L dh))), log Tb staged per layer
+    P = S[F16T_ATM_PBRK + b] * exp(S[ATM_EXPP + b] * (S[ATM_LTB + b] - log(Tb + L * dh)));
   } else {
     P = S[F16T_ATM_PBRK + b] * exp(dh * S[ATM_KISO + b]);
   }
-  double rho = P / (F16C_Reng * T);
+  const double ia = rsqrt(F16C_SHRatio * F16C_Reng * T);
+  double rho = P * (F16C_SHRatio * ia * ia);          // P / (R T), with 1 / (R T) = gamma ia^2
   o.T = T;
   o.P = P;
   o.rho = rho;
-  o.ia = rsqrt(F16C_SHRatio * F16C_Reng * T);
+  o.ia = ia;
   o.sigma = rho * (1.0 / (F16C_StdDaySLpressure / (F16C_Reng * F16C_StdDaySLtemperature)));
   // density altitude (fdm.cuh:195-206)
   int d = 7;
@@ -230,7 +233,7 @@ __device__ __forceinline__ void mass_props(double fuel, Mass& o) {
   o.k6 = (Ixx * Iyy) * den;
   o.Ixx = Ixx; o.Iyy = Iyy; o.Izz = Izz; o.Ixz = Ixz;
   o.mass = ls * w;
-  o.inv_mass = 1.0 / o.mass;
+  o.inv_mass = iw * (1.0 / ls);
   o.rpx = F16C_INCHTOFT * (o.cgx - -189.5);
   o.rpz = F16C_INCHTOFT * (o.cgz - 3.9);
 }
