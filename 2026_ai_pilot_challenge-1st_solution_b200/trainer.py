@@ -30,6 +30,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib
+from . import splitmm
 from .policy import HEAD_CATEGORICAL, HEAD_VALUE, MlpWeights, PolicySet
 from .rollout import RunningNorm, cast_bf16, gae, make_action_grid
 
@@ -83,11 +84,23 @@ class MLPActorCritic(nn.Module):
     def critic_parameters(self):
         return list(self.critic.parameters())
 
+    # set by the PPO update on CUDA: linear layers through splitmm (fp32-accurate products on the
+    # bf16 tensor cores) instead of SGEMM; the modules and their parameters are the same
+    split_products = False
+
+    def _run(self, seq, x):
+        if not self.split_products:
+            return seq(x)
+        for m in seq:
+            x = splitmm.linear(m, x) if isinstance(m, nn.Linear) else m(x)
+        return x
+
     def _dist(self, obs):
-        return torch.distributions.Categorical(logits=self.actor_logits(obs).view(-1, self.act_dim, self.num_bins))
+        return torch.distributions.Categorical(logits=self._run(self.actor_logits, obs).view(-1, self.act_dim,
+                                                                                              self.num_bins))
 
     def get_value(self, obs):
-        return self.critic(obs).squeeze(-1)
+        return self._run(self.critic, obs).squeeze(-1)
 
     def evaluate_actions(self, obs, action):
         """(summed log-prob, summed entropy) of category indices under the current actor."""
@@ -159,7 +172,8 @@ def _allreduce_mean_(tensors, group, world):
         off += n
 
 
-def ppo_update(model, actor_opt, critic_opt, cfg, obs, act, old_logp, b_val, adv, ret, group=None, generator=None):
+def ppo_update(model, actor_opt, critic_opt, cfg, obs, act, old_logp, b_val, adv, ret, group=None, generator=None,
+               split_products=None):
     """Clipped PPO over one rollout (ppo_gpu.py:2020-2144, ``aux_pred`` off).
 
     obs (T, n, 184) fp32, act (T, n, 4) indices (any integer dtype), old_logp / b_val / adv / ret
@@ -169,6 +183,19 @@ def ppo_update(model, actor_opt, critic_opt, cfg, obs, act, old_logp, b_val, adv
     of the ranks' minibatches, so all ranks take identical optimiser steps and the update equals
     a single-rank update whose minibatch is the concatenation of the ranks' minibatches.
     """
+    world = _world(group)
+    dev = obs.device
+    # fp32-accurate split products on the tensor cores for the CUDA update (splitmm); the CPU
+    # path (and split_products=False) multiplies in plain fp32
+    prev_split = model.split_products
+    model.split_products = (dev.type == "cuda") if split_products is None else bool(split_products)
+    try:
+        return _ppo_update(model, actor_opt, critic_opt, cfg, obs, act, old_logp, b_val, adv, ret, group, generator)
+    finally:
+        model.split_products = prev_split
+
+
+def _ppo_update(model, actor_opt, critic_opt, cfg, obs, act, old_logp, b_val, adv, ret, group, generator):
     world = _world(group)
     dev = obs.device
     obs_f = obs.flatten(0, 1)
@@ -491,9 +518,14 @@ class PPOTrainer:
         return out
 
     # ---- update (ppo_gpu.py:2020-2144) ----
+    # None: fp32-accurate split products on CUDA (splitmm); False: plain fp32 matmuls (then TF32
+    # when torch.backends.cuda.matmul.allow_tf32 is set)
+    split_products = None
+
     def update(self, adv, ret, generator=None):
         res = ppo_update(self.model, self.actor_opt, self.critic_opt, self.cfg, self.b_obs, self.b_act, self.b_logp,
-                         self.b_val, adv, ret, group=self.group, generator=generator)
+                         self.b_val, adv, ret, group=self.group, generator=generator,
+                         split_products=self.split_products)
         self.refresh_policy()
         return res
 

@@ -528,7 +528,8 @@ def run_ppo(args, dev, world, rank):
     (clip 0.2) with gradients, advantage statistics and approx-KL all-reduced over NCCL, so all
     ranks apply identical optimiser steps (weak scaling: 131,072 envs per GPU).  The update runs
     in torch at the reference's precision: fp32 matmuls (PyTorch's default, which the reference
-    keeps); --tf32 opts into TF32 matmuls and says so in the line's dtype."""
+    keeps), computed as fp32-accurate split products on the bf16 tensor cores (splitmm);
+    --tf32 opts into TF32 SGEMM instead and says so in the line's dtype."""
     import torch
     import torch.distributed as dist
     torch.backends.cuda.matmul.allow_tf32 = bool(args.tf32)
@@ -547,6 +548,7 @@ def run_ppo(args, dev, world, rank):
     t = tr.PPOTrainer(env, cfg, model=tr.MLPActorCritic(hidden=(512, 512), activation="relu"), opponents=opps,
                       opp_mode="blocks", group=pg)
     t.reset(stagger=False)
+    t.split_products = False if args.tf32 else None
     stream = torch.cuda.current_stream(dev)
     K, W = args.steps, max(3, args.warmup)
     for _ in range(W):
@@ -601,7 +603,9 @@ def run_ppo(args, dev, world, rank):
         nparams = sum(p.numel() for p in t.model.parameters())
         line = {"metric": "decision-steps/s over full PPO iterations (rollout + update)", "value": value,
                 "unit": "decision-steps/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_it,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64+bf16 (update " + ("tf32" if args.tf32 else "fp32") + ")",
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64+bf16 (update " + ("tf32" if args.tf32 else
+                                                 "fp32-level: bf16x3-split products, fp32 accumulate, "
+                                                 "within 4x of SGEMM error") + ")",
                 "data": "synthetic ICs, random-init networks",
                 "config": {"workload": "configs[4]: PPO league iteration, 131,072 envs per GPU, T=64, 4 epochs x 16 "
                                        "minibatches, clip 0.2, 16 frozen opponents, NCCL gradient allreduce",

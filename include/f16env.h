@@ -409,6 +409,15 @@ typedef struct {
 } f16_payoff_args;
 int f16_payoff_record(int64_t nenv, const f16_payoff_args* args, f16_stream_t stream);
 
+/* Three-term bf16 split of fp32 rows for the PPO update's fp32-accurate tensor-core products
+ * (no counterpart kernel in the reference, whose update multiplies in fp32 with cuBLAS):
+ * for each element v of x [rows][cols] (row stride ldx), hi = bf16(v), lo = bf16(v - hi),
+ * mid = bf16(v - hi - lo) (round to nearest; the differences are exact in fp32), written as
+ * out[r][0..cols) = hi, out[r][cols..2 cols) = lo, out[r][2 cols..3 cols) = mid (row stride
+ * ldo >= 3 cols), so hi + lo + mid carries the value's 24 significant bits. */
+int f16_split3_bf16(const float* x, int64_t rows, int cols, int64_t ldx, void* out, int64_t ldo,
+                    f16_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------
  * Diagnostics (no counterpart in the reference): FP64 FMA-pipe probe, the measured roofline
  * denominator of the FDM kernel.  Launches `blocks` x 256 threads running 8 independent FMA
