@@ -97,6 +97,8 @@ _SIGS = {
     "f16_rollout_record": ([_I64, C.POINTER(RecordArgs), _P], C.c_int),
     "f16_payoff_record": ([_I64, C.POINTER(PayoffArgs), _P], C.c_int),
     "f16_split3_bf16": ([_P, _I64, C.c_int, _I64, _P, _I64, _P], C.c_int),
+    "f16_bias_act_split": ([_P, _I64, C.c_int, _I64, _P, C.c_int, _P, _I64, _P], C.c_int),
+    "f16_act_grad_split": ([_P, _I64, _P, _I64, _I64, C.c_int, C.c_int, _P, _I64, _P, C.c_int, _P], C.c_int),
     "f16_seed_ic": ([_P, _I64, _P, C.c_int, _I64, C.c_double, _P], C.c_int),
     "f16_probe_fp64": ([_P, _I64, C.c_int, C.POINTER(C.c_double), _P], C.c_int),
     "f16_version": ([], C.c_char_p),

@@ -415,44 +415,6 @@ extern "C" int f16_payoff_record(int64_t nenv, const f16_payoff_args* a, f16_str
   return launch_status();
 }
 
-namespace f16 {
-namespace ro {
-// One thread per 4 consecutive elements of a row (16-byte load; 8-byte stores of each term).
-__global__ void __launch_bounds__(256) k_split3(const float* __restrict__ x, int64_t rows, int cols, int64_t ldx,
-                                                __nv_bfloat16* __restrict__ out, int64_t ldo) {
-  const int g = cols >> 2;
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= rows * g) return;
-  const int64_t r = i / g;
-  const int c = (int)(i % g) * 4;
-  const float4 v = *reinterpret_cast<const float4*>(x + r * ldx + c);
-  const float a[4] = {v.x, v.y, v.z, v.w};
-  __nv_bfloat16 hi[4], lo[4], mi[4];
-#pragma unroll
-  for (int k = 0; k < 4; k++) {
-    hi[k] = __float2bfloat16_rn(a[k]);
-    const float r1 = __fsub_rn(a[k], __bfloat162float(hi[k]));
-    lo[k] = __float2bfloat16_rn(r1);
-    mi[k] = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(lo[k])));
-  }
-  __nv_bfloat16* o = out + r * ldo + c;
-  *reinterpret_cast<uint2*>(o) = *reinterpret_cast<const uint2*>(hi);
-  *reinterpret_cast<uint2*>(o + cols) = *reinterpret_cast<const uint2*>(lo);
-  *reinterpret_cast<uint2*>(o + 2 * cols) = *reinterpret_cast<const uint2*>(mi);
-}
-}  // namespace ro
-}  // namespace f16
-
-extern "C" int f16_split3_bf16(const float* x, int64_t rows, int cols, int64_t ldx, void* out, int64_t ldo,
-                               f16_stream_t stream) {
-  if (!x || !out || rows <= 0 || cols <= 0 || cols % 4 || ldx < cols || ldo < 3 * (int64_t)cols) return F16_ERR_ARG;
-  if (!aligned(x, 16) || ldx % 4 || !aligned(out, 8) || ldo % 4) return F16_ERR_ALIGN;
-  const int64_t n = rows * (cols / 4);
-  ro::k_split3<<<(unsigned)((n + 255) / 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, rows, cols, ldx, reinterpret_cast<__nv_bfloat16*>(out), ldo);
-  return launch_status();
-}
-
 extern "C" int f16_gae(const float* rew, const float* val, const float* done, const float* last_val,
                        const float* next_done, int T, int64_t n, int64_t ld, double gamma, double lam, float* adv,
                        float* ret, f16_stream_t stream) {

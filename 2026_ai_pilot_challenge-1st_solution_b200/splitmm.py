@@ -3,19 +3,30 @@
 The reference's update (R/cuda_fdm/ppo_gpu.py:2020-2144) multiplies in fp32 (PyTorch's default
 matmul precision, which it keeps), so on a B200 its linear layers run as cuBLAS SGEMM on the
 CUDA cores.  Here every fp32 operand v is split into three bf16 terms, hi = bf16(v),
-lo = bf16(v - hi), mid = bf16(v - hi - lo) (``f16_split3_bf16``; hi + lo + mid carries v's 24
-significant bits), and a product A B is assembled from the six term products whose order of
-magnitude reaches fp32's unit roundoff -- hi*hi, hi*lo, lo*hi, hi*mid, lo*lo, mid*hi; the three
-dropped ones are below 2^-24 relative -- each a bf16 tensor-core GEMM with fp32 accumulation
-(``torch.mm(..., out_dtype=torch.float32)``).  Terms that share an operand run as one GEMM over
-concatenated K (x's terms are stored side by side: [hi | lo | mid]), so a forward product is
-three GEMM calls.  Against fp64 the results stay within 4x of an fp32 SGEMM's error on the
-same operands (about 1e-6 relative; TF32 is near 1e-3), at tensor-core speed.
+lo = bf16(v - hi), mid = bf16(v - hi - lo) (hi + lo + mid carries v's 24 significant bits),
+stored as a row of three parts [mid | lo | hi], and a product A B is assembled from the six term
+products whose order of magnitude reaches fp32's unit roundoff -- hi*hi, hi*lo, lo*hi, hi*mid,
+lo*lo, mid*hi; the three dropped ones are below 2^-24 relative -- each a bf16 tensor-core GEMM
+with fp32 accumulation (``torch.mm(..., out_dtype=torch.float32)``).  Terms that share an
+operand run as one GEMM over concatenated K, so a product is three GEMM calls.
 
-``SplitLinear.apply(x, weight, bias)`` is a drop-in for ``F.linear`` with its own backward
-(dx = g W, dW = g^T x, db = sum g, all in the same split arithmetic).
+Accuracy depends on the order: the tensor cores' fp32 accumulation loses more per addition than
+an SGEMM's round-to-nearest FMA chain, so the number of additions made at the full magnitude of
+the result is kept small.  The five small terms accumulate first (at 2^-8 of the result's
+magnitude, where their rounding is negligible), and hi*hi comes last as a GEMM of its own whose
+result joins them in cuBLAS's fp32 epilogue (beta = 1, in place).  A weight gradient reduces
+over all rows of a minibatch, so its hi*hi product is a batched GEMM over ``ROW_CHUNK``-row
+slices whose partial products are summed in fp32.  Against fp64 the products stay within a few
+times an SGEMM's error on the same operands (about 1e-6 relative; TF32 is near 1e-3).
+
+``run_tower(seq, x)`` runs a Linear/activation ``nn.Sequential`` as ``SplitBlock`` autograd
+functions: per layer the products, then one kernel for bias + activation that also writes the
+split the next layer reads (``f16_bias_act_split``); backward one kernel for the activation
+derivative, the split of the gradient and the bias-gradient partial sums
+(``f16_act_grad_split``), then the input- and weight-gradient products.
 """
 import torch
+import torch.nn as nn
 import torch.nn.functional as F
 
 from . import _lib
@@ -23,91 +34,196 @@ from . import _lib
 _BF = torch.bfloat16
 _F32 = torch.float32
 
+ACT_NONE, ACT_RELU, ACT_TANH = 0, 1, 2
+_ACT_CODES = {nn.ReLU: ACT_RELU, nn.Tanh: ACT_TANH}
+ROW_CHUNK = 1024            # rows per tensor-core reduction of a weight gradient's hi*hi term
+GRAD_BLOCKS = 148 * 8       # blocks (bias-gradient partial rows) of f16_act_grad_split
+MAX_COLS = 1024             # widest layer output f16_act_grad_split takes
 
-def split3(x):
-    """(rows, cols) fp32 -> (rows, 3 cols) bf16 [hi | lo | mid]."""
-    if x.dim() != 2:
-        raise ValueError("split3 takes a 2-D tensor")
+
+def part_width(cols):
+    """Column count of one split part: `cols` rounded up to 8 (16 bytes of bf16)."""
+    return (cols + 7) & ~7
+
+
+def _fp32_operand(x):
     if x.stride(1) != 1 or x.stride(0) % 4 or x.data_ptr() % 16:
         x = x.contiguous()
+    return x
+
+
+def split3(x):
+    """(rows, cols) fp32 -> (rows, 3 p) bf16 [mid | lo | hi], p = part_width(cols), pad columns
+    zero (cols must be a multiple of 4)."""
+    if x.dim() != 2:
+        raise ValueError("split3 takes a 2-D tensor")
+    x = _fp32_operand(x)
     rows, cols = x.shape
-    out = torch.empty(rows, 3 * cols, dtype=_BF, device=x.device)
-    L = _lib.load()
-    _lib.check(L.f16_split3_bf16(x.data_ptr(), rows, cols, x.stride(0), out.data_ptr(), 3 * cols,
-                                 _lib.stream_of(x)), "f16_split3_bf16")
+    p = part_width(cols)
+    out = torch.empty(rows, 3 * p, dtype=_BF, device=x.device)
+    _lib.check(_lib.load().f16_split3_bf16(x.data_ptr(), rows, cols, x.stride(0), out.data_ptr(), 3 * p,
+                                           _lib.stream_of(x)), "f16_split3_bf16")
     return out
 
 
+def bias_act_split(y, bias, act, want_split):
+    """y := act(y + bias) in place (y a fresh fp32 product); returns the split of the result when
+    `want_split`, else None."""
+    rows, cols = y.shape
+    hs = torch.empty(rows, 3 * part_width(cols), dtype=_BF, device=y.device) if want_split else None
+    bias = bias.detach().contiguous()
+    _lib.check(_lib.load().f16_bias_act_split(y.data_ptr(), rows, cols, y.stride(0), bias.data_ptr(), act,
+                                              hs.data_ptr() if hs is not None else None,
+                                              hs.stride(0) if hs is not None else 0, _lib.stream_of(y)),
+               "f16_bias_act_split")
+    return hs
+
+
+def act_grad_split(gh, h, act):
+    """(split of g_y, bias gradient) for g_y = act'(gh; h)."""
+    gh = _fp32_operand(gh)
+    rows, cols = gh.shape
+    nblk = max(1, min(GRAD_BLOCKS, (rows + 63) // 64))
+    gys = torch.empty(rows, 3 * part_width(cols), dtype=_BF, device=gh.device)
+    part = torch.empty(nblk, cols, dtype=_F32, device=gh.device)
+    _lib.check(_lib.load().f16_act_grad_split(gh.data_ptr(), gh.stride(0), h.data_ptr(), h.stride(0), rows, cols, act,
+                                              gys.data_ptr(), gys.stride(0), part.data_ptr(), nblk,
+                                              _lib.stream_of(gh)), "f16_act_grad_split")
+    return gys, part.sum(0)
+
+
 def _mm(a, b, acc=None):
+    """a b in fp32 (bf16 operands, fp32 accumulation); with `acc`, added into it in place."""
     if acc is None:
         return torch.mm(a, b, out_dtype=_F32)
-    return torch.addmm(acc, a, b, out_dtype=_F32)
+    return torch.addmm(acc, a, b, out_dtype=_F32, out=acc)
+
+
+def _parts(s, p):
+    """(mid, lo, hi) views of a split."""
+    return s[:, :p], s[:, p:2 * p], s[:, 2 * p:3 * p]
 
 
 def matmul_nt(xs, ws, k):
-    """x W^T from the splits xs = [xh | xl | xm] (M x 3k) and ws = [wh | wl | wm] (N x 3k)."""
-    wh, wl, wm = ws[:, :k], ws[:, k:2 * k], ws[:, 2 * k:]
-    y = _mm(xs, torch.cat([wh, wh, wh], 1).t())                   # xh wh + xl wh + xm wh
-    y = _mm(xs[:, :2 * k], torch.cat([wl, wl], 1).t(), y)         # + xh wl + xl wl
-    return _mm(xs[:, :k], wm.t(), y)                              # + xh wm
+    """x W^T from the splits xs (M x 3k) and ws (N x 3k); k a multiple of 8."""
+    wm, wl, wh = _parts(ws, k)
+    y = _mm(xs, torch.cat([wh, wh, wm], 1).t())                   # xm wh + xl wh + xh wm
+    y = _mm(xs[:, k:], torch.cat([wl, wl], 1).t(), y)             # + xl wl + xh wl
+    return _mm(xs[:, 2 * k:], wh.t(), y)                          # + xh wh
 
 
 def matmul_nn(gs, ws, n, k):
-    """g W from gs = [gh | gl | gm] (M x 3n) and ws (W = n x k as [wh | wl | wm], n x 3k)."""
-    wh, wl, wm = ws[:, :k], ws[:, k:2 * k], ws[:, 2 * k:]
-    y = _mm(gs, torch.cat([wh, wh, wh], 0))                       # gh wh + gl wh + gm wh
-    y = _mm(gs[:, :2 * n], torch.cat([wl, wl], 0), y)             # + gh wl + gl wl
-    return _mm(gs[:, :n], wm, y)                                  # + gh wm
+    """g W from gs (M x 3p, p = part_width(n)) and ws (W = n x k, split n x 3k); W's terms get
+    p - n zero rows against g's zero pad columns."""
+    p = part_width(n)
+    wm, wl, wh = _parts(ws, k)
+    if p != n:
+        pad = ws.new_zeros(p - n, k)
+        wm, wl, wh = (torch.cat([t, pad], 0) for t in (wm, wl, wh))
+    y = _mm(gs, torch.cat([wh, wh, wm], 0))                       # gm wh + gl wh + gh wm
+    y = _mm(gs[:, p:], torch.cat([wl, wl], 0), y)                 # + gl wl + gh wl
+    return _mm(gs[:, 2 * p:], wh, y)                              # + gh wh
+
+
+def _tn_chunked(a, b):
+    """a^T b over M rows (a: M x p, b: M x k views) as ROW_CHUNK-row tensor-core products whose
+    (p x k) partials are summed in fp32."""
+    m = a.shape[0]
+    c = m // ROW_CHUNK
+    if c < 2:
+        return _mm(a.t(), b)
+    m0 = c * ROW_CHUNK
+    out = torch.bmm(a[:m0].unflatten(0, (c, ROW_CHUNK)).transpose(1, 2), b[:m0].unflatten(0, (c, ROW_CHUNK)),
+                    out_dtype=_F32).sum(0)
+    if m0 < m:
+        out += _mm(a[m0:].t(), b[m0:])
+    return out
 
 
 def matmul_tn(gs, xs, n, k):
-    """g^T x (n x k) from gs = [gh | gl | gm] (M x 3n) and xs = [xh | xl | xm] (M x 3k)."""
-    gh, gl, gm = gs[:, :n], gs[:, n:2 * n], gs[:, 2 * n:]
-    t1 = _mm(gh.t(), xs)                                          # [gh xh | gh xl | gh xm]
-    t2 = _mm(gl.t(), xs[:, :2 * k])                               # [gl xh | gl xl]
-    t3 = _mm(gm.t(), xs[:, :k])                                   # gm xh
-    return ((t3 + t2[:, k:]) + (t1[:, 2 * k:] + t2[:, :k])) + (t1[:, k:2 * k] + t1[:, :k])
+    """g^T x (n x k) from gs (M x 3p, p = part_width(n)) and xs (M x 3k)."""
+    gm, gl, gh = _parts(gs, part_width(n))
+    xh = xs[:, 2 * k:]
+    a = _mm(gh.t(), xs[:, :2 * k])                                # [gh xm | gh xl]
+    b = _mm(gl.t(), xs[:, k:])                                    # [gl xl | gl xh]
+    c = _mm(gm.t(), xh)                                           # gm xh
+    small = ((c + b[:, :k]) + a[:, :k]) + (a[:, k:] + b[:, k:])
+    return (_tn_chunked(gh, xh) + small)[:n]
 
 
-class SplitLinear(torch.autograd.Function):
-    """F.linear(x, weight, bias) with fp32-accurate tensor-core products (module docstring)."""
+class SplitBlock(torch.autograd.Function):
+    """h = act(x W^T + b) with fp32-accurate tensor-core products (module docstring).
 
-    @staticmethod
-    def forward(ctx, x, weight, bias):
-        k = x.shape[1]
-        ws = split3(weight.detach())
-        y = matmul_nt(split3(x.detach()), ws, k)
-        if bias is not None:
-            y = y + bias
-        ctx.save_for_backward(x, weight)
-        ctx.has_bias = bias is not None
-        return y
+    Inputs: x (fp32, for the autograd graph), xs = split3(x) (the operand actually read), the
+    layer's weight and bias, the activation code and whether to return the split of h.
+    Returns (h, hs); hs is empty when not requested and never carries a gradient."""
 
     @staticmethod
-    def backward(ctx, g):
-        x, weight = ctx.saved_tensors
+    def forward(ctx, x, xs, weight, bias, act, want_split):
+        ctx.set_materialize_grads(False)
+        k = weight.shape[1]
+        y = matmul_nt(xs, split3(weight.detach()), k)
+        hs = bias_act_split(y, bias, act, want_split)
+        if hs is None:
+            hs = y.new_empty(0, dtype=_BF)
+        ctx.mark_non_differentiable(hs)
+        ctx.act = act
+        ctx.save_for_backward(xs, weight, y)          # y now holds h
+        return y, hs
+
+    @staticmethod
+    def backward(ctx, gh, _ghs):
+        if gh is None:
+            return None, None, None, None, None, None
+        xs, weight, h = ctx.saved_tensors
         n, k = weight.shape
-        g = g.contiguous()
-        gs = split3(g)
-        gx = gw = gb = None
-        if ctx.needs_input_grad[0]:
-            gx = matmul_nn(gs, split3(weight), n, k)
-        if ctx.needs_input_grad[1]:
-            gw = matmul_tn(gs, split3(x), n, k)
-        if ctx.has_bias and ctx.needs_input_grad[2]:
-            gb = g.sum(0)
-        return gx, gw, gb
+        gys, gb = act_grad_split(gh, h, ctx.act)
+        gx = matmul_nn(gys, split3(weight.detach()), n, k) if ctx.needs_input_grad[0] else None
+        gw = matmul_tn(gys, xs, n, k) if ctx.needs_input_grad[2] else None
+        return gx, None, gw, (gb if ctx.needs_input_grad[3] else None), None, None
+
+
+def _dims_ok(layer):
+    return (layer.in_features % 8 == 0 and layer.out_features % 4 == 0 and layer.in_features >= 64
+            and 64 <= layer.out_features <= MAX_COLS)
 
 
 def usable(layer, x):
-    """Whether a linear layer's product can take the split path (CUDA fp32, dims in 16-byte
-    units and wide enough to be worth it); other layers stay plain fp32."""
-    return (x.is_cuda and x.dtype == _F32 and x.dim() == 2 and layer.in_features % 8 == 0
-            and layer.out_features % 8 == 0 and layer.in_features >= 64 and layer.out_features >= 64)
+    """Whether a linear layer's product can take the split path (CUDA fp32 input, input width in
+    16-byte units, output width a multiple of 4 -- padded to 8 inside -- and both wide enough to
+    be worth it); other layers stay plain fp32."""
+    return x.is_cuda and x.dtype == _F32 and x.dim() == 2 and _dims_ok(layer)
 
 
-def linear(layer, x):
-    """layer(x) for an nn.Linear, through SplitLinear when `usable`."""
-    if usable(layer, x):
-        return SplitLinear.apply(x, layer.weight, layer.bias)
-    return F.linear(x, layer.weight, layer.bias)
+def split_linear(x, weight, bias, act=ACT_NONE):
+    """act(F.linear(x, weight, bias)) through one SplitBlock."""
+    return SplitBlock.apply(x, split3(x.detach()), weight, bias, act, False)[0]
+
+
+def run_tower(seq, x):
+    """seq(x) for a Sequential of Linear and ReLU/Tanh modules: each Linear (+ the activation
+    that follows it) the split path takes runs as a SplitBlock, the others as plain fp32 torch."""
+    mods = list(seq)
+    xs = None
+    i = 0
+    while i < len(mods):
+        m = mods[i]
+        if not isinstance(m, nn.Linear):
+            x, xs = m(x), None
+            i += 1
+            continue
+        act_mod = mods[i + 1] if i + 1 < len(mods) and not isinstance(mods[i + 1], nn.Linear) else None
+        code = ACT_NONE if act_mod is None else _ACT_CODES.get(type(act_mod))
+        if code is None or not usable(m, x):
+            x, xs = F.linear(x, m.weight, m.bias), None
+            i += 1
+            continue
+        if xs is None:
+            xs = split3(x.detach())
+        step = 1 if act_mod is None else 2
+        nxt = mods[i + step] if i + step < len(mods) else None
+        want = isinstance(nxt, nn.Linear) and _dims_ok(nxt)
+        x, hs = SplitBlock.apply(x, xs, m.weight, m.bias, code, want)
+        xs = hs if want else None
+        i += step
+    return x

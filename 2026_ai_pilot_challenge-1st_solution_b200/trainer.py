@@ -91,9 +91,7 @@ class MLPActorCritic(nn.Module):
     def _run(self, seq, x):
         if not self.split_products:
             return seq(x)
-        for m in seq:
-            x = splitmm.linear(m, x) if isinstance(m, nn.Linear) else m(x)
-        return x
+        return splitmm.run_tower(seq, x)
 
     def _dist(self, obs):
         return torch.distributions.Categorical(logits=self._run(self.actor_logits, obs).view(-1, self.act_dim,

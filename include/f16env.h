@@ -409,14 +409,36 @@ typedef struct {
 } f16_payoff_args;
 int f16_payoff_record(int64_t nenv, const f16_payoff_args* args, f16_stream_t stream);
 
-/* Three-term bf16 split of fp32 rows for the PPO update's fp32-accurate tensor-core products
- * (no counterpart kernel in the reference, whose update multiplies in fp32 with cuBLAS):
- * for each element v of x [rows][cols] (row stride ldx), hi = bf16(v), lo = bf16(v - hi),
- * mid = bf16(v - hi - lo) (round to nearest; the differences are exact in fp32), written as
- * out[r][0..cols) = hi, out[r][cols..2 cols) = lo, out[r][2 cols..3 cols) = mid (row stride
- * ldo >= 3 cols), so hi + lo + mid carries the value's 24 significant bits. */
+/* ------------------------------------------------------------------------------------------
+ * PPO update: fp32-accurate products on the bf16 tensor cores (no counterpart kernels in the
+ * reference, whose update R/cuda_fdm/ppo_gpu.py:2020-2144 multiplies in fp32 with cuBLAS
+ * SGEMM).  An fp32 value v is carried as three bf16 terms, hi = bf16(v), lo = bf16(v - hi),
+ * mid = bf16(v - hi - lo) (round to nearest; both differences are exact in fp32), so
+ * mid + lo + hi carries v's 24 significant bits.  A split row of `cols` values is three parts of
+ * p = cols rounded up to 8 columns, [mid | lo | hi] (out[r][0..p) = mid, [p..2p) = lo,
+ * [2p..3p) = hi), each part's columns cols..p zero, so every part starts 16-byte aligned.  cols
+ * is a multiple of 4 everywhere; fp32 pointers are 16-byte aligned with row strides a multiple
+ * of 4 elements, split pointers 8-byte aligned with row strides >= 3p and a multiple of 4. */
+#define F16_ACT_NONE 0
+#define F16_ACT_RELU 1   /* torch.relu: clamp_min(v, 0); backward threshold_backward(g, h, 0) */
+#define F16_ACT_TANH 2   /* torch.tanh; backward g (1 - h h) */
+
+/* Split of x [rows][cols] (row stride ldx) into out (row stride ldo). */
 int f16_split3_bf16(const float* x, int64_t rows, int cols, int64_t ldx, void* out, int64_t ldo,
                     f16_stream_t stream);
+
+/* A layer's epilogue (the bias add of torch's F.linear and the activation module that follows
+ * it, R/claude_code/model.py:34-44): y [rows][cols] := act(y + bias) in place; if hs is
+ * non-null also its split (row stride ldhs), the next layer's operand. */
+int f16_bias_act_split(float* y, int64_t rows, int cols, int64_t ldy, const float* bias, int act,
+                       void* hs, int64_t ldhs, f16_stream_t stream);
+
+/* A layer's backward prologue: g_y = act'(g_h; h) (h = the layer's activated output, unread for
+ * F16_ACT_NONE), written as its split gys (row stride ldgs), and col_part [nblk][cols]: block b's
+ * column sums of g_y over rows [b rpb, (b + 1) rpb), rpb = ceil(rows / nblk), summed in a fixed
+ * order (the bias gradient is the sum of the nblk rows).  cols <= 1024. */
+int f16_act_grad_split(const float* gh, int64_t ldg, const float* h, int64_t ldh, int64_t rows, int cols,
+                       int act, void* gys, int64_t ldgs, float* col_part, int nblk, f16_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------
  * Diagnostics (no counterpart in the reference): FP64 FMA-pipe probe, the measured roofline

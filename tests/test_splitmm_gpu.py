@@ -1,11 +1,18 @@
 """fp32-accurate split products (splitmm) on a B200.
 
-* f16_split3_bf16: hi + lo + mid reproduces every fp32 input to within 2^-24 relative.
-* SplitLinear forward, input gradient and weight gradient against fp64 references: errors no
-  larger than 4x those of fp32 SGEMM on the same operands (and below 5e-6 of the largest
-  output; TF32 products are near 1e-3), for the update's layer shapes (184 -> 512, 512 -> 512)
-  with 65,536 rows -- the weight gradient's reduction over the rows accumulates in the tensor
-  cores' fp32 adders, measured at 2-3.5x SGEMM's error.
+* f16_split3_bf16: the parts are [mid | lo | hi] with hi = bf16(v), and mid + lo + hi reproduces
+  every fp32 input to within 2^-24 relative; a width that is not a multiple of 8 gets zero pad
+  columns in each part.
+* f16_bias_act_split: act(y + b) equal to torch's F.linear bias add followed by nn.ReLU /
+  nn.Identity (bit for bit, NaN kept by relu) or nn.Tanh (within 1 ulp), and its split.
+* f16_act_grad_split: torch's threshold_backward / tanh_backward / identity, its split, and the
+  bias gradient (the column sums) against fp64 sums.
+* A SplitBlock product (forward, input gradient, weight gradient) against fp64 references: errors
+  no larger than 4x those of fp32 SGEMM on the same operands and below 5e-6 of the largest
+  output (TF32 products are near 1e-3), for the update's layer shapes (184 -> 512, 512 -> 512,
+  512 -> 84 with zero-padded parts) with 65,536 rows.
+* A whole actor tower through run_tower against the same tower in fp64: output and every
+  parameter gradient within 1e-5 relative.
 * A PPO update on the GPU with split products and one with plain fp32 matmuls give the same
   statistics within 1e-4 and parameters within 1e-5 relative.
 """
@@ -21,16 +28,85 @@ def rel(a, ref):
     return float((a.double() - ref).abs().max() / ref.abs().max())
 
 
+def recon(s, cols):
+    p = (cols + 7) & ~7
+    return s[:, :cols].double() + s[:, p:p + cols].double() + s[:, 2 * p:2 * p + cols].double()
+
+
 def test_split3_reconstructs(cuda):
     sm = pkg_module("splitmm")
     g = torch.Generator(device=cuda).manual_seed(1)
     x = torch.randn(1000, 184, device=cuda, generator=g) * torch.exp(torch.randn(1000, 184, device=cuda, generator=g) * 5)
     s = sm.split3(x)
-    back = s[:, :184].double() + s[:, 184:368].double() + s[:, 368:].double()
+    assert torch.equal(s[:, 368:], x.bfloat16())
+    back = recon(s, 184)
     assert float(((back - x.double()).abs() / x.double().abs().clamp_min(1e-30)).max()) <= 2.0 ** -24
 
 
-@pytest.mark.parametrize("k,n", [(184, 512), (512, 512)])
+def test_split3_pads_parts(cuda):
+    sm = pkg_module("splitmm")
+    g = torch.Generator(device=cuda).manual_seed(2)
+    x = torch.randn(333, 84, device=cuda, generator=g)
+    s = sm.split3(x)
+    assert s.shape == (333, 264)
+    for j in range(3):
+        assert bool((s[:, 88 * j + 84:88 * (j + 1)] == 0).all())
+    back = recon(s, 84)
+    assert float(((back - x.double()).abs() / x.double().abs().clamp_min(1e-30)).max()) <= 2.0 ** -24
+
+
+@pytest.mark.parametrize("act", ["none", "relu", "tanh"])
+def test_bias_act_split(cuda, act):
+    sm = pkg_module("splitmm")
+    code = {"none": sm.ACT_NONE, "relu": sm.ACT_RELU, "tanh": sm.ACT_TANH}[act]
+    g = torch.Generator(device=cuda).manual_seed(3)
+    rows, cols = 4099, 84
+    y = torch.randn(rows, cols, device=cuda, generator=g) * 3
+    y[5, 7] = float("nan")
+    b = torch.randn(cols, device=cuda, generator=g)
+    pre = y + b
+    ref = {"none": pre, "relu": torch.relu(pre), "tanh": torch.tanh(pre)}[act]
+    yk = y.clone()
+    hs = sm.bias_act_split(yk, b, code, True)
+    assert bool(torch.isnan(yk[5, 7]))
+    fin = torch.isfinite(ref)
+    if act == "tanh":
+        ulp = (yk[fin].view(torch.int32) - ref[fin].view(torch.int32)).abs().max()
+        assert int(ulp) <= 1
+    else:
+        assert torch.equal(yk[fin], ref[fin])
+    back = recon(hs, cols)
+    keep = torch.isfinite(back)
+    assert bool(keep.sum() == fin.sum())
+    assert float(((back - yk.double())[keep].abs() / yk.double()[keep].abs().clamp_min(1e-30)).max()) <= 2.0 ** -24
+    assert sm.bias_act_split(y.clone(), b, code, False) is None
+
+
+@pytest.mark.parametrize("act", ["none", "relu", "tanh"])
+def test_act_grad_split(cuda, act):
+    sm = pkg_module("splitmm")
+    code = {"none": sm.ACT_NONE, "relu": sm.ACT_RELU, "tanh": sm.ACT_TANH}[act]
+    g = torch.Generator(device=cuda).manual_seed(4)
+    rows, cols = 70001, 512
+    gh = torch.randn(rows, cols, device=cuda, generator=g)
+    pre = torch.randn(rows, cols, device=cuda, generator=g)
+    h = {"none": pre, "relu": torch.relu(pre), "tanh": torch.tanh(pre)}[act]
+    if act == "relu":
+        ref = torch.ops.aten.threshold_backward(gh, h, 0.0)
+    elif act == "tanh":
+        ref = torch.ops.aten.tanh_backward(gh, h)
+    else:
+        ref = gh
+    gys, gb = sm.act_grad_split(gh, h, code)
+    back = recon(gys, cols)
+    err = (back - ref.double()).abs() / ref.double().abs().clamp_min(1e-30)
+    assert float(err.max()) <= 2.0 ** -24
+    want = ref.double().sum(0)
+    scale = ref.double().abs().sum(0)
+    assert float(((gb.double() - want).abs() / scale).max()) <= 1e-6
+
+
+@pytest.mark.parametrize("k,n", [(184, 512), (512, 512), (512, 84)])
 def test_split_linear_matches_fp64(cuda, k, n):
     sm = pkg_module("splitmm")
     torch.backends.cuda.matmul.allow_tf32 = False
@@ -40,7 +116,7 @@ def test_split_linear_matches_fp64(cuda, k, n):
     w = (torch.randn(n, k, device=cuda, generator=g) / k ** 0.5).requires_grad_(True)
     b = torch.randn(n, device=cuda, generator=g).requires_grad_(True)
     gy = torch.randn(m, n, device=cuda, generator=g)
-    y = sm.SplitLinear.apply(x, w, b)
+    y = sm.split_linear(x, w, b)
     y.backward(gy)
     xd, wd, gd = x.detach().double(), w.detach().double(), gy.double()
     ry = xd @ wd.t() + b.detach().double()
@@ -50,6 +126,28 @@ def test_split_linear_matches_fp64(cuda, k, n):
     for got, ref, base in ((y.detach(), ry, y32), (x.grad, rgx, gx32), (w.grad, rgw, gw32)):
         e, e32 = rel(got, ref), rel(base, ref)
         assert e <= max(4.0 * e32, 1e-7) and e <= 5e-6, (e, e32)
+    assert rel(b.grad, gd.sum(0)) <= 1e-6
+
+
+@pytest.mark.parametrize("activation", ["relu", "tanh"])
+def test_tower_matches_fp64(cuda, activation):
+    sm = pkg_module("splitmm")
+    tr = pkg_module("trainer")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(5)
+    net = tr.mlp(184, (512, 512), 84, activation).to(cuda)
+    ref_net = tr.mlp(184, (512, 512), 84, activation).double().to(cuda)
+    ref_net.load_state_dict({k: v.double() for k, v in net.state_dict().items()})
+    g = torch.Generator(device=cuda).manual_seed(6)
+    x = torch.randn(20000, 184, device=cuda, generator=g)
+    gout = torch.randn(20000, 84, device=cuda, generator=g)
+    out = sm.run_tower(net, x)
+    out.backward(gout)
+    ref = ref_net(x.double())
+    ref.backward(gout.double())
+    assert rel(out.detach(), ref.detach()) <= 1e-5
+    for p, q in zip(net.parameters(), ref_net.parameters()):
+        assert rel(p.grad, q.grad) <= 1e-5
 
 
 def test_ppo_update_split_vs_fp32(cuda):
