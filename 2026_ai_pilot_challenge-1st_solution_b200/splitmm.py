@@ -23,7 +23,10 @@ times an SGEMM's error on the same operands (about 1e-6 relative; TF32 is near 1
 functions: per layer the products, then one kernel for bias + activation that also writes the
 split the next layer reads (``f16_bias_act_split``); backward one kernel for the activation
 derivative, the split of the gradient and the bias-gradient partial sums
-(``f16_act_grad_split``), then the input- and weight-gradient products.
+(``f16_act_grad_split``), then the input- and weight-gradient products.  A last hidden layer
+followed by a width-1 Linear (the critic's value head) runs as ``SplitValueBlock``: the head's
+dot product joins the epilogue kernel (``f16_bias_act_value``) and its backward the prologue
+kernel (``f16_act_grad_split_value``).
 """
 import torch
 import torch.nn as nn
@@ -90,6 +93,30 @@ def act_grad_split(gh, h, act):
                                               gys.data_ptr(), gys.stride(0), part.data_ptr(), nblk,
                                               _lib.stream_of(gh)), "f16_act_grad_split")
     return gys, part.sum(0)
+
+
+def bias_act_value(y, bias, act, wv, bv):
+    """y := act(y + bias) in place; returns v = y wv + bv (M,) (wv, bv device tensors)."""
+    rows, cols = y.shape
+    v = torch.empty(rows, dtype=_F32, device=y.device)
+    _lib.check(_lib.load().f16_bias_act_value(y.data_ptr(), rows, cols, y.stride(0), bias.detach().contiguous().data_ptr(),
+                                              act, wv.data_ptr(), bv.data_ptr(), v.data_ptr(), _lib.stream_of(y)),
+               "f16_bias_act_value")
+    return v
+
+
+def act_grad_split_value(gv, wv, h, act):
+    """(split of g_y, bias gradient, value-weight gradient) for g_y = act'(gv wv^T; h)."""
+    rows, cols = h.shape
+    nblk = max(1, min(GRAD_BLOCKS, (rows + 63) // 64))
+    gys = torch.empty(rows, 3 * part_width(cols), dtype=_BF, device=h.device)
+    part = torch.empty(nblk, cols, dtype=_F32, device=h.device)
+    vpart = torch.empty(nblk, cols, dtype=_F32, device=h.device)
+    _lib.check(_lib.load().f16_act_grad_split_value(gv.data_ptr(), wv.data_ptr(), h.data_ptr(), h.stride(0), rows,
+                                                    cols, act, gys.data_ptr(), gys.stride(0), part.data_ptr(),
+                                                    vpart.data_ptr(), nblk, _lib.stream_of(h)),
+               "f16_act_grad_split_value")
+    return gys, part.sum(0), vpart.sum(0)
 
 
 def _mm(a, b, acc=None):
@@ -161,8 +188,16 @@ class SplitBlock(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, xs, weight, bias, act, want_split):
         ctx.set_materialize_grads(False)
-        k = weight.shape[1]
-        y = matmul_nt(xs, split3(weight.detach()), k)
+        n, k = weight.shape
+        ws = split3(weight.detach())
+        p = part_width(n)
+        if p != n:
+            # a width off the 16-byte grid (the 84 logits): multiply by p - n extra zero rows so
+            # the product's rows stay aligned, and return the first n columns
+            ws = torch.cat([ws, ws.new_zeros(p - n, ws.shape[1])], 0)
+        y = matmul_nt(xs, ws, k)
+        if p != n:
+            y = y[:, :n]
         hs = bias_act_split(y, bias, act, want_split)
         if hs is None:
             hs = y.new_empty(0, dtype=_BF)
@@ -181,6 +216,36 @@ class SplitBlock(torch.autograd.Function):
         gx = matmul_nn(gys, split3(weight.detach()), n, k) if ctx.needs_input_grad[0] else None
         gw = matmul_tn(gys, xs, n, k) if ctx.needs_input_grad[2] else None
         return gx, None, gw, (gb if ctx.needs_input_grad[3] else None), None, None
+
+
+class SplitValueBlock(torch.autograd.Function):
+    """v = act(x W^T + b) wv^T + bv: a SplitBlock whose output feeds a width-1 Linear (the
+    critic's value head), the head folded into the layer's epilogue and backward prologue.
+    Returns v as (M, 1) like the Linear it replaces."""
+
+    @staticmethod
+    def forward(ctx, x, xs, weight, bias, act, wv, bv):
+        ctx.set_materialize_grads(False)
+        k = weight.shape[1]
+        y = matmul_nt(xs, split3(weight.detach()), k)
+        v = bias_act_value(y, bias, act, wv.detach().reshape(-1).contiguous(), bv.detach().reshape(-1).contiguous())
+        ctx.act = act
+        ctx.save_for_backward(xs, weight, y, wv)      # y now holds h
+        return v.unsqueeze(1)
+
+    @staticmethod
+    def backward(ctx, gvo):
+        if gvo is None:
+            return None, None, None, None, None, None, None
+        xs, weight, h, wv = ctx.saved_tensors
+        n, k = weight.shape
+        gv = gvo.reshape(-1).contiguous()
+        gys, gb, gwv = act_grad_split_value(gv, wv.detach().reshape(-1).contiguous(), h, ctx.act)
+        need = ctx.needs_input_grad
+        gx = matmul_nn(gys, split3(weight.detach()), n, k) if need[0] else None
+        gw = matmul_tn(gys, xs, n, k) if need[2] else None
+        return (gx, None, gw, gb if need[3] else None, None, gwv.view(1, n) if need[5] else None,
+                gv.sum().reshape(1) if need[6] else None)
 
 
 def _dims_ok(layer):
@@ -220,6 +285,10 @@ def run_tower(seq, x):
             continue
         if xs is None:
             xs = split3(x.detach())
+        head = mods[i + 2] if act_mod is not None and i + 3 == len(mods) else None
+        if (isinstance(head, nn.Linear) and head.out_features == 1 and head.in_features == m.out_features
+                and m.out_features % 8 == 0 and head.bias is not None):
+            return SplitValueBlock.apply(x, xs, m.weight, m.bias, code, head.weight, head.bias)
         step = 1 if act_mod is None else 2
         nxt = mods[i + step] if i + step < len(mods) else None
         want = isinstance(nxt, nn.Linear) and _dims_ok(nxt)

@@ -30,6 +30,7 @@ import torch
 import torch.nn as nn
 
 from . import _lib
+from . import categorical
 from . import splitmm
 from .policy import HEAD_CATEGORICAL, HEAD_VALUE, MlpWeights, PolicySet
 from .rollout import RunningNorm, cast_bf16, gae, make_action_grid
@@ -85,7 +86,8 @@ class MLPActorCritic(nn.Module):
         return list(self.critic.parameters())
 
     # set by the PPO update on CUDA: linear layers through splitmm (fp32-accurate products on the
-    # bf16 tensor cores) instead of SGEMM; the modules and their parameters are the same
+    # bf16 tensor cores) instead of SGEMM and the categorical head through its fused kernels; the
+    # modules and their parameters are the same
     split_products = False
 
     def _run(self, seq, x):
@@ -102,6 +104,12 @@ class MLPActorCritic(nn.Module):
 
     def evaluate_actions(self, obs, action):
         """(summed log-prob, summed entropy) of category indices under the current actor."""
+        if self.split_products and obs.dim() == 2:
+            logits = self._run(self.actor_logits, obs)
+            if categorical.usable(logits, self.act_dim, self.num_bins):
+                return categorical.logp_entropy(logits, action, self.act_dim, self.num_bins)
+            dist = torch.distributions.Categorical(logits=logits.view(-1, self.act_dim, self.num_bins))
+            return dist.log_prob(action.long()).sum(-1), dist.entropy().sum(-1)
         dist = self._dist(obs)
         action = action.long()
         return dist.log_prob(action).sum(-1), dist.entropy().sum(-1)

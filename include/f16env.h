@@ -440,6 +440,35 @@ int f16_bias_act_split(float* y, int64_t rows, int cols, int64_t ldy, const floa
 int f16_act_grad_split(const float* gh, int64_t ldg, const float* h, int64_t ldh, int64_t rows, int cols,
                        int act, void* gys, int64_t ldgs, float* col_part, int nblk, f16_stream_t stream);
 
+/* A hidden layer followed by a width-1 Linear (the critic's value head, model.py:34-44 with
+ * out_dim 1): y := act(y + bias) in place as f16_bias_act_split, and v[r] = sum_c y[r][c] wv[c]
+ * + bv[0] (wv [cols], bv a device scalar). */
+int f16_bias_act_value(float* y, int64_t rows, int cols, int64_t ldy, const float* bias, int act,
+                       const float* wv, const float* bv, float* v, f16_stream_t stream);
+
+/* Its backward: f16_act_grad_split with g_h[r][c] = gv[r] wv[c] formed in the kernel, plus
+ * v_part [nblk][cols], block b's column sums of gv[r] h[r][c] (the head weight's gradient is
+ * the sum of the nblk rows). */
+int f16_act_grad_split_value(const float* gv, const float* wv, const float* h, int64_t ldh, int64_t rows,
+                             int cols, int act, void* gys, int64_t ldgs, float* col_part, float* v_part,
+                             int nblk, f16_stream_t stream);
+
+/* The update's categorical head: torch.distributions.Categorical(logits=z.view(-1, A, B)) with
+ * log_prob(action).sum(-1) and entropy().sum(-1) (MLPDiscreteActorCritic.evaluate_actions,
+ * R/claude_code/model.py:198-215).  logits [M][A*B] (row stride ldz), action [M][A] as uint8
+ * (act_bytes 1) or int64 (8), B <= 32, A*B <= 128.  Per group l = z - logsumexp(z),
+ * p = softmax(l), log_prob = l[action], entropy = -sum(max(l, -FLT_MAX) p).  Forward writes
+ * logp[M], ent[M] and ORs into *flags (zeroed by the caller) 1 for a NaN logit and 2 for an
+ * action outside [0, B) -- the argument checks torch's distribution makes (the host raises). */
+int f16_categorical_fwd(const float* logits, int64_t ldz, int64_t M, int A, int B, const void* action,
+                        int act_bytes, float* logp, float* ent, int* flags, f16_stream_t stream);
+
+/* Its gradient: gz [M][A*B] (row stride ldg) = g_lp (onehot(action) - p) - g_ent p (max(l, -FLT_MAX) + H)
+ * per group, H the group's entropy; g_lp / g_ent [M] may be null (zero). */
+int f16_categorical_bwd(const float* logits, int64_t ldz, int64_t M, int A, int B, const void* action,
+                        int act_bytes, const float* g_lp, const float* g_ent, float* gz, int64_t ldg,
+                        f16_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------
  * Diagnostics (no counterpart in the reference): FP64 FMA-pipe probe, the measured roofline
  * denominator of the FDM kernel.  Launches `blocks` x 256 threads running 8 independent FMA

@@ -11,8 +11,14 @@
   no larger than 4x those of fp32 SGEMM on the same operands and below 5e-6 of the largest
   output (TF32 products are near 1e-3), for the update's layer shapes (184 -> 512, 512 -> 512,
   512 -> 84 with zero-padded parts) with 65,536 rows.
-* A whole actor tower through run_tower against the same tower in fp64: output and every
-  parameter gradient within 1e-5 relative.
+* A whole actor tower (84 logits) and critic tower (the value head fused into the last hidden
+  layer) through run_tower against the same tower in fp64: output within 1e-5 relative, every
+  parameter gradient within 1e-5 for tanh towers; for relu towers within 3x the error of torch's
+  own fp32 tower (ReLU mask flips at pre-activations within rounding of zero move whole
+  gradient rows in any fp32 evaluation).
+* The fused categorical head against torch.distributions.Categorical: log-prob, entropy and the
+  logits gradient within 1e-5, infinite logits included; NaN logits and out-of-range actions
+  raise ValueError as torch's argument validation does.
 * A PPO update on the GPU with split products and one with plain fp32 matmuls give the same
   statistics within 1e-4 and parameters within 1e-5 relative.
 """
@@ -130,24 +136,40 @@ def test_split_linear_matches_fp64(cuda, k, n):
 
 
 @pytest.mark.parametrize("activation", ["relu", "tanh"])
-def test_tower_matches_fp64(cuda, activation):
+@pytest.mark.parametrize("out_dim", [84, 1])
+def test_tower_matches_fp64(cuda, activation, out_dim):
     sm = pkg_module("splitmm")
     tr = pkg_module("trainer")
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.manual_seed(5)
-    net = tr.mlp(184, (512, 512), 84, activation).to(cuda)
-    ref_net = tr.mlp(184, (512, 512), 84, activation).double().to(cuda)
+    net = tr.mlp(184, (512, 512), out_dim, activation).to(cuda)
+    with torch.no_grad():
+        for mod in net:
+            if isinstance(mod, torch.nn.Linear):
+                mod.bias.normal_(0.0, 0.1)
+    ref_net = tr.mlp(184, (512, 512), out_dim, activation).double().to(cuda)
     ref_net.load_state_dict({k: v.double() for k, v in net.state_dict().items()})
     g = torch.Generator(device=cuda).manual_seed(6)
     x = torch.randn(20000, 184, device=cuda, generator=g)
-    gout = torch.randn(20000, 84, device=cuda, generator=g)
+    gout = torch.randn(20000, out_dim, device=cuda, generator=g)
+    n32 = tr.mlp(184, (512, 512), out_dim, activation).to(cuda)
+    n32.load_state_dict(net.state_dict())
     out = sm.run_tower(net, x)
     out.backward(gout)
+    o32 = n32(x)
+    o32.backward(gout)
     ref = ref_net(x.double())
     ref.backward(gout.double())
     assert rel(out.detach(), ref.detach()) <= 1e-5
-    for p, q in zip(net.parameters(), ref_net.parameters()):
-        assert rel(p.grad, q.grad) <= 1e-5
+    for p, q, r in zip(net.parameters(), n32.parameters(), ref_net.parameters()):
+        e, e32 = rel(p.grad, r.grad), rel(q.grad, r.grad)
+        if activation == "tanh":
+            assert e <= 1e-5, (e, e32)
+        else:
+            # relu: a pre-activation within rounding of zero takes the other side of the mask in
+            # any fp32 evaluation, moving a whole weight-gradient row; torch's own fp32 tower
+            # shows the same (or larger) gradient errors, measured at 1e-4..1e-2 against fp64
+            assert e <= max(3.0 * e32, 1e-5), (e, e32)
 
 
 def test_ppo_update_split_vs_fp32(cuda):
@@ -178,3 +200,64 @@ def test_ppo_update_split_vs_fp32(cuda):
         assert abs(a - b) <= 1e-4 * max(1.0, abs(b)), (key, a, b)
     for p, q in zip(*params):
         assert float((p - q).abs().max()) <= 1e-5 * max(1.0, float(q.abs().max()))
+
+
+def _torch_head(z, a, A=4, B=21):
+    dist = torch.distributions.Categorical(logits=z.view(-1, A, B))
+    return dist.log_prob(a.long()).sum(-1), dist.entropy().sum(-1)
+
+
+@pytest.mark.parametrize("adtype", [torch.uint8, torch.int64])
+def test_categorical_head_matches_torch(cuda, adtype):
+    cat = pkg_module("categorical")
+    g = torch.Generator(device=cuda).manual_seed(8)
+    m = 30001
+    z = (torch.randn(m, 84, device=cuda, generator=g) * 4).requires_grad_(True)
+    with torch.no_grad():
+        z[3, 0:21] = -float("inf")
+        z[3, 5] = 2.0
+        z[7, 30] = 1e30
+    a = torch.randint(0, 21, (m, 4), device=cuda, generator=g).to(adtype)
+    a[3, 0] = 5
+    g_lp = torch.randn(m, device=cuda, generator=g)
+    g_ent = torch.randn(m, device=cuda, generator=g)
+    lp, ent = cat.logp_entropy(z, a, 4, 21)
+    (lp * g_lp + ent * g_ent).sum().backward()
+    gz = z.grad.clone()
+    z.grad = None
+    rlp, rent = _torch_head(z, a)
+    (rlp * g_lp + rent * g_ent).sum().backward()
+    for got, ref in ((lp, rlp), (ent, rent), (gz, z.grad)):
+        got, ref = got.detach(), ref.detach()
+        assert bool(torch.isfinite(got).all())
+        assert float((got - ref).abs().max()) <= 1e-5 * max(1.0, float(ref.abs().max()))
+    # log-prob only (the entropy unused): its gradient path alone
+    z.grad = None
+    lp, _ = cat.logp_entropy(z, a, 4, 21)
+    lp.sum().backward()
+    gz = z.grad.clone()
+    z.grad = None
+    _torch_head(z, a)[0].sum().backward()
+    # p enters as exp(z - logsumexp) in torch's logsumexp backward and as the softmax of the
+    # normalised logits here: a few ulps apart
+    assert float((gz - z.grad).abs().max()) <= 1e-5 * max(1.0, float(z.grad.abs().max()))
+
+
+def test_categorical_head_validates(cuda):
+    cat = pkg_module("categorical")
+    z = torch.randn(100, 84, device=cuda)
+    a = torch.randint(0, 21, (100, 4), device=cuda).to(torch.uint8)
+    lp, ent = cat.logp_entropy(z, a, 4, 21)
+    assert lp.shape == (100,) and ent.shape == (100,)
+    bad = a.clone()
+    bad[9, 2] = 21
+    with pytest.raises(ValueError, match="support"):
+        cat.logp_entropy(z, bad, 4, 21)
+    with pytest.raises(ValueError):
+        _torch_head(z, bad)
+    zn = z.clone()
+    zn[4, 50] = float("nan")
+    with pytest.raises(ValueError, match="constraint"):
+        cat.logp_entropy(zn, a, 4, 21)
+    with pytest.raises(ValueError):
+        _torch_head(zn, a)
