@@ -96,11 +96,13 @@ _SIGS = {
     "f16_fdm_step_ex": ([_P, C.c_int, _I64, _I64, C.POINTER(FdmIO), C.c_int, C.c_double, _P], C.c_int),
     "f16_rollout_record": ([_I64, C.POINTER(RecordArgs), _P], C.c_int),
     "f16_payoff_record": ([_I64, C.POINTER(PayoffArgs), _P], C.c_int),
-    "f16_split3_bf16": ([_P, _I64, C.c_int, _I64, _P, _I64, _P], C.c_int),
-    "f16_bias_act_split": ([_P, _I64, C.c_int, _I64, _P, C.c_int, _P, _I64, _P], C.c_int),
-    "f16_act_grad_split": ([_P, _I64, _P, _I64, _I64, C.c_int, C.c_int, _P, _I64, _P, C.c_int, _P], C.c_int),
+    "f16_split3_bf16": ([_P, _I64, C.c_int, _I64, _P, _I64, C.c_int, _P], C.c_int),
+    "f16_bias_act_split": ([_P, _I64, C.c_int, _I64, _P, C.c_int, _P, _I64, C.c_int, _P], C.c_int),
+    "f16_act_grad_split": ([_P, _I64, _P, _I64, _I64, C.c_int, C.c_int, _P, _I64, C.c_int, _P, C.c_int, _P],
+                           C.c_int),
     "f16_bias_act_value": ([_P, _I64, C.c_int, _I64, _P, C.c_int, _P, _P, _P, _P], C.c_int),
-    "f16_act_grad_split_value": ([_P, _P, _P, _I64, _I64, C.c_int, C.c_int, _P, _I64, _P, _P, C.c_int, _P], C.c_int),
+    "f16_act_grad_split_value": ([_P, _P, _P, _I64, _I64, C.c_int, C.c_int, _P, _I64, C.c_int, _P, _P, C.c_int, _P],
+                                 C.c_int),
     "f16_categorical_fwd": ([_P, _I64, _I64, C.c_int, C.c_int, _P, C.c_int, _P, _P, _P, _P], C.c_int),
     "f16_categorical_bwd": ([_P, _I64, _I64, C.c_int, C.c_int, _P, C.c_int, _P, _P, _P, _I64, _P], C.c_int),
     "f16_seed_ic": ([_P, _I64, _P, C.c_int, _I64, C.c_double, _P], C.c_int),

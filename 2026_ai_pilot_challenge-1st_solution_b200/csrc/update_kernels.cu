@@ -20,7 +20,9 @@
 //                     actions and summed entropy per row, and their gradient.
 //
 // Every part of a split row is `cols` rounded up to 8 columns (16 bytes of bf16), the pad columns
-// zero, so every part starts 16-byte aligned for the tensor-core GEMMs.
+// zero, so every part starts 16-byte aligned for the tensor-core GEMMs.  A split has three parts
+// [mid | lo | hi] or six, [mid | lo | hi | lo | hi | hi]: the A operand of ONE GEMM over all six
+// term products (against B = [hi; hi; mid; lo; lo; hi]), the hi*hi product last in K.
 #include <cuda_bf16.h>
 #include <cfloat>
 #include "common.cuh"
@@ -35,8 +37,9 @@ __host__ __device__ __forceinline__ int part_of(int cols) { return (cols + 7) & 
 
 // hi = bf16(v), lo = bf16(v - hi), mid = bf16(v - hi - lo), round to nearest; both differences
 // are exact in fp32 (each is v minus a prefix of v's significand), so mid + lo + hi carries all
-// 24 significant bits of v.  Stored as the row's mid, lo and hi parts.
-__device__ __forceinline__ void split_store(const float a[4], __nv_bfloat16* o, int part) {
+// 24 significant bits of v.  Stored as the row's mid, lo and hi parts, and with six parts also
+// lo, hi, hi again (the A operand of a single GEMM over all six term products).
+__device__ __forceinline__ void split_store(const float a[4], __nv_bfloat16* o, int part, bool six) {
   __nv_bfloat16 hi[4], lo[4], mi[4];
 #pragma unroll
   for (int k = 0; k < 4; k++) {
@@ -45,16 +48,22 @@ __device__ __forceinline__ void split_store(const float a[4], __nv_bfloat16* o, 
     lo[k] = __float2bfloat16_rn(r1);
     mi[k] = __float2bfloat16_rn(__fsub_rn(r1, __bfloat162float(lo[k])));
   }
-  *reinterpret_cast<uint2*>(o) = *reinterpret_cast<const uint2*>(mi);
-  *reinterpret_cast<uint2*>(o + part) = *reinterpret_cast<const uint2*>(lo);
-  *reinterpret_cast<uint2*>(o + 2 * part) = *reinterpret_cast<const uint2*>(hi);
+  const uint2 m2 = *reinterpret_cast<const uint2*>(mi), l2 = *reinterpret_cast<const uint2*>(lo),
+              h2 = *reinterpret_cast<const uint2*>(hi);
+  *reinterpret_cast<uint2*>(o) = m2;
+  *reinterpret_cast<uint2*>(o + part) = l2;
+  *reinterpret_cast<uint2*>(o + 2 * part) = h2;
+  if (six) {
+    *reinterpret_cast<uint2*>(o + 3 * part) = l2;
+    *reinterpret_cast<uint2*>(o + 4 * part) = h2;
+    *reinterpret_cast<uint2*>(o + 5 * part) = h2;
+  }
 }
 
-__device__ __forceinline__ void zero_store(__nv_bfloat16* o, int part) {
+__device__ __forceinline__ void zero_store(__nv_bfloat16* o, int part, bool six) {
   const uint2 z = make_uint2(0u, 0u);
-  *reinterpret_cast<uint2*>(o) = z;
-  *reinterpret_cast<uint2*>(o + part) = z;
-  *reinterpret_cast<uint2*>(o + 2 * part) = z;
+  const int n = six ? 6 : 3;
+  for (int k = 0; k < n; k++) *reinterpret_cast<uint2*>(o + k * part) = z;
 }
 
 // torch.relu (clamp_min(v, 0), NaN kept) / torch.tanh / identity.
@@ -74,7 +83,7 @@ __device__ __forceinline__ float act_bwd(float g, float h, int act) {
 
 // One thread per 4 consecutive columns of a row part (16-byte load; 8-byte stores of each term).
 __global__ void __launch_bounds__(THREADS) k_split3(const float* __restrict__ x, int64_t rows, int cols, int64_t ldx,
-                                                    __nv_bfloat16* __restrict__ out, int64_t ldo) {
+                                                    __nv_bfloat16* __restrict__ out, int64_t ldo, bool six) {
   const int part = part_of(cols);
   const int g = part >> 2;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -83,19 +92,19 @@ __global__ void __launch_bounds__(THREADS) k_split3(const float* __restrict__ x,
   const int c = (int)(i % g) * 4;
   __nv_bfloat16* o = out + r * ldo + c;
   if (c >= cols) {
-    zero_store(o, part);
+    zero_store(o, part, six);
     return;
   }
   const float4 v = *reinterpret_cast<const float4*>(x + r * ldx + c);
   const float a[4] = {v.x, v.y, v.z, v.w};
-  split_store(a, o, part);
+  split_store(a, o, part, six);
 }
 
 // h = act(y + bias) written over y; with hs, also the split of h.  Same thread map as k_split3
 // (the pad groups exist only when hs is written).
 __global__ void __launch_bounds__(THREADS) k_bias_act_split(float* __restrict__ y, int64_t rows, int cols, int64_t ldy,
                                                             const float* __restrict__ bias, int act,
-                                                            __nv_bfloat16* __restrict__ hs, int64_t ldhs) {
+                                                            __nv_bfloat16* __restrict__ hs, int64_t ldhs, bool six) {
   const int part = hs ? part_of(cols) : cols;
   const int g = part >> 2;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -103,7 +112,7 @@ __global__ void __launch_bounds__(THREADS) k_bias_act_split(float* __restrict__ 
   const int64_t r = i / g;
   const int c = (int)(i % g) * 4;
   if (c >= cols) {
-    zero_store(hs + r * ldhs + c, part);
+    zero_store(hs + r * ldhs + c, part, six);
     return;
   }
   float4* yp = reinterpret_cast<float4*>(y + r * ldy + c);
@@ -112,7 +121,7 @@ __global__ void __launch_bounds__(THREADS) k_bias_act_split(float* __restrict__ 
   const float a[4] = {act_fwd(__fadd_rn(v.x, b.x), act), act_fwd(__fadd_rn(v.y, b.y), act),
                       act_fwd(__fadd_rn(v.z, b.z), act), act_fwd(__fadd_rn(v.w, b.w), act)};
   *yp = make_float4(a[0], a[1], a[2], a[3]);
-  if (hs) split_store(a, hs + r * ldhs + c, part);
+  if (hs) split_store(a, hs + r * ldhs + c, part, six);
 }
 
 // h = act(y + bias) written over y and the value head on it, v[r] = sum_c h[r][c] wv[c] + bv[0]
@@ -152,7 +161,7 @@ __global__ void __launch_bounds__(THREADS) k_act_grad_split(const float* __restr
                                                             int cols, int act, __nv_bfloat16* __restrict__ gys,
                                                             int64_t ldgs, float* __restrict__ col_part, int64_t rpb,
                                                             const float* __restrict__ gv, const float* __restrict__ wv,
-                                                            float* __restrict__ v_part) {
+                                                            float* __restrict__ v_part, bool six) {
   __shared__ float4 red[THREADS];
   __shared__ float4 red_v[THREADS];
   const int part = part_of(cols);
@@ -170,7 +179,7 @@ __global__ void __launch_bounds__(THREADS) k_act_grad_split(const float* __restr
     for (int64_t r = r0 + slot; r < r1; r += RS) {
       __nv_bfloat16* o = gys + r * ldgs + c;
       if (c >= cols) {
-        zero_store(o, part);
+        zero_store(o, part, six);
         continue;
       }
       float4 g;
@@ -194,7 +203,7 @@ __global__ void __launch_bounds__(THREADS) k_act_grad_split(const float* __restr
         acc_v.z = __fmaf_rn(gr, hv.z, acc_v.z);
         acc_v.w = __fmaf_rn(gr, hv.w, acc_v.w);
       }
-      split_store(a, o, part);
+      split_store(a, o, part, six);
     }
   }
   red[tid] = acc;
@@ -386,32 +395,35 @@ inline unsigned grid_for(int64_t n) { return (unsigned)((n + THREADS - 1) / THRE
 using namespace f16;
 
 extern "C" int f16_split3_bf16(const float* x, int64_t rows, int cols, int64_t ldx, void* out, int64_t ldo,
-                               f16_stream_t stream) {
-  if (!x || !out || rows <= 0 || cols <= 0 || cols % 4 || ldx < cols || ldo < 3 * (int64_t)upd::part_of(cols))
+                               int parts, f16_stream_t stream) {
+  if (!x || !out || rows <= 0 || cols <= 0 || cols % 4 || ldx < cols || (parts != 3 && parts != 6) ||
+      ldo < parts * (int64_t)upd::part_of(cols))
     return F16_ERR_ARG;
   if (!aligned(x, 16) || ldx % 4 || !aligned(out, 8) || ldo % 4) return F16_ERR_ALIGN;
   const int64_t n = rows * (upd::part_of(cols) / 4);
   upd::k_split3<<<upd::grid_for(n), upd::THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, rows, cols, ldx, reinterpret_cast<__nv_bfloat16*>(out), ldo);
+      x, rows, cols, ldx, reinterpret_cast<__nv_bfloat16*>(out), ldo, parts == 6);
   return launch_status();
 }
 
 extern "C" int f16_bias_act_split(float* y, int64_t rows, int cols, int64_t ldy, const float* bias, int act,
-                                  void* hs, int64_t ldhs, f16_stream_t stream) {
+                                  void* hs, int64_t ldhs, int parts, f16_stream_t stream) {
   if (!y || !bias || rows <= 0 || cols <= 0 || cols % 4 || ldy < cols || act < F16_ACT_NONE || act > F16_ACT_TANH)
     return F16_ERR_ARG;
-  if (hs && ldhs < 3 * (int64_t)upd::part_of(cols)) return F16_ERR_ARG;
+  if (hs && ((parts != 3 && parts != 6) || ldhs < parts * (int64_t)upd::part_of(cols))) return F16_ERR_ARG;
   if (!aligned(y, 16) || ldy % 4 || !aligned(bias, 16) || (hs && (!aligned(hs, 8) || ldhs % 4))) return F16_ERR_ALIGN;
   const int64_t n = rows * ((hs ? upd::part_of(cols) : cols) / 4);
   upd::k_bias_act_split<<<upd::grid_for(n), upd::THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      y, rows, cols, ldy, bias, act, reinterpret_cast<__nv_bfloat16*>(hs), ldhs);
+      y, rows, cols, ldy, bias, act, reinterpret_cast<__nv_bfloat16*>(hs), ldhs, parts == 6);
   return launch_status();
 }
 
 extern "C" int f16_act_grad_split(const float* gh, int64_t ldg, const float* h, int64_t ldh, int64_t rows, int cols,
-                                  int act, void* gys, int64_t ldgs, float* col_part, int nblk, f16_stream_t stream) {
+                                  int act, void* gys, int64_t ldgs, int parts, float* col_part, int nblk,
+                                  f16_stream_t stream) {
   if (!gh || !gys || !col_part || rows <= 0 || cols <= 0 || cols % 4 || cols > upd::MAX_GRAD_COLS || ldg < cols ||
-      ldgs < 3 * (int64_t)upd::part_of(cols) || nblk <= 0 || act < F16_ACT_NONE || act > F16_ACT_TANH)
+      (parts != 3 && parts != 6) || ldgs < parts * (int64_t)upd::part_of(cols) || nblk <= 0 || act < F16_ACT_NONE ||
+      act > F16_ACT_TANH)
     return F16_ERR_ARG;
   if (act != F16_ACT_NONE && (!h || ldh < cols)) return F16_ERR_ARG;
   if (!aligned(gh, 16) || ldg % 4 || !aligned(gys, 8) || ldgs % 4 || !aligned(col_part, 16) ||
@@ -420,7 +432,7 @@ extern "C" int f16_act_grad_split(const float* gh, int64_t ldg, const float* h, 
   const int64_t rpb = (rows + nblk - 1) / nblk;
   upd::k_act_grad_split<<<(unsigned)nblk, upd::THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       gh, ldg, h, ldh, rows, cols, act, reinterpret_cast<__nv_bfloat16*>(gys), ldgs, col_part, rpb, nullptr, nullptr,
-      nullptr);
+      nullptr, parts == 6);
   return launch_status();
 }
 
@@ -437,18 +449,19 @@ extern "C" int f16_bias_act_value(float* y, int64_t rows, int cols, int64_t ldy,
 }
 
 extern "C" int f16_act_grad_split_value(const float* gv, const float* wv, const float* h, int64_t ldh, int64_t rows,
-                                        int cols, int act, void* gys, int64_t ldgs, float* col_part, float* v_part,
-                                        int nblk, f16_stream_t stream) {
+                                        int cols, int act, void* gys, int64_t ldgs, int parts, float* col_part,
+                                        float* v_part, int nblk, f16_stream_t stream) {
   if (!gv || !wv || !h || !gys || !col_part || !v_part || rows <= 0 || cols <= 0 || cols % 4 ||
-      cols > upd::MAX_GRAD_COLS || ldh < cols || ldgs < 3 * (int64_t)upd::part_of(cols) || nblk <= 0 ||
-      act < F16_ACT_NONE || act > F16_ACT_TANH)
+      cols > upd::MAX_GRAD_COLS || ldh < cols || (parts != 3 && parts != 6) ||
+      ldgs < parts * (int64_t)upd::part_of(cols) || nblk <= 0 || act < F16_ACT_NONE || act > F16_ACT_TANH)
     return F16_ERR_ARG;
   if (!aligned(wv, 16) || !aligned(h, 16) || ldh % 4 || !aligned(gys, 8) || ldgs % 4 || !aligned(col_part, 16) ||
       !aligned(v_part, 16))
     return F16_ERR_ALIGN;
   const int64_t rpb = (rows + nblk - 1) / nblk;
   upd::k_act_grad_split<<<(unsigned)nblk, upd::THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      nullptr, 0, h, ldh, rows, cols, act, reinterpret_cast<__nv_bfloat16*>(gys), ldgs, col_part, rpb, gv, wv, v_part);
+      nullptr, 0, h, ldh, rows, cols, act, reinterpret_cast<__nv_bfloat16*>(gys), ldgs, col_part, rpb, gv, wv, v_part,
+      parts == 6);
   return launch_status();
 }
 

@@ -8,13 +8,16 @@ stored as a row of three parts [mid | lo | hi], and a product A B is assembled f
 products whose order of magnitude reaches fp32's unit roundoff -- hi*hi, hi*lo, lo*hi, hi*mid,
 lo*lo, mid*hi; the three dropped ones are below 2^-24 relative -- each a bf16 tensor-core GEMM
 with fp32 accumulation (``torch.mm(..., out_dtype=torch.float32)``).  Terms that share an
-operand run as one GEMM over concatenated K, so a product is three GEMM calls.
+operand run as one GEMM over concatenated K, so a product is three GEMM calls -- or one, when the
+producer of the big operand writes it as six parts [mid | lo | hi | lo | hi | hi] against
+B = [hi; hi; mid; lo; lo; hi] (``parts_for`` picks the layout that moves fewer bytes).
 
 Accuracy depends on the order: the tensor cores' fp32 accumulation loses more per addition than
 an SGEMM's round-to-nearest FMA chain, so the number of additions made at the full magnitude of
 the result is kept small.  The five small terms accumulate first (at 2^-8 of the result's
-magnitude, where their rounding is negligible), and hi*hi comes last as a GEMM of its own whose
-result joins them in cuBLAS's fp32 epilogue (beta = 1, in place).  A weight gradient reduces
+magnitude, where their rounding is negligible), and hi*hi comes last: as the last K range of the
+single GEMM, or as a GEMM of its own whose result joins them in cuBLAS's fp32 epilogue (beta = 1,
+in place).  A weight gradient reduces
 over all rows of a minibatch, so its hi*hi product is a batched GEMM over ``ROW_CHUNK``-row
 slices whose partial products are summed in fp32.  Against fp64 the products stay within a few
 times an SGEMM's error on the same operands (about 1e-6 relative; TF32 is near 1e-3).
@@ -55,42 +58,50 @@ def _fp32_operand(x):
     return x
 
 
-def split3(x):
-    """(rows, cols) fp32 -> (rows, 3 p) bf16 [mid | lo | hi], p = part_width(cols), pad columns
-    zero (cols must be a multiple of 4)."""
+def parts_for(out_cols, part):
+    """Split layout of a product's A operand (`part` columns per term) whose result has `out_cols`
+    columns: six parts -- one GEMM -- when the two read-modify-write passes over the fp32 result it
+    saves (16 bytes per output column and row) outweigh the three extra parts written (6 bytes
+    per column and row), else three parts and three GEMMs."""
+    return 6 if 16 * out_cols > 6 * part else 3
+
+
+def split3(x, parts=3):
+    """(rows, cols) fp32 -> (rows, parts p) bf16 [mid | lo | hi] (+ [lo | hi | hi] for six parts),
+    p = part_width(cols), pad columns zero (cols must be a multiple of 4)."""
     if x.dim() != 2:
         raise ValueError("split3 takes a 2-D tensor")
     x = _fp32_operand(x)
     rows, cols = x.shape
     p = part_width(cols)
-    out = torch.empty(rows, 3 * p, dtype=_BF, device=x.device)
-    _lib.check(_lib.load().f16_split3_bf16(x.data_ptr(), rows, cols, x.stride(0), out.data_ptr(), 3 * p,
+    out = torch.empty(rows, parts * p, dtype=_BF, device=x.device)
+    _lib.check(_lib.load().f16_split3_bf16(x.data_ptr(), rows, cols, x.stride(0), out.data_ptr(), parts * p, parts,
                                            _lib.stream_of(x)), "f16_split3_bf16")
     return out
 
 
-def bias_act_split(y, bias, act, want_split):
-    """y := act(y + bias) in place (y a fresh fp32 product); returns the split of the result when
-    `want_split`, else None."""
+def bias_act_split(y, bias, act, parts):
+    """y := act(y + bias) in place (y a fresh fp32 product); returns the split of the result in
+    `parts` parts (3 or 6), or None for parts 0."""
     rows, cols = y.shape
-    hs = torch.empty(rows, 3 * part_width(cols), dtype=_BF, device=y.device) if want_split else None
+    hs = torch.empty(rows, parts * part_width(cols), dtype=_BF, device=y.device) if parts else None
     bias = bias.detach().contiguous()
     _lib.check(_lib.load().f16_bias_act_split(y.data_ptr(), rows, cols, y.stride(0), bias.data_ptr(), act,
                                               hs.data_ptr() if hs is not None else None,
-                                              hs.stride(0) if hs is not None else 0, _lib.stream_of(y)),
-               "f16_bias_act_split")
+                                              hs.stride(0) if hs is not None else 0, parts if parts else 3,
+                                              _lib.stream_of(y)), "f16_bias_act_split")
     return hs
 
 
-def act_grad_split(gh, h, act):
-    """(split of g_y, bias gradient) for g_y = act'(gh; h)."""
+def act_grad_split(gh, h, act, parts=3):
+    """(split of g_y in `parts` parts, bias gradient) for g_y = act'(gh; h)."""
     gh = _fp32_operand(gh)
     rows, cols = gh.shape
     nblk = max(1, min(GRAD_BLOCKS, (rows + 63) // 64))
-    gys = torch.empty(rows, 3 * part_width(cols), dtype=_BF, device=gh.device)
+    gys = torch.empty(rows, parts * part_width(cols), dtype=_BF, device=gh.device)
     part = torch.empty(nblk, cols, dtype=_F32, device=gh.device)
     _lib.check(_lib.load().f16_act_grad_split(gh.data_ptr(), gh.stride(0), h.data_ptr(), h.stride(0), rows, cols, act,
-                                              gys.data_ptr(), gys.stride(0), part.data_ptr(), nblk,
+                                              gys.data_ptr(), gys.stride(0), parts, part.data_ptr(), nblk,
                                               _lib.stream_of(gh)), "f16_act_grad_split")
     return gys, part.sum(0)
 
@@ -105,15 +116,16 @@ def bias_act_value(y, bias, act, wv, bv):
     return v
 
 
-def act_grad_split_value(gv, wv, h, act):
-    """(split of g_y, bias gradient, value-weight gradient) for g_y = act'(gv wv^T; h)."""
+def act_grad_split_value(gv, wv, h, act, parts=3):
+    """(split of g_y in `parts` parts, bias gradient, value-weight gradient) for
+    g_y = act'(gv wv^T; h)."""
     rows, cols = h.shape
     nblk = max(1, min(GRAD_BLOCKS, (rows + 63) // 64))
-    gys = torch.empty(rows, 3 * part_width(cols), dtype=_BF, device=h.device)
+    gys = torch.empty(rows, parts * part_width(cols), dtype=_BF, device=h.device)
     part = torch.empty(nblk, cols, dtype=_F32, device=h.device)
     vpart = torch.empty(nblk, cols, dtype=_F32, device=h.device)
     _lib.check(_lib.load().f16_act_grad_split_value(gv.data_ptr(), wv.data_ptr(), h.data_ptr(), h.stride(0), rows,
-                                                    cols, act, gys.data_ptr(), gys.stride(0), part.data_ptr(),
+                                                    cols, act, gys.data_ptr(), gys.stride(0), parts, part.data_ptr(),
                                                     vpart.data_ptr(), nblk, _lib.stream_of(h)),
                "f16_act_grad_split_value")
     return gys, part.sum(0), vpart.sum(0)
@@ -132,24 +144,28 @@ def _parts(s, p):
 
 
 def matmul_nt(xs, ws, k):
-    """x W^T from the splits xs (M x 3k) and ws (N x 3k); k a multiple of 8."""
+    """x W^T from the splits xs (M x 3k or 6k) and ws (N x 3k); k a multiple of 8."""
     wm, wl, wh = _parts(ws, k)
-    y = _mm(xs, torch.cat([wh, wh, wm], 1).t())                   # xm wh + xl wh + xh wm
-    y = _mm(xs[:, k:], torch.cat([wl, wl], 1).t(), y)             # + xl wl + xh wl
-    return _mm(xs[:, 2 * k:], wh.t(), y)                          # + xh wh
+    if xs.shape[1] == 6 * k:                                      # [xm | xl | xh | xl | xh | xh]
+        return _mm(xs, torch.cat([wh, wh, wm, wl, wl, wh], 1).t())
+    y = _mm(xs[:, :3 * k], torch.cat([wh, wh, wm], 1).t())        # xm wh + xl wh + xh wm
+    y = _mm(xs[:, k:3 * k], torch.cat([wl, wl], 1).t(), y)        # + xl wl + xh wl
+    return _mm(xs[:, 2 * k:3 * k], wh.t(), y)                     # + xh wh
 
 
 def matmul_nn(gs, ws, n, k):
-    """g W from gs (M x 3p, p = part_width(n)) and ws (W = n x k, split n x 3k); W's terms get
-    p - n zero rows against g's zero pad columns."""
+    """g W from gs (M x 3p or 6p, p = part_width(n)) and ws (W = n x k, split n x 3k); W's terms
+    get p - n zero rows against g's zero pad columns."""
     p = part_width(n)
     wm, wl, wh = _parts(ws, k)
     if p != n:
         pad = ws.new_zeros(p - n, k)
         wm, wl, wh = (torch.cat([t, pad], 0) for t in (wm, wl, wh))
-    y = _mm(gs, torch.cat([wh, wh, wm], 0))                       # gm wh + gl wh + gh wm
-    y = _mm(gs[:, p:], torch.cat([wl, wl], 0), y)                 # + gl wl + gh wl
-    return _mm(gs[:, 2 * p:], wh, y)                              # + gh wh
+    if gs.shape[1] == 6 * p:                                      # [gm | gl | gh | gl | gh | gh]
+        return _mm(gs, torch.cat([wh, wh, wm, wl, wl, wh], 0))
+    y = _mm(gs[:, :3 * p], torch.cat([wh, wh, wm], 0))            # gm wh + gl wh + gh wm
+    y = _mm(gs[:, p:3 * p], torch.cat([wl, wl], 0), y)            # + gl wl + gh wl
+    return _mm(gs[:, 2 * p:3 * p], wh, y)                         # + gh wh
 
 
 def _tn_chunked(a, b):
@@ -168,25 +184,32 @@ def _tn_chunked(a, b):
 
 
 def matmul_tn(gs, xs, n, k):
-    """g^T x (n x k) from gs (M x 3p, p = part_width(n)) and xs (M x 3k)."""
+    """g^T x (n x k) from gs (p = part_width(n) per part) and xs (k per part), three or six parts
+    each (only the first three are read)."""
     gm, gl, gh = _parts(gs, part_width(n))
-    xh = xs[:, 2 * k:]
+    xh = xs[:, 2 * k:3 * k]
     a = _mm(gh.t(), xs[:, :2 * k])                                # [gh xm | gh xl]
-    b = _mm(gl.t(), xs[:, k:])                                    # [gl xl | gl xh]
+    b = _mm(gl.t(), xs[:, k:3 * k])                               # [gl xl | gl xh]
     c = _mm(gm.t(), xh)                                           # gm xh
     small = ((c + b[:, :k]) + a[:, :k]) + (a[:, k:] + b[:, k:])
     return (_tn_chunked(gh, xh) + small)[:n]
+
+
+def _grad_parts(ctx, n, k):
+    """Layout of a layer's output-gradient split: six parts when the input gradient g W (k
+    columns) is computed and gains by it, else three (the weight gradient reads three)."""
+    return parts_for(k, part_width(n)) if ctx.needs_input_grad[0] else 3
 
 
 class SplitBlock(torch.autograd.Function):
     """h = act(x W^T + b) with fp32-accurate tensor-core products (module docstring).
 
     Inputs: x (fp32, for the autograd graph), xs = split3(x) (the operand actually read), the
-    layer's weight and bias, the activation code and whether to return the split of h.
-    Returns (h, hs); hs is empty when not requested and never carries a gradient."""
+    layer's weight and bias, the activation code and the part count (0, 3 or 6) of the split of
+    h to return.  Returns (h, hs); hs is empty when not requested and never carries a gradient."""
 
     @staticmethod
-    def forward(ctx, x, xs, weight, bias, act, want_split):
+    def forward(ctx, x, xs, weight, bias, act, out_parts):
         ctx.set_materialize_grads(False)
         n, k = weight.shape
         ws = split3(weight.detach())
@@ -198,7 +221,7 @@ class SplitBlock(torch.autograd.Function):
         y = matmul_nt(xs, ws, k)
         if p != n:
             y = y[:, :n]
-        hs = bias_act_split(y, bias, act, want_split)
+        hs = bias_act_split(y, bias, act, out_parts)
         if hs is None:
             hs = y.new_empty(0, dtype=_BF)
         ctx.mark_non_differentiable(hs)
@@ -212,7 +235,7 @@ class SplitBlock(torch.autograd.Function):
             return None, None, None, None, None, None
         xs, weight, h = ctx.saved_tensors
         n, k = weight.shape
-        gys, gb = act_grad_split(gh, h, ctx.act)
+        gys, gb = act_grad_split(gh, h, ctx.act, _grad_parts(ctx, n, k))
         gx = matmul_nn(gys, split3(weight.detach()), n, k) if ctx.needs_input_grad[0] else None
         gw = matmul_tn(gys, xs, n, k) if ctx.needs_input_grad[2] else None
         return gx, None, gw, (gb if ctx.needs_input_grad[3] else None), None, None
@@ -240,7 +263,8 @@ class SplitValueBlock(torch.autograd.Function):
         xs, weight, h, wv = ctx.saved_tensors
         n, k = weight.shape
         gv = gvo.reshape(-1).contiguous()
-        gys, gb, gwv = act_grad_split_value(gv, wv.detach().reshape(-1).contiguous(), h, ctx.act)
+        gys, gb, gwv = act_grad_split_value(gv, wv.detach().reshape(-1).contiguous(), h, ctx.act,
+                                            _grad_parts(ctx, n, k))
         need = ctx.needs_input_grad
         gx = matmul_nn(gys, split3(weight.detach()), n, k) if need[0] else None
         gw = matmul_tn(gys, xs, n, k) if need[2] else None
@@ -260,9 +284,14 @@ def usable(layer, x):
     return x.is_cuda and x.dtype == _F32 and x.dim() == 2 and _dims_ok(layer)
 
 
+def _in_parts(layer):
+    return parts_for(layer.out_features, part_width(layer.in_features))
+
+
 def split_linear(x, weight, bias, act=ACT_NONE):
     """act(F.linear(x, weight, bias)) through one SplitBlock."""
-    return SplitBlock.apply(x, split3(x.detach()), weight, bias, act, False)[0]
+    xs = split3(x.detach(), parts_for(weight.shape[0], part_width(weight.shape[1])))
+    return SplitBlock.apply(x, xs, weight, bias, act, 0)[0]
 
 
 def run_tower(seq, x):
@@ -284,15 +313,15 @@ def run_tower(seq, x):
             i += 1
             continue
         if xs is None:
-            xs = split3(x.detach())
+            xs = split3(x.detach(), _in_parts(m))
         head = mods[i + 2] if act_mod is not None and i + 3 == len(mods) else None
         if (isinstance(head, nn.Linear) and head.out_features == 1 and head.in_features == m.out_features
                 and m.out_features % 8 == 0 and head.bias is not None):
             return SplitValueBlock.apply(x, xs, m.weight, m.bias, code, head.weight, head.bias)
         step = 1 if act_mod is None else 2
         nxt = mods[i + step] if i + step < len(mods) else None
-        want = isinstance(nxt, nn.Linear) and _dims_ok(nxt)
-        x, hs = SplitBlock.apply(x, xs, m.weight, m.bias, code, want)
-        xs = hs if want else None
+        out_parts = _in_parts(nxt) if isinstance(nxt, nn.Linear) and _dims_ok(nxt) else 0
+        x, hs = SplitBlock.apply(x, xs, m.weight, m.bias, code, out_parts)
+        xs = hs if out_parts else None
         i += step
     return x

@@ -416,29 +416,32 @@ int f16_payoff_record(int64_t nenv, const f16_payoff_args* args, f16_stream_t st
  * mid = bf16(v - hi - lo) (round to nearest; both differences are exact in fp32), so
  * mid + lo + hi carries v's 24 significant bits.  A split row of `cols` values is three parts of
  * p = cols rounded up to 8 columns, [mid | lo | hi] (out[r][0..p) = mid, [p..2p) = lo,
- * [2p..3p) = hi), each part's columns cols..p zero, so every part starts 16-byte aligned.  cols
+ * [2p..3p) = hi), each part's columns cols..p zero, so every part starts 16-byte aligned; with
+ * parts = 6 the row continues [lo | hi | hi], the A operand of one GEMM over all six term
+ * products (B = [hi; hi; mid; lo; lo; hi]: hi*hi last in K).  Row strides >= parts * p.  cols
  * is a multiple of 4 everywhere; fp32 pointers are 16-byte aligned with row strides a multiple
- * of 4 elements, split pointers 8-byte aligned with row strides >= 3p and a multiple of 4. */
+ * of 4 elements, split pointers 8-byte aligned with row strides a multiple of 4. */
 #define F16_ACT_NONE 0
 #define F16_ACT_RELU 1   /* torch.relu: clamp_min(v, 0); backward threshold_backward(g, h, 0) */
 #define F16_ACT_TANH 2   /* torch.tanh; backward g (1 - h h) */
 
 /* Split of x [rows][cols] (row stride ldx) into out (row stride ldo). */
 int f16_split3_bf16(const float* x, int64_t rows, int cols, int64_t ldx, void* out, int64_t ldo,
-                    f16_stream_t stream);
+                    int parts, f16_stream_t stream);
 
 /* A layer's epilogue (the bias add of torch's F.linear and the activation module that follows
  * it, R/claude_code/model.py:34-44): y [rows][cols] := act(y + bias) in place; if hs is
  * non-null also its split (row stride ldhs), the next layer's operand. */
 int f16_bias_act_split(float* y, int64_t rows, int cols, int64_t ldy, const float* bias, int act,
-                       void* hs, int64_t ldhs, f16_stream_t stream);
+                       void* hs, int64_t ldhs, int parts, f16_stream_t stream);
 
 /* A layer's backward prologue: g_y = act'(g_h; h) (h = the layer's activated output, unread for
  * F16_ACT_NONE), written as its split gys (row stride ldgs), and col_part [nblk][cols]: block b's
  * column sums of g_y over rows [b rpb, (b + 1) rpb), rpb = ceil(rows / nblk), summed in a fixed
  * order (the bias gradient is the sum of the nblk rows).  cols <= 1024. */
 int f16_act_grad_split(const float* gh, int64_t ldg, const float* h, int64_t ldh, int64_t rows, int cols,
-                       int act, void* gys, int64_t ldgs, float* col_part, int nblk, f16_stream_t stream);
+                       int act, void* gys, int64_t ldgs, int parts, float* col_part, int nblk,
+                       f16_stream_t stream);
 
 /* A hidden layer followed by a width-1 Linear (the critic's value head, model.py:34-44 with
  * out_dim 1): y := act(y + bias) in place as f16_bias_act_split, and v[r] = sum_c y[r][c] wv[c]
@@ -450,8 +453,8 @@ int f16_bias_act_value(float* y, int64_t rows, int cols, int64_t ldy, const floa
  * v_part [nblk][cols], block b's column sums of gv[r] h[r][c] (the head weight's gradient is
  * the sum of the nblk rows). */
 int f16_act_grad_split_value(const float* gv, const float* wv, const float* h, int64_t ldh, int64_t rows,
-                             int cols, int act, void* gys, int64_t ldgs, float* col_part, float* v_part,
-                             int nblk, f16_stream_t stream);
+                             int cols, int act, void* gys, int64_t ldgs, int parts, float* col_part,
+                             float* v_part, int nblk, f16_stream_t stream);
 
 /* The update's categorical head: torch.distributions.Categorical(logits=z.view(-1, A, B)) with
  * log_prob(action).sum(-1) and entropy().sum(-1) (MLPDiscreteActorCritic.evaluate_actions,

@@ -2,7 +2,7 @@
 
 * f16_split3_bf16: the parts are [mid | lo | hi] with hi = bf16(v), and mid + lo + hi reproduces
   every fp32 input to within 2^-24 relative; a width that is not a multiple of 8 gets zero pad
-  columns in each part.
+  columns in each part; the six-part layout repeats [lo | hi | hi].
 * f16_bias_act_split: act(y + b) equal to torch's F.linear bias add followed by nn.ReLU /
   nn.Identity (bit for bit, NaN kept by relu) or nn.Tanh (within 1 ulp), and its split.
 * f16_act_grad_split: torch's threshold_backward / tanh_backward / identity, its split, and the
@@ -61,6 +61,17 @@ def test_split3_pads_parts(cuda):
     assert float(((back - x.double()).abs() / x.double().abs().clamp_min(1e-30)).max()) <= 2.0 ** -24
 
 
+def test_split3_six_parts(cuda):
+    sm = pkg_module("splitmm")
+    g = torch.Generator(device=cuda).manual_seed(9)
+    x = torch.randn(777, 84, device=cuda, generator=g)
+    s3, s6 = sm.split3(x), sm.split3(x, 6)
+    assert s6.shape == (777, 528) and torch.equal(s6[:, :264], s3)
+    lo, hi = s3[:, 88:176], s3[:, 176:264]
+    assert torch.equal(s6[:, 264:352], lo) and torch.equal(s6[:, 352:440], hi) and torch.equal(s6[:, 440:], hi)
+    assert sm.parts_for(512, 184) == 6 and sm.parts_for(88, 512) == 3
+
+
 @pytest.mark.parametrize("act", ["none", "relu", "tanh"])
 def test_bias_act_split(cuda, act):
     sm = pkg_module("splitmm")
@@ -73,7 +84,7 @@ def test_bias_act_split(cuda, act):
     pre = y + b
     ref = {"none": pre, "relu": torch.relu(pre), "tanh": torch.tanh(pre)}[act]
     yk = y.clone()
-    hs = sm.bias_act_split(yk, b, code, True)
+    hs = sm.bias_act_split(yk, b, code, 3)
     assert bool(torch.isnan(yk[5, 7]))
     fin = torch.isfinite(ref)
     if act == "tanh":
@@ -85,7 +96,13 @@ def test_bias_act_split(cuda, act):
     keep = torch.isfinite(back)
     assert bool(keep.sum() == fin.sum())
     assert float(((back - yk.double())[keep].abs() / yk.double()[keep].abs().clamp_min(1e-30)).max()) <= 2.0 ** -24
-    assert sm.bias_act_split(y.clone(), b, code, False) is None
+    assert sm.bias_act_split(y.clone(), b, code, 0) is None
+    y6 = y.clone()
+    hs6 = sm.bias_act_split(y6, b, code, 6)
+    bits, bits6 = hs.view(torch.int16), hs6.view(torch.int16)     # bitwise: the planted NaN included
+    assert torch.equal(y6[fin], yk[fin]) and torch.equal(bits6[:, :264], bits)
+    assert torch.equal(bits6[:, 264:352], bits[:, 88:176]) and torch.equal(bits6[:, 352:440], bits[:, 176:264])
+    assert torch.equal(bits6[:, 440:528], bits[:, 176:264])
 
 
 @pytest.mark.parametrize("act", ["none", "relu", "tanh"])
