@@ -55,6 +55,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--tf32", action="store_true", help="ppo workload: TF32 matmuls in the update (below the "
                                                          "reference's fp32; reported in dtype)")
+    p.add_argument("--breakdown", action="store_true", help="ppo workload: print the per-kernel device time of "
+                                                              "one extra, untimed iteration to stderr")
     p.add_argument("--workload", default="fdm",
                    choices=["fdm", "obs", "rollout", "ppo", "mlp", "seed", "external", "warmup", "payoff"],
                    help="fdm = configs[1] headline (default); obs = configs[2] fused obs/reward kernel; "
@@ -522,6 +524,26 @@ def run_rollout(args, dev, world, rank):
 PPO_OPP = 16
 
 
+def own_kernel_launches(step, dev, top=20):
+    """(launches of this build's kernels in one call of `step`, per-kernel device-time table) from
+    torch's profiler; the call is untimed."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize(dev)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step()
+        torch.cuda.synchronize(dev)
+    ev = [e for e in prof.key_averages() if e.device_type.name == "CUDA"]
+    own = sum(e.count for e in ev if "f16::" in e.key.split("(")[0])
+    ev.sort(key=lambda e: -e.device_time_total)
+    tot = sum(e.device_time_total for e in ev) or 1.0
+    lines = [f"device time per call {tot / 1e3:.1f} ms (profiled, untimed); top kernels:"]
+    for e in ev[:top]:
+        lines.append(f"  {e.device_time_total / 1e3:9.2f} ms {100 * e.device_time_total / tot:5.1f}% "
+                     f"x{e.count:<5d} {e.key[:110]}")
+    return own, "\n".join(lines)
+
+
 def run_ppo(args, dev, world, rank):
     """one PPO league iteration per step on every rank: a 64-step rollout of 131,072
     envs against 16 frozen opponents (env blocks), then 4 epochs x 16 minibatches of clipped PPO
@@ -598,14 +620,18 @@ def run_ppo(args, dev, world, rank):
     e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
-    launches_per_rollout = ROLL_T * ((4 if world > 1 else 3) + 5) + 3
+    # one more iteration, untimed, under torch's profiler: this build's kernels (namespace f16)
+    # are counted from its launch list, and --breakdown prints the per-kernel device time
+    launches_per_iteration, table = own_kernel_launches(t.iteration, dev)
+    if rank == 0 and args.breakdown:
+        print(table, file=sys.stderr, flush=True)
     if rank == 0:
         nparams = sum(p.numel() for p in t.model.parameters())
         line = {"metric": "decision-steps/s over full PPO iterations (rollout + update)", "value": value,
                 "unit": "decision-steps/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_it,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64+bf16 (update " + ("tf32" if args.tf32 else
                                                  "fp32-level: bf16x3-split products, fp32 accumulate, "
-                                                 "within 4x of SGEMM error") + ")",
+                                                 "errors at or below SGEMM's") + ")",
                 "data": "synthetic ICs, random-init networks",
                 "config": {"workload": "configs[4]: PPO league iteration, 131,072 envs per GPU, T=64, 4 epochs x 16 "
                                        "minibatches, clip 0.2, 16 frozen opponents, NCCL gradient allreduce",
@@ -618,7 +644,7 @@ def run_ppo(args, dev, world, rank):
                 "e2e": {"value": world * units / (float(e_ms.item()) * 1e-3), "unit": "decision-steps/s",
                         "h2d_bytes_per_step": 0, "d2h_bytes_per_step": d2h,
                         "api": "PPOTrainer.iteration, learner parameters to host", "steps": 1},
-                "gpu_launches": K * launches_per_rollout, "clocks": clk.summary()}
+                "gpu_launches": K * launches_per_iteration, "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     del t
     if world > 1:

@@ -8,9 +8,11 @@
 * f16_act_grad_split: torch's threshold_backward / tanh_backward / identity, its split, and the
   bias gradient (the column sums) against fp64 sums.
 * A SplitBlock product (forward, input gradient, weight gradient) against fp64 references: errors
-  no larger than 4x those of fp32 SGEMM on the same operands and below 5e-6 of the largest
-  output (TF32 products are near 1e-3), for the update's layer shapes (184 -> 512, 512 -> 512,
-  512 -> 84 with zero-padded parts) with 65,536 rows.
+  no larger than 2.5x those of fp32 SGEMM on the same operands and below 2e-6 of the largest
+  output (measured: 0.2-1.7x SGEMM's at 65,536 rows, below SGEMM's at the update's 524,288;
+  TF32 products are 2e-4..1.4e-3), for the update's layer shapes (184 -> 512, 512 -> 512,
+  512 -> 84 with zero-padded parts) with 65,536 rows, and 512 -> 512 at the update's 524,288-row
+  minibatch (pytest -s prints the errors).
 * A whole actor tower (84 logits) and critic tower (the value head fused into the last hidden
   layer) through run_tower against the same tower in fp64: output within 1e-5 relative, every
   parameter gradient within 1e-5 for tanh towers; for relu towers within 3x the error of torch's
@@ -129,12 +131,11 @@ def test_act_grad_split(cuda, act):
     assert float(((gb.double() - want).abs() / scale).max()) <= 1e-6
 
 
-@pytest.mark.parametrize("k,n", [(184, 512), (512, 512), (512, 84)])
-def test_split_linear_matches_fp64(cuda, k, n):
+@pytest.mark.parametrize("k,n,m", [(184, 512, 65536), (512, 512, 65536), (512, 84, 65536), (512, 512, 524288)])
+def test_split_linear_matches_fp64(cuda, k, n, m):
     sm = pkg_module("splitmm")
     torch.backends.cuda.matmul.allow_tf32 = False
     g = torch.Generator(device=cuda).manual_seed(k + n)
-    m = 65536
     x = torch.randn(m, k, device=cuda, generator=g).requires_grad_(True)
     w = (torch.randn(n, k, device=cuda, generator=g) / k ** 0.5).requires_grad_(True)
     b = torch.randn(n, device=cuda, generator=g).requires_grad_(True)
@@ -146,9 +147,10 @@ def test_split_linear_matches_fp64(cuda, k, n):
     rgx, rgw = gd @ wd, gd.t() @ xd
     y32 = x.detach() @ w.detach().t() + b.detach()
     gx32, gw32 = gy @ w.detach(), gy.t() @ x.detach()
-    for got, ref, base in ((y.detach(), ry, y32), (x.grad, rgx, gx32), (w.grad, rgw, gw32)):
+    for what, got, ref, base in (("y", y.detach(), ry, y32), ("dx", x.grad, rgx, gx32), ("dW", w.grad, rgw, gw32)):
         e, e32 = rel(got, ref), rel(base, ref)
-        assert e <= max(4.0 * e32, 1e-7) and e <= 5e-6, (e, e32)
+        print(f"{m} x {k} -> {n} {what}: split {e:.2g}, SGEMM {e32:.2g} (relative to the largest |fp64|)")
+        assert e <= max(2.5 * e32, 1e-7) and e <= 2e-6, (e, e32)
     assert rel(b.grad, gd.sum(0)) <= 1e-6
 
 
