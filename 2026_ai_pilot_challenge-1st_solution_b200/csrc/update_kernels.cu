@@ -32,6 +32,7 @@ namespace upd {
 
 constexpr int THREADS = 256;
 constexpr int MAX_GRAD_COLS = 4 * THREADS;   // one column group of 4 per thread of a block
+constexpr int GRAD_UNROLL = 4;               // rows per pass of k_act_grad_split
 
 __host__ __device__ __forceinline__ int part_of(int cols) { return (cols + 7) & ~7; }
 
@@ -176,34 +177,50 @@ __global__ void __launch_bounds__(THREADS) k_act_grad_split(const float* __restr
   if (slot < RS) {
     const int64_t r0 = (int64_t)blockIdx.x * rpb;
     const int64_t r1 = r0 + rpb < rows ? r0 + rpb : rows;
-    for (int64_t r = r0 + slot; r < r1; r += RS) {
-      __nv_bfloat16* o = gys + r * ldgs + c;
-      if (c >= cols) {
-        zero_store(o, part, six);
-        continue;
+    // GRAD_UNROLL rows per pass: all their loads are issued before any is used, so each thread
+    // keeps several 16-byte loads in flight; rows are still summed in order r, r + RS, ...
+    for (int64_t rb = r0 + slot; rb < r1; rb += (int64_t)GRAD_UNROLL * RS) {
+      float4 gl[GRAD_UNROLL], hl[GRAD_UNROLL];
+      float gr[GRAD_UNROLL];
+#pragma unroll
+      for (int u = 0; u < GRAD_UNROLL; u++) {
+        const int64_t r = rb + (int64_t)u * RS;
+        gr[u] = 0.0f;
+        gl[u] = hl[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (r >= r1 || c >= cols) continue;
+        if (gv) {   // the value head's input gradient g_v[r] wv[c], formed here instead of read
+          gr[u] = gv[r];
+          gl[u] = make_float4(__fmul_rn(gr[u], w.x), __fmul_rn(gr[u], w.y), __fmul_rn(gr[u], w.z),
+                              __fmul_rn(gr[u], w.w));
+        } else {
+          gl[u] = *reinterpret_cast<const float4*>(gh + r * ldg + c);
+        }
+        hl[u] = act == F16_ACT_NONE && !gv ? gl[u] : *reinterpret_cast<const float4*>(h + r * ldh + c);
       }
-      float4 g;
-      if (gv) {   // the value head's input gradient g_v[r] wv[c], formed here instead of read
-        const float gr = gv[r];
-        g = make_float4(__fmul_rn(gr, w.x), __fmul_rn(gr, w.y), __fmul_rn(gr, w.z), __fmul_rn(gr, w.w));
-      } else {
-        g = *reinterpret_cast<const float4*>(gh + r * ldg + c);
+#pragma unroll
+      for (int u = 0; u < GRAD_UNROLL; u++) {
+        const int64_t r = rb + (int64_t)u * RS;
+        if (r >= r1) break;
+        __nv_bfloat16* o = gys + r * ldgs + c;
+        if (c >= cols) {
+          zero_store(o, part, six);
+          continue;
+        }
+        const float4 g = gl[u], hv = hl[u];
+        const float a[4] = {act_bwd(g.x, hv.x, act), act_bwd(g.y, hv.y, act), act_bwd(g.z, hv.z, act),
+                            act_bwd(g.w, hv.w, act)};
+        acc.x = __fadd_rn(acc.x, a[0]);
+        acc.y = __fadd_rn(acc.y, a[1]);
+        acc.z = __fadd_rn(acc.z, a[2]);
+        acc.w = __fadd_rn(acc.w, a[3]);
+        if (gv) {   // the value weight's gradient: column sums of g_v[r] h[r][c]
+          acc_v.x = __fmaf_rn(gr[u], hv.x, acc_v.x);
+          acc_v.y = __fmaf_rn(gr[u], hv.y, acc_v.y);
+          acc_v.z = __fmaf_rn(gr[u], hv.z, acc_v.z);
+          acc_v.w = __fmaf_rn(gr[u], hv.w, acc_v.w);
+        }
+        split_store(a, o, part, six);
       }
-      const float4 hv = act == F16_ACT_NONE && !gv ? g : *reinterpret_cast<const float4*>(h + r * ldh + c);
-      const float a[4] = {act_bwd(g.x, hv.x, act), act_bwd(g.y, hv.y, act), act_bwd(g.z, hv.z, act),
-                          act_bwd(g.w, hv.w, act)};
-      acc.x = __fadd_rn(acc.x, a[0]);
-      acc.y = __fadd_rn(acc.y, a[1]);
-      acc.z = __fadd_rn(acc.z, a[2]);
-      acc.w = __fadd_rn(acc.w, a[3]);
-      if (gv) {   // the value weight's gradient: column sums of g_v[r] h[r][c]
-        const float gr = gv[r];
-        acc_v.x = __fmaf_rn(gr, hv.x, acc_v.x);
-        acc_v.y = __fmaf_rn(gr, hv.y, acc_v.y);
-        acc_v.z = __fmaf_rn(gr, hv.z, acc_v.z);
-        acc_v.w = __fmaf_rn(gr, hv.w, acc_v.w);
-      }
-      split_store(a, o, part, six);
     }
   }
   red[tid] = acc;
