@@ -283,11 +283,12 @@ __device__ __forceinline__ int64_t cat_action(const void* action, int act_bytes,
                         : reinterpret_cast<const int64_t*>(action)[i];
 }
 
-// l (normalised logits), p and the entropy H of one group of B logits held in l on entry.
-__device__ __forceinline__ float cat_group(float (&l)[CAT_MAXB], float (&p)[CAT_MAXB], int B, bool& nan) {
+// l (normalised logits), p and the entropy H of one group of B <= NB logits held in l on entry.
+template <int NB>
+__device__ __forceinline__ float cat_group(float (&l)[NB], float (&p)[NB], int B, bool& nan) {
   float mx = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < CAT_MAXB; j++)
+  for (int j = 0; j < NB; j++)
     if (j < B) {
       nan |= l[j] != l[j];
       mx = fmaxf(mx, l[j]);
@@ -295,26 +296,26 @@ __device__ __forceinline__ float cat_group(float (&l)[CAT_MAXB], float (&p)[CAT_
   if (fabsf(mx) == INFINITY) mx = 0.0f;
   float sum = 0.0f;
 #pragma unroll
-  for (int j = 0; j < CAT_MAXB; j++)
+  for (int j = 0; j < NB; j++)
     if (j < B) sum = __fadd_rn(sum, expf(__fsub_rn(l[j], mx)));
   const float lse = __fadd_rn(logf(sum), mx);
   float m2 = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < CAT_MAXB; j++)
+  for (int j = 0; j < NB; j++)
     if (j < B) {
       l[j] = __fsub_rn(l[j], lse);
       m2 = fmaxf(m2, l[j]);
     }
   float s2 = 0.0f;
 #pragma unroll
-  for (int j = 0; j < CAT_MAXB; j++)
+  for (int j = 0; j < NB; j++)
     if (j < B) {
       p[j] = expf(__fsub_rn(l[j], m2));
       s2 = __fadd_rn(s2, p[j]);
     }
   float acc = 0.0f;
 #pragma unroll
-  for (int j = 0; j < CAT_MAXB; j++)
+  for (int j = 0; j < NB; j++)
     if (j < B) {
       p[j] = __fdiv_rn(p[j], s2);
       acc = __fadd_rn(acc, __fmul_rn(fmaxf(l[j], -FLT_MAX), p[j]));
@@ -322,6 +323,7 @@ __device__ __forceinline__ float cat_group(float (&l)[CAT_MAXB], float (&p)[CAT_
   return -acc;
 }
 
+template <int NB>
 __global__ void __launch_bounds__(CAT_THREADS) k_cat_fwd(const float* __restrict__ z, int64_t ldz, int64_t M, int A,
                                                          int B, bool vec, const void* __restrict__ action,
                                                          int act_bytes, float* __restrict__ logp,
@@ -335,16 +337,16 @@ __global__ void __launch_bounds__(CAT_THREADS) k_cat_fwd(const float* __restrict
   __syncthreads();
   const int r = threadIdx.x / A, a = threadIdx.x - r * A;
   if (r < nrow) {
-    float l[CAT_MAXB], p[CAT_MAXB];
+    float l[NB], p[NB];
     const float* row = s + r * (W + 1) + a * B;
 #pragma unroll
-    for (int j = 0; j < CAT_MAXB; j++) l[j] = j < B ? row[j] : 0.0f;
+    for (int j = 0; j < NB; j++) l[j] = j < B ? row[j] : 0.0f;
     bool nan = false;
     const float H = cat_group(l, p, B, nan);
     const int64_t act = cat_action(action, act_bytes, (r0 + r) * A + a);
     float lp = 0.0f;
 #pragma unroll
-    for (int j = 0; j < CAT_MAXB; j++)
+    for (int j = 0; j < NB; j++)
       if (j == act) lp = l[j];
     grp[threadIdx.x] = make_float2(lp, H);
     const bool bad = act < 0 || act >= B;
@@ -366,6 +368,7 @@ __global__ void __launch_bounds__(CAT_THREADS) k_cat_fwd(const float* __restrict
 // dz = g_lp (onehot(action) - p) - g_ent p (max(l, -FLT_MAX) + H) per group (the gradient of
 // g_lp log_prob + g_ent entropy through logsumexp, softmax and the clamp); absent upstream
 // gradients count as zero.
+template <int NB>
 __global__ void __launch_bounds__(CAT_THREADS) k_cat_bwd(const float* __restrict__ z, int64_t ldz, int64_t M, int A,
                                                          int B, bool vec, const void* __restrict__ action,
                                                          int act_bytes, const float* __restrict__ g_lp,
@@ -383,14 +386,14 @@ __global__ void __launch_bounds__(CAT_THREADS) k_cat_bwd(const float* __restrict
     const int64_t m = r0 + r;
     const float gl = g_lp ? g_lp[m] : 0.0f;
     const float ge = g_ent ? g_ent[m] : 0.0f;
-    float l[CAT_MAXB], p[CAT_MAXB];
+    float l[NB], p[NB];
 #pragma unroll
-    for (int j = 0; j < CAT_MAXB; j++) l[j] = j < B ? row[j] : 0.0f;
+    for (int j = 0; j < NB; j++) l[j] = j < B ? row[j] : 0.0f;
     bool nan = false;
     const float H = cat_group(l, p, B, nan);
     const int64_t act = cat_action(action, act_bytes, m * A + a);
 #pragma unroll
-    for (int j = 0; j < CAT_MAXB; j++)
+    for (int j = 0; j < NB; j++)
       if (j < B) {
         const float d = __fsub_rn(j == act ? 1.0f : 0.0f, p[j]);
         const float e = __fmul_rn(p[j], __fadd_rn(fmaxf(l[j], -FLT_MAX), H));
@@ -500,7 +503,8 @@ extern "C" int f16_categorical_fwd(const float* logits, int64_t ldz, int64_t M, 
   if (!logp || !ent || !flags) return F16_ERR_ARG;
   const int R = upd::CAT_THREADS / A;
   const unsigned grid = (unsigned)((M + R - 1) / R);
-  upd::k_cat_fwd<<<grid, upd::CAT_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  auto k = B == 21 ? upd::k_cat_fwd<21> : upd::k_cat_fwd<upd::CAT_MAXB>;   // the reference's 21 bins, exact size
+  k<<<grid, upd::CAT_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       logits, ldz, M, A, B, cat_vec(logits, ldz, A * B), action, act_bytes, logp, ent, flags);
   return launch_status();
 }
@@ -513,7 +517,8 @@ extern "C" int f16_categorical_bwd(const float* logits, int64_t ldz, int64_t M, 
   if (!gz || ldg < A * B) return F16_ERR_ARG;
   const int R = upd::CAT_THREADS / A;
   const unsigned grid = (unsigned)((M + R - 1) / R);
-  upd::k_cat_bwd<<<grid, upd::CAT_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  auto k = B == 21 ? upd::k_cat_bwd<21> : upd::k_cat_bwd<upd::CAT_MAXB>;
+  k<<<grid, upd::CAT_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       logits, ldz, M, A, B, cat_vec(logits, ldz, A * B), action, act_bytes, g_lp, g_ent, gz, ldg);
   return launch_status();
 }

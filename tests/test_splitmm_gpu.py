@@ -226,25 +226,28 @@ def _torch_head(z, a, A=4, B=21):
     return dist.log_prob(a.long()).sum(-1), dist.entropy().sum(-1)
 
 
-@pytest.mark.parametrize("adtype", [torch.uint8, torch.int64])
-def test_categorical_head_matches_torch(cuda, adtype):
+@pytest.mark.parametrize("adtype,A,B", [(torch.uint8, 4, 21), (torch.int64, 4, 21), (torch.uint8, 3, 13)])
+def test_categorical_head_matches_torch(cuda, adtype, A, B):
     cat = pkg_module("categorical")
     g = torch.Generator(device=cuda).manual_seed(8)
-    m = 30001
-    z = (torch.randn(m, 84, device=cuda, generator=g) * 4).requires_grad_(True)
+    m, W = 30001, A * B
+    z = (torch.randn(m, W, device=cuda, generator=g) * 4).requires_grad_(True)
     with torch.no_grad():
-        z[3, 0:21] = -float("inf")
+        z[3, 0:B] = -float("inf")
         z[3, 5] = 2.0
-        z[7, 30] = 1e30
-    a = torch.randint(0, 21, (m, 4), device=cuda, generator=g).to(adtype)
+        z[7, B + 9] = 1e30
+    a = torch.randint(0, B, (m, A), device=cuda, generator=g).to(adtype)
     a[3, 0] = 5
     g_lp = torch.randn(m, device=cuda, generator=g)
-    g_ent = torch.randn(m, device=cuda, generator=g)
-    lp, ent = cat.logp_entropy(z, a, 4, 21)
+    # the update's upstream entropy gradient is -ent_coef / rows, far below 1: torch clamps -inf
+    # logits at -FLT_MAX, so on a row with -inf logits an entropy gradient above 1 in magnitude
+    # overflows inside its softmax backward (inf * 0 = NaN) where the kernel returns the limit 0
+    g_ent = torch.randn(m, device=cuda, generator=g) * 1e-2
+    lp, ent = cat.logp_entropy(z, a, A, B)
     (lp * g_lp + ent * g_ent).sum().backward()
     gz = z.grad.clone()
     z.grad = None
-    rlp, rent = _torch_head(z, a)
+    rlp, rent = _torch_head(z, a, A, B)
     (rlp * g_lp + rent * g_ent).sum().backward()
     for got, ref in ((lp, rlp), (ent, rent), (gz, z.grad)):
         got, ref = got.detach(), ref.detach()
@@ -252,11 +255,11 @@ def test_categorical_head_matches_torch(cuda, adtype):
         assert float((got - ref).abs().max()) <= 1e-5 * max(1.0, float(ref.abs().max()))
     # log-prob only (the entropy unused): its gradient path alone
     z.grad = None
-    lp, _ = cat.logp_entropy(z, a, 4, 21)
+    lp, _ = cat.logp_entropy(z, a, A, B)
     lp.sum().backward()
     gz = z.grad.clone()
     z.grad = None
-    _torch_head(z, a)[0].sum().backward()
+    _torch_head(z, a, A, B)[0].sum().backward()
     # p enters as exp(z - logsumexp) in torch's logsumexp backward and as the softmax of the
     # normalised logits here: a few ulps apart
     assert float((gz - z.grad).abs().max()) <= 1e-5 * max(1.0, float(z.grad.abs().max()))
