@@ -288,6 +288,21 @@ def _in_parts(layer):
     return parts_for(layer.out_features, part_width(layer.in_features))
 
 
+def _input_split(x, parts):
+    """split3(x, parts) for a tower's input, kept on the tensor so a second tower on the same
+    input (the critic after the actor, on one minibatch) reuses it; the tensor's version
+    counter invalidates it if x is modified in place."""
+    cached = getattr(x, "_f16_split", None)
+    if cached is not None and cached[0] == parts and cached[1] == x._version:
+        return cached[2]
+    xs = split3(x.detach(), parts)
+    try:
+        x._f16_split = (parts, x._version, xs)
+    except (AttributeError, RuntimeError):
+        pass
+    return xs
+
+
 def split_linear(x, weight, bias, act=ACT_NONE):
     """act(F.linear(x, weight, bias)) through one SplitBlock."""
     xs = split3(x.detach(), parts_for(weight.shape[0], part_width(weight.shape[1])))
@@ -313,7 +328,7 @@ def run_tower(seq, x):
             i += 1
             continue
         if xs is None:
-            xs = split3(x.detach(), _in_parts(m))
+            xs = _input_split(x, _in_parts(m))
         head = mods[i + 2] if act_mod is not None and i + 3 == len(mods) else None
         if (isinstance(head, nn.Linear) and head.out_features == 1 and head.in_features == m.out_features
                 and m.out_features % 8 == 0 and head.bias is not None):

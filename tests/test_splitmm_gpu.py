@@ -283,3 +283,23 @@ def test_categorical_head_validates(cuda):
         cat.logp_entropy(zn, a, 4, 21)
     with pytest.raises(ValueError):
         _torch_head(zn, a)
+
+
+def test_tower_input_split_reused_and_invalidated(cuda):
+    sm = pkg_module("splitmm")
+    tr = pkg_module("trainer")
+    torch.manual_seed(12)
+    actor = tr.mlp(184, (512, 512), 84, "relu").to(cuda)
+    critic = tr.mlp(184, (512, 512), 1, "relu").to(cuda)
+    x = torch.randn(4096, 184, device=cuda)
+    a1 = sm.run_tower(actor, x)
+    xs = x._f16_split[2]
+    v1 = sm.run_tower(critic, x)
+    assert x._f16_split[2] is xs                     # the critic reused the actor's split
+    ref = sm.run_tower(critic, x.clone())
+    assert torch.equal(v1, ref)
+    x.mul_(2.0)                                      # in place: the cached split is stale
+    v2 = sm.run_tower(critic, x)
+    assert x._f16_split[2] is not xs
+    assert torch.equal(v2, sm.run_tower(critic, x.clone()))
+    assert torch.equal(a1, sm.run_tower(actor, (x / 2.0).clone()))
