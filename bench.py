@@ -137,9 +137,11 @@ def physical_gpu_index(local_rank):
 
 
 # --------------------------------------------------------------------------- CPU reference
-def cpu_reference_rate(nsample_per_thread=256, min_seconds=4.0, lineage="root"):
+def cpu_reference_sampler(nsample_per_thread=256, lineage="root"):
     """The reference's fdm.cuh (oracle/_ref) on all host threads over a bounded sample of the
-    cfg2 workload; returns (frames/s, threads, sample description, kind)."""
+    cfg2 workload, set up once: returns (run, threads, aircraft, kind); run(min_seconds) steps the
+    sample for at least that long (seeded ICs restored every RESEED_EVERY decisions) and returns
+    (frames/s, decisions)."""
     from oracle import fdm as ofdm
     ic = importlib.import_module(PKG + ".ic")
     kind = "reference"
@@ -154,38 +156,54 @@ def cpu_reference_rate(nsample_per_thread=256, min_seconds=4.0, lineage="root"):
     rows = ic.baseline_ics(n // 2, 20260102)
     seeds = ofdm.oracle_seed(rows, FCS_DT)
     rng = np.random.default_rng(7)
-    import torch
     grid = ic.action_grid(NUM_BINS).double().numpy()
-    frames, t0, reps = 0, time.perf_counter(), 0
-    s = seeds
-    while True:
-        if reps % RESEED_EVERY == 0:
-            s = seeds
-        b = rng.integers(0, NUM_BINS, (n, 4))
-        c = grid[b]
-        c[:, 3] = (0.5 * grid[b[:, 3]].astype(np.float32) + 0.5).astype(np.float64)
-        s, _ = step(s, c)
-        frames += n * SUBSTEPS
-        reps += 1
-        el = time.perf_counter() - t0
-        if el >= min_seconds:
-            break
-    sample = f"{n} aircraft x {reps} decisions x {SUBSTEPS} frames of the cfg2 workload"
-    return frames / el, threads, sample, kind
+    st = {"s": seeds, "reps": 0}
+
+    def run(min_seconds):
+        frames, reps, t0 = 0, 0, time.perf_counter()
+        while True:
+            if st["reps"] % RESEED_EVERY == 0:
+                st["s"] = seeds
+            b = rng.integers(0, NUM_BINS, (n, 4))
+            c = grid[b]
+            c[:, 3] = (0.5 * grid[b[:, 3]].astype(np.float32) + 0.5).astype(np.float64)
+            st["s"], _ = step(st["s"], c)
+            frames += n * SUBSTEPS
+            reps += 1
+            st["reps"] += 1
+            el = time.perf_counter() - t0
+            if el >= min_seconds:
+                return frames / el, reps
+
+    return run, threads, n, kind
+
+
+def cpu_reference_rate(nsample_per_thread=256, min_seconds=4.0, lineage="root"):
+    """One bounded sample of the reference on the host cores: (frames/s, threads, sample, kind)."""
+    run, threads, n, kind = cpu_reference_sampler(nsample_per_thread, lineage)
+    rate, reps = run(min_seconds)
+    return rate, threads, f"{n} aircraft x {reps} decisions x {SUBSTEPS} frames of the cfg2 workload", kind
+
+
+REF_ARM_SECONDS = 60.0      # CPU time of the whole --impl reference run, split evenly over its steps
 
 
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    vals, info = [], None
+    # each step a bounded sample sized so the whole run stays near REF_ARM_SECONDS of CPU time
+    run, thr, n, kind = cpu_reference_sampler()
+    per_step = max(0.02, REF_ARM_SECONDS / (args.warmup + args.steps))
+    vals, reps = [], 0
     for i in range(args.warmup + args.steps):
-        v, thr, sample, kind = cpu_reference_rate(min_seconds=1.0)
+        v, r = run(per_step)
         if i >= args.warmup:
             vals.append(v)
-            info = (thr, sample, kind)
+            reps += r
     val = float(np.mean(vals))
-    thr, sample, kind = info
+    sample = (f"{n} aircraft x {reps} decisions x {SUBSTEPS} frames of the cfg2 workload over {args.steps} "
+              f"steps of >= {per_step * 1e3:.0f} ms")
     line = {"metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * SUBSTEPS * 2 * NENV / val, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": val / REF_PUBLISHED, "dtype": "f64", "data": "synthetic",
