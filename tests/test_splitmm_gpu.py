@@ -46,7 +46,13 @@ def test_split3_reconstructs(cuda):
     g = torch.Generator(device=cuda).manual_seed(1)
     x = torch.randn(1000, 184, device=cuda, generator=g) * torch.exp(torch.randn(1000, 184, device=cuda, generator=g) * 5)
     s = sm.split3(x)
-    assert torch.equal(s[:, 368:], x.bfloat16())
+    hi = x.bfloat16()                                   # the terms restated with torch's RN casts
+    r1 = x - hi.float()
+    lo = r1.bfloat16()
+    mid = (r1 - lo.float()).bfloat16()
+    bits = lambda t: t.contiguous().view(torch.int16)
+    assert torch.equal(bits(s[:, 368:]), bits(hi)) and torch.equal(bits(s[:, 184:368]), bits(lo))
+    assert torch.equal(bits(s[:, :184]), bits(mid))
     back = recon(s, 184)
     assert float(((back - x.double()).abs() / x.double().abs().clamp_min(1e-30)).max()) <= 2.0 ** -24
 

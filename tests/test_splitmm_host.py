@@ -6,6 +6,9 @@
   reference's CPU update keeps plain fp32 torch arithmetic (and its golden test holds).
 * The fused categorical head only takes CUDA fp32 (M, A*B) logits within its size limits; the
   actor's evaluate_actions on CPU is torch.distributions.Categorical's.
+* The split's arithmetic (restated with torch's round-to-nearest casts on the CPU): both
+  differences x - hi and (x - hi) - lo are exact in fp32, so mid + lo + hi is within 2^-24 of x
+  across the whole normal range (the kernel's parts are pinned to this restatement on the GPU).
 """
 import torch
 
@@ -60,3 +63,19 @@ def test_categorical_head_eligibility_and_cpu_path():
     dist = torch.distributions.Categorical(logits=model.actor_logits(obs).view(-1, 4, 21))
     assert torch.equal(lp, dist.log_prob(act.long()).sum(-1))
     assert torch.equal(ent, dist.entropy().sum(-1))
+
+
+def test_split_arithmetic_is_exact_in_fp32():
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(200000, generator=g) * torch.exp(torch.randn(200000, generator=g) * 20)
+    x = x[torch.isfinite(x) & (x.abs() > 1e-30) & (x.abs() < 1e30)]
+    hi = x.bfloat16()
+    r1 = x - hi.float()
+    lo = r1.bfloat16()
+    r2 = r1 - lo.float()
+    mid = r2.bfloat16()
+    xd = x.double()
+    assert torch.equal(r1.double(), xd - hi.double())                      # exact differences
+    assert torch.equal(r2.double(), xd - hi.double() - lo.double())
+    back = hi.double() + lo.double() + mid.double()
+    assert float(((back - xd).abs() / xd.abs()).max()) <= 2.0 ** -24
