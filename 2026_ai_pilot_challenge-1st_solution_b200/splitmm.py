@@ -288,10 +288,16 @@ def _in_parts(layer):
     return parts_for(layer.out_features, part_width(layer.in_features))
 
 
+SHARE_SPLIT = "_f16_share_split"     # set True on an input tensor to keep its split for reuse
+
+
 def _input_split(x, parts):
-    """split3(x, parts) for a tower's input, kept on the tensor so a second tower on the same
-    input (the critic after the actor, on one minibatch) reuses it; the tensor's version
-    counter invalidates it if x is modified in place."""
+    """split3(x, parts) for a tower's input.  An input marked with SHARE_SPLIT (the trainer marks
+    each minibatch's observations) keeps its split on the tensor, so a second tower on the same
+    input (the critic after the actor) reuses it; the tensor's version counter invalidates it if
+    x is modified in place.  Unmarked inputs keep nothing (no memory held past the call)."""
+    if not getattr(x, SHARE_SPLIT, False):
+        return split3(x.detach(), parts)
     cached = getattr(x, "_f16_split", None)
     if cached is not None and cached[0] == parts and cached[1] == x._version:
         return cached[2]

@@ -229,6 +229,7 @@ def _ppo_update(model, actor_opt, critic_opt, cfg, obs, act, old_logp, b_val, ad
         for s in range(0, count, mb_size):
             mb = perm[s:s + mb_size]
             mb_obs = obs_f.index_select(0, mb)
+            setattr(mb_obs, splitmm.SHARE_SPLIT, True)   # actor and critic share its split
             new_logp, entropy = model.evaluate_actions(mb_obs, act_f.index_select(0, mb))
             log_ratio = new_logp - old_logp_f.index_select(0, mb)
             ratio = log_ratio.exp()

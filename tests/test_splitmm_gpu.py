@@ -297,7 +297,11 @@ def test_tower_input_split_reused_and_invalidated(cuda):
     torch.manual_seed(12)
     actor = tr.mlp(184, (512, 512), 84, "relu").to(cuda)
     critic = tr.mlp(184, (512, 512), 1, "relu").to(cuda)
+    y = torch.randn(4096, 184, device=cuda)
+    sm.run_tower(actor, y)
+    assert not hasattr(y, "_f16_split")              # unmarked inputs keep nothing
     x = torch.randn(4096, 184, device=cuda)
+    setattr(x, sm.SHARE_SPLIT, True)
     a1 = sm.run_tower(actor, x)
     xs = x._f16_split[2]
     v1 = sm.run_tower(critic, x)
