@@ -46,3 +46,24 @@ def test_entry_points_reject_bad_arguments_before_any_launch():
     assert lib.f16_fdm_step(ctypes.cast(buf, ctypes.c_void_p), 7, 2, 2, ctypes.cast(buf, ctypes.c_void_p),
                             6, 1 / 60, None, None) == 1
     assert lib.f16_seed_ic(None, 4, None, 0, 4, 1 / 60, None) == 1
+
+
+def test_update_entry_points_reject_bad_arguments_before_any_launch():
+    """The PPO-update kernels' entry points check shapes, part counts, activation codes and the
+    categorical head's limits on the host (F16_ERR_ARG = 1) before any launch."""
+    lib = pkg_module("_lib").load()
+    buf = (ctypes.c_float * 4096)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    assert lib.f16_split3_bf16(None, 4, 8, 8, p, 24, 3, None) == 1
+    assert lib.f16_split3_bf16(p, 4, 6, 8, p, 24, 3, None) == 1          # cols not a multiple of 4
+    assert lib.f16_split3_bf16(p, 4, 8, 8, p, 24, 5, None) == 1          # parts must be 3 or 6
+    assert lib.f16_split3_bf16(p, 4, 8, 8, p, 40, 6, None) == 1          # row stride below 6 parts
+    assert lib.f16_bias_act_split(p, 4, 8, 8, p, 3, None, 0, 3, None) == 1   # unknown activation
+    assert lib.f16_bias_act_split(p, 4, 8, 8, p, 1, p, 16, 3, None) == 1     # split row stride too small
+    assert lib.f16_act_grad_split(p, 8, None, 8, 4, 8, 1, p, 24, 3, p, 1, None) == 1   # relu without h
+    assert lib.f16_act_grad_split(p, 2048, p, 2048, 4, 2048, 0, p, 6144, 3, p, 1, None) == 1  # > 1024 cols
+    assert lib.f16_bias_act_value(p, 4, 8, 8, p, 1, None, p, p, None) == 1            # no head weight
+    assert lib.f16_act_grad_split_value(p, p, p, 8, 4, 8, 1, p, 24, 3, p, p, 0, None) == 1   # nblk 0
+    assert lib.f16_categorical_fwd(p, 84, 4, 4, 33, p, 1, p, p, p, None) == 1      # B > 32
+    assert lib.f16_categorical_fwd(p, 84, 4, 4, 21, p, 2, p, p, p, None) == 1      # action bytes 2
+    assert lib.f16_categorical_bwd(p, 84, 4, 4, 21, p, 1, None, None, p, 80, None) == 1   # ldg < A*B
