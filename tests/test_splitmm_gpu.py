@@ -17,7 +17,8 @@
   layer) through run_tower against the same tower in fp64: output within 1e-5 relative, every
   parameter gradient within 1e-5 for tanh towers; for relu towers within 3x the error of torch's
   own fp32 tower (ReLU mask flips at pre-activations within rounding of zero move whole
-  gradient rows in any fp32 evaluation).
+  gradient rows in any fp32 evaluation); the reference's final shape (three 384-wide tanh
+  layers) within 1e-5 for both towers.
 * The fused categorical head against torch.distributions.Categorical: log-prob, entropy and the
   logits gradient within 1e-5, infinite logits included; NaN logits and out-of-range actions
   raise ValueError as torch's argument validation does.
@@ -313,3 +314,30 @@ def test_tower_input_split_reused_and_invalidated(cuda):
     assert x._f16_split[2] is not xs
     assert torch.equal(v2, sm.run_tower(critic, x.clone()))
     assert torch.equal(a1, sm.run_tower(actor, (x / 2.0).clone()))
+
+
+@pytest.mark.parametrize("out_dim", [84, 1])
+def test_tower_reference_final_shape(cuda, out_dim):
+    """The reference's final model shape (three 384-wide tanh layers): actor and critic towers
+    through run_tower within 1e-5 of fp64, output and every parameter gradient."""
+    sm = pkg_module("splitmm")
+    tr = pkg_module("trainer")
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(13)
+    net = tr.mlp(184, (384, 384, 384), out_dim, "tanh").to(cuda)
+    with torch.no_grad():
+        for mod in net:
+            if isinstance(mod, torch.nn.Linear):
+                mod.bias.normal_(0.0, 0.1)
+    ref_net = tr.mlp(184, (384, 384, 384), out_dim, "tanh").double().to(cuda)
+    ref_net.load_state_dict({k: v.double() for k, v in net.state_dict().items()})
+    g = torch.Generator(device=cuda).manual_seed(14)
+    x = torch.randn(30000, 184, device=cuda, generator=g)
+    gout = torch.randn(30000, out_dim, device=cuda, generator=g)
+    out = sm.run_tower(net, x)
+    out.backward(gout)
+    ref = ref_net(x.double())
+    ref.backward(gout.double())
+    assert rel(out.detach(), ref.detach()) <= 1e-5
+    for p, q in zip(net.parameters(), ref_net.parameters()):
+        assert rel(p.grad, q.grad) <= 1e-5
