@@ -22,7 +22,10 @@ import re
 import sys
 from pathlib import Path
 
-SRC_DEFAULT = "/root/reference/cuda_fdm/gen/f16_gen.cuh"
+# The reference checkout: $F16_REFERENCE, else a "reference" directory beside this repository.
+import os  # noqa: E402
+REF_ROOT = Path(os.environ.get("F16_REFERENCE") or Path(__file__).resolve().parents[3] / "reference")
+SRC_DEFAULT = str(REF_ROOT / "cuda_fdm" / "gen" / "f16_gen.cuh")
 
 
 def parse(path):

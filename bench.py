@@ -137,6 +137,14 @@ def physical_gpu_index(local_rank):
 
 
 # --------------------------------------------------------------------------- CPU reference
+def host_cores():
+    """Host cores available to this process (its CPU affinity set)."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return max(1, os.cpu_count() or 1)
+
+
 def cpu_reference_sampler(nsample_per_thread=256, lineage="root"):
     """The reference's fdm.cuh (oracle/_ref) on all host threads over a bounded sample of the
     cfg2 workload, set up once: returns (run, threads, aircraft, kind); run(min_seconds) steps the
@@ -146,8 +154,9 @@ def cpu_reference_sampler(nsample_per_thread=256, lineage="root"):
     ic = importlib.import_module(PKG + ".ic")
     kind = "reference"
     if ofdm.ref_available(lineage):
-        lib = ofdm.ref_lib(lineage)
-        threads = int(lib.f16ref_max_threads())
+        # every host core this process may run on, passed explicitly: under torchrun the
+        # environment sets OMP_NUM_THREADS=1, which the OpenMP default would follow
+        threads = host_cores()
         step = lambda s, c: ofdm.ref_step(s, c, SUBSTEPS, lineage, with_obs=True, nthreads=threads)
     else:                                      # the C restatement, one core
         kind, threads = "port", 1
@@ -217,18 +226,45 @@ def run_reference_arm(args):
 
 
 # --------------------------------------------------------------------------- GPU arm
+# Kernel sources behind each committed ncu summary: a summary's traffic figure is used only while
+# the sha256 of these files still equals the `kernel_source_sha16:` line the summary records.
+PROFILE_SOURCES = {
+    "fdm_step_cfg2.md": ["fdm_kernels.cu", "fdm_device.cuh", "f16_tables.h", "common.cuh"],
+    "obs_step_cfg3.md": ["obs_kernels.cu", "obs_device.cuh", "common.cuh"],
+    "mlp_policy_cfg4.md": ["mlp_kernels.cu", "common.cuh"],
+}
+
+
+def kernel_source_sha16(name):
+    import hashlib
+    h = hashlib.sha256()
+    for f in PROFILE_SOURCES[name]:
+        h.update((ROOT / PKG / "csrc" / f).read_bytes())
+    return h.hexdigest()[:16]
+
+
 def profile_traffic(name="fdm_step_cfg2.md"):
-    """DRAM bytes per launch of the summarised kernel from a committed ncu summary (or None)."""
+    """(DRAM bytes per launch, note) of the summarised kernel from a committed ncu summary.  The
+    figure is returned only when the summary's recorded source hash matches the current kernel
+    sources; otherwise (None, reason), so an edited kernel never reports a stale capture."""
     p = ROOT / "profiles" / name
     if not p.exists():
-        return None
+        return None, "no ncu summary committed"
+    vals = {}
     for ln in p.read_text().splitlines():
-        if ln.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(ln.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+        if ":" in ln and ln.split(":", 1)[0].strip() in ("traffic_bytes_per_launch", "kernel_source_sha16"):
+            k, v = ln.split(":", 1)
+            vals[k.strip()] = v.strip()
+    try:
+        cur = kernel_source_sha16(name)
+    except (KeyError, OSError):
+        return None, "kernel sources unknown"
+    if vals.get("kernel_source_sha16") != cur:
+        return None, f"ncu summary {name} predates the current kernel sources (sha16 {cur}); not re-captured"
+    try:
+        return float(vals["traffic_bytes_per_launch"]), f"ncu capture summarised in profiles/{name} (sources sha16 {cur})"
+    except (KeyError, ValueError):
+        return None, f"profiles/{name} has no traffic line"
 
 
 OBS_NENV = 262_144          # BASELINE configs[2]
@@ -322,6 +358,7 @@ def run_obs(args, dev, world, rank):
         dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
     peak, peak_src = peak_of("hbm_gbs")
     achieved = OBS_BYTES_PER_ENV * nenv / (ms * 1e-3) / 1e9
+    obs_traffic = profile_traffic("obs_step_cfg3.md")
     if rank == 0:
         line = {"metric": "fused obs184+reward+termination envs/s", "value": value, "unit": "envs/s",
                 "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
@@ -333,7 +370,7 @@ def run_obs(args, dev, world, rank):
                         "api": "BatchObsReward.kernel_step on host state/actions, obs + reward back to host"},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak if peak else None,
-                             "traffic": profile_traffic("obs_step_cfg3.md"), "kernel": "k_obs_step",
+                             "traffic": obs_traffic[0], "traffic_source": obs_traffic[1], "kernel": "k_obs_step",
                              "bytes_per_unit": OBS_BYTES_PER_ENV, "unit_basis": "environment",
                              "peak_source": peak_src},
                 "gpu_launches": K, "clocks": clk.summary()}
@@ -497,6 +534,7 @@ def run_rollout(args, dev, world, rank):
 
     peak, peak_src = peak_of("bf16_tflops_sustained")
     achieved = (ACTOR_FLOP + CRITIC_FLOP) * ROLL_NENV / (main_ms * 1e-3) / 1e12
+    mlp_traffic = profile_traffic("mlp_policy_cfg4.md")
     # this library's kernels per rollout: per decision the norm update (3 kernels; 4 when the
     # statistics are all-reduced), normalise, actor+critic, opponents, FDM, post-step; then
     # normalise + bootstrap critic + GAE
@@ -507,7 +545,7 @@ def run_rollout(args, dev, world, rank):
         cpu = None
         if not args.no_cpu_baseline and world == 1:
             v, thr, kind, sample = _cpu_rollout_rate(tr.MLPActorCritic(hidden=(512, 512), activation="relu"),
-                                                      os.cpu_count() or 1)
+                                                      host_cores())
             cpu = {"value": v, "unit": "decision-steps/s", "cores": thr, "kind": kind, "sample": sample}
         line = {"metric": "decision-steps/s (env step + obs/reward + actor sample)", "value": value,
                 "unit": "decision-steps/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms,
@@ -526,7 +564,7 @@ def run_rollout(args, dev, world, rank):
                         "steps": Ke},
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak if peak else None,
-                             "traffic": profile_traffic("mlp_policy_cfg4.md"),
+                             "traffic": mlp_traffic[0], "traffic_source": mlp_traffic[1],
                              "kernel": "k_policy (main actor + critic, one launch per decision)",
                              "flop_per_unit": ACTOR_FLOP + CRITIC_FLOP, "unit_basis": "env-decision",
                              "peak_source": peak_src},
@@ -839,6 +877,7 @@ def run_mlp(args, dev, world, rank):
     ms = float(np.mean([a.elapsed_time(b) for a, b in es]))
     peak, peak_src = peak_of("bf16_tflops")
     achieved = (ACTOR_FLOP + CRITIC_FLOP) * n / (ms * 1e-3) / 1e12
+    mlp_traffic = profile_traffic("mlp_policy_cfg4.md")
     if rank == 0:
         line = {"metric": "actor+critic rows/s (k_policy alone)", "value": world * n / (ms * 1e-3), "unit": "rows/s",
                 "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
@@ -847,7 +886,7 @@ def run_mlp(args, dev, world, rank):
                                        "(sampled bins, log-prob, env commands) + critic 184-512-512-1",
                            "l2": "256 MB flush and a fresh input copy before each timed launch"},
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                             "frac": achieved / peak, "traffic": profile_traffic("mlp_policy_cfg4.md"),
+                             "frac": achieved / peak, "traffic": mlp_traffic[0], "traffic_source": mlp_traffic[1],
                              "kernel": "k_policy", "flop_per_unit": ACTOR_FLOP + CRITIC_FLOP, "unit_basis": "row",
                              "peak_source": peak_src + " (burst: one launch timed alone)"},
                 "gpu_launches": K, "clocks": clk.summary()}
@@ -968,8 +1007,10 @@ def main():
     value = world * frames_per_step / (ms_step * 1e-3)
 
     # ---- e2e through the reference-facing API: host actions in, obs17 back to the host ----
+    # The e2e leg draws its own Ke decisions of commands: the timed leg's buffer holds only W + K
+    # rows, and Ke is independent of K.
     Ke = max(1, args.e2e_steps)
-    host_cmd = cmd[W:W + Ke].cpu().pin_memory()
+    host_cmd = commands(Ke).cpu().pin_memory()
     host_obs = torch.empty(nac, 17, dtype=torch.float64).pin_memory()
     sim.states_soa.copy_(seeds)
     for k in range(2):                      # untimed: the API's side streams and first launches
@@ -1008,7 +1049,7 @@ def main():
     torch.cuda.synchronize(dev)
     peak_tflops = flops.value / (pe0.elapsed_time(pe1) * 1e-3) / 1e12
     achieved_tflops = FLOP_PER_FRAME * frames_per_step / (ms_rank * 1e-3) / 1e12
-    traffic = profile_traffic()
+    traffic, traffic_src = profile_traffic("fdm_step_cfg2.md")
 
     if world > 1:
         dist.barrier()
@@ -1032,7 +1073,7 @@ def main():
                            "(2 aircraft slices on two streams: copies overlap the physics of the other slice)",
                     "steps": Ke},
             "roofline": {"bound": "fp64", "achieved": achieved_tflops, "peak": peak_tflops, "unit": "TFLOP/s",
-                         "frac": achieved_tflops / peak_tflops, "traffic": traffic,
+                         "frac": achieved_tflops / peak_tflops, "traffic": traffic, "traffic_source": traffic_src,
                          "kernel": "k_fdm_step", "flop_per_unit": FLOP_PER_FRAME, "unit_basis": "aircraft-frame",
                          "peak_source": "measured: FP64 DFMA-chain probe (f16_probe_fp64) on this GPU"},
             "gpu_launches": K,

@@ -10,7 +10,7 @@
   (research/competition_36500/runtime/cuda_fdm/gen/obs_kernel.cu with external_observation.cu),
   host-compiled through ref_obs_driver.cpp.
 
-The ``_ref`` builds need the reference tree (the ``F16_REFERENCE`` directory, default: the local reference checkout); on a
+The ``_ref`` builds need the reference tree (``$F16_REFERENCE``, else a ``reference`` directory beside this repository); on a
 machine without it they are skipped and the previously built files are used as they are.
 Flags follow the reference's own host validation: ``-O2 -ffp-contract=off``.
 """
@@ -20,7 +20,9 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("F16_REFERENCE", "/root/reference"))
+# The reference checkout: $F16_REFERENCE, else a "reference" directory beside this repository;
+# where neither exists the _ref builds are skipped.
+REF = Path(os.environ.get("F16_REFERENCE") or HERE.parent.parent / "reference")
 CFLAGS = ["-O2", "-ffp-contract=off", "-fPIC", "-shared"]
 REF_LINEAGES = {
     "root": REF / "cuda_fdm" / "gen",

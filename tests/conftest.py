@@ -44,5 +44,7 @@ def cuda():
 
 
 def reference_tree():
-    p = Path(os.environ.get("F16_REFERENCE", "/root/reference"))
+    """The reference checkout ($F16_REFERENCE, else a "reference" directory beside this
+    repository), or None where it is absent (tests that need it skip with that message)."""
+    p = Path(os.environ.get("F16_REFERENCE") or ROOT.parent / "reference")
     return p if (p / "cuda_fdm").exists() else None

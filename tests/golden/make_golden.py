@@ -23,7 +23,7 @@ from pathlib import Path
 import numpy as np
 
 ROOT = Path(__file__).resolve().parents[2]
-REF = Path(os.environ.get("F16_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("F16_REFERENCE") or ROOT.parent / "reference")
 OUT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(OUT))
