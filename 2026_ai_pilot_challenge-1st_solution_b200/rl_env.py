@@ -163,12 +163,11 @@ class GpuDogfightVecEnv:
         return self.obr.kernel_build_obs(self.sim.states).view(self.nenv, 2, self.OBS_SIZE)
 
     # ---- reset (rl_env.py:368-441) ----
-    def reset(self, stagger=True, max_stagger_steps=256, warmup_action_fn=None, sync_free=True):
+    def reset(self, stagger=True, max_stagger_steps=256, warmup_action_fn=None):
         """Fresh ICs for every env; with ``stagger`` each env is then advanced a random number of
-        valid steps (rl_env.py:386-441).  ``sync_free`` (default) runs that warm-up entirely on
-        the device (departed envs re-seeded from the IC pool); ``sync_free=False`` follows the
-        reference loop, which checks masks on the host every step and re-seeds departed envs with
-        freshly sampled ICs."""
+        valid steps in [0, max_stagger_steps) (the reference's staggered start, rl_env.py:386-441),
+        entirely on the device: departed envs are re-seeded from the IC pool and the host is
+        never synchronised inside the warm-up."""
         seeds = self._build_all_seeds()
         if not bool(torch.isfinite(seeds).all()):
             raise FloatingPointError("non-finite initial physical states")
@@ -176,10 +175,7 @@ class GpuDogfightVecEnv:
         self.obr.reset_all()
         self.obr.kernel_init_reward_state(self.sim.states)
         if stagger and max_stagger_steps > 0:
-            if sync_free:
-                self._staggered_warmup_device(max_stagger_steps, warmup_action_fn)
-            else:
-                self._staggered_warmup(max_stagger_steps, warmup_action_fn)
+            self._staggered_warmup_device(max_stagger_steps, warmup_action_fn)
         return self.obr.kernel_build_obs(self.sim.states).view(self.nenv, 2, self.OBS_SIZE)
 
     def _staggered_warmup_device(self, max_steps, action_fn, check_every=0):
@@ -199,9 +195,12 @@ class GpuDogfightVecEnv:
         self.obr.restore(obr_buf)
         self.obr.kernel_init_reward_state(self.sim.states)
 
-    def _warmup_loop_device(self, max_steps, action_fn, targ, check_every=0):
+    def _warmup_loop_device(self, max_steps, action_fn, targ, check_every=0, pool_picks=None):
         """Loop of _staggered_warmup_device; returns (captured states, captured reconstruction
-        buffers, finite flag), all on the device."""
+        buffers, finite flag), all on the device.  ``pool_picks`` optionally fixes the IC-pool row
+        each env would be re-seeded from: a (max_steps + 1, nenv) int64 device tensor, row i used
+        at step i and the last row for the envs never captured (default: uniform draws on the
+        device)."""
         dev = self.device
         age = torch.zeros(self.nenv, dtype=torch.long, device=dev)
         captured_mask = targ == 0
@@ -210,8 +209,9 @@ class GpuDogfightVecEnv:
         warm_finite = torch.ones((), dtype=torch.bool, device=dev)
         st3 = self.sim.states.view(self.nenv, 2, STATE_N)
 
-        def reseed(mask):
-            pick = torch.randint(0, self.ic_pool_size, (self.nenv,), device=dev)
+        def reseed(mask, i):
+            pick = (pool_picks[i] if pool_picks is not None
+                    else torch.randint(0, self.ic_pool_size, (self.nenv,), device=dev))
             st3.copy_(torch.where(mask.view(-1, 1, 1), self.ic_pool[pick], st3))
             self.obr.reset_envs(mask)
             self.obr.kernel_init_reward_state(self.sim.states, mask)
@@ -227,7 +227,7 @@ class GpuDogfightVecEnv:
             self.obr.kernel_advance(self.sim.states, a.contiguous(), cfg=self.reward_cfg,
                                     min_alt=self.min_altitude_m, max_time=self.max_engage_time_s)
             dep = self._departed_envs(self.state9_flat()) & (~captured_mask)
-            reseed(dep)
+            reseed(dep, i)
             age = torch.where(dep, torch.zeros_like(age), age) + (~captured_mask).long()
             hit = (~captured_mask) & (age == targ)
             captured.copy_(torch.where(hit.repeat_interleave(2).view(-1, 1), self.sim.states, captured))
@@ -236,80 +236,24 @@ class GpuDogfightVecEnv:
             if check_every > 0 and (i + 1) % check_every == 0 and bool(captured_mask.all()):
                 break
         rest = ~captured_mask                                   # still short of their phase
-        reseed(rest)
+        reseed(rest, max_steps)
         captured.copy_(torch.where(rest.repeat_interleave(2).view(-1, 1), self.sim.states, captured))
         self.obr.capture_where(obr_buf, rest)
         return captured, obr_buf, warm_finite
 
-    def _staggered_warmup(self, max_steps, action_fn):
-        """Advance each env a random number of valid steps in [0, max_steps) and capture it there;
-        envs that depart (altitude < 100 m or non-finite) are re-seeded and restart their count."""
-        dev = self.device
-        targ = torch.tensor(self.rng.integers(0, max_steps, size=self.nenv), device=dev)
-        age = torch.zeros(self.nenv, dtype=torch.long, device=dev)
-        captured_mask = targ == 0
-        captured = self.sim.states.clone()
-        obr_buf = self.obr.clone_state()
-        warm_finite = torch.ones((), dtype=torch.bool, device=dev)
-        for _ in range(max_steps):
-            if action_fn is None:
-                a = self._random_actions()
-            else:
-                a = action_fn(self.obr.kernel_build_obs(self.sim.states)).to(torch.float64).reshape(self.nac, 4)
-            self.sim.step(a, substeps=self.substeps)
-            fin = torch.isfinite(self.sim.states).view(self.nenv, 2, STATE_N).all(dim=2).all(dim=1)
-            warm_finite.logical_and_((fin | captured_mask).all())
-            self.obr.kernel_advance(self.sim.states, a.contiguous(), cfg=self.reward_cfg,
-                                    min_alt=self.min_altitude_m, max_time=self.max_engage_time_s)
-            s9 = self.state9_flat()
-            dep = self._departed_envs(s9) & (~captured_mask)
-            if bool(dep.any()):
-                self._seed_envs(torch.nonzero(dep, as_tuple=False).flatten().tolist())
-                self.obr.reset_envs(dep)
-                self.obr.kernel_init_reward_state(self.sim.states, dep)
-                age[dep] = 0
-            age = age + (~captured_mask).long()
-            hit = (~captured_mask) & (age == targ)
-            if bool(hit.any()):
-                rows = hit.repeat_interleave(2)
-                captured[rows] = self.sim.states[rows]
-                self.obr.capture_into(obr_buf, hit)
-                captured_mask |= hit
-            if bool(captured_mask.all()):
-                break
-        if not bool(captured_mask.all()):
-            rest = ~captured_mask
-            self._seed_envs(torch.nonzero(rest, as_tuple=False).flatten().tolist())
-            self.obr.reset_envs(rest)
-            self.obr.kernel_init_reward_state(self.sim.states, rest)
-            rows = rest.repeat_interleave(2)
-            captured[rows] = self.sim.states[rows]
-            self.obr.capture_into(obr_buf, rest)
-        if not bool(warm_finite):
-            raise FloatingPointError("non-finite physical trajectory during staggered initialization")
-        self.sim.states.copy_(captured)
-        self.obr.restore(obr_buf)
-        self.obr.kernel_init_reward_state(self.sim.states)
-
     def _departed_envs(self, s9_flat=None, floor_m=100.0):
-        s9 = (self.state9() if s9_flat is None else s9_flat.view(self.nenv, 2, 9))
-        alt = -s9[:, :, S9["D"]]
-        bad = (alt < floor_m) | (~torch.isfinite(s9).all(dim=2))
-        return bad.any(dim=1)
-
-    def _seed_envs(self, env_indices):
-        if not env_indices:
-            return
-        rows = self._initialize_physical_seeds(self._sample_ic_rows(len(env_indices)))
-        ac = torch.tensor([2 * e + k for e in env_indices for k in (0, 1)], device=self.device)
-        self.sim.states[ac] = rows
+        """Per env: True when either aircraft is below ``floor_m`` of MSL altitude or has a
+        non-finite 9-DoF state (the warm-up's departure test)."""
+        s9 = self.state9() if s9_flat is None else s9_flat.view(self.nenv, 2, 9)
+        ok = torch.isfinite(s9).all(dim=2) & (s9[:, :, S9["D"]] <= -floor_m)
+        return ~ok.all(dim=1)
 
     def _random_actions(self):
-        """Warm-up actions: sticks U(-0.2, 0.2), throttle U(0.6, 0.9) (rl_env.py:468-473)."""
-        a = torch.empty(self.nac, 4, dtype=torch.float64, device=self.device)
-        a[:, 0:3].uniform_(-0.2, 0.2)
-        a[:, 3].uniform_(0.6, 0.9)
-        return a
+        """Warm-up commands (rl_env.py:468-473): the three sticks uniform in [-0.2, 0.2], throttle
+        uniform in [0.6, 0.9], one row per aircraft."""
+        lo = torch.tensor([-0.2, -0.2, -0.2, 0.6], dtype=torch.float64, device=self.device)
+        span = torch.tensor([0.4, 0.4, 0.4, 0.3], dtype=torch.float64, device=self.device)
+        return torch.rand(self.nac, 4, dtype=torch.float64, device=self.device) * span + lo
 
     def _to_nac4(self, actions):
         a = torch.as_tensor(actions, dtype=torch.float64, device=self.device)

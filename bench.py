@@ -785,7 +785,7 @@ def run_aux(args, dev, world, rank):
     elif args.workload == "warmup":
         rl_env = importlib.import_module(PKG + ".rl_env")
         env = rl_env.GpuDogfightVecEnv(ROLL_NENV, substeps=SUBSTEPS, seed=20260105 + rank, device=dev)
-        go = lambda: env.reset(stagger=True, sync_free=True)
+        go = lambda: env.reset(stagger=True)
         go()
         torch.cuda.synchronize(dev)
         with ClockSampler(clk_idx) as clk:
