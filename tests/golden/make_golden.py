@@ -12,8 +12,8 @@ fdm_cfg1.npz  BASELINE configs[0]: 64 envs x 2 F-16s, seeded ICs (altitude U(6,9
               repository-root lineage, FCS dt 1/120).
 fdm_r36.npz   the same ICs (first 16 envs) through the research/competition_36500 lineage
               (FCS dt 1/60) seed builder and fdm.cuh, 60 frames.
-obs_traj.npz, gae.npz, norm.npz, ppo_update.npz: see make_obs_golden, make_gae_golden,
-              make_norm_golden and make_ppo_golden below.
+obs_traj.npz, gae.npz, norm.npz, ppo_update.npz, payoff.npz: see make_obs_golden,
+              make_gae_golden, make_norm_golden, make_ppo_golden and make_payoff_golden below.
 """
 import importlib
 import os
@@ -322,9 +322,106 @@ def make_ppo_golden(seed=20260106):
     print("ppo_update.npz", res["epochs"], res["early"], res["optimizer_steps"])
 
 
+def make_payoff_golden(seed=20260107, per_order=4, capacity=3, nright=3, nsteps=14):
+    """payoff.npz: the reference's own batched payoff loop (R/cuda_fdm/batched_payoff.py
+    evaluate_chunk, scoring :131-156, summaries via PPOGPUTrainer._summarize_clean_pair,
+    ppo_gpu.py:1517-1575) run on CPU with a scripted environment whose step returns the
+    payoff_case.payoff_steps() terminal values; stores each matchup's scores, crash flags,
+    completion step and summary (without the bootstrap interval, which is league statistics)."""
+    import json
+    import types
+    import torch
+    from payoff_case import payoff_steps
+    r36 = REF / "research" / "competition_36500" / "runtime"
+    for k in list(sys.modules):
+        if k == "cuda_fdm" or k.startswith("cuda_fdm.") or k == "claude_code" or k.startswith("claude_code."):
+            del sys.modules[k]
+    sys.path.insert(0, str(r36))
+    sys.path.insert(0, str(REF / "src"))
+    import cuda_fdm.batched_payoff as BP
+    import cuda_fdm.ppo_gpu as P
+    lanes = 2 * per_order
+    nenv = lanes * capacity
+    script = payoff_steps(seed, nenv, nsteps)
+
+    class Obr:
+        dt = 0.1
+
+        def reset_all(self):
+            pass
+
+        def kernel_init_reward_state(self, states, env_mask=None):
+            pass
+
+        def kernel_build_obs(self, states, env_mask=None):
+            return torch.zeros(2 * nenv, 184)
+
+    class Env:
+        OBS_SIZE = 184
+        max_engage_time_s = (nsteps - 4) * 0.1
+        min_altitude_m = 304.8
+        ic_pool_size = 16
+
+        def __init__(self):
+            self.nenv = nenv
+            self.obr = Obr()
+            self.sim = types.SimpleNamespace(states=torch.zeros(2 * nenv, 101), load_seed=lambda t: None)
+            self.k = 0
+
+        def step(self, controls, reset_indices=None):
+            d = script[self.k]
+            self.k += 1
+            info = {"terminal_hp": torch.as_tensor(d["hp"]), "terminal_alt_m": torch.as_tensor(d["alt"]),
+                    "terminal_state_finite": torch.as_tensor(d["finite"])}
+            return (torch.zeros(nenv, 2, 184), torch.as_tensor(d["reward"]), torch.as_tensor(d["done"]), info)
+
+    class Template:
+        ic_pool, ic_pool_size = torch.zeros(16, 2, 101), 16
+        _evaluation_seed_bank = torch.zeros(lanes * 2, 101)
+
+        def reset_evaluation(self, paired=True, seed_block=0):
+            pass
+
+        def _ensure_ic_pool(self):
+            pass
+
+    class Net:
+        num_bins = 21
+
+        def actor_logits(self, x):
+            return torch.zeros(x.shape[0], 84)
+
+    recorded = []
+    trainer = types.SimpleNamespace(cfg=types.SimpleNamespace(seed=5, device="cpu", num_bins=21),
+                                    grid=P.make_action_grid(21, "cpu"), _batch_captured_actions=False,
+                                    _outcome_summary=P.PPOGPUTrainer._outcome_summary)
+    trainer._league_eval_env = lambda blocks: (Template(), per_order)
+    trainer._batched_payoff_env = ((capacity, per_order), Env())
+
+    def summarize(*a):
+        recorded.append([np.asarray(x.detach().cpu().numpy()) if torch.is_tensor(x) else x for x in a])
+        return P.PPOGPUTrainer._summarize_clean_pair(trainer, *a)
+    trainer._summarize_clean_pair = summarize
+    pol = (Net(), None, None)
+    res = BP.evaluate_chunk(trainer, pol, [pol] * nright, lanes, 0, capacity)
+    out = {"seed": np.array(seed), "per_order": np.array(per_order), "capacity": np.array(capacity),
+           "nright": np.array(nright), "nsteps": np.array(nsteps), "min_alt": np.array(Env.min_altitude_m)}
+    for i, (r, rec) in enumerate(zip(res, recorded)):
+        scores, own, opp, po, sb, es, st = rec
+        out[f"scores{i}"] = scores.astype(np.float32)
+        out[f"own{i}"] = own.astype(np.uint8)
+        out[f"opp{i}"] = opp.astype(np.uint8)
+        out[f"final_step{i}"] = np.array(st)
+        r = {k: v for k, v in r.items() if k not in ("lcb95", "ucb95")}
+        out[f"summary{i}"] = np.array(json.dumps(r, sort_keys=True))
+    np.savez_compressed(OUT / "payoff.npz", **out)
+    print("payoff.npz", [int(out[f"final_step{i}"]) for i in range(nright)])
+
+
 if __name__ == "__main__":
     main()
     make_obs_golden()
     make_gae_golden()
     make_norm_golden()
     make_ppo_golden()
+    make_payoff_golden()

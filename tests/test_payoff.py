@@ -1,86 +1,79 @@
 """Batched payoff scoring oracle (CPU).
 
-oracle/payoff.py restates the per-lane scoring of R/cuda_fdm/batched_payoff.py:131-156.  Here
-it is pinned against a line-by-line torch transcription of those expressions (the reference
-computes them inline in evaluate_chunk, which needs its trainer and a CUDA env) over random
-multi-step inputs with ties, altitude losses, double kills and non-finite values, and against
-hand-scored cases.  summarize_pair's counts are checked against the oracle's outcome_summary.
+oracle/payoff.py restates the per-lane scoring of R/cuda_fdm/batched_payoff.py:131-156.  It is
+pinned to the reference itself: tests/golden/payoff.npz holds what the reference's own
+``evaluate_chunk`` loop (scoring inline at :131-156, summaries from
+PPOGPUTrainer._summarize_clean_pair, ppo_gpu.py:1517-1575) produced on CPU for a scripted
+sequence of terminal values (tests/golden/payoff_case.py; ties, 1e-9 HP margins, altitude losses,
+non-finite values on finished lanes).  Replaying the same steps through the oracle must give the
+reference's scores, crash flags and completion steps, and ``payoff.summarize_pair`` its summary
+fields.  Hand-scored cases cover both seat orders.
 """
-import numpy as np
-import torch
+import json
+import sys
 
-from conftest import pkg_module
+import numpy as np
+
+from conftest import GOLDEN, pkg_module
 from oracle import payoff as OP
 
-
-def torch_reference_step(st, done, hp, alt, finite, reward, left_slot, min_alt, lanes, step):
-    """batched_payoff.py:131-156 as written (torch, nenv lanes, the reference's names)."""
-    nenv = done.shape[0]
-    all_rows = torch.arange(nenv)
-    active = ~st["finished"]
-    fin = (finite & torch.isfinite(hp).all(dim=1) & torch.isfinite(alt).all(dim=1)
-           & torch.isfinite(reward).all(dim=1))
-    finite_ok = bool((fin | ~active).all())
-    newly = done.bool() & active
-    lhp, rhp = hp[all_rows, left_slot], hp[all_rows, 1 - left_slot]
-    lalt, ralt = alt[all_rows, left_slot], alt[all_rows, 1 - left_slot]
-    ld = (lhp <= 0) | (lalt < min_alt)
-    rd = (rhp <= 0) | (ralt < min_alt)
-    alive = ~ld & ~rd
-    win = (rd & ~ld) | (alive & (lhp > rhp + 1e-9))
-    loss = (ld & ~rd) | (alive & (lhp < rhp - 1e-9))
-    st["scores"] = torch.where(newly, win.float() + .5 * (~win & ~loss).float(), st["scores"])
-    st["own"] = torch.where(newly, lalt < min_alt, st["own"])
-    st["opp"] = torch.where(newly, ralt < min_alt, st["opp"])
-    st["finished"] |= newly
-    done_m = st["finished"].view(-1, lanes).all(dim=1).tolist()
-    for i, d in enumerate(done_m):
-        if d and not st["steps"][i]:
-            st["steps"][i] = step
-    return finite_ok
+if str(GOLDEN) not in sys.path:
+    sys.path.insert(0, str(GOLDEN))
 
 
-def random_step(rng, nenv, p_done=0.3, p_bad=0.0):
-    hp = rng.choice([0.0, 0.25, 0.5, 0.5 + 5e-10, 0.5 + 2e-9, 1.0], size=(nenv, 2))
-    alt = rng.choice([200.0, 304.8, 304.9, 5000.0], size=(nenv, 2))
-    done = (rng.random(nenv) < p_done).astype(np.uint8)
-    finite = np.ones(nenv, np.uint8)
-    reward = rng.normal(size=(nenv, 2))
-    if p_bad:
-        bad = rng.random(nenv) < p_bad
-        hp[bad, 0] = np.nan
-    return done, hp, alt, finite, reward
+def replay_payoff_fixture(record):
+    """Replay payoff.npz's steps through ``record(step, d, left_slot, lanes, min_alt, state)`` (the
+    oracle or the kernel); returns (fixture, state) with state's arrays after the last step."""
+    from payoff_case import payoff_steps
+    g = np.load(GOLDEN / "payoff.npz")
+    per_order, capacity, nsteps = int(g["per_order"]), int(g["capacity"]), int(g["nsteps"])
+    lanes = 2 * per_order
+    nenv = lanes * capacity
+    left_slot = np.tile(np.repeat(np.array([0, 1], np.uint8), per_order), capacity)
+    state = dict(fin=np.zeros(nenv, np.uint8), sc=np.full(nenv, np.nan, np.float32), oc=np.zeros(nenv, np.uint8),
+                 pc=np.zeros(nenv, np.uint8), cnt=np.zeros(capacity, np.int64), fs=np.zeros(capacity, np.int64),
+                 bad=[])
+    for k, d in enumerate(payoff_steps(g["seed"], nenv, nsteps)):
+        record(k + 1, d, left_slot, lanes, float(g["min_alt"]), state)
+        if state["fs"].all():
+            break
+    return g, state
 
 
-def test_oracle_matches_reference_expressions():
-    rng = np.random.default_rng(7)
-    nenv, lanes, min_alt = 48, 8, 304.8
-    left_slot = (np.arange(nenv) % lanes >= lanes // 2).astype(np.uint8)
-    st = {"finished": torch.zeros(nenv, dtype=torch.bool), "scores": torch.full((nenv,), float("nan")),
-          "own": torch.zeros(nenv, dtype=torch.bool), "opp": torch.zeros(nenv, dtype=torch.bool),
-          "steps": [0] * (nenv // lanes)}
-    fin = np.zeros(nenv, np.uint8)
-    sc = np.full(nenv, np.nan, np.float32)
-    oc = np.zeros(nenv, np.uint8)
-    pc = np.zeros(nenv, np.uint8)
-    cnt = np.zeros(nenv // lanes, np.int64)
-    fs = np.zeros(nenv // lanes, np.int64)
-    for step in range(1, 13):
-        done, hp, alt, finite, reward = random_step(rng, nenv, p_bad=0.05 if step == 6 else 0.0)
-        if step == 12:
-            done[:] = 1
-        ok_ref = torch_reference_step(st, torch.as_tensor(done), torch.as_tensor(hp), torch.as_tensor(alt),
-                                      torch.as_tensor(finite.astype(bool)), torch.as_tensor(reward),
-                                      torch.as_tensor(left_slot.astype(np.int64)), min_alt, lanes, step)
-        bad = OP.payoff_record(done, hp.ravel(), alt.ravel(), finite, reward.ravel(), left_slot, lanes, min_alt,
-                               step, fin, sc, oc, pc, cnt, fs)
-        assert (bad == 0) == ok_ref
-        assert np.array_equal(fin.astype(bool), st["finished"].numpy())
-        np.testing.assert_array_equal(sc, st["scores"].numpy())
-        assert np.array_equal(oc.astype(bool), st["own"].numpy())
-        assert np.array_equal(pc.astype(bool), st["opp"].numpy())
-        assert fs.tolist() == st["steps"]
-    assert fin.all() and set(np.unique(sc).tolist()) <= {0.0, 0.5, 1.0}
+def oracle_record(step, d, left_slot, lanes, min_alt, st):
+    st["bad"].append(OP.payoff_record(d["done"].astype(np.uint8), d["hp"].ravel(), d["alt"].ravel(),
+                                      d["finite"].astype(np.uint8), d["reward"].ravel(), left_slot, lanes, min_alt,
+                                      step, st["fin"], st["sc"], st["oc"], st["pc"], st["cnt"], st["fs"]))
+
+
+def check_against_reference(g, st):
+    lanes = 2 * int(g["per_order"])
+    for i in range(int(g["nright"])):
+        r = slice(i * lanes, (i + 1) * lanes)
+        np.testing.assert_array_equal(st["sc"][r], g[f"scores{i}"])
+        assert st["oc"][r].tolist() == g[f"own{i}"].tolist()
+        assert st["pc"][r].tolist() == g[f"opp{i}"].tolist()
+        assert int(st["fs"][i]) == int(g[f"final_step{i}"])
+    assert not any(st["bad"]), "non-finite values fell only on finished lanes"
+
+
+def test_oracle_matches_reference_run():
+    g, st = replay_payoff_fixture(oracle_record)
+    check_against_reference(g, st)
+
+
+def test_summarize_pair_matches_reference_summary():
+    payoff = pkg_module("payoff")
+    g = np.load(GOLDEN / "payoff.npz")
+    po = int(g["per_order"])
+    for i in range(int(g["nright"])):
+        ref = json.loads(str(g[f"summary{i}"]))
+        got = payoff.summarize_pair(g[f"scores{i}"], g[f"own{i}"].astype(bool), g[f"opp{i}"].astype(bool), po,
+                                    int(g[f"final_step{i}"]), seed_block=ref["seed_block"],
+                                    eval_seed=ref["policy_rng_seed"])
+        assert set(got) == set(ref), set(got) ^ set(ref)
+        for k in ref:
+            assert got[k] == ref[k], (k, got[k], ref[k])
 
 
 def test_hand_scored_cases():

@@ -1,8 +1,8 @@
 """Batched payoff evaluation on a B200.
 
-* f16_payoff_record against oracle/payoff.py (itself pinned to the reference's expressions)
-  over twelve random steps: scores, crash flags, finished lanes, matchup completion step and
-  the non-finite count, bit for bit.
+* f16_payoff_record against oracle/payoff.py over twelve random steps: scores, crash flags,
+  finished lanes, matchup completion step and the non-finite count, bit for bit; and over the
+  steps of tests/golden/payoff.npz against what the reference's own evaluate_chunk loop scored.
 * BatchedPayoff with argmax policies: a matchup's result does not depend on the other
   matchups in the batch (rights [B, C, B] give matchups 0 and 2 identical results, equal to a
   run of [B] alone), with a normaliser on one policy and a 214-D external-observation policy.
@@ -63,6 +63,45 @@ def test_payoff_record_kernel_matches_oracle(cuda):
         assert dv["fs"].cpu().numpy().tolist() == o["fs"].tolist()
     assert o["fin"].all()
 
+
+
+def test_payoff_record_kernel_matches_reference_run(cuda):
+    """The kernel over payoff.npz's scripted steps gives the reference loop's scores, crash
+    flags and completion steps (batched_payoff.py:131-156 run on CPU when the fixture was made)."""
+    from test_payoff import check_against_reference, replay_payoff_fixture
+    _lib = pkg_module("_lib")
+    L = _lib.load()
+    dv = {}
+
+    def kernel_record(step, d, left_slot, lanes, min_alt, st):
+        nenv = d["done"].shape[0]
+        if not dv:
+            dv.update(fin=torch.zeros(nenv, dtype=torch.uint8, device=cuda),
+                      sc=torch.full((nenv,), float("nan"), device=cuda),
+                      oc=torch.zeros(nenv, dtype=torch.uint8, device=cuda),
+                      pc=torch.zeros(nenv, dtype=torch.uint8, device=cuda),
+                      cnt=torch.zeros(len(st["cnt"]), dtype=torch.int32, device=cuda),
+                      fs=torch.zeros(len(st["fs"]), dtype=torch.int32, device=cuda),
+                      bad=torch.zeros(1, dtype=torch.int32, device=cuda),
+                      ls=torch.as_tensor(left_slot, device=cuda))
+        t = {k: torch.as_tensor(np.ascontiguousarray(v), device=cuda)
+             for k, v in dict(done=d["done"].astype(np.uint8), hp=d["hp"].ravel(), alt=d["alt"].ravel(),
+                              finite=d["finite"].astype(np.uint8), reward=d["reward"].ravel()).items()}
+        dv["bad"].zero_()
+        a = _lib.PayoffArgs(done=t["done"].data_ptr(), terminal_hp=t["hp"].data_ptr(), terminal_alt=t["alt"].data_ptr(),
+                            finite=t["finite"].data_ptr(), reward=t["reward"].data_ptr(),
+                            left_slot=dv["ls"].data_ptr(), lanes=lanes, min_alt=min_alt, step=step,
+                            finished=dv["fin"].data_ptr(), scores=dv["sc"].data_ptr(), own_crash=dv["oc"].data_ptr(),
+                            opp_crash=dv["pc"].data_ptr(), finished_count=dv["cnt"].data_ptr(),
+                            final_step=dv["fs"].data_ptr(), nonfinite=dv["bad"].data_ptr())
+        _lib.check(L.f16_payoff_record(nenv, a, _lib.stream_of(dv["sc"])), "f16_payoff_record")
+        torch.cuda.synchronize()
+        st["bad"].append(int(dv["bad"].item()))
+        for k in ("fin", "sc", "oc", "pc", "cnt", "fs"):
+            st[k][:] = dv[k].cpu().numpy()
+
+    g, st = replay_payoff_fixture(kernel_record)
+    check_against_reference(g, st)
 
 def _policies(cuda):
     tr = pkg_module("trainer")
