@@ -151,3 +151,55 @@ def test_step_host_matches_step(cfg1, mods, cuda):
         torch.cuda.synchronize()
         torch.testing.assert_close(a.states, b.states, rtol=0, atol=0)
         torch.testing.assert_close(oa.cpu(), ob.reshape(128, 17), rtol=0, atol=0)
+
+
+def envelope_ics(n, seed):
+    """IC rows spread over the flight envelope's edges: 300 ft to 80,000 ft (troposphere,
+    tropopause and both stratosphere layers), 150 to 1,900 ft/s (subsonic through Mach ~1.9,
+    which runs the supersonic calibrated-airspeed iteration), alpha -15..45 deg, beta +-20 deg,
+    rolled / inverted / steep attitudes, nearly empty to full tanks."""
+    rng = np.random.default_rng(seed)
+    rows = np.zeros((n, 12))
+    rows[:, 0] = 37.24 + rng.uniform(-1.0, 1.0, n)
+    rows[:, 1] = 131.87 + rng.uniform(-1.0, 1.0, n)
+    rows[:, 2] = rng.choice([300.0, 5000.0, 36089.0, 45000.0, 65000.0, 80000.0], n)
+    rows[:, 3] = rng.choice([150.0, 400.0, 900.0, 1300.0, 1900.0], n)
+    rows[:, 4] = rng.choice([0.0, 90.0, -170.0], n)
+    rows[:, 5] = rng.choice([-80.0, 0.0, 60.0], n)
+    rows[:, 6] = rng.uniform(0.0, 360.0, n)
+    rows[:, 7] = rng.choice([-15.0, 0.0, 25.0, 45.0], n)
+    rows[:, 8] = rng.choice([-20.0, 0.0, 15.0], n)
+    rows[:, 9] = rng.choice([50.0, 3000.0, 6000.0], n)
+    return rows
+
+
+@pytest.mark.parametrize("fcs_dt", [1.0 / 120.0, 1.0 / 60.0])
+def test_envelope_edges_and_edge_commands(mods, cuda, fcs_dt):
+    """Extreme states under full-deflection / afterburner / idle / zero commands, 1, 2, 3 and 7
+    frames per launch: GPU vs oracle within the one-frame tolerance for one frame and within
+    1e-8 (scaled) over several, with non-finite values (if any) in the same places."""
+    ge, _ = mods
+    n = 256
+    rows = envelope_ics(n, 20260108)
+    seeds = ofdm.oracle_seed(rows, fcs_dt)
+    assert np.isfinite(seeds).all()
+    cmds_ = [np.tile([1.0, -1.0, 1.0, 1.0], (n, 1)), np.tile([-1.0, 1.0, -1.0, 0.0], (n, 1)),
+             np.zeros((n, 4)), np.tile([0.3, 0.44, -0.2, 0.55], (n, 1))]
+    worst = {}
+    for ci, c in enumerate(cmds_):
+        for ss in (1, 2, 3, 7):
+            sim = ge.GpuDogfight(n // 2, substeps=ss, fcs_dt=fcs_dt, device=cuda)
+            sim.load_seed(torch.as_tensor(seeds))
+            obs = sim.step(torch.as_tensor(c).to(cuda), substeps=ss).reshape(n, 17).cpu().numpy()
+            got = sim.states.cpu().numpy()
+            exp, exp_obs = ofdm.oracle_step(seeds, c, ss, fcs_dt)
+            fin = np.isfinite(exp)
+            assert np.array_equal(np.isfinite(got), fin), f"cmd {ci} ss {ss}: non-finite pattern differs"
+            rows_ok = fin.all(axis=1)
+            err = scaled_err(got[rows_ok], exp[rows_ok]).max()
+            oerr = scaled_err(obs[rows_ok], exp_obs[rows_ok]).max()
+            worst[(ci, ss)] = (err, oerr)
+            bound = TOL_FRAME if ss == 1 else 1e-8
+            assert err <= bound and oerr <= bound, f"cmd {ci} ss {ss}: state {err:.3e} obs17 {oerr:.3e}"
+    print("worst scaled error per (command, frames):",
+          {k: f"{v[0]:.1e}/{v[1]:.1e}" for k, v in worst.items()})

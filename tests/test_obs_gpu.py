@@ -127,37 +127,63 @@ def test_aux_features(OR, g, cuda):
     assert within(b.aux_features.cpu().numpy(), eaux, 1e-9)
 
 
-def test_large_random_batch_vs_oracle(OR, cuda):
-    """cfg3-style random pairs at 4,096 envs: fused step vs oracle advance + build."""
+def cfg3_rows(nenv, rng):
+    """BASELINE configs[2]'s state distribution: NED horizontal U(+-20 km), altitude U(1,12) km,
+    speed U(150,350) m/s along the body axis with alpha U(-2,6) deg, uniformly random attitude
+    quaternions (as roll / pitch / yaw), fuel 3000 lb."""
     ic = pkg_module("ic")
-    rng = np.random.default_rng(5)
-    nenv = 4096
-    rows = np.zeros((2 * nenv, 12))
-    lat, lon, alt_ft = ic.official_seed_latlon(rng.uniform(-2e4, 2e4, 2 * nenv), rng.uniform(-2e4, 2e4, 2 * nenv),
-                                               -rng.uniform(1000, 12000, 2 * nenv))
+    n = 2 * nenv
+    rows = np.zeros((n, 12))
+    lat, lon, alt_ft = ic.official_seed_latlon(rng.uniform(-2e4, 2e4, n), rng.uniform(-2e4, 2e4, n),
+                                               -rng.uniform(1000, 12000, n))
     rows[:, 0], rows[:, 1], rows[:, 2] = lat, lon, alt_ft
-    rows[:, 3] = rng.uniform(150, 350, 2 * nenv) / 0.3048
-    rows[:, 4] = rng.uniform(-180, 180, 2 * nenv)
-    rows[:, 5] = rng.uniform(-85, 85, 2 * nenv)
-    rows[:, 6] = rng.uniform(0, 360, 2 * nenv)
-    rows[:, 7] = rng.uniform(-5, 10, 2 * nenv)
+    rows[:, 3] = rng.uniform(150, 350, n) / 0.3048
+    q = rng.normal(size=(n, 4))
+    q /= np.linalg.norm(q, axis=1, keepdims=True)
+    w, x, y, z = q.T
+    rows[:, 4] = np.degrees(np.arctan2(2 * (w * x + y * z), 1 - 2 * (x * x + y * y)))
+    rows[:, 5] = np.degrees(np.arcsin(np.clip(2 * (w * y - z * x), -1, 1)))
+    rows[:, 6] = np.degrees(np.arctan2(2 * (w * z + x * y), 1 - 2 * (y * y + z * z))) % 360
+    rows[:, 7] = rng.uniform(-2, 6, n)
     rows[:, 9] = 3000.0
-    states = ofdm.oracle_seed(rows, 1.0 / 60.0)
+    return rows
+
+
+def test_configs2_full_size_vs_oracle(OR, cuda):
+    """BASELINE configs[2] at its full 262,144 envs x 2: every reconstruction buffer set from the
+    config's distributions (HP / fuel U(0,1), time U(0,200) s, body rates N(0,0.3) rad/s, random
+    action histories, previous attitudes 3 deg (one frame) away).  (1) The observation rebuild
+    alone, which reads the body-rate buffer as given, and (2) the fused advance + rebuild step (the
+    advance rewrites the body rates from the attitude change) against the oracle: observations
+    and rewards within 1e-5, flags exact, reconstruction buffers within 1e-9."""
+    ic = pkg_module("ic")
+    nenv = 262_144
+    nac = 2 * nenv
+    rng = np.random.default_rng(20260103)
+    rows = cfg3_rows(nenv, rng)
+    st_soa = ic.seed_states(rows, 1.0 / 60.0, device=cuda)
+    states = st_soa.t()
+    states_np = states.cpu().numpy()
     b = OR.BatchObsReward(nenv, device=cuda)
     o = ObsOracle(nenv)
-    hp = rng.uniform(0.0, 1.0, 2 * nenv)
-    t = rng.uniform(0, 200, nenv)
-    pqr = rng.normal(0, 0.3, (2 * nenv, 3))
-    b.hp.copy_(torch.as_tensor(hp)); o.hp[:] = hp
-    b.t_sec.copy_(torch.as_tensor(t)); o.t_sec[:] = t
-    b.prev_att.copy_(torch.as_tensor(rows[:, 4:7])); o.prev_att[:] = rows[:, 4:7]
-    b.prev_valid.fill_(True); o.prev_valid[:] = 1
-    act = rng.uniform(-1, 1, (2 * nenv, 4))
-    obs, rew, term, trunc = b.kernel_step(soa(states, cuda), torch.as_tensor(act).to(cuda))
-    er, et, etr = o.advance(states, act)
-    eobs = o.build_obs(states)
+    bufs = dict(hp=rng.uniform(0, 1, nac), fuel=rng.uniform(0, 1, nac), t_sec=rng.uniform(0, 200, nenv),
+                pqr=rng.normal(0, 0.3, (nac, 3)), act_hist=rng.uniform(-1, 1, (nac, 5, 4)),
+                prev_att=rows[:, 4:7] + rng.normal(0, 3.0, (nac, 3)))
+    for k, v in bufs.items():
+        getattr(b, k).copy_(torch.as_tensor(v))
+        getattr(o, k)[:] = v
+    b.prev_valid.fill_(True)
+    o.prev_valid[:] = 1
+    b.kernel_init_reward_state(states)
+    o.init_reward(states_np)
+    ob = b.kernel_build_obs(states)
+    assert within(ob.cpu().numpy(), o.build_obs(states_np), 1e-5)
+    act = rng.uniform(-1, 1, (nac, 4))
+    obs, rew, term, trunc = b.kernel_step(states, torch.as_tensor(act).to(cuda))
+    er, et, etr = o.advance(states_np, act)
     np.testing.assert_array_equal(term.cpu().numpy(), et)
     np.testing.assert_array_equal(trunc.cpu().numpy(), etr)
-    assert within(rew.cpu().numpy(), er, 1e-9)
-    assert within(obs.cpu().numpy(), eobs, 1e-5)
-    del pqr
+    assert within(rew.cpu().numpy(), er, 1e-5)
+    for k in ("hp", "fuel", "t_sec", "pqr"):
+        assert within(getattr(b, k).cpu().numpy(), getattr(o, k), 1e-9), k
+    assert within(obs.cpu().numpy(), o.build_obs(states_np), 1e-5)

@@ -5,6 +5,9 @@
 * frames: the oracle must reproduce the reference's own fdm.cuh (host-compiled, oracle/_ref)
   trajectories stored in tests/golden, bit for bit, for both FCS-dt lineages.
 """
+import sys
+from pathlib import Path
+
 import numpy as np
 import pytest
 
@@ -74,3 +77,22 @@ def test_oracle_matches_ref_on_edge_commands(cfg1):
             b, ob = ofdm.ref_step(seeds, c, ss, "root")
             np.testing.assert_array_equal(a, b)
             np.testing.assert_array_equal(oa, ob)
+
+
+@pytest.mark.skipif(not (ofdm.ref_available("root") and ofdm.ref_available("r36")),
+                    reason="oracle/_ref not built (needs the reference tree)")
+def test_oracle_matches_ref_at_envelope_edges():
+    """The envelope-edge ICs of the GPU test (300-80,000 ft, up to Mach ~1.9, extreme attitudes)
+    under edge commands: the oracle equals the reference's fdm.cuh bit for bit, both lineages."""
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from test_fdm_gpu import envelope_ics
+    rows = envelope_ics(256, 20260108)
+    for lineage, dt in (("root", 1.0 / 120.0), ("r36", 1.0 / 60.0)):
+        seeds = ofdm.oracle_seed(rows, dt)
+        for c in ([1.0, -1.0, 1.0, 1.0], [-1.0, 1.0, -1.0, 0.0], [0.0] * 4, [0.3, 0.44, -0.2, 0.55]):
+            cm = np.tile(c, (256, 1))
+            for ss in (1, 7):
+                a, oa = ofdm.oracle_step(seeds, cm, ss, dt)
+                b, ob = ofdm.ref_step(seeds, cm, ss, lineage)
+                np.testing.assert_array_equal(a, b)
+                np.testing.assert_array_equal(oa, ob)
