@@ -81,6 +81,9 @@ class GpuDogfightVecEnv:
         self._s9 = torch.zeros(self.nac, 9, dtype=torch.float64, device=dev)
         self._finite = torch.ones(self.nac, dtype=torch.uint8, device=dev)
         self.terminal_obs_enabled = True
+        # warm-up command range per channel (lower end, width), kept on the device
+        self._warm_lo = torch.tensor([-0.2, -0.2, -0.2, 0.6], dtype=torch.float64, device=dev)
+        self._warm_span = torch.tensor([0.4, 0.4, 0.4, 0.3], dtype=torch.float64, device=dev)
 
     # ---- IC sampling (rl_env.py:224-252), vectorised ----
     def _sample_ic_rows(self, n, rng=None, alt_ft=None, speed=None, side_swap=None, head_swap=None, dist_ft=None):
@@ -251,9 +254,8 @@ class GpuDogfightVecEnv:
     def _random_actions(self):
         """Warm-up commands (rl_env.py:468-473): the three sticks uniform in [-0.2, 0.2], throttle
         uniform in [0.6, 0.9], one row per aircraft."""
-        lo = torch.tensor([-0.2, -0.2, -0.2, 0.6], dtype=torch.float64, device=self.device)
-        span = torch.tensor([0.4, 0.4, 0.4, 0.3], dtype=torch.float64, device=self.device)
-        return torch.rand(self.nac, 4, dtype=torch.float64, device=self.device) * span + lo
+        a = torch.rand(self.nac, 4, dtype=torch.float64, device=self.device)
+        return a.mul_(self._warm_span).add_(self._warm_lo)
 
     def _to_nac4(self, actions):
         a = torch.as_tensor(actions, dtype=torch.float64, device=self.device)

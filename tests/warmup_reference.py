@@ -43,7 +43,7 @@ def host_checked_warmup(env, max_steps, actions, targ, pool_picks):
         a = actions[i]
         env.sim.step(a, substeps=env.substeps)
         steps += 1
-        finite_env = torch.isfinite(env.sim.states).view(env.nenv, -1).all(dim=1)
+        finite_env = torch.isfinite(env.sim.states).reshape(env.nenv, -1).all(dim=1)
         warm_finite.logical_and_((finite_env | captured_mask).all())
         env.obr.kernel_advance(env.sim.states, a.contiguous(), cfg=env.reward_cfg, min_alt=env.min_altitude_m,
                                max_time=env.max_engage_time_s)
