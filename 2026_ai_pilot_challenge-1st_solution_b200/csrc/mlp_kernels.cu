@@ -6,7 +6,8 @@
 // summed log-probability (Gumbel-max, fused into the last layer's epilogue).
 //
 // One persistent CTA per SM processes "jobs" = (128-row tile, network).  Per job and layer:
-//   * the A operand (the 128 x K activation tile, bf16) lives in a 128 KB shared-memory region in
+//   * the A operand (the 128 x K activation tile, 16-bit: bf16 or fp16, one type per network set)
+//     lives in a 128 KB shared-memory region in
 //     the K-major 128-byte-swizzled layout the tensor core reads; layer 0's A is loaded by TMA,
 //     layer l's A is written there by layer l-1's epilogue;
 //   * weight tiles (nn.Linear layout = K-major B) stream through a 3-stage ring of 32 KB TMA
@@ -14,7 +15,12 @@
 //   * one thread issues tcgen05.mma (M=128, N<=256, K=16 per instruction) accumulating fp32 in
 //     TMEM (all 512 columns = a full 128 x 512 layer);
 //   * four epilogue warps tcgen05.ld their 32 TMEM lanes, add bias, apply ReLU/tanh, and write the
-//     bf16 activations back to shared memory (or run the output head).
+//     16-bit activations back to shared memory (or run the output head).
+// Operand type: bf16 (8-bit significand) or fp16 (11-bit significand, same tensor throughput).
+// Against the fp32 network fp16 operands cut the logit error about eightfold (round-off 2^-11
+// instead of 2^-8 per input, weight and hidden activation), which brings logits and log-probs
+// within 1e-3 of fp32; fp16 hidden activations are converted with saturation (+-65504), so an
+// out-of-range activation clamps instead of becoming infinite.
 // Every mbarrier wait is bounded by a clock deadline; a timeout sets an error code and all roles
 // leave their loops, so a malformed launch returns an error instead of hanging.
 #include <cuda.h>
@@ -65,6 +71,7 @@ struct NetParams {
   int act;                                       // 0 relu, 1 tanh
   int head;                                      // Head
   int num_bins, act_dim;                         // categorical head: act_dim groups of num_bins
+  int fp16;                                      // operands: 0 bf16, 1 fp16 (one type per set)
 };
 
 struct Launch {
@@ -185,9 +192,12 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   d |= (uint64_t)2 << 61;
   return d;
 }
-// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M = 128.
-__device__ __forceinline__ uint32_t idesc_bf16(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// kind::f16 instruction descriptor: fp32 accumulate, A and B both bf16 (format 1) or both fp16
+// (format 0), both K-major, M = 128.
+template <bool FP16>
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+  const uint32_t ab = FP16 ? 0u : ((1u << 7) | (1u << 10));
+  return (1u << 4) | ab | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
 // ---------------------------------------------------------------- job decoding
@@ -271,13 +281,20 @@ __device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-// pack two fp32 (lo, hi) into bf16x2 with round-to-nearest, optionally clamping at 0 first
-// (relu(round(x)) == round(relu(x)), so the fused clamp gives the same bits as relu then round)
-__device__ __forceinline__ uint32_t pack_bf16x2(uint64_t v, bool relu) {
+// pack two fp32 (lo, hi) into bf16x2 or fp16x2 with round-to-nearest, optionally clamping at 0
+// first (relu(round(x)) == round(relu(x)), so the fused clamp gives the same bits as relu then
+// round); fp16 saturates at +-65504 (NaN stays NaN)
+template <bool FP16>
+__device__ __forceinline__ uint32_t pack_x2(uint64_t v, bool relu) {
   const float lo = __uint_as_float((uint32_t)v), hi = __uint_as_float((uint32_t)(v >> 32));
   uint32_t d;
-  if (relu) asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  else asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  if (FP16) {
+    if (relu) asm("cvt.rn.relu.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    else asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  } else {
+    if (relu) asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    else asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  }
   return d;
 }
 
@@ -285,7 +302,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(uint64_t v, bool relu) {
 // row's 128-byte swizzled line of the next layer's A operand: all bias loads first (one exposed
 // latency per chunk), the bias added two lanes per instruction, one activation branch per chunk,
 // ReLU fused into the conversion
-// bias + activation of one 32-column chunk packed as the four 16-byte bf16 units it stores
+// bias + activation of one 32-column chunk packed as the four 16-byte units it stores
+template <bool FP16>
 __device__ __forceinline__ void pack32(const uint32_t (&r)[32], const float* __restrict__ bias, int c0, bool relu,
                                        uint4 (&w)[4]) {
   const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(bias + c0);
@@ -308,10 +326,10 @@ __device__ __forceinline__ void pack32(const uint32_t (&r)[32], const float* __r
   }
 #pragma unroll
   for (int u = 0; u < 4; u++) {
-    w[u].x = pack_bf16x2(x[4 * u + 0], relu);
-    w[u].y = pack_bf16x2(x[4 * u + 1], relu);
-    w[u].z = pack_bf16x2(x[4 * u + 2], relu);
-    w[u].w = pack_bf16x2(x[4 * u + 3], relu);
+    w[u].x = pack_x2<FP16>(x[4 * u + 0], relu);
+    w[u].y = pack_x2<FP16>(x[4 * u + 1], relu);
+    w[u].z = pack_x2<FP16>(x[4 * u + 2], relu);
+    w[u].w = pack_x2<FP16>(x[4 * u + 3], relu);
   }
 }
 // the packed chunk into the swizzled A region of the next layer (row m, columns c0..c0+31)
@@ -322,6 +340,7 @@ __device__ __forceinline__ void store32(const uint4 (&w)[4], uint8_t* rowbase, i
   for (int u = 0; u < 4; u++) *reinterpret_cast<uint4*>(rowp + (((unit0 + u) ^ (m & 7)) * 16)) = w[u];
 }
 
+template <bool FP16>
 __device__ __forceinline__ void convert32(const uint32_t (&r)[32], const float* __restrict__ bias, int c0,
                                           uint8_t* rowbase, int m, bool relu) {
   const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(bias + c0);
@@ -347,10 +366,10 @@ __device__ __forceinline__ void convert32(const uint32_t (&r)[32], const float* 
 #pragma unroll
   for (int u = 0; u < 4; u++) {                    // 16-byte unit = 8 columns
     uint4 w;
-    w.x = pack_bf16x2(x[4 * u + 0], relu);
-    w.y = pack_bf16x2(x[4 * u + 1], relu);
-    w.z = pack_bf16x2(x[4 * u + 2], relu);
-    w.w = pack_bf16x2(x[4 * u + 3], relu);
+    w.x = pack_x2<FP16>(x[4 * u + 0], relu);
+    w.y = pack_x2<FP16>(x[4 * u + 1], relu);
+    w.z = pack_x2<FP16>(x[4 * u + 2], relu);
+    w.w = pack_x2<FP16>(x[4 * u + 3], relu);
     *reinterpret_cast<uint4*>(rowp + (((unit0 + u) ^ (m & 7)) * 16)) = w;
   }
 }
@@ -456,6 +475,7 @@ __device__ __noinline__ void cat_head_generic(uint32_t lane_addr, const float* _
   if (valid && L.logp) L.logp[row] = logp;
 }
 
+template <bool FP16>
 __global__ void __launch_bounds__(THREADS, 1)
 k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ nets_dev,
          const NetParams* __restrict__ nets, const __grid_constant__ Launch L) {
@@ -551,7 +571,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           const bool split = split_layer(P, l);
           for (int n0 = 0; n0 < N && ok; n0 += NCHUNK) {
             int nc = (N - n0) < NCHUNK ? (N - n0) : NCHUNK;
-            uint32_t idesc = idesc_bf16(nc);
+            uint32_t idesc = idesc_f16<FP16>(nc);
             for (int k0 = 0; k0 < K; k0 += KCHUNK, it++) {
               int s = it % STAGES;
               uint32_t round = it / STAGES;
@@ -625,7 +645,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
               uint32_t ra[32];
               tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
               tmem_wait_ld();
-              pack32(ra, bias, c, relu, held[i]);
+              pack32<FP16>(ra, bias, c, relu, held[i]);
             }
             // the layer's second-half MMAs are done with the activations being replaced
             bool got2 = mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
@@ -643,7 +663,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
               uint32_t ra[32];
               tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
               tmem_wait_ld();
-              convert32(ra, bias, c, rowbase, m, relu);
+              convert32<FP16>(ra, bias, c, rowbase, m, relu);
             }
           } else {
             // the next chunk's TMEM load in flight while this one is converted
@@ -655,12 +675,12 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             }
             while (c < N) {
               if (c + STEP < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + STEP), rb);
-              convert32(ra, bias, c, rowbase, m, relu);
+              convert32<FP16>(ra, bias, c, rowbase, m, relu);
               tmem_wait_ld();
               c += STEP;
               if (c >= N) break;
               if (c + STEP < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + STEP), ra);
-              convert32(rb, bias, c, rowbase, m, relu);
+              convert32<FP16>(rb, bias, c, rowbase, m, relu);
               tmem_wait_ld();
               c += STEP;
             }
@@ -748,15 +768,17 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// bf16 row-major [rows][cols] (row stride ld elements) with a 128-byte-swizzled box of 64 x box_rows
-static bool make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// 16-bit (bf16 or fp16) row-major [rows][cols] (row stride ld elements) with a 128-byte-swizzled
+// box of 64 x box_rows
+static bool make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                     bool fp16) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
   cuuint32_t box[2] = {(cuuint32_t)KCHUNK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+  CUresult r = fn(m, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -767,6 +789,7 @@ static bool make_map(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols
 
 struct f16_mlp_set_s {
   int n;
+  int fp16;                        // operand type of every network in the set
   f16::mlp::NetDev* dev_maps;      // device [n]
   f16::mlp::NetParams* dev_params; // device [n]
   f16::mlp::NetParams host_params[f16::mlp::MAX_NETS];
@@ -786,10 +809,13 @@ extern "C" int f16_mlp_set_create(const f16_mlp_desc* descs, int n, f16_mlp_set*
     NetParams& P = s->host_params[i];
     memset(&P, 0, sizeof(P));
     if (d.n_layers < 1 || d.n_layers > MAX_LAYERS || d.in_dim <= 0 || d.in_dim % 8 != 0 || d.in_dim > 512 ||
-        (d.activation != 0 && d.activation != 1) || (d.head != HEAD_CATEGORICAL && d.head != HEAD_VALUE)) {
+        (d.activation != 0 && d.activation != 1) || (d.head != HEAD_CATEGORICAL && d.head != HEAD_VALUE) ||
+        (d.operand != F16_OPERAND_BF16 && d.operand != F16_OPERAND_FP16) || d.operand != descs[0].operand) {
       delete s;
       return F16_ERR_ARG;
     }
+    P.fp16 = d.operand == F16_OPERAND_FP16;
+    s->fp16 = P.fp16;
     P.n_layers = d.n_layers;
     P.in_pad = (d.in_dim + KCHUNK - 1) / KCHUNK * KCHUNK;
     P.act = d.activation;
@@ -813,7 +839,10 @@ extern "C" int f16_mlp_set_create(const f16_mlp_desc* descs, int n, f16_mlp_set*
       P.width_pad[l] = wp;
       P.bias[l] = d.bias[l];
       int box_rows = wp < NCHUNK ? wp : NCHUNK;
-      if (!make_map(&maps[i].w[l], d.weight[l], w, in_l, in_l, box_rows)) { delete s; return F16_ERR_CUDA; }
+      if (!make_map(&maps[i].w[l], d.weight[l], w, in_l, in_l, box_rows, P.fp16 != 0)) {
+        delete s;
+        return F16_ERR_CUDA;
+      }
       in_l = w;
     }
   }
@@ -882,19 +911,22 @@ extern "C" int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args*
   if (a->cmd && (!a->grid || a->cmd_stride < 0 || a->cmd_offset < 0)) return F16_ERR_ARG;
   L.cmd = a->cmd; L.cmd_stride = a->cmd_stride; L.cmd_offset = a->cmd_offset; L.grid = a->grid;
   CUtensorMap xmap;
-  if (!make_map(&xmap, a->x, a->rows, a->ldx, a->ldx, TILE_M)) return F16_ERR_CUDA;
+  if (!make_map(&xmap, a->x, a->rows, a->ldx, a->ldx, TILE_M, set->fp16 != 0)) return F16_ERR_CUDA;
   int64_t njobs = tiles * a->nets_per_group;
   if (njobs == 0) return F16_OK;
-  static bool attr[64] = {false};
+  static bool attr[2][64] = {{false}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    if (cudaFuncSetAttribute(k_policy, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
-      return F16_ERR_LAUNCH;
-    attr[dev] = true;
+  const int t = set->fp16 ? 1 : 0;
+  if (dev >= 0 && dev < 64 && !attr[t][dev]) {
+    cudaError_t e = t ? cudaFuncSetAttribute(k_policy<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES)
+                      : cudaFuncSetAttribute(k_policy<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return F16_ERR_LAUNCH;
+    attr[t][dev] = true;
   }
   int grid = (int)(njobs < sm_count() ? njobs : sm_count());
-  k_policy<<<grid, THREADS, SMEM_BYTES, reinterpret_cast<cudaStream_t>(stream)>>>(xmap, set->dev_maps,
-                                                                                 set->dev_params, L);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (t) k_policy<true><<<grid, THREADS, SMEM_BYTES, st>>>(xmap, set->dev_maps, set->dev_params, L);
+  else k_policy<false><<<grid, THREADS, SMEM_BYTES, st>>>(xmap, set->dev_maps, set->dev_params, L);
   return launch_status();
 }

@@ -11,6 +11,7 @@
 // Chan merge in fp32), and the normalise-clamp that produces the policy input, optionally also
 // as a zero-padded bf16 matrix (the MLP kernel's A operand).
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <mutex>
 #include "common.cuh"
 
@@ -173,15 +174,28 @@ __global__ void k_norm_count(float* __restrict__ count, int64_t B) {
   if (threadIdx.x == 0 && blockIdx.x == 0) count[0] = __fadd_rn(count[0], (float)B);
 }
 
-// y = clamp((x - mean) / sqrt(var + eps), -clip, clip); fp32 out and/or bf16 out padded to ldb
-// columns (zeros beyond D).  With mean == NULL the values pass through unchanged (a cast into
-// the bf16 layout).  One thread per column (den and mean loaded once), APPLY_ROWS rows per
-// block; `nonfinite` (optional) counts warps that produced a non-finite output.
+// One fp32 value as the 16-bit policy-input element: bf16, or fp16 saturated at +-65504 (NaN
+// stays NaN), both round-to-nearest.
+template <bool FP16>
+__device__ __forceinline__ uint16_t to_half_bits(float o) {
+  if (FP16) {
+    const float c = o > 65504.0f ? 65504.0f : (o < -65504.0f ? -65504.0f : o);
+    return __half_as_ushort(__float2half_rn(c));
+  }
+  return __bfloat16_as_ushort(__float2bfloat16_rn(o));
+}
+
+// y = clamp((x - mean) / sqrt(var + eps), -clip, clip); fp32 out and/or 16-bit (bf16 or fp16)
+// out padded to ldb columns (zeros beyond D).  With mean == NULL the values pass through
+// unchanged (a cast into the 16-bit layout).  One thread per column (den and mean loaded once),
+// APPLY_ROWS rows per block; `nonfinite` (optional) counts warps that produced a non-finite
+// output.
 constexpr int APPLY_ROWS = 32;
+template <bool FP16>
 __global__ void __launch_bounds__(NORM_THREADS)
 k_norm_apply(const float* __restrict__ x, int64_t B, int D, int64_t ldx, const float* __restrict__ mean,
              const float* __restrict__ var, float eps, float clip, float* __restrict__ y, int64_t ldy,
-             __nv_bfloat16* __restrict__ yb, int64_t ldb, unsigned* __restrict__ nonfinite) {
+             uint16_t* __restrict__ yb, int64_t ldb, unsigned* __restrict__ nonfinite) {
   const int ncol = yb ? (int)ldb : D;
   const int64_t r0 = (int64_t)blockIdx.x * APPLY_ROWS;
   const int64_t r1 = r0 + APPLY_ROWS < B ? r0 + APPLY_ROWS : B;
@@ -200,10 +214,10 @@ k_norm_apply(const float* __restrict__ x, int64_t B, int D, int64_t ldx, const f
         }
         bad |= !isfinite(o);
         if (y) y[rr * ldy + d] = o;
-        if (yb) yb[rr * ldb + d] = __float2bfloat16_rn(o);
+        if (yb) yb[rr * ldb + d] = to_half_bits<FP16>(o);
       }
     } else {
-      for (int64_t rr = r0; rr < r1; rr++) yb[rr * ldb + d] = __float2bfloat16_rn(0.0f);
+      for (int64_t rr = r0; rr < r1; rr++) yb[rr * ldb + d] = 0;
     }
   }
   if (nonfinite && __any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicAdd(nonfinite, 1u);
@@ -211,7 +225,7 @@ k_norm_apply(const float* __restrict__ x, int64_t B, int D, int64_t ldx, const f
 
 // The same transform with 16-byte accesses, when D, the row strides and the pointers allow it:
 // thread t handles columns 4c..4c+3 (c = t mod G, G = the written column groups: D/4, or ldb/4
-// with the bf16 padding) of rows r0 + j, r0 + j + S, ... (stripe j = t div G, S = 256 div G);
+// with the 16-bit padding) of rows r0 + j, r0 + j + S, ... (stripe j = t div G, S = 256 div G);
 // the per-element arithmetic is k_norm_apply's, so the outputs are identical.
 constexpr int APPLY4_ROWS = 64;
 __device__ __forceinline__ float norm_elem(float v, float mu, float den, bool norm, float clip) {
@@ -219,6 +233,7 @@ __device__ __forceinline__ float norm_elem(float v, float mu, float den, bool no
   float o = __fdiv_rn(__fsub_rn(v, mu), den);
   return o < -clip ? -clip : (o > clip ? clip : o);
 }
+template <bool FP16>
 __global__ void __launch_bounds__(NORM_THREADS)
 k_norm_apply4(const float4* __restrict__ x, int64_t B, int D, int64_t ldx4, const float* __restrict__ mean,
               const float* __restrict__ var, float eps, float clip, float4* __restrict__ y, int64_t ldy4,
@@ -252,10 +267,9 @@ k_norm_apply4(const float4* __restrict__ x, int64_t B, int D, int64_t ldx4, cons
         bad |= !isfinite(o.x) || !isfinite(o.y) || !isfinite(o.z) || !isfinite(o.w);
         if (y) y[r * ldy4 + cg] = o;
         if (yb) {
-          __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y), hi = __floats2bfloat162_rn(o.z, o.w);
           uint2 packed;
-          packed.x = *reinterpret_cast<unsigned*>(&lo);
-          packed.y = *reinterpret_cast<unsigned*>(&hi);
+          packed.x = (uint32_t)to_half_bits<FP16>(o.x) | ((uint32_t)to_half_bits<FP16>(o.y) << 16);
+          packed.y = (uint32_t)to_half_bits<FP16>(o.z) | ((uint32_t)to_half_bits<FP16>(o.w) << 16);
           yb[r * ldb4 + cg] = packed;
         }
       }
@@ -268,19 +282,28 @@ k_norm_apply4(const float4* __restrict__ x, int64_t B, int D, int64_t ldx4, cons
 
 // Launch of the normalise / cast: the 16-byte kernel when the layout allows it.
 inline void launch_apply(const float* x, int64_t B, int D, int64_t ldx, const float* mean, const float* var,
-                         float eps, float clip, float* y, int64_t ldy, __nv_bfloat16* yb, int64_t ldb,
+                         float eps, float clip, float* y, int64_t ldy, void* yh, int64_t ldb, bool fp16,
                          unsigned* nonfinite, cudaStream_t s) {
+  uint16_t* yb = reinterpret_cast<uint16_t*>(yh);
   const bool vec = D % 4 == 0 && ldx % 4 == 0 && aligned(x, 16) && (!y || (ldy % 4 == 0 && aligned(y, 16))) &&
                    (!yb || (ldb % 4 == 0 && aligned(yb, 8))) && (yb ? ldb / 4 : D / 4) <= NORM_THREADS;
   if (!vec) {
     const unsigned grid = (unsigned)((B + APPLY_ROWS - 1) / APPLY_ROWS);
-    k_norm_apply<<<grid, NORM_THREADS, 0, s>>>(x, B, D, ldx, mean, var, eps, clip, y, ldy, yb, ldb, nonfinite);
+    if (fp16) k_norm_apply<true><<<grid, NORM_THREADS, 0, s>>>(x, B, D, ldx, mean, var, eps, clip, y, ldy, yb, ldb,
+                                                               nonfinite);
+    else k_norm_apply<false><<<grid, NORM_THREADS, 0, s>>>(x, B, D, ldx, mean, var, eps, clip, y, ldy, yb, ldb,
+                                                           nonfinite);
     return;
   }
   const unsigned grid = (unsigned)((B + APPLY4_ROWS - 1) / APPLY4_ROWS);
-  k_norm_apply4<<<grid, NORM_THREADS, 0, s>>>(reinterpret_cast<const float4*>(x), B, D, ldx / 4, mean, var, eps,
-                                              clip, reinterpret_cast<float4*>(y), ldy / 4,
-                                              reinterpret_cast<uint2*>(yb), ldb / 4, nonfinite);
+  if (fp16)
+    k_norm_apply4<true><<<grid, NORM_THREADS, 0, s>>>(reinterpret_cast<const float4*>(x), B, D, ldx / 4, mean, var,
+                                                      eps, clip, reinterpret_cast<float4*>(y), ldy / 4,
+                                                      reinterpret_cast<uint2*>(yb), ldb / 4, nonfinite);
+  else
+    k_norm_apply4<false><<<grid, NORM_THREADS, 0, s>>>(reinterpret_cast<const float4*>(x), B, D, ldx / 4, mean, var,
+                                                       eps, clip, reinterpret_cast<float4*>(y), ldy / 4,
+                                                       reinterpret_cast<uint2*>(yb), ldb / 4, nonfinite);
 }
 
 // ---------------------------------------------------------------- rollout bookkeeping
@@ -504,8 +527,8 @@ extern "C" int f16_norm_apply(const float* x, int64_t B, int D, int64_t ldx, con
                               f16_stream_t stream) {
   if (!x || !mean || !var || B <= 0 || D <= 0 || ldx < D || (!y && !y_bf16)) return F16_ERR_ARG;
   if ((y && ldy < D) || (y_bf16 && ldb < D)) return F16_ERR_ARG;
-  ro::launch_apply(x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy,
-                   reinterpret_cast<__nv_bfloat16*>(y_bf16), ldb, nullptr, reinterpret_cast<cudaStream_t>(stream));
+  ro::launch_apply(x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy, y_bf16, ldb, false, nullptr,
+                   reinterpret_cast<cudaStream_t>(stream));
   return launch_status();
 }
 
@@ -514,8 +537,19 @@ extern "C" int f16_norm_apply_checked(const float* x, int64_t B, int D, int64_t 
                                       int64_t ldb, uint32_t* nonfinite, f16_stream_t stream) {
   if (!x || B <= 0 || D <= 0 || ldx < D || (!y && !y_bf16) || (!mean != !var)) return F16_ERR_ARG;
   if ((y && ldy < D) || (y_bf16 && ldb < D)) return F16_ERR_ARG;
-  ro::launch_apply(x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy,
-                   reinterpret_cast<__nv_bfloat16*>(y_bf16), ldb, nonfinite, reinterpret_cast<cudaStream_t>(stream));
+  ro::launch_apply(x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy, y_bf16, ldb, false, nonfinite,
+                   reinterpret_cast<cudaStream_t>(stream));
+  return launch_status();
+}
+
+extern "C" int f16_norm_apply_half(const float* x, int64_t B, int D, int64_t ldx, const float* mean,
+                                   const float* var, double eps, double clip, float* y, int64_t ldy, void* y_half,
+                                   int64_t ldh, int operand, uint32_t* nonfinite, f16_stream_t stream) {
+  if (!x || B <= 0 || D <= 0 || ldx < D || (!y && !y_half) || (!mean != !var)) return F16_ERR_ARG;
+  if ((y && ldy < D) || (y_half && ldh < D)) return F16_ERR_ARG;
+  if (operand != F16_OPERAND_BF16 && operand != F16_OPERAND_FP16) return F16_ERR_ARG;
+  ro::launch_apply(x, B, D, ldx, mean, var, (float)eps, (float)clip, y, ldy, y_half, ldh,
+                   operand == F16_OPERAND_FP16, nonfinite, reinterpret_cast<cudaStream_t>(stream));
   return launch_status();
 }
 

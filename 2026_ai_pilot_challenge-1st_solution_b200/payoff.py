@@ -10,7 +10,7 @@ initial conditions.  Every lane's first finished game is scored for the left pol
 Per step, on the device and without a host synchronisation:
   * one gather of every policy's observation rows (row groups: the left policy's rows for all
     matchups, then each right policy's rows, every group starting on a 128-row tile);
-  * one normalise / bf16 cast per policy (its own RunningNorm, or none);
+  * one normalise / 16-bit cast per policy (its own RunningNorm, or none);
   * ONE grouped ``f16_policy_forward`` launch for all policies -- each group with its own
     frozen weights -- sampling the 4 x 21-bin actions (Gumbel-max) and writing the env
     commands (action_to_env) in the epilogue;
@@ -37,7 +37,7 @@ import torch
 from . import _lib
 from .policy import HEAD_CATEGORICAL, MlpWeights, PolicySet
 from .rl_env import GpuDogfightVecEnv
-from .rollout import cast_bf16, make_action_grid
+from .rollout import cast_half, make_action_grid
 
 TILE_ROWS = 128
 MAX_POLICIES = 20            # networks one registered policy set can hold
@@ -103,7 +103,7 @@ class BatchedPayoff:
     (R/cuda_fdm/batched_payoff.py evaluate_chunk / evaluate_row)."""
 
     def __init__(self, per_order, capacity=16, *, substeps=6, seed=0, device="cuda", min_altitude_m=304.8,
-                 max_engage_time_s=200.0, reward_cfg=None, alt_hunt_coef=5.0, num_bins=21):
+                 max_engage_time_s=200.0, reward_cfg=None, alt_hunt_coef=5.0, num_bins=21, operand="fp16"):
         per_order = int(per_order)
         if per_order < 4 or per_order % 4:
             raise ValueError("per_order must be a positive multiple of 4 (ppo_gpu.py:1388)")
@@ -111,6 +111,7 @@ class BatchedPayoff:
             raise ValueError(f"capacity must be between 1 and {MAX_POLICIES - 1}")
         self.per_order, self.capacity, self.lanes = per_order, int(capacity), 2 * per_order
         self.seed, self.num_bins = int(seed), int(num_bins)
+        self.operand = operand                      # 16-bit operand type of the policy kernel
         kw = dict(substeps=substeps, seed=seed, device=device, min_altitude_m=min_altitude_m,
                   max_engage_time_s=max_engage_time_s, reward_cfg=reward_cfg, reward_mode=0,
                   alt_hunt_coef=alt_hunt_coef)
@@ -171,7 +172,7 @@ class BatchedPayoff:
         # one launch shares one input layout: with a 214-D policy every first layer is widened
         # to 216 zero-padded columns
         nets = [MlpWeights.from_sequential(p.actor, HEAD_CATEGORICAL, dev, 4, self.num_bins,
-                                           in_width=216 if external else None) for p in pols]
+                                           in_width=216 if external else None, operand=self.operand) for p in pols]
         pset = PolicySet(nets)
         if external:
             env.obr.enable_external_observations()
@@ -180,7 +181,7 @@ class BatchedPayoff:
         total = src.numel()
         x184 = torch.zeros(total, 184, device=dev)
         x214 = torch.zeros(total, 214, device=dev) if external else None
-        xb = torch.zeros(total, in_pad, dtype=torch.bfloat16, device=dev)
+        xb = torch.zeros(total, in_pad, dtype=pset.dtype, device=dev)
         cmd_rows = torch.zeros(total, 4, dtype=torch.float64, device=dev)
 
         # the mirrored bank of one matchup, repeated per matchup (batched_payoff.py:82-89)
@@ -216,9 +217,9 @@ class BatchedPayoff:
             for p, (a, b) in zip(pols, spans):
                 x = (x214 if p.obs_dim == 214 else x184)[a:b]
                 if p.norm is not None:
-                    p.norm.normalize_bf16(x, out_bf16=xb[a:b], pad_to=in_pad)
+                    p.norm.normalize_half(x, out_half=xb[a:b], pad_to=in_pad)
                 else:
-                    cast_bf16(x, xb[a:b])
+                    cast_half(x, xb[a:b])
             pset.forward(xb, groups, seed=eval_seed, step=1, step_dev=counter, deterministic=not sample,
                          cmd=cmd_rows, cmd_stride=4, cmd_offset=0, grid=self.grid)
             cmd.index_copy_(0, dst, cmd_rows.index_select(0, valid))

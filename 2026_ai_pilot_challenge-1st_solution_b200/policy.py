@@ -1,8 +1,11 @@
 """Rollout-time policy / value forwards on the tcgen05 MLP kernel (csrc/mlp_kernels.cu).
 
 ``MlpWeights.from_sequential`` takes the reference's ``nn.Sequential`` stacks
-(R/claude_code/model.py ``_mlp`` :34-44 -> ``actor_logits`` / ``critic``) and keeps bf16 copies of
-the Linear weights and fp32 biases on the device.  ``PolicySet`` registers up to 20 such networks
+(R/claude_code/model.py ``_mlp`` :34-44 -> ``actor_logits`` / ``critic``) and keeps 16-bit copies
+of the Linear weights and fp32 biases on the device.  The 16-bit operand type is bf16 or fp16
+(``operand``, one per ``PolicySet``): both run at the same tensor-core rate; fp16's 11-bit
+significand keeps logits and log-probs within 1e-3 of the fp32 network (bf16: about 4e-3 of the
+largest logit), with activations saturated at +-65504.  ``PolicySet`` registers up to 20 such networks
 once (per weight update / pool refresh) and ``forward`` runs any mix of them over row groups:
 the main actor + critic on the same rows, or the frozen opponents of a league pool on their
 contiguous row blocks, sampling each 21-bin channel with Gumbel-max and summing the log-probs
@@ -16,13 +19,15 @@ from . import _lib
 
 HEAD_CATEGORICAL = 1
 HEAD_VALUE = 2
+OPERANDS = {"bf16": (0, torch.bfloat16), "fp16": (1, torch.float16)}
+FP16_MAX = 65504.0
 ACTIVATIONS = {"relu": 0, "tanh": 1}
 
 
 class MlpDesc(C.Structure):
     _fields_ = [("in_dim", C.c_int), ("n_layers", C.c_int), ("width", C.c_int * 4), ("activation", C.c_int),
                 ("head", C.c_int), ("act_dim", C.c_int), ("num_bins", C.c_int), ("weight", C.c_void_p * 4),
-                ("bias", C.c_void_p * 4)]
+                ("bias", C.c_void_p * 4), ("operand", C.c_int)]
 
 
 class PolicyArgs(C.Structure):
@@ -36,11 +41,19 @@ class PolicyArgs(C.Structure):
 
 
 class MlpWeights:
-    """Device bf16 weights + fp32 biases of one Linear stack."""
+    """Device 16-bit weights (``operand`` "bf16" or "fp16") + fp32 biases of one Linear stack."""
 
     def __init__(self, weights, biases, activation="relu", head=HEAD_CATEGORICAL, act_dim=4, num_bins=21,
-                 in_width=None):
-        self.weights = [w.detach().to(torch.bfloat16).contiguous() for w in weights]
+                 in_width=None, operand="bf16"):
+        if operand not in OPERANDS:
+            raise ValueError(f"operand must be one of {sorted(OPERANDS)}")
+        self.operand = operand
+        dt = OPERANDS[operand][1]
+        if operand == "fp16":
+            big = max(float(w.detach().abs().max()) for w in weights)
+            if not big <= FP16_MAX:
+                raise ValueError(f"a weight of magnitude {big:.3g} does not fit fp16; use operand='bf16'")
+        self.weights = [w.detach().to(dt).contiguous() for w in weights]
         self.biases = [b.detach().to(torch.float32).contiguous() for b in biases]
         # the kernel reads the input in 16-byte units, and all networks of one launch share the
         # input row layout: the first layer gets zero columns up to in_width (default: the next
@@ -61,14 +74,14 @@ class MlpWeights:
         self.in_dim = self.weights[0].shape[1]
 
     @classmethod
-    def from_sequential(cls, seq, head, device, act_dim=4, num_bins=21, in_width=None):
+    def from_sequential(cls, seq, head, device, act_dim=4, num_bins=21, in_width=None, operand="bf16"):
         linears = [m for m in seq if isinstance(m, torch.nn.Linear)]
         acts = {type(m).__name__.lower() for m in seq if not isinstance(m, torch.nn.Linear)}
         act = "tanh" if "tanh" in acts else "relu"
         if acts - {"tanh", "relu"}:
             raise ValueError(f"unsupported activation(s): {acts}")
         return cls([l.weight.to(device) for l in linears], [l.bias.to(device) for l in linears], act, head,
-                   act_dim, num_bins, in_width)
+                   act_dim, num_bins, in_width, operand)
 
     @torch.no_grad()
     def load_from(self, seq):
@@ -95,6 +108,7 @@ class MlpWeights:
         d.activation = ACTIVATIONS[self.activation]
         d.head = self.head
         d.act_dim, d.num_bins = self.act_dim, self.num_bins
+        d.operand = OPERANDS[self.operand][0]
         return d
 
 
@@ -104,6 +118,11 @@ class PolicySet:
     def __init__(self, nets):
         self.lib = _lib.load()
         self.nets = list(nets)           # keeps the device buffers alive
+        ops = {n.operand for n in self.nets}
+        if len(ops) != 1:
+            raise ValueError("every network of a policy set must use the same operand type")
+        self.operand = ops.pop()
+        self.dtype = OPERANDS[self.operand][1]
         arr = (MlpDesc * len(self.nets))(*[n.desc() for n in self.nets])
         handle = C.c_void_p()
         _lib.check(self.lib.f16_mlp_set_create(arr, len(self.nets), C.byref(handle)), "f16_mlp_set_create")
@@ -121,17 +140,18 @@ class PolicySet:
         except Exception:
             pass
 
-    def forward(self, x_bf16, groups, nets_per_group=1, bins=None, bins_stride=4, bins_offset=0, act_idx=None,
+    def forward(self, x, groups, nets_per_group=1, bins=None, bins_stride=4, bins_offset=0, act_idx=None,
                 logp=None, value=None, logits=None, seed=0, step=0, deterministic=False, cmd=None, cmd_stride=4,
                 cmd_offset=0, grid=None, step_dev=None):
-        """groups: list of (row_end, [net indices]) with every group starting at a multiple of 128.
+        """groups: list of (row_end, [net indices]) with every group starting at a multiple of 128;
+        ``x`` is the (rows, ldx) policy input in the set's operand dtype (``self.dtype``).
 
         ``cmd`` (fp64, optional) receives action_to_env of the sampled bins at
         ``cmd[r * cmd_stride + cmd_offset + c]`` using the fp32 ``grid`` (num_bins values).
         ``step_dev`` (device int64 [1], optional) is added to ``step`` when the kernel runs, so a
         captured CUDA graph draws fresh samples on every replay."""
-        _lib.require_cuda_tensor(x_bf16, torch.bfloat16, None, "policy input", None)
-        rows, ldx = x_bf16.shape[0], x_bf16.stride(0)
+        _lib.require_cuda_tensor(x, self.dtype, None, "policy input", None)
+        rows, ldx = x.shape[0], x.stride(0)
         ends = (C.c_int64 * len(groups))(*[int(g[0]) for g in groups])
         flat = []
         for _, ids in groups:
@@ -139,7 +159,7 @@ class PolicySet:
             flat.extend(ids[:nets_per_group])
         netv = (C.c_int * len(flat))(*flat)
         a = PolicyArgs()
-        a.x = x_bf16.data_ptr(); a.rows = rows; a.ldx = ldx
+        a.x = x.data_ptr(); a.rows = rows; a.ldx = ldx
         a.n_groups = len(groups); a.group_end = ends; a.group_net = netv; a.nets_per_group = nets_per_group
         a.bins = bins.data_ptr() if bins is not None else None
         a.bins_stride = bins_stride; a.bins_offset = bins_offset
@@ -151,16 +171,16 @@ class PolicySet:
         a.seed = seed & (2 ** 64 - 1); a.step = step & (2 ** 64 - 1); a.deterministic = int(bool(deterministic))
         a.err = self.err.data_ptr()
         if step_dev is not None:
-            _lib.require_cuda_tensor(step_dev, torch.int64, (1,), "step counter", x_bf16.device)
+            _lib.require_cuda_tensor(step_dev, torch.int64, (1,), "step counter", x.device)
             a.step_dev = step_dev.data_ptr()
         if cmd is not None:
-            _lib.require_cuda_tensor(cmd, torch.float64, None, "env commands", x_bf16.device)
-            _lib.require_cuda_tensor(grid, torch.float32, None, "action grid", x_bf16.device)
+            _lib.require_cuda_tensor(cmd, torch.float64, None, "env commands", x.device)
+            _lib.require_cuda_tensor(grid, torch.float32, None, "action grid", x.device)
             a.cmd = cmd.data_ptr(); a.cmd_stride = cmd_stride; a.cmd_offset = cmd_offset
             a.grid = grid.contiguous().data_ptr() if grid.is_contiguous() else None
             if a.grid is None:
                 raise ValueError("action grid must be contiguous")
-        _lib.check(self.lib.f16_policy_forward(self.handle, C.byref(a), _lib.stream_of(x_bf16)), "f16_policy_forward")
+        _lib.check(self.lib.f16_policy_forward(self.handle, C.byref(a), _lib.stream_of(x)), "f16_policy_forward")
 
     def check_error(self):
         """Host-synchronising check of the kernel's bounded-wait flag."""

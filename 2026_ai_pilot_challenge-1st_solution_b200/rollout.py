@@ -3,7 +3,8 @@
 * ``RunningNorm``      -- drop-in for ppo_gpu.RunningNorm (:184-222): same attributes
   (mean, var, count fp32 tensors, clip, eps) and methods (update, normalize, state_dict,
   load_state_dict, clone); update / normalize run f16_norm_update / f16_norm_apply, and
-  ``normalize_bf16`` also emits the zero-padded bf16 matrix the MLP kernel consumes.
+  ``normalize_half`` (``normalize_bf16``) also emits the zero-padded 16-bit matrix (bf16 or fp16,
+  the policy set's operand type) the MLP kernel consumes.
 * ``gae``              -- the GAE loop of collect_rollout (:1983-1995) in one launch, bit-exact.
 * ``make_action_grid`` / ``action_to_env`` -- the reference action mapping (:178-180, :361-369).
 """
@@ -87,18 +88,24 @@ class RunningNorm:
         return y
 
     @torch.no_grad()
-    def normalize_bf16(self, x, out_f32=None, out_bf16=None, pad_to=192, nonfinite=None):
-        """Normalised rows as fp32 (optional) and as a (B, pad_to) zero-padded bf16 matrix;
-        ``nonfinite`` (a device uint32/int32 counter, optional) is incremented when an output
-        value is NaN or infinite."""
+    def normalize_half(self, x, out_f32=None, out_half=None, pad_to=192, nonfinite=None, dtype=torch.bfloat16):
+        """Normalised rows as fp32 (optional) and as a (B, pad_to) zero-padded 16-bit matrix
+        (``out_half``'s dtype, else ``dtype``: bf16 or fp16); ``nonfinite`` (a device uint32/int32
+        counter, optional) is incremented when an output value is NaN or infinite."""
         x = self._x(x)
-        yb = torch.empty(x.shape[0], pad_to, dtype=torch.bfloat16, device=x.device) if out_bf16 is None else out_bf16
-        _lib.check(self.lib.f16_norm_apply_checked(
+        yh = torch.empty(x.shape[0], pad_to, dtype=dtype, device=x.device) if out_half is None else out_half
+        _lib.check(self.lib.f16_norm_apply_half(
             _lib.ptr(x), x.shape[0], self.dim, x.stride(0), _lib.ptr(self.mean), _lib.ptr(self.var), self.eps,
             self.clip, _lib.ptr(out_f32) if out_f32 is not None else None,
-            out_f32.stride(0) if out_f32 is not None else 0, _lib.ptr(yb), yb.stride(0),
-            _lib.ptr(nonfinite) if nonfinite is not None else None, _lib.stream_of(x)), "f16_norm_apply_checked")
-        return yb
+            out_f32.stride(0) if out_f32 is not None else 0, _lib.ptr(yh), yh.stride(0), half_operand(yh),
+            _lib.ptr(nonfinite) if nonfinite is not None else None, _lib.stream_of(x)), "f16_norm_apply_half")
+        return yh
+
+    def normalize_bf16(self, x, out_f32=None, out_bf16=None, pad_to=192, nonfinite=None):
+        """normalize_half with a bf16 output."""
+        if out_bf16 is not None and out_bf16.dtype != torch.bfloat16:
+            raise TypeError("normalize_bf16 writes a bf16 matrix")
+        return self.normalize_half(x, out_f32, out_bf16, pad_to, nonfinite, torch.bfloat16)
 
     def state_dict(self):
         return {"mean": self.mean.clone(), "var": self.var.clone(), "count": self.count.clone()}
@@ -112,20 +119,34 @@ class RunningNorm:
         return c
 
 
+def half_operand(t):
+    """C-ABI operand code of a 16-bit policy-input tensor (bf16 0, fp16 1)."""
+    if t.dtype == torch.bfloat16:
+        return 0
+    if t.dtype == torch.float16:
+        return 1
+    raise TypeError(f"policy input must be bf16 or fp16, got {t.dtype}")
+
+
 @torch.no_grad()
-def cast_bf16(x, out_bf16, out_f32=None, nonfinite=None):
-    """Un-normalised rows (B, D) fp32 into a zero-padded (B, ldb) bf16 policy input (and
-    optionally an fp32 copy) in one kernel: the input of a network without a normaliser."""
+def cast_half(x, out_half, out_f32=None, nonfinite=None):
+    """Un-normalised rows (B, D) fp32 into a zero-padded (B, ldb) 16-bit policy input (bf16 or
+    fp16, ``out_half``'s dtype; and optionally an fp32 copy) in one kernel: the input of a
+    network without a normaliser."""
     _lib.require_cuda_tensor(x, torch.float32, None, "observations", None)
     if x.dim() != 2 or x.stride(1) != 1:
         raise ValueError("observations must be (B, D) with unit column stride")
     L = _lib.load()
-    _lib.check(L.f16_norm_apply_checked(_lib.ptr(x), x.shape[0], x.shape[1], x.stride(0), None, None, 0.0, 0.0,
-                                        _lib.ptr(out_f32) if out_f32 is not None else None,
-                                        out_f32.stride(0) if out_f32 is not None else 0, _lib.ptr(out_bf16),
-                                        out_bf16.stride(0), _lib.ptr(nonfinite) if nonfinite is not None else None,
-                                        _lib.stream_of(x)), "f16_norm_apply_checked")
-    return out_bf16
+    _lib.check(L.f16_norm_apply_half(_lib.ptr(x), x.shape[0], x.shape[1], x.stride(0), None, None, 0.0, 0.0,
+                                     _lib.ptr(out_f32) if out_f32 is not None else None,
+                                     out_f32.stride(0) if out_f32 is not None else 0, _lib.ptr(out_half),
+                                     out_half.stride(0), half_operand(out_half),
+                                     _lib.ptr(nonfinite) if nonfinite is not None else None,
+                                     _lib.stream_of(x)), "f16_norm_apply_half")
+    return out_half
+
+
+cast_bf16 = cast_half
 
 
 def gae(b_rew, b_val, b_done, last_value, next_done, gamma, gae_lambda, adv=None, ret=None):

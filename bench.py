@@ -53,6 +53,10 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--e2e-steps", type=int, default=100)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--policy-operand", default="fp16", choices=["fp16", "bf16"],
+                   help="16-bit operand type of the tcgen05 policy kernel (rollout / ppo / mlp / payoff): fp16 "
+                        "(default; logits within 1e-3 of fp32) or bf16 (the type BASELINE's configs[3] names; "
+                        "same tensor rate, about 4e-3)")
     p.add_argument("--tf32", action="store_true", help="ppo workload: TF32 matmuls in the update (below the "
                                                          "reference's fp32; reported in dtype)")
     p.add_argument("--breakdown", action="store_true", help="ppo workload: print the per-kernel device time of "
@@ -423,7 +427,7 @@ def run_rollout(args, dev, world, rank):
     pg = dist.group.WORLD if world > 1 else None
     env = rl_env.GpuDogfightVecEnv(ROLL_NENV, substeps=SUBSTEPS, seed=20260104 + rank, device=dev)
     cfg = tr.PPOConfig(rollout_steps=ROLL_T, gamma=0.99, gae_lambda=0.95, hidden=(512, 512), activation="relu",
-                       seed=20260104)
+                       seed=20260104, policy_operand=args.policy_operand)
     opps = []
     for i in range(ROLL_OPP):
         torch.manual_seed(i + 1)
@@ -549,10 +553,11 @@ def run_rollout(args, dev, world, rank):
             cpu = {"value": v, "unit": "decision-steps/s", "cores": thr, "kind": kind, "sample": sample}
         line = {"metric": "decision-steps/s (env step + obs/reward + actor sample)", "value": value,
                 "unit": "decision-steps/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64+bf16",
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": f"f64+{args.policy_operand} (policy operands, fp32 accumulate)",
                 "data": "synthetic ICs, random-init networks",
                 "config": {"workload": "configs[3]: full rollout, 131,072 envs per GPU, T=64 (384 FDM frames), "
-                                       "actor 184-512-512-84 ReLU bf16 with fused sampling, critic 184-512-512-1, "
+                                       f"actor 184-512-512-84 ReLU {args.policy_operand} with fused sampling, critic 184-512-512-1, "
                                        "8 frozen opponents on env blocks, GAE 0.99/0.95",
                            "envs_per_gpu": ROLL_NENV, "rollout_steps": ROLL_T, "step": "one rollout",
                            "parallelism": f"env-shard x{world}" + (" + NCCL RunningNorm allreduce" if world > 1 else ""),
@@ -617,7 +622,8 @@ def run_ppo(args, dev, world, rank):
     pg = dist.group.WORLD if world > 1 else None
     env = rl_env.GpuDogfightVecEnv(ROLL_NENV, substeps=SUBSTEPS, seed=20260105 + rank, device=dev)
     cfg = tr.PPOConfig(rollout_steps=ROLL_T, gamma=0.99, gae_lambda=0.95, hidden=(512, 512), activation="relu",
-                       update_epochs=4, num_minibatches=16, clip_coef=0.2, target_kl=None, seed=20260105)
+                       update_epochs=4, num_minibatches=16, clip_coef=0.2, target_kl=None, seed=20260105,
+                       policy_operand=args.policy_operand)
     opps = []
     for i in range(PPO_OPP):
         torch.manual_seed(100 + i)
@@ -685,7 +691,7 @@ def run_ppo(args, dev, world, rank):
         nparams = sum(p.numel() for p in t.model.parameters())
         line = {"metric": "decision-steps/s over full PPO iterations (rollout + update)", "value": value,
                 "unit": "decision-steps/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms_it,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64+bf16 (update " + ("tf32" if args.tf32 else
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": f"f64+{args.policy_operand} policy (update " + ("tf32" if args.tf32 else
                                                  "fp32-level: bf16x3-split products, fp32 accumulate, "
                                                  "errors at or below SGEMM's") + ")",
                 "data": "synthetic ICs, random-init networks",
@@ -798,7 +804,8 @@ def run_aux(args, dev, world, rank):
         mk = lambda s: (torch.manual_seed(s), tr.MLPActorCritic(hidden=(512, 512), activation="relu").to(dev))[1]
         left = payoff.EvalPolicy(mk(100))
         rights = [payoff.EvalPolicy(mk(200 + i)) for i in range(16)]
-        bp = payoff.BatchedPayoff(per_order=32, capacity=16, seed=11 + rank, device=dev)
+        bp = payoff.BatchedPayoff(per_order=32, capacity=16, seed=11 + rank, device=dev,
+                                  operand=args.policy_operand)
         bp.evaluate(left, rights[:2], seed_block=0)
         torch.cuda.synchronize(dev)
         steps = []
@@ -818,7 +825,7 @@ def run_aux(args, dev, world, rank):
     if rank == 0:
         line = {"metric": metric, "value": world * units / (ms * 1e-3), "unit": unit, "n_gpus": world, "steps": K,
                 "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f64" if args.workload != "payoff" else "f64+bf16", "data": "synthetic",
+                "dtype": "f64" if args.workload != "payoff" else f"f64+{args.policy_operand}", "data": "synthetic",
                 "config": config, "clocks": clk.summary()}
         if launches is not None:
             line["gpu_launches"] = launches
@@ -831,7 +838,7 @@ def run_aux(args, dev, world, rank):
 
 def run_mlp(args, dev, world, rank):
     """The rollout's main policy launch alone: actor 184-512-512-84 ReLU with Gumbel-max sampling,
-    log-prob and env commands, and critic 184-512-512-1, on 131,072 bf16 rows (k_policy, one
+    log-prob and env commands, and critic 184-512-512-1, on 131,072 16-bit rows (k_policy, one
     launch per step), with the input rows rewritten between steps so every launch reads them
     from HBM.  The kernel-level figure behind the rollout's roofline line."""
     import torch
@@ -840,14 +847,15 @@ def run_mlp(args, dev, world, rank):
     ro = importlib.import_module(PKG + ".rollout")
     torch.manual_seed(0)
     model = tr.MLPActorCritic(hidden=(512, 512), activation="relu").to(dev)
-    nets = [pol.MlpWeights.from_sequential(model.actor_logits, pol.HEAD_CATEGORICAL, dev),
-            pol.MlpWeights.from_sequential(model.critic, pol.HEAD_VALUE, dev)]
+    nets = [pol.MlpWeights.from_sequential(model.actor_logits, pol.HEAD_CATEGORICAL, dev,
+                                           operand=args.policy_operand),
+            pol.MlpWeights.from_sequential(model.critic, pol.HEAD_VALUE, dev, operand=args.policy_operand)]
     ps = pol.PolicySet(nets)
     n = ROLL_NENV
     g = torch.Generator(device=dev).manual_seed(3)
-    src = torch.randn(2, n, 192, device=dev, generator=g).to(torch.bfloat16)
+    src = torch.randn(2, n, 192, device=dev, generator=g).to(ps.dtype)
     src[:, :, 184:] = 0
-    x = torch.empty(n, 192, dtype=torch.bfloat16, device=dev)
+    x = torch.empty(n, 192, dtype=ps.dtype, device=dev)
     bins = torch.empty(n, 4, dtype=torch.uint8, device=dev)
     logp = torch.empty(n, device=dev)
     val = torch.empty(n, device=dev)
@@ -881,7 +889,8 @@ def run_mlp(args, dev, world, rank):
     if rank == 0:
         line = {"metric": "actor+critic rows/s (k_policy alone)", "value": world * n / (ms * 1e-3), "unit": "rows/s",
                 "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
+                "scaling": "weak", "vs_baseline": None, "dtype": f"{args.policy_operand} (fp32 accumulate)",
+                "data": "synthetic",
                 "config": {"workload": "the rollout's main policy launch: 131,072 rows, actor 184-512-512-84 ReLU "
                                        "(sampled bins, log-prob, env commands) + critic 184-512-512-1",
                            "l2": "256 MB flush and a fresh input copy before each timed launch"},

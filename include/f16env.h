@@ -241,7 +241,8 @@ int f16_external_obs(const double* state, int layout, int64_t ld, int64_t nac, c
  * per-channel Categorical sample (Gumbel-max, counter-based RNG) and its summed log-probability
  * fused into the last layer.
  *
- * A network: n_layers <= 4 Linear layers (nn.Linear layout: weight [out][in] bf16 row-major,
+ * A network: n_layers <= 4 Linear layers (nn.Linear layout: weight [out][in] bf16 or fp16
+ * row-major (the descriptor's operand type),
  * device, 16-byte aligned, in a multiple of 8), hidden widths multiples of 64 up to 512, ReLU
  * (activation 0) or tanh (1) after every hidden layer; head 1 = categorical with
  * width[last] = act_dim * num_bins <= 96, head 2 = value with width[last] = 1.
@@ -255,7 +256,13 @@ typedef struct {
   int act_dim, num_bins;
   const void* weight[4];
   const float* bias[4];
+  int operand;              /* F16_OPERAND_BF16 (0, a zero-initialised descriptor) or
+                               F16_OPERAND_FP16: the type of the weights, of the policy input x
+                               and of the hidden activations; one type for every network of a set */
 } f16_mlp_desc;
+
+#define F16_OPERAND_BF16 0
+#define F16_OPERAND_FP16 1
 
 typedef struct f16_mlp_set_s f16_mlp_set;   /* opaque: up to 20 networks with their TMA maps */
 
@@ -264,7 +271,8 @@ int f16_mlp_set_create(const f16_mlp_desc* descs, int n, f16_mlp_set** out);
 int f16_mlp_set_destroy(f16_mlp_set* set);
 
 typedef struct {
-  const void* x;            /* bf16 [rows][ldx] policy input (normalised observations), device */
+  const void* x;            /* [rows][ldx] policy input (normalised observations) in the set's operand
+                               type (bf16 or fp16), device */
   int64_t rows, ldx;
   int n_groups;             /* row groups; group g owns rows [group_end[g-1], group_end[g]), every
                                group starting at a multiple of 128 rows */
@@ -351,6 +359,14 @@ int f16_norm_apply(const float* x, int64_t B, int D, int64_t ldx, const float* m
 int f16_norm_apply_checked(const float* x, int64_t B, int D, int64_t ldx, const float* mean,
                            const float* var, double eps, double clip, float* y, int64_t ldy,
                            void* y_bf16, int64_t ldb, uint32_t* nonfinite, f16_stream_t stream);
+
+/* f16_norm_apply_checked with the 16-bit output in either policy operand type: operand
+ * F16_OPERAND_BF16 writes what f16_norm_apply_checked writes; F16_OPERAND_FP16 writes fp16
+ * (round to nearest, saturated at +-65504, NaN kept) into y_half [B][ldh], the input of an
+ * fp16 network set. */
+int f16_norm_apply_half(const float* x, int64_t B, int D, int64_t ldx, const float* mean,
+                        const float* var, double eps, double clip, float* y, int64_t ldy,
+                        void* y_half, int64_t ldh, int operand, uint32_t* nonfinite, f16_stream_t stream);
 
 /* Per-step bookkeeping of collect_rollout (ppo_gpu.py:1914-1960) in one launch, after the env
  * step: b_rew[e] = (float)reward[2e]; next_done[e] = done[e]; ep_ret / ep_len updated and

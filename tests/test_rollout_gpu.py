@@ -96,3 +96,24 @@ def test_checked_normalise_cast_and_nonfinite_count(cuda):
     rn.normalize_bf16(x, out_f32=y2, out_bf16=b2, nonfinite=cnt)
     torch.cuda.synchronize()
     assert int(cnt) >= 1 and bool(torch.isnan(y2[17, 5]))
+
+
+def test_norm_apply_half_fp16(cuda):
+    """f16_norm_apply_half with the fp16 operand: the fp16 rows are the fp32 rows rounded to
+    nearest (zero padding beyond the features), values past fp16's range saturate at +-65504,
+    and the bf16 operand reproduces f16_norm_apply_checked bit for bit."""
+    ro = pkg_module("rollout")
+    g = torch.Generator(device=cuda).manual_seed(4)
+    x = torch.randn(3000, 184, device=cuda, generator=g) * 3.0
+    rn = ro.RunningNorm(184, cuda)
+    rn.update(x)
+    yf = torch.zeros(3000, 184, device=cuda)
+    yh = rn.normalize_half(x, out_f32=yf, dtype=torch.float16)
+    assert yh.dtype == torch.float16
+    assert torch.equal(yh[:, :184], yf.to(torch.float16)) and bool((yh[:, 184:] == 0).all())
+    yb = rn.normalize_half(x, dtype=torch.bfloat16)
+    assert torch.equal(yb, rn.normalize_bf16(x))
+    big = torch.tensor([[1e6, -1e6, 70000.0, 1.5] + [0.0] * 180], device=cuda)
+    c = torch.full((1, 192), 9.0, device=cuda).to(torch.float16)
+    ro.cast_half(big, c)
+    assert c[0, :4].tolist() == [65504.0, -65504.0, 65504.0, 1.5] and bool((c[0, 184:] == 0).all())

@@ -1,9 +1,9 @@
 """PPOTrainer rollout + update on a B200 (trainer.py).
 
 A short rollout through the real env and kernels, checked against torch on the rollout buffers:
-* log-probs of the sampled bins and values vs a bf16 emulation of the actor / critic (bf16
-  weights and inputs, fp32 accumulation): within 5e-2 (sum of four channel log-probs) and
-  1e-2 + 1e-2 relative;
+* log-probs of the sampled bins and values vs an emulation of the actor / critic in the trainer's
+  16-bit operand type (fp16 by default: 16-bit weights and inputs, fp32 accumulation): within
+  5e-2 (sum of four channel log-probs) and 1e-2 + 1e-2 relative;
 * the env commands of the last step equal the reference action_to_env of the stored bins
   exactly (main, even aircraft) and of the argmax of the assigned opponent's emulated logits
   (deterministic opponents, odd aircraft; >= 99 % of rows, the rest are near-ties);
@@ -21,13 +21,15 @@ pytestmark = pytest.mark.gpu
 
 
 def emulate(seq, xb):
+    """The policy kernel's numerics in torch, in xb's 16-bit type."""
+    dt = xb.dtype
     lin = [m for m in seq if isinstance(m, nn.Linear)]
     act = [m for m in seq if not isinstance(m, nn.Linear)]
     h = xb.float()
     for i, l in enumerate(lin):
-        h = h @ l.weight.detach().to(torch.bfloat16).float().T + l.bias.detach().float()
+        h = h @ l.weight.detach().to(dt).float().T + l.bias.detach().float()
         if i < len(lin) - 1:
-            h = act[i](h).to(torch.bfloat16).float()
+            h = act[i](h).to(dt).float()
     return h
 
 
@@ -80,7 +82,7 @@ def check_rollout(t, adv, ret):
     model = t.model
     grid = t.grid
     for s in range(cfg.rollout_steps):
-        xb = t.b_obs[s].to(torch.bfloat16)
+        xb = t.b_obs[s].to(t.policy.dtype)
         lg = emulate(model.actor_logits, xb).view(-1, 4, 21)
         lsm = torch.log_softmax(lg, -1)
         exp_logp = lsm.gather(-1, t.b_act[s].long().unsqueeze(-1)).squeeze(-1).sum(-1)
