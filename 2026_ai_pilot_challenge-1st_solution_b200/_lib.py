@@ -93,6 +93,8 @@ _SIGS = {
                                 _P], C.c_int),
     "f16_norm_apply_half": ([_P, _I64, C.c_int, _I64, _P, _P, C.c_double, C.c_double, _P, _I64, _P, _I64, C.c_int,
                              _P, _P], C.c_int),
+    "f16_norm_apply_scatter": ([_P, _I64, C.c_int, _I64, _P, _P, _P, _P, C.c_int, C.c_double, C.c_double, _P, _I64,
+                                C.c_int, _P, _P], C.c_int),
     "f16_fdm_step": ([_P, C.c_int, _I64, _I64, _P, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_fdm_step_bins": ([_P, C.c_int, _I64, _I64, _P, _P, C.c_int, C.c_int, C.c_double, _P, _P], C.c_int),
     "f16_fdm_step_ex": ([_P, C.c_int, _I64, _I64, C.POINTER(FdmIO), C.c_int, C.c_double, _P], C.c_int),

@@ -78,6 +78,9 @@ struct Launch {
   int64_t rows;                                  // valid rows of X
   int n_groups;                                  // row groups (frozen-opponent pools); group g owns
   int64_t group_end[MAX_NETS + 1];               //   rows [group_end[g-1], group_end[g]); starts % 128 == 0
+  const int64_t* group_end_dev;                  // the same ends read from device memory instead (a
+                                                 //   grouping computed on the device); tiles_total is
+                                                 //   then an upper bound and surplus jobs are skipped
   int group_net[MAX_NETS][2];                    // networks per group (second = -1 if none)
   int nets_per_group;
   int64_t tiles_total;                           // sum over groups of ceil(rows_g / 128)
@@ -219,7 +222,9 @@ __device__ __forceinline__ bool decode_job(const Launch& L, int64_t j, Job& J) {
   int slot = (int)(j % L.nets_per_group);
   int64_t start = 0;
   for (int g = 0; g < L.n_groups; g++) {
-    int64_t end = L.group_end[g];
+    int64_t end = L.group_end_dev ? __ldg(L.group_end_dev + g) : L.group_end[g];
+    end = end < L.rows ? end : L.rows;           // never past the input rows
+    end = end > start ? end : start;             // an empty (or malformed) group has no tiles
     int64_t nt = (end - start + TILE_M - 1) / TILE_M;
     if (tile < nt) {
       J.row0 = start + tile * TILE_M;
@@ -882,11 +887,17 @@ extern "C" int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args*
   L.nets_per_group = a->nets_per_group;
   int64_t start = 0, tiles = 0;
   int in_pad = -1;
+  const bool dev_ends = a->group_end_dev != nullptr;
+  if (dev_ends && !aligned(a->group_end_dev, 8)) return F16_ERR_ALIGN;
+  L.group_end_dev = a->group_end_dev;
   for (int g = 0; g < a->n_groups; g++) {
-    int64_t end = a->group_end[g];
-    if (end < start || end > a->rows || start % TILE_M != 0) return F16_ERR_ARG;
-    L.group_end[g] = end;
-    tiles += (end - start + TILE_M - 1) / TILE_M;
+    if (!dev_ends) {
+      int64_t end = a->group_end[g];
+      if (end < start || end > a->rows || start % TILE_M != 0) return F16_ERR_ARG;
+      L.group_end[g] = end;
+      tiles += (end - start + TILE_M - 1) / TILE_M;
+      start = end;
+    }
     for (int k = 0; k < 2; k++) {
       int net = k < a->nets_per_group ? a->group_net[g * a->nets_per_group + k] : -1;
       if (net >= set->n) return F16_ERR_ARG;
@@ -899,8 +910,10 @@ extern "C" int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args*
       }
       L.group_net[g][k] = net;
     }
-    start = end;
   }
+  // device-resident ends: every tile of every group lies in [0, rows), at most one partial tile
+  // per group
+  if (dev_ends) tiles = (a->rows + TILE_M - 1) / TILE_M + a->n_groups;
   if (in_pad < 0 || a->ldx < 8) return F16_ERR_ARG;
   L.tiles_total = tiles;
   L.bins = a->bins; L.bins_stride = a->bins_stride; L.bins_offset = a->bins_offset;

@@ -553,6 +553,71 @@ extern "C" int f16_norm_apply_half(const float* x, int64_t B, int D, int64_t ldx
   return launch_status();
 }
 
+namespace f16 {
+namespace ro {
+// One warp per input row: the row's group picks its normaliser (or none), the 16-bit result goes
+// to the row's destination in the grouped, tile-aligned policy input.
+template <bool FP16>
+__global__ void __launch_bounds__(NORM_THREADS)
+k_norm_apply_scatter(const float* __restrict__ x, int64_t B, int D, int64_t ldx, const int64_t* __restrict__ grp,
+                     const int64_t* __restrict__ dst, const float* const* __restrict__ means,
+                     const float* const* __restrict__ vars, int n_groups, float eps, float clip,
+                     uint16_t* __restrict__ y, int64_t ldh, unsigned* __restrict__ nonfinite) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * (NORM_THREADS / 32) + (threadIdx.x >> 5);
+  if (r >= B) return;
+  const int64_t g = grp[r];
+  if (g < 0 || g >= n_groups) {
+    if (lane == 0 && nonfinite) atomicOr(nonfinite, 0x80000000u);
+    return;
+  }
+  const float* mu = means[g];
+  const float* va = vars[g];
+  const bool norm = mu != nullptr && va != nullptr;
+  uint16_t* out = y + dst[r] * ldh;
+  bool bad = false;
+  for (int d = lane; d < ldh; d += 32) {
+    if (d < D) {
+      float o = x[r * ldx + d];
+      if (norm) {
+        o = __fdiv_rn(__fsub_rn(o, mu[d]), __fsqrt_rn(__fadd_rn(va[d], eps)));
+        o = o < -clip ? -clip : (o > clip ? clip : o);
+      }
+      bad |= !isfinite(o);
+      out[d] = to_half_bits<FP16>(o);
+    } else {
+      out[d] = 0;
+    }
+  }
+  if (nonfinite && __any_sync(0xffffffffu, bad) && lane == 0) atomicAdd(nonfinite, 1u);
+}
+}  // namespace ro
+}  // namespace f16
+
+extern "C" int f16_norm_apply_scatter(const float* x, int64_t B, int D, int64_t ldx, const int64_t* group_of_row,
+                                      const int64_t* dst_row, const float* const* mean_ptrs,
+                                      const float* const* var_ptrs, int n_groups, double eps, double clip,
+                                      void* y_half, int64_t ldh, int operand, uint32_t* nonfinite,
+                                      f16_stream_t stream) {
+  if (!x || !group_of_row || !dst_row || !mean_ptrs || !var_ptrs || !y_half || B < 0 || D <= 0 || ldx < D ||
+      ldh < D || n_groups < 1)
+    return F16_ERR_ARG;
+  if (operand != F16_OPERAND_BF16 && operand != F16_OPERAND_FP16) return F16_ERR_ARG;
+  if (B == 0) return F16_OK;
+  const unsigned grid = (unsigned)((B + ro::NORM_THREADS / 32 - 1) / (ro::NORM_THREADS / 32));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint16_t* y = reinterpret_cast<uint16_t*>(y_half);
+  if (operand == F16_OPERAND_FP16)
+    ro::k_norm_apply_scatter<true><<<grid, ro::NORM_THREADS, 0, s>>>(x, B, D, ldx, group_of_row, dst_row, mean_ptrs,
+                                                                     var_ptrs, n_groups, (float)eps, (float)clip, y,
+                                                                     ldh, nonfinite);
+  else
+    ro::k_norm_apply_scatter<false><<<grid, ro::NORM_THREADS, 0, s>>>(x, B, D, ldx, group_of_row, dst_row, mean_ptrs,
+                                                                      var_ptrs, n_groups, (float)eps, (float)clip, y,
+                                                                      ldh, nonfinite);
+  return launch_status();
+}
+
 // ---------------------------------------------------------------------------------------------
 // RunningNorm update with library-owned scratch (no counterpart in the reference).
 //

@@ -37,7 +37,7 @@ class PolicyArgs(C.Structure):
                 ("logp", C.c_void_p), ("value", C.c_void_p), ("logits", C.c_void_p), ("logits_ld", C.c_int64),
                 ("seed", C.c_uint64), ("step", C.c_uint64), ("deterministic", C.c_int), ("err", C.c_void_p),
                 ("cmd", C.c_void_p), ("cmd_stride", C.c_int64), ("cmd_offset", C.c_int), ("grid", C.c_void_p),
-                ("step_dev", C.c_void_p)]
+                ("step_dev", C.c_void_p), ("group_end_dev", C.c_void_p)]
 
 
 class MlpWeights:
@@ -142,17 +142,22 @@ class PolicySet:
 
     def forward(self, x, groups, nets_per_group=1, bins=None, bins_stride=4, bins_offset=0, act_idx=None,
                 logp=None, value=None, logits=None, seed=0, step=0, deterministic=False, cmd=None, cmd_stride=4,
-                cmd_offset=0, grid=None, step_dev=None):
+                cmd_offset=0, grid=None, step_dev=None, group_end_dev=None):
         """groups: list of (row_end, [net indices]) with every group starting at a multiple of 128;
         ``x`` is the (rows, ldx) policy input in the set's operand dtype (``self.dtype``).
 
         ``cmd`` (fp64, optional) receives action_to_env of the sampled bins at
         ``cmd[r * cmd_stride + cmd_offset + c]`` using the fp32 ``grid`` (num_bins values).
         ``step_dev`` (device int64 [1], optional) is added to ``step`` when the kernel runs, so a
-        captured CUDA graph draws fresh samples on every replay."""
+        captured CUDA graph draws fresh samples on every replay.  ``group_end_dev`` (device int64
+        [len(groups)], optional) supplies the groups' cumulative row ends from device memory, so a
+        grouping computed on the device needs no host round trip; the row ends in ``groups`` are
+        then ignored (only the network indices are used)."""
         _lib.require_cuda_tensor(x, self.dtype, None, "policy input", None)
         rows, ldx = x.shape[0], x.stride(0)
-        ends = (C.c_int64 * len(groups))(*[int(g[0]) for g in groups])
+        if group_end_dev is not None:
+            _lib.require_cuda_tensor(group_end_dev, torch.int64, (len(groups),), "group ends", x.device)
+        ends = (C.c_int64 * len(groups))(*[0 if group_end_dev is not None else int(g[0]) for g in groups])
         flat = []
         for _, ids in groups:
             ids = list(ids) + [-1] * (nets_per_group - len(ids))
@@ -170,6 +175,7 @@ class PolicySet:
         a.logits_ld = logits.stride(0) if logits is not None else 0
         a.seed = seed & (2 ** 64 - 1); a.step = step & (2 ** 64 - 1); a.deterministic = int(bool(deterministic))
         a.err = self.err.data_ptr()
+        a.group_end_dev = group_end_dev.data_ptr() if group_end_dev is not None else None
         if step_dev is not None:
             _lib.require_cuda_tensor(step_dev, torch.int64, (1,), "step counter", x.device)
             a.step_dev = step_dev.data_ptr()

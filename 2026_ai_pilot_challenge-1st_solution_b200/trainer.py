@@ -19,7 +19,10 @@ Mirrors ``PPOGPUTrainer`` of the reference (R/cuda_fdm/ppo_gpu.py) for the MLP a
 Opponents: ``opp_mode="blocks"`` gives opponent g the contiguous environment block g (the
 benchmark configuration); ``opp_mode="pool"`` keeps a per-environment assignment resampled at
 episode ends from ``opp_weights`` (``_sample_opp``, :1306-1309) and regroups the rows each step
-(one small host transfer of the group sizes, as ``ActiveLeaguePool.act`` does, :879-880).
+on the device -- counts, tile-padded group ends and destination rows from torch ops, one
+normalise-and-scatter launch with each opponent's own normaliser, one grouped policy launch that
+reads the group ends from device memory -- so, unlike ``ActiveLeaguePool.act``'s
+``bincount().cpu()`` (:879-880), a step never waits on the host.
 """
 import ctypes as C
 import dataclasses
@@ -33,13 +36,14 @@ from . import _lib
 from . import categorical
 from . import splitmm
 from .policy import HEAD_CATEGORICAL, HEAD_VALUE, MlpWeights, PolicySet
-from .rollout import RunningNorm, cast_half, gae, make_action_grid
+from .rollout import RunningNorm, cast_half, gae, half_operand, make_action_grid
 
 OBS_DIM = 184
 ACT_DIM = 4
 ACTION_BINS = 21
-IN_PAD = 192            # bf16 policy input row: 184 features + zero padding to a 64-byte multiple
+IN_PAD = 192            # 16-bit policy input row: 184 features + zero padding to a 64-byte multiple
 TILE_ROWS = 128         # MLP kernel row tile; opponent groups start on a multiple of it
+NORM_CLIP, NORM_EPS = 10.0, 1e-8    # RunningNorm's clip and eps (ppo_gpu.py:184-222)
 
 _ACTIVATIONS = {"tanh": nn.Tanh, "relu": nn.ReLU}
 
@@ -365,8 +369,21 @@ class PPOTrainer:
         self.x_main = torch.zeros(n, IN_PAD, dtype=self.policy.dtype, device=dev)
         pad_rows = n + P * TILE_ROWS
         self.x_opp = torch.zeros(pad_rows, IN_PAD, dtype=self.policy.dtype, device=dev)
-        self._opp_f32 = torch.zeros(pad_rows, OBS_DIM, device=dev) if opp_mode == "pool" else None
         self._opp_cmd = torch.zeros(pad_rows, ACT_DIM, dtype=torch.float64, device=dev) if opp_mode == "pool" else None
+        if opp_mode == "pool":
+            # device-side grouping buffers and each opponent's normaliser statistics (NULL: none)
+            self._pool_counts = torch.zeros(P, dtype=torch.int64, device=dev)
+            self._pool_ends = torch.zeros(P, dtype=torch.int64, device=dev)
+            self._pool_ones = torch.ones(n, dtype=torch.int64, device=dev)
+            self._pool_iota = torch.arange(n, dtype=torch.int64, device=dev)
+            self._pool_rank = torch.zeros(n, dtype=torch.int64, device=dev)
+            for o in self.opponents:
+                if o.norm is not None and (o.norm.clip != NORM_CLIP or o.norm.eps != NORM_EPS):
+                    raise ValueError("pool-mode opponent normalisers must use the trainer's clip and eps")
+            self._pool_mean_ptrs = torch.tensor([o.norm.mean.data_ptr() if o.norm is not None else 0
+                                                 for o in self.opponents], dtype=torch.int64, device=dev)
+            self._pool_var_ptrs = torch.tensor([o.norm.var.data_ptr() if o.norm is not None else 0
+                                                for o in self.opponents], dtype=torch.int64, device=dev)
         self.last_value = torch.zeros(n, device=dev)
         self.ep_ret = torch.zeros(n, device=dev)
         self.ep_len = torch.zeros(n, device=dev)
@@ -431,24 +448,26 @@ class PPOTrainer:
             self.policy.forward(self.x_opp[:self.nenv], groups, cmd=cmd, cmd_stride=2 * ACT_DIM, cmd_offset=ACT_DIM,
                                 **kw)
             return
+        # pool: rows grouped by assigned opponent on the device (no host round trip): per-group
+        # counts, tile-padded cumulative ends, and each env's destination row (its rank within
+        # its group after a stable sort, as the reference's argsort + split, ppo_gpu.py:877-898)
         rows = self.opp_assign
-        counts = torch.bincount(rows, minlength=len(self.opponents)).cpu().tolist()
+        P = len(self.opponents)
+        counts = self._pool_counts.zero_().index_add_(0, rows, self._pool_ones)
+        padded = (counts + (TILE_ROWS - 1)) // TILE_ROWS * TILE_ROWS
+        torch.cumsum(padded, 0, out=self._pool_ends)
         order = torch.argsort(rows, stable=True)
-        groups, lanes, dst, off, c0 = [], [], [], 0, 0
-        for g, c in enumerate(counts):
-            if c == 0:
-                continue
-            ln = order[c0:c0 + c]
-            c0 += c
-            torch.index_select(opp_obs, 0, ln, out=self._opp_f32[off:off + c])
-            self._normalize_into(self.opponents[g].norm, self._opp_f32[off:off + c], self.x_opp[off:off + c])
-            lanes.append(ln)
-            dst.append(torch.arange(off, off + c, device=self.device))
-            off += -(-c // TILE_ROWS) * TILE_ROWS     # groups are contiguous: pad rows to the tile
-            groups.append((off, [2 + g]))
-        self.policy.forward(self.x_opp[:off], groups, cmd=self._opp_cmd, cmd_stride=ACT_DIM, cmd_offset=0, **kw)
-        cmd.view(self.nenv, 2 * ACT_DIM)[:, ACT_DIM:].index_copy_(
-            0, torch.cat(lanes), self._opp_cmd.index_select(0, torch.cat(dst)))
+        self._pool_rank.index_copy_(0, order, self._pool_iota)
+        first = torch.cumsum(counts, 0) - counts                  # sorted position of each group's first row
+        dst = (self._pool_ends - padded).index_select(0, rows) + self._pool_rank - first.index_select(0, rows)
+        _lib.check(self._lib.f16_norm_apply_scatter(
+            _lib.ptr(opp_obs), self.nenv, OBS_DIM, opp_obs.stride(0), _lib.ptr(rows), _lib.ptr(dst),
+            _lib.ptr(self._pool_mean_ptrs), _lib.ptr(self._pool_var_ptrs), P, NORM_EPS, NORM_CLIP,
+            _lib.ptr(self.x_opp), self.x_opp.stride(0), half_operand(self.x_opp), None,
+            _lib.stream_of(self.x_opp)), "f16_norm_apply_scatter")
+        self.policy.forward(self.x_opp, [(0, [2 + g]) for g in range(P)], group_end_dev=self._pool_ends,
+                            cmd=self._opp_cmd, cmd_stride=ACT_DIM, cmd_offset=0, **kw)
+        cmd.view(self.nenv, 2 * ACT_DIM)[:, ACT_DIM:].copy_(self._opp_cmd.index_select(0, dst))
 
     # ---- rollout (ppo_gpu.py:1856-2017) ----
     @torch.no_grad()

@@ -301,6 +301,11 @@ typedef struct {
   /* optional device counter added to `step` when the kernel runs (NULL: none), so one captured
    * CUDA graph can be replayed with a fresh RNG step each time */
   const uint64_t* step_dev;
+  /* optional device int64 [n_groups]: the groups' cumulative row ends read by the kernel instead
+   * of group_end (which is then ignored), for a grouping computed on the device without a host
+   * round trip (the frozen-opponent pool, ppo_gpu.py:877-898).  Ends past `rows` are clamped;
+   * group_net stays a host array. */
+  const int64_t* group_end_dev;
 } f16_policy_args;
 
 int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args* args, f16_stream_t stream);
@@ -367,6 +372,19 @@ int f16_norm_apply_checked(const float* x, int64_t B, int D, int64_t ldx, const 
 int f16_norm_apply_half(const float* x, int64_t B, int D, int64_t ldx, const float* mean,
                         const float* var, double eps, double clip, float* y, int64_t ldy,
                         void* y_half, int64_t ldh, int operand, uint32_t* nonfinite, f16_stream_t stream);
+
+/* Per-row-group normalise + scatter into a 16-bit policy input (no counterpart in the
+ * reference, which runs one torch normalise per pool entry after a host-synchronised split,
+ * ppo_gpu.py:877-898): row r of x [B][ldx] fp32 (D features) is normalised with the statistics
+ * of group g = group_of_row[r] (mean_ptrs[g] / var_ptrs[g], device arrays of n_groups device
+ * pointers to fp32 [D]; a NULL pair passes the row through unchanged) and written to row
+ * dst_row[r] of y_half [*][ldh] (columns D..ldh-1 zero).  group_of_row and dst_row: device int64
+ * [B]; a group index outside [0, n_groups) is an error recorded in *nonfinite's bit 31 (the row
+ * is skipped), so nothing is read from a bad pointer. */
+int f16_norm_apply_scatter(const float* x, int64_t B, int D, int64_t ldx, const int64_t* group_of_row,
+                           const int64_t* dst_row, const float* const* mean_ptrs, const float* const* var_ptrs,
+                           int n_groups, double eps, double clip, void* y_half, int64_t ldh, int operand,
+                           uint32_t* nonfinite, f16_stream_t stream);
 
 /* Per-step bookkeeping of collect_rollout (ppo_gpu.py:1914-1960) in one launch, after the env
  * step: b_rew[e] = (float)reward[2e]; next_done[e] = done[e]; ep_ret / ep_len updated and

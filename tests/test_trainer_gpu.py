@@ -124,9 +124,18 @@ def test_rollout_blocks_and_update(cuda):
 
 
 def test_rollout_pool_assignment(cuda):
+    """Pool mode: the whole rollout runs without a host synchronisation (torch's sync debug mode
+    raises on any), and each env's opponent command is its assigned opponent's argmax on its
+    (normalised) input, grouped in tile-aligned blocks as the reference's argsort + split."""
     t, tr = make_trainer(cuda, 512, 3, "pool", 4)
     t.reset(stagger=False)
-    adv, ret, _ = t.collect_rollout()
+    t.collect_rollout()                      # first use of every buffer, outside the check
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        adv, ret, _ = t.collect_rollout()
+    finally:
+        torch.cuda.set_sync_debug_mode("default")
     torch.cuda.synchronize()
     check_rollout(t, adv, ret)
     rows = t.opp_assign
