@@ -418,7 +418,12 @@ class PPOTrainer:
             self.opp_assign = self._sample_opp(self.nenv)
 
     def _sample_opp(self, n):
-        return torch.multinomial(self.opp_weights, n, replacement=True)
+        """n opponent indices drawn with probabilities proportional to ``opp_weights`` (the
+        reference's multinomial with replacement, :1306-1309), as an inverse-CDF lookup of
+        uniform draws so no step waits on the host."""
+        cdf = torch.cumsum(self.opp_weights, 0)
+        u = torch.rand(n, device=self.device) * cdf[-1]
+        return torch.searchsorted(cdf, u, right=True).clamp_(max=len(self.opponents) - 1)
 
     def _normalize_into(self, norm, x, out_half, out_f32=None, nonfinite=None):
         if norm is not None:

@@ -124,18 +124,29 @@ def test_rollout_blocks_and_update(cuda):
 
 
 def test_rollout_pool_assignment(cuda):
-    """Pool mode: the whole rollout runs without a host synchronisation (torch's sync debug mode
-    raises on any), and each env's opponent command is its assigned opponent's argmax on its
-    (normalised) input, grouped in tile-aligned blocks as the reference's argsort + split."""
+    """Pool mode: a decision's opponent path (assignment resampling at episode ends, device-side
+    grouping, grouped normalise, grouped policy launch, command scatter) and env step run without
+    a host synchronisation (torch's sync debug mode raises on any; the rollout's once-per-rollout
+    finiteness check stays outside), and each env's opponent command is its assigned opponent's
+    argmax on its (normalised) input, grouped in tile-aligned blocks as the reference's
+    argsort + split."""
     t, tr = make_trainer(cuda, 512, 3, "pool", 4)
     t.reset(stagger=False)
     t.collect_rollout()                      # first use of every buffer, outside the check
     torch.cuda.synchronize()
+    cmd = t.env.action_buffer
     torch.cuda.set_sync_debug_mode("error")
     try:
-        adv, ret, _ = t.collect_rollout()
+        for _ in range(3):
+            sampled = t._sample_opp(t.nenv)
+            t.opp_assign = torch.where(t._next_done.bool(), sampled, t.opp_assign)
+            t._opponents_act(cmd)
+            obs, _, done, _ = t.env.step(cmd)
+            t._next_opp_obs = obs[:, 1, :]
+            t._next_done.copy_(done)
     finally:
         torch.cuda.set_sync_debug_mode("default")
+    adv, ret, _ = t.collect_rollout()
     torch.cuda.synchronize()
     check_rollout(t, adv, ret)
     rows = t.opp_assign
@@ -152,3 +163,6 @@ def test_rollout_pool_assignment(cuda):
         agree += int((cmd[lanes, 1] == action_to_env(lg.argmax(-1), t.grid)).all(-1).sum())
         off += -(-c // 128) * 128
     assert agree >= 0.99 * t.nenv, f"opponent commands agree on {agree}/{t.nenv} rows"
+    # the assignment follows opp_weights (1 : 1.5 : 2 over three opponents, 512 envs resampled)
+    freq = torch.bincount(t._sample_opp(200_000), minlength=3).float() / 200_000
+    assert torch.allclose(freq.cpu(), torch.tensor([1.0, 1.5, 2.0]) / 4.5, atol=0.01)
