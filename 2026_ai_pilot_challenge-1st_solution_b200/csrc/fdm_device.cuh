@@ -39,6 +39,13 @@ constexpr int ATM_RDB = ATM_TOL + 8;             // 1/rho_b                     
 constexpr int ATM_LTB = ATM_RDB + 9;             // log(T_b)                       (8)
 constexpr int SMEM_DOUBLES = ATM_LTB + 8;
 
+// Threads per block of the FDM kernels (one aircraft per thread).
+#ifndef F16_FDM_THREADS
+#define F16_FDM_THREADS 256
+#endif
+constexpr int FDM_THREADS = F16_FDM_THREADS;
+
+
 __device__ const double g_tab[F16_TAB_LEN] = {F16_TAB_VALUES};
 
 constexpr double DT = 1.0 / 60.0;
@@ -103,11 +110,14 @@ __device__ __forceinline__ void stage_tables(double* __restrict__ S) {
     double d = S[i + 1] - S[i];
     S[TAB_RSPAN + i] = (d != 0.0) ? 1.0 / d : 0.0;
   }
-  if (threadIdx.x == 0) {
+  // per-layer atmosphere constants: thread b computes layer b (the block waits at the barrier
+  // below for the slowest layer only)
+  if (threadIdx.x < 8) {
     const double* AL = S + F16T_ATM_ALT;
     const double* LA = S + F16T_ATM_LAPSE;
     const double gm = F16C_g0 * F16C_Mair;
-    for (int b = 0; b < 8; b++) {
+    {
+      const int b = threadIdx.x;
       // base temperature as the reference evaluates it: T(geometric(base altitude)) (fdm.cuh:190)
       double gp_b = AL[b];
       double h = (gp_b * F16C_EarthRadius) / (F16C_EarthRadius - gp_b);
@@ -138,8 +148,8 @@ __device__ __forceinline__ void stage_tables(double* __restrict__ S) {
       S[ATM_TOL + b] = (L != 0.0) ? Tt / L : 0.0;
       S[ATM_LTB + b] = log(Tb);
     }
-    for (int b = 0; b < 9; b++) S[ATM_RDB + b] = 1.0 / S[F16T_ATM_DBRK + b];
   }
+  if (threadIdx.x < 9) S[ATM_RDB + threadIdx.x] = 1.0 / S[F16T_ATM_DBRK + threadIdx.x];
   __syncthreads();
 }
 
@@ -521,10 +531,11 @@ __device__ __forceinline__ void propagate(Ac& s) {
 
 // Kinematics + force path + derivative update of the reference fdm_step (fdm.cuh:629-648).
 // gear_pos: landing-gear actuator output, constant per launch (seeded to 0.30 every frame).
-template <bool WANT_OUT>
+// want_out: this frame's air data / euler angles go to `out` and the accelerations to the state's
+// previous-frame fields (a literal at the call site folds the branches away)
 __device__ __forceinline__ void dynamics(const double* __restrict__ S, Ac& s, double c_ail, double c_ele,
                                          double c_rud, double c_thr, double fcs_dt, double inv_fcs_dt,
-                                         double gear_pos, FrameOut& out) {
+                                         double gear_pos, FrameOut& out, const bool WANT_OUT) {
   // ---- kinematics (fdm.cuh:544-563) in ECI ----
   const double px = s.pos[0], py = s.pos[1], pz = s.pos[2];
   // reciprocal square roots, the lengths as products (rounding-level differences from

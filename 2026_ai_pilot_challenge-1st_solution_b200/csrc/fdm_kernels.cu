@@ -15,13 +15,9 @@ namespace f16 {
 // 128x3 (168 regs) 0.304 ms, 128x4 0.259 ms, 128x5 (96 regs) 0.286 ms, 256x2 0.253 ms; at higher
 // occupancy the spills win nothing back: 256x3 (85 regs) 1.9e9 frames/s, 256x4 / 128x8
 // (64 regs) 2.3e9 / 2.2e9 against 3.0e9 for 256x2.
-#ifndef F16_FDM_THREADS
-#define F16_FDM_THREADS 256
-#endif
 #ifndef F16_FDM_MIN_BLOCKS
 #define F16_FDM_MIN_BLOCKS 2
 #endif
-constexpr int FDM_THREADS = F16_FDM_THREADS;
 constexpr int FDM_MIN_BLOCKS = F16_FDM_MIN_BLOCKS;
 constexpr size_t FDM_SMEM = SMEM_DOUBLES * sizeof(double);
 
@@ -66,40 +62,42 @@ __device__ __forceinline__ void load_state(const StateRef<LAYOUT>& R, int64_t a,
   load_factor(s.fuel, s.pbacc, s.ppqridot, s.ppqri, s.nld);
 }
 
-// Non-finite test on the exponent bits (all-ones exponent = inf or NaN); `bad` ORs it up.
+// Non-finite test on the exponent bits (all-ones exponent = inf or NaN); `bad` ORs it up.  The
+// kernels that report no finite flag are built with CHECK = false and skip the test.
+template <bool CHECK = true>
 __device__ __forceinline__ double fin(double v, unsigned& bad) {
-  bad |= (unsigned)((__double2hiint(v) & 0x7ff00000) == 0x7ff00000);
+  if (CHECK) bad |= (unsigned)((__double2hiint(v) & 0x7ff00000) == 0x7ff00000);
   return v;
 }
 
-template <int LAYOUT>
+template <int LAYOUT, bool CHECK = true>
 __device__ __forceinline__ void store_state(const StateRef<LAYOUT>& R, int64_t a, const Ac& s, unsigned& bad) {
 #pragma unroll
   for (int i = 0; i < 3; i++) {
-    R(a, F16_S_POS + i) = fin(s.pos[i], bad);
-    R(a, F16_S_VEL + i) = fin(s.vel[i], bad);
-    R(a, F16_S_PQRI + i) = fin(s.pqri[i], bad);
-    R(a, F16_S_UVWIDOT + i) = fin(s.uvwidot[i], bad);
-    R(a, F16_S_PQRIDOT + i) = fin(s.pqridot[i], bad);
-    R(a, F16_S_PREV_BACC + i) = fin(s.pbacc[i], bad);
-    R(a, F16_S_PREV_PQRIDOT + i) = fin(s.ppqridot[i], bad);
-    R(a, F16_S_PREV_PQRI + i) = fin(s.ppqri[i], bad);
+    R(a, F16_S_POS + i) = fin<CHECK>(s.pos[i], bad);
+    R(a, F16_S_VEL + i) = fin<CHECK>(s.vel[i], bad);
+    R(a, F16_S_PQRI + i) = fin<CHECK>(s.pqri[i], bad);
+    R(a, F16_S_UVWIDOT + i) = fin<CHECK>(s.uvwidot[i], bad);
+    R(a, F16_S_PQRIDOT + i) = fin<CHECK>(s.pqridot[i], bad);
+    R(a, F16_S_PREV_BACC + i) = fin<CHECK>(s.pbacc[i], bad);
+    R(a, F16_S_PREV_PQRIDOT + i) = fin<CHECK>(s.ppqridot[i], bad);
+    R(a, F16_S_PREV_PQRI + i) = fin<CHECK>(s.ppqri[i], bad);
   }
 #pragma unroll
   for (int i = 0; i < 4; i++) {
-    R(a, F16_S_Q + i) = fin(s.q[i], bad);
-    R(a, F16_S_QDOT + i) = fin(s.qdot[i], bad);
-    R(a, F16_S_ENG + i) = fin(s.eng[i], bad);
+    R(a, F16_S_Q + i) = fin<CHECK>(s.q[i], bad);
+    R(a, F16_S_QDOT + i) = fin<CHECK>(s.qdot[i], bad);
+    R(a, F16_S_ENG + i) = fin<CHECK>(s.eng[i], bad);
   }
-  R(a, F16_S_EPA) = fin(s.epa, bad);
-  R(a, F16_S_FUEL) = fin(s.fuel, bad);
+  R(a, F16_S_EPA) = fin<CHECK>(s.epa, bad);
+  R(a, F16_S_FUEL) = fin<CHECK>(s.fuel, bad);
 #pragma unroll
   for (int i = 0; i < 9; i++) {
-    R(a, F16_S_PREV_AUX + i) = fin(s.pa[i], bad);
-    R(a, F16_S_PID + i) = fin(s.pid[i], bad);
+    R(a, F16_S_PREV_AUX + i) = fin<CHECK>(s.pa[i], bad);
+    R(a, F16_S_PID + i) = fin<CHECK>(s.pid[i], bad);
   }
 #pragma unroll
-  for (int i = 0; i < 6; i++) R(a, F16_S_KIN + i) = fin(s.kin[i], bad);
+  for (int i = 0; i < 6; i++) R(a, F16_S_KIN + i) = fin<CHECK>(s.kin[i], bad);
 }
 
 template <int LAYOUT>
@@ -110,16 +108,16 @@ __device__ __forceinline__ void store_state(const StateRef<LAYOUT>& R, int64_t a
 
 // Store the values pushed into the four integrator histories in frame i into the deque slot
 // j = substeps-1-i they occupy when the launch ends (only slots j <= 2 exist).
-template <int LAYOUT>
+template <int LAYOUT, bool CHECK = true>
 __device__ __forceinline__ void store_history(const StateRef<LAYOUT>& R, int64_t a, int j, const Ac& s,
                                               unsigned& bad) {
 #pragma unroll
-  for (int i = 0; i < 4; i++) R(a, F16_S_DEQ_Q + 4 * j + i) = fin(s.qdot[i], bad);
+  for (int i = 0; i < 4; i++) R(a, F16_S_DEQ_Q + 4 * j + i) = fin<CHECK>(s.qdot[i], bad);
 #pragma unroll
   for (int i = 0; i < 3; i++) {
-    R(a, F16_S_DEQ_PQRI + 3 * j + i) = fin(s.pqridot[i], bad);
-    R(a, F16_S_DEQ_IVEL + 3 * j + i) = fin(s.vel[i], bad);
-    R(a, F16_S_DEQ_UVWIDOT + 3 * j + i) = fin(s.uvwidot[i], bad);
+    R(a, F16_S_DEQ_PQRI + 3 * j + i) = fin<CHECK>(s.pqridot[i], bad);
+    R(a, F16_S_DEQ_IVEL + 3 * j + i) = fin<CHECK>(s.vel[i], bad);
+    R(a, F16_S_DEQ_UVWIDOT + 3 * j + i) = fin<CHECK>(s.uvwidot[i], bad);
   }
 }
 
@@ -130,7 +128,7 @@ __device__ __forceinline__ void store_history(const StateRef<LAYOUT>& R, int64_t
 }
 
 // With fewer than 3 frames per launch the oldest surviving slots are the old ones shifted.
-template <int LAYOUT>
+template <int LAYOUT, bool CHECK = true>
 __device__ __forceinline__ void shift_old_history(const StateRef<LAYOUT>& R, int64_t a, int substeps, unsigned& bad) {
   if (substeps >= 3) return;
   double q0[4], q1[4], p0[3], p1[3], v0[3], v1[3], u0[3], u1[3];
@@ -146,17 +144,17 @@ __device__ __forceinline__ void shift_old_history(const StateRef<LAYOUT>& R, int
   for (int j = substeps; j <= 2; j++) {
     int o = j - substeps;
 #pragma unroll
-    for (int i = 0; i < 4; i++) R(a, F16_S_DEQ_Q + 4 * j + i) = fin(o == 0 ? q0[i] : q1[i], bad);
+    for (int i = 0; i < 4; i++) R(a, F16_S_DEQ_Q + 4 * j + i) = fin<CHECK>(o == 0 ? q0[i] : q1[i], bad);
 #pragma unroll
     for (int i = 0; i < 3; i++) {
-      R(a, F16_S_DEQ_PQRI + 3 * j + i) = fin(o == 0 ? p0[i] : p1[i], bad);
-      R(a, F16_S_DEQ_IVEL + 3 * j + i) = fin(o == 0 ? v0[i] : v1[i], bad);
-      R(a, F16_S_DEQ_UVWIDOT + 3 * j + i) = fin(o == 0 ? u0[i] : u1[i], bad);
+      R(a, F16_S_DEQ_PQRI + 3 * j + i) = fin<CHECK>(o == 0 ? p0[i] : p1[i], bad);
+      R(a, F16_S_DEQ_IVEL + 3 * j + i) = fin<CHECK>(o == 0 ? v0[i] : v1[i], bad);
+      R(a, F16_S_DEQ_UVWIDOT + 3 * j + i) = fin<CHECK>(o == 0 ? u0[i] : u1[i], bad);
     }
   }
 }
 
-template <int LAYOUT, bool BINS>
+template <int LAYOUT, bool BINS, bool CHECK>
 __global__ void __launch_bounds__(FDM_THREADS, FDM_MIN_BLOCKS)
 k_fdm_step(double* __restrict__ st, int64_t ld, int64_t nac, const double* __restrict__ cmd,
            const uint8_t* __restrict__ bins, const BinGrid grid, int substeps, double fcs_dt,
@@ -180,19 +178,19 @@ k_fdm_step(double* __restrict__ st, int64_t ld, int64_t nac, const double* __res
     Ac s;
     unsigned bad = 0;                       // any stored state value non-finite
     load_state(R, a, s);
-    shift_old_history(R, a, substeps, bad);
+    shift_old_history<LAYOUT, CHECK>(R, a, substeps, bad);
     FrameOut out;
     for (int i = 0; i < substeps - 1; i++) {
       int j = substeps - 1 - i;
-      if (j <= 2) store_history(R, a, j, s, bad);
+      if (j <= 2) store_history<LAYOUT, CHECK>(R, a, j, s, bad);
       propagate(s);
-      dynamics<false>(S, s, c0, c1, c2, c3, fcs_dt, inv_fcs_dt, gear, out);
+      dynamics(S, s, c0, c1, c2, c3, fcs_dt, inv_fcs_dt, gear, out, false);
     }
-    store_history(R, a, 0, s, bad);
+    store_history<LAYOUT, CHECK>(R, a, 0, s, bad);
     propagate(s);
-    dynamics<true>(S, s, c0, c1, c2, c3, fcs_dt, inv_fcs_dt, gear, out);
-    store_state(R, a, s, bad);
-    if (finite) finite[a] = bad ? 0 : 1;
+    dynamics(S, s, c0, c1, c2, c3, fcs_dt, inv_fcs_dt, gear, out, true);
+    store_state<LAYOUT, CHECK>(R, a, s, bad);
+    if (CHECK) finite[a] = bad ? 0 : 1;
     if (obs17) {
       double* o = obs17 + 17 * a;
       o[0] = s.pos[0]; o[1] = s.pos[1]; o[2] = s.pos[2];
@@ -316,7 +314,7 @@ k_seed_ic(const double* __restrict__ ic, int64_t nac, double* __restrict__ st, i
     for (int i = 0; i < 3; i++) { s.pbacc[i] = 0.0; s.ppqridot[i] = 0.0; s.ppqri[i] = s.pqri[i]; }
     load_factor(s.fuel, s.pbacc, s.ppqridot, s.ppqri, s.nld);
     FrameOut out;
-    dynamics<true>(S, s, 0.0, 0.0, 0.0, 0.8, fcs_dt, 1.0 / fcs_dt, gear, out);
+    dynamics(S, s, 0.0, 0.0, 0.0, 0.8, fcs_dt, 1.0 / fcs_dt, gear, out, true);
     // outputs: the derivatives; everything else returns to the fresh / IC values
     s.fuel = fuel;
     for (int i = 0; i < 9; i++) s.pa[i] = pa_ic[i];
@@ -343,13 +341,13 @@ int persistent_grid(K kernel, int64_t nac, size_t smem) {
 template <int LAYOUT, bool BINS>
 int launch_step(double* st, int64_t ld, int64_t nac, const double* cmd, const uint8_t* bins, const BinGrid& g,
                 int substeps, double fcs_dt, double* obs17, cudaStream_t stream, uint8_t* finite = nullptr) {
-  auto k = k_fdm_step<LAYOUT, BINS>;
-  static bool attr_set[64] = {false};
+  auto k = finite ? k_fdm_step<LAYOUT, BINS, true> : k_fdm_step<LAYOUT, BINS, false>;
+  static bool attr_set[2][64] = {{false}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+  if (dev >= 0 && dev < 64 && !attr_set[finite ? 1 : 0][dev]) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FDM_SMEM);
-    attr_set[dev] = true;
+    attr_set[finite ? 1 : 0][dev] = true;
   }
   int grid = persistent_grid(k, nac, FDM_SMEM);
   k<<<grid, FDM_THREADS, FDM_SMEM, stream>>>(st, ld, nac, cmd, bins, g, substeps, fcs_dt, obs17, finite);
