@@ -67,3 +67,19 @@ def test_update_entry_points_reject_bad_arguments_before_any_launch():
     assert lib.f16_categorical_fwd(p, 84, 4, 4, 33, p, 1, p, p, p, None) == 1      # B > 32
     assert lib.f16_categorical_fwd(p, 84, 4, 4, 21, p, 2, p, p, p, None) == 1      # action bytes 2
     assert lib.f16_categorical_bwd(p, 84, 4, 4, 21, p, 1, None, None, p, 80, None) == 1   # ldg < A*B
+
+
+def test_dropin_trace_fixture_covers_the_trainer_contract():
+    """The recorded reference-trainer contract (tests/golden/dropin_trace.json, replayed on the
+    GPU by test_dropin_gpu.py) holds the reset, one step per rollout step with the three info
+    keys the trainer reads, and the checkpoint reads / writes."""
+    import json
+    from conftest import GOLDEN
+    t = json.loads((GOLDEN / "dropin_trace.json").read_text())
+    calls = [e["path"] for e in t["ops"] if e["op"] == "call"]
+    assert calls.count("env.step") == t["rollout_steps"] and "env.reset" in calls
+    assert {"env.obr.clone_state", "env.obr.restore"} <= set(calls)
+    items = {e["path"].split("[")[-1] for e in t["ops"] if e["op"] == "item"}
+    assert items == {"'terminal_state_finite']", "'terminal_hp']", "'terminal_alt_m']"}
+    sets = {e["path"] for e in t["ops"] if e["op"] == "set"}
+    assert {"env.reward_mode", "env.alt_hunt_coef", "env.ic_pool"} <= sets
