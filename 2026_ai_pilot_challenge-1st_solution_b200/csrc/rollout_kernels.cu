@@ -624,8 +624,10 @@ extern "C" int f16_norm_apply_scatter(const float* x, int64_t B, int D, int64_t 
 // For callers that cannot allocate device memory at the point of the update: a fixed-size
 // memory pool or arena that is sealed once training starts, or a host driver that forbids
 // allocation inside its step loop.  The fp64 partial sums live in a file-scope device array of
-// F16_NORM_STATIC_SCRATCH_PAIRS double2 (2 MiB) instead of a caller buffer; its address is read
-// once per device with cudaGetSymbolAddress.  Every scratch slot that the merge kernel reads is
+// F16_NORM_STATIC_SCRATCH_PAIRS double2 (2 MiB) instead of a caller buffer; its device address
+// comes from cudaGetSymbolAddress with the device current: looked up again on every call made
+// outside a stream capture (so a device reset between calls leaves no stale address), and the
+// last address found is used inside a capture.  Every scratch slot that the merge kernel reads is
 // written by the partial kernel of the same call first, so nothing needs to start at zero.
 // There is one array per device, so two calls in flight at the same time on one device (two
 // streams, or two host threads) race on it; calls queued on one stream are ordered and safe.
@@ -637,12 +639,18 @@ constexpr int kMaxDevices = 64;
 std::mutex g_norm_static_mu;
 double2* g_norm_static_addr[kMaxDevices] = {};
 
-// Device address of g_norm_static_scratch on the current device (looked up on first use).
-int norm_static_scratch(double2** out) {
+// Device address of g_norm_static_scratch on the current device: looked up whenever `s` is not
+// capturing, the cached one while it is.
+int norm_static_scratch(cudaStream_t s, double2** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return F16_ERR_CUDA;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return F16_ERR_CUDA;
+  }
   std::lock_guard<std::mutex> lock(g_norm_static_mu);
-  if (!g_norm_static_addr[dev]) {
+  if (cs == cudaStreamCaptureStatusNone || !g_norm_static_addr[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_norm_static_scratch) != cudaSuccess || !p) {
       cudaGetLastError();
@@ -660,10 +668,10 @@ extern "C" int f16_norm_update_static(const float* x, int64_t B, int D, int64_t 
   if (!x || !mean || !var || !count || B <= 0 || D <= 0 || ldx < D) return F16_ERR_ARG;
   int64_t nblk = (B + ro::NORM_ROWS_PER_BLOCK - 1) / ro::NORM_ROWS_PER_BLOCK;
   if (nblk * D > (int64_t)F16_NORM_STATIC_SCRATCH_PAIRS) return F16_ERR_TOO_LARGE;
-  double2* part = nullptr;
-  int rc = norm_static_scratch(&part);
-  if (rc != F16_OK) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  double2* part = nullptr;
+  int rc = norm_static_scratch(s, &part);
+  if (rc != F16_OK) return rc;
   ro::launch_partial(x, B, D, ldx, part, nblk, s);
   ro::k_norm_merge<<<(D + 31) / 32, ro::NORM_THREADS, 0, s>>>(
       part, (int)nblk, B, D, mean, var, count);

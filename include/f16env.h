@@ -342,9 +342,10 @@ int f16_norm_merge_sums(const double* sums, int64_t B_total, int D, float* mean,
  * that may not allocate device memory inside their step loop (a sealed memory pool or arena):
  * the fp64 partial sums go to a library-owned device array of F16_NORM_STATIC_SCRATCH_PAIRS
  * (sum, sum of squares) pairs, so ceil(B / 512) * D must not exceed it (else
- * F16_ERR_TOO_LARGE, nothing launched).  No allocation happens in any call.  The first call on
- * a device looks up that array's address (cudaGetSymbolAddress, with the device current), so
- * make the first call before any stream capture.  Nothing needs to be zeroed beforehand.  The
+ * F16_ERR_TOO_LARGE, nothing launched).  No allocation happens in any call.  Every call made
+ * outside a stream capture looks that array's address up (cudaGetSymbolAddress, with the device
+ * current), so a device reset between calls is harmless; a call inside a capture uses the address
+ * the last uncaptured call found, so make one call on the device before any stream capture.  Nothing needs to be zeroed beforehand.  The
  * array is shared per device: calls that may run at the same time on one device (different
  * streams or host threads) race; calls on one stream are ordered. */
 #define F16_NORM_STATIC_SCRATCH_PAIRS 131072
