@@ -3,7 +3,8 @@
 // Replaces the rollout-time forwards of R/claude_code/model.py MLPDiscreteActorCritic
 // (actor_logits / critic, :162-241) as driven by ppo_gpu.py actor_step / value_step (:273-291)
 // and the frozen-opponent pools (:536-592, :877-898), including the Categorical sample and its
-// summed log-probability (Gumbel-max, fused into the last layer's epilogue).
+// summed log-probability (inverse-CDF sampling on the softmax weights, fused into the last layer's
+// epilogue).
 //
 // One persistent CTA per SM processes "jobs" = (128-row tile, network).  Per job and layer:
 //   * the A operand (the 128 x K activation tile, 16-bit: bf16 or fp16, one type per network set)
@@ -220,6 +221,11 @@ __device__ __forceinline__ bool split_layer(const NetParams& P, int l) {
 __device__ __forceinline__ bool decode_job(const Launch& L, int64_t j, Job& J) {
   int64_t tile = j / L.nets_per_group;
   int slot = (int)(j % L.nets_per_group);
+  // CTA b runs jobs b, b + G, b + 2G, ...: with two networks per group and an even grid G every
+  // job of a CTA would have b's parity (the same network); swapping the two networks on
+  // alternate rounds gives each CTA both (jobs 2t, 2t+1 share a round, so this stays a
+  // one-to-one map of jobs)
+  if (L.nets_per_group == 2 && (gridDim.x & 1) == 0) slot ^= (int)((j / gridDim.x) & 1);
   int64_t start = 0;
   for (int g = 0; g < L.n_groups; g++) {
     int64_t end = L.group_end_dev ? __ldg(L.group_end_dev + g) : L.group_end[g];
@@ -245,21 +251,22 @@ __device__ __forceinline__ uint64_t mix64(uint64_t x) {
   x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
   return x ^ (x >> 31);
 }
-// Sampling noise: a 64-bit key per (call, row) from splitmix64, then per (channel, bin) a
-// 32-bit avalanche mix (Wellons' "lowbias32" constants) of the key and the bin index, giving a
-// 24-bit uniform u in (0,1) and the Gumbel variate -log(-log u).
+// Sampling noise: a 64-bit key per (call, row) from splitmix64, then per channel a 32-bit
+// avalanche mix (Wellons' "lowbias32" constants) of the key and the channel index, giving a
+// 24-bit uniform u in (0,1).  The channel's bin is the first whose running sum of the softmax
+// weights exp(x - max) exceeds u times their total: inverse-CDF sampling, one uniform per
+// channel, reusing the exponentials of the log-sum-exp.
 __device__ __forceinline__ uint64_t row_key(uint64_t seed, uint64_t step, int64_t row) {
   return mix64(seed ^ mix64((step << 32) ^ ((uint64_t)row * 0x9E3779B97F4A7C15ull)));
 }
-__device__ __forceinline__ float gumbel(uint64_t key, uint32_t idx) {
+__device__ __forceinline__ float uniform24(uint64_t key, uint32_t idx) {
   uint32_t x = ((uint32_t)key ^ (idx * 0x9E3779B9u)) + (uint32_t)(key >> 32);
   x ^= x >> 16;
   x *= 0x7feb352du;
   x ^= x >> 15;
   x *= 0x846ca68bu;
   x ^= x >> 16;
-  const float u = ((float)(x >> 8) + 0.5f) * (1.0f / 16777216.0f);
-  return -__logf(-__logf(u));
+  return ((float)(x >> 8) + 0.5f) * (1.0f / 16777216.0f);
 }
 
 struct Smem {
@@ -393,8 +400,8 @@ __device__ __forceinline__ void emit_choice(const Launch& L, int act_dim, int64_
 
 // Categorical head with compile-time shape (the reference's 4 channels x 21 bins), split over
 // the PARTS epilogue warps of a lane quarter: part H handles channels [H*A/PARTS, (H+1)*A/PARTS).
-// Logits stay in registers; per channel max, log-sum-exp, Gumbel-max (or argmax); returns this
-// part's share of the summed log-prob.
+// Logits stay in registers; per channel max, log-sum-exp, inverse-CDF sample (or argmax);
+// returns this part's share of the summed log-prob.
 template <int A, int NB, int H, int PARTS>
 __device__ __forceinline__ float cat_head(uint32_t lane_addr, const float* __restrict__ bias, const Launch& L,
                                           int64_t row, bool valid) {
@@ -420,17 +427,32 @@ __device__ __forceinline__ float cat_head(uint32_t lane_addr, const float* __res
     float mx = x[0];
 #pragma unroll
     for (int b = 1; b < NB; b++) mx = fmaxf(mx, x[b]);
+    float ex[NB];
     float se = 0.0f;
 #pragma unroll
-    for (int b = 0; b < NB; b++) se += __expf(x[b] - mx);
+    for (int b = 0; b < NB; b++) {
+      ex[b] = __expf(x[b] - mx);
+      se += ex[b];
+    }
     const float lse = mx + logf(se);
     int best = 0;
-    float bestv = -INFINITY;
+    if (L.deterministic) {
+      float bestv = -INFINITY;
 #pragma unroll
-    for (int b = 0; b < NB; b++) {
-      float sc = x[b];
-      if (!L.deterministic) sc += gumbel(key, (uint32_t)(g * 64 + b));
-      if (sc > bestv) { bestv = sc; best = b; }
+      for (int b = 0; b < NB; b++)
+        if (x[b] > bestv) { bestv = x[b]; best = b; }
+    } else {
+      // the first bin whose running weight exceeds u * total = the number of bins whose running
+      // weight does not (running sums never decrease); the last bin if rounding leaves none
+      const float target = uniform24(key, (uint32_t)(g * 64)) * se;
+      float cum = 0.0f;
+      int below = 0;
+#pragma unroll
+      for (int b = 0; b < NB; b++) {
+        cum += ex[b];
+        below += cum <= target ? 1 : 0;
+      }
+      best = below < NB - 1 ? below : NB - 1;
     }
     float chosen = x[0];
 #pragma unroll
@@ -465,15 +487,25 @@ __device__ __noinline__ void cat_head_generic(uint32_t lane_addr, const float* _
     for (int b = 0; b < nb; b++) mx = fmaxf(mx, tmem_ld1(lane_addr + (uint32_t)(c0 + b)) + __ldg(bias + c0 + b));
     float se = 0.0f;
     int best = 0;
-    float bestv = -INFINITY, chosen = 0.0f;
+    float bestv = -INFINITY;
     for (int b = 0; b < nb; b++) {
       const float x = tmem_ld1(lane_addr + (uint32_t)(c0 + b)) + __ldg(bias + c0 + b);
       se += __expf(x - mx);
-      float sc = x;
-      if (!L.deterministic) sc += gumbel(key, (uint32_t)(g * 64 + b));
-      if (sc > bestv) { bestv = sc; best = b; chosen = x; }
+      if (x > bestv) { bestv = x; best = b; }
       if (valid && L.logits) L.logits[row * L.logits_ld + c0 + b] = x;
     }
+    if (!L.deterministic) {
+      // inverse-CDF sample as in cat_head (second pass over the channel's logits)
+      const float target = uniform24(key, (uint32_t)(g * 64)) * se;
+      float cum = 0.0f;
+      int below = 0;
+      for (int b = 0; b < nb; b++) {
+        cum += __expf(tmem_ld1(lane_addr + (uint32_t)(c0 + b)) + __ldg(bias + c0 + b) - mx);
+        below += cum <= target ? 1 : 0;
+      }
+      best = below < nb - 1 ? below : nb - 1;
+    }
+    const float chosen = tmem_ld1(lane_addr + (uint32_t)(c0 + best)) + __ldg(bias + c0 + best);
     logp += chosen - (mx + logf(se));
     if (valid) emit_choice(L, P.act_dim, row, g, best);
   }
