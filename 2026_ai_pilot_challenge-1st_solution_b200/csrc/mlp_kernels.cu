@@ -494,18 +494,23 @@ __device__ __noinline__ void cat_head_generic(uint32_t lane_addr, const float* _
       if (x > bestv) { bestv = x; best = b; }
       if (valid && L.logits) L.logits[row * L.logits_ld + c0 + b] = x;
     }
+    float chosen = bestv;
     if (!L.deterministic) {
-      // inverse-CDF sample as in cat_head (second pass over the channel's logits)
+      // inverse-CDF sample as in cat_head (a second pass over the channel's logits; every TMEM
+      // load reads the same column across the warp, the choice is kept per thread)
       const float target = uniform24(key, (uint32_t)(g * 64)) * se;
       float cum = 0.0f;
-      int below = 0;
+      bool found = false;
       for (int b = 0; b < nb; b++) {
-        cum += __expf(tmem_ld1(lane_addr + (uint32_t)(c0 + b)) + __ldg(bias + c0 + b) - mx);
-        below += cum <= target ? 1 : 0;
+        const float x = tmem_ld1(lane_addr + (uint32_t)(c0 + b)) + __ldg(bias + c0 + b);
+        cum += __expf(x - mx);
+        if (!found && (cum > target || b == nb - 1)) {
+          found = true;
+          best = b;
+          chosen = x;
+        }
       }
-      best = below < nb - 1 ? below : nb - 1;
     }
-    const float chosen = tmem_ld1(lane_addr + (uint32_t)(c0 + best)) + __ldg(bias + c0 + best);
     logp += chosen - (mx + logf(se));
     if (valid) emit_choice(L, P.act_dim, row, g, best);
   }
