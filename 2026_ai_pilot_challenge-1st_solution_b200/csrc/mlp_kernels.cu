@@ -218,6 +218,17 @@ __device__ __forceinline__ bool split_layer(const NetParams& P, int l) {
   return l < P.n_layers - 1 && P.width_pad[l] == 2 * NCHUNK;
 }
 
+// K-chunks per ring stage of a layer: a layer at most 128 outputs wide moves boxes of at most
+// 128 rows, so several K-chunks share one 32 KB stage (the output head's weights then arrive in
+// one or a few stages, mostly prefetched while the previous layer runs); wider layers move one
+// 256-row box per stage.
+__device__ __forceinline__ int chunks_per_stage(int N, int K) {
+  const int rows = N < NCHUNK ? N : NCHUNK;
+  if (rows > NCHUNK / 2) return 1;
+  const int c = NCHUNK / rows, kc = K / KCHUNK;
+  return c < kc ? c : kc;
+}
+
 __device__ __forceinline__ bool decode_job(const Launch& L, int64_t j, Job& J) {
   int64_t tile = j / L.nets_per_group;
   int slot = (int)(j % L.nets_per_group);
@@ -575,15 +586,20 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
         for (int l = 0; l < P.n_layers && ok; l++) {
           int K = (l == 0) ? P.in_pad : P.width_pad[l - 1];
           int N = P.width_pad[l];
-          // every box of this layer's map moves box_rows x 128 B (rows past N arrive zero-filled)
+          // every box of this layer's map moves box_rows x 128 B (rows past N arrive zero-filled);
+          // cps boxes (consecutive K-chunks) share a stage
           const uint32_t box_bytes = (uint32_t)((N < NCHUNK ? N : NCHUNK) * 128);
+          const int cps = chunks_per_stage(N, K);
           for (int n0 = 0; n0 < N && ok; n0 += NCHUNK) {
-            for (int k0 = 0; k0 < K; k0 += KCHUNK, it++) {
+            for (int k0 = 0; k0 < K; k0 += cps * KCHUNK, it++) {
               int s = it % STAGES;
               uint32_t round = it / STAGES;
+              const int nk = (K - k0) / KCHUNK < cps ? (K - k0) / KCHUNK : cps;
               if (!mbar_wait(smem_u32(&S->empty[s]), (round & 1) ^ 1, abort_flag)) { ok = false; break; }
-              mbar_expect_tx(smem_u32(&S->full[s]), box_bytes);
-              tma_load_2d(smem_u32(stages + s * STAGE_BYTES), &D.w[l], k0, n0, smem_u32(&S->full[s]));
+              mbar_expect_tx(smem_u32(&S->full[s]), box_bytes * (uint32_t)nk);
+              for (int c = 0; c < nk; c++)
+                tma_load_2d(smem_u32(stages + s * STAGE_BYTES + c * box_bytes), &D.w[l], k0 + c * KCHUNK, n0,
+                            smem_u32(&S->full[s]));
             }
           }
         }
@@ -611,20 +627,25 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           int K = (l == 0) ? P.in_pad : P.width_pad[l - 1];
           int N = P.width_pad[l];
           const bool split = split_layer(P, l);
+          const uint32_t box_bytes = (uint32_t)((N < NCHUNK ? N : NCHUNK) * 128);
+          const int cps = chunks_per_stage(N, K);
           for (int n0 = 0; n0 < N && ok; n0 += NCHUNK) {
             int nc = (N - n0) < NCHUNK ? (N - n0) : NCHUNK;
             uint32_t idesc = idesc_f16<FP16>(nc);
-            for (int k0 = 0; k0 < K; k0 += KCHUNK, it++) {
+            for (int k0 = 0; k0 < K; k0 += cps * KCHUNK, it++) {
               int s = it % STAGES;
               uint32_t round = it / STAGES;
+              const int nk = (K - k0) / KCHUNK < cps ? (K - k0) / KCHUNK : cps;
               if (!mbar_wait(smem_u32(&S->full[s]), round & 1, abort_flag)) { ok = false; break; }
               tc_fence_after();
-              uint32_t a_base = smem_u32(act + (k0 / KCHUNK) * TILE_M * 128);
-              uint32_t b_base = smem_u32(stages + s * STAGE_BYTES);
+              for (int c = 0; c < nk; c++) {
+                uint32_t a_base = smem_u32(act + (k0 / KCHUNK + c) * TILE_M * 128);
+                uint32_t b_base = smem_u32(stages + s * STAGE_BYTES + c * box_bytes);
 #pragma unroll
-              for (int kk = 0; kk < KCHUNK / 16; kk++)
-                tc_mma(tmem + (uint32_t)n0, sdesc(a_base + kk * 32), sdesc(b_base + kk * 32), idesc,
-                       (k0 > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < KCHUNK / 16; kk++)
+                  tc_mma(tmem + (uint32_t)n0, sdesc(a_base + kk * 32), sdesc(b_base + kk * 32), idesc,
+                         (k0 > 0 || c > 0 || kk > 0) ? 1u : 0u);
+              }
               tc_commit(smem_u32(&S->empty[s]));
             }
             if (split && n0 == 0) tc_commit(smem_u32(&S->acc_h0));
