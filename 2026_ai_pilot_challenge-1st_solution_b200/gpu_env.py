@@ -97,12 +97,12 @@ class GpuDogfight:
                                          _lib.stream_of(self.states_soa)), "f16_fdm_step")
         return self.obs.view(self.nenv, self.ppe, OBS_N)
 
-    def step_host(self, actions, obs_out=None, substeps=None, chunks=2):
+    def step_host(self, actions, obs_out=None, substeps=None, chunks=4):
         """step() driven from host memory: ``actions`` (nac, 4) fp64 on the host (pinned, so the
         copies are asynchronous) and obs17 written into ``obs_out`` (nac, 17) fp64 host memory
         (pinned; allocated once when omitted).  The aircraft are split into ``chunks`` slices
-        whose host-to-device copy, FDM launch and device-to-host copy run on two alternating
-        streams, so the copies of one slice overlap the physics of the next; the caller's
+        whose host-to-device copy, FDM launch and device-to-host copy run on a stream of their
+        own, so the copies of one slice overlap the physics of the others; the caller's
         current stream waits for all of it.  Results are step()'s bit for bit (aircraft are
         independent).  Returns ``obs_out`` viewed (nenv, ppe, 17)."""
         ss = self.substeps if substeps is None else int(substeps)
@@ -117,25 +117,27 @@ class GpuDogfight:
         if obs_out.device.type != "cpu" or obs_out.dtype != torch.float64 or obs_out.numel() != self.nac * OBS_N:
             raise ValueError("obs_out must be a (nac, 17) float64 host tensor")
         out = obs_out.view(self.nac, OBS_N)
+        n, chunks = self.nac, max(1, min(int(chunks), self.nac))
         if getattr(self, "_side_streams", None) is None:
-            self._side_streams = [torch.cuda.Stream(self.device) for _ in range(2)]
+            self._side_streams = []
+        while len(self._side_streams) < chunks:            # one stream per slice
+            self._side_streams.append(torch.cuda.Stream(self.device))
         cur = torch.cuda.current_stream(self.device)
         start = torch.cuda.Event()
         start.record(cur)
-        n, chunks = self.nac, max(1, min(int(chunks), self.nac))
         st, act, obs = self.states_soa.data_ptr(), self.actions.data_ptr(), self.obs.data_ptr()
         for i in range(chunks):
             lo, hi = n * i // chunks, n * (i + 1) // chunks
             if hi == lo:
                 continue
-            s = self._side_streams[i % 2]
+            s = self._side_streams[i]
             s.wait_event(start)
             with torch.cuda.stream(s):
                 self.actions[lo:hi].copy_(a[lo:hi], non_blocking=True)
                 _lib.check(self.lib.f16_fdm_step(st + 8 * lo, _lib.LAYOUT_SOA, self.nac, hi - lo, act + 32 * lo, ss,
                                                  self.fcs_dt, obs + 8 * OBS_N * lo, s.cuda_stream), "f16_fdm_step")
                 out[lo:hi].copy_(self.obs[lo:hi], non_blocking=True)
-        for s in self._side_streams:
+        for s in self._side_streams[:chunks]:
             cur.wait_stream(s)
         return out.view(self.nenv, self.ppe, OBS_N)
 

@@ -1079,7 +1079,7 @@ def main():
                        "timed_region_wall_s": wall},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": nac * 4 * 8,
                     "d2h_bytes_per_step": nac * 17 * 8, "api": "GpuDogfight.step_host(pinned host fp64 actions) -> obs17 into pinned host memory "
-                           "(2 aircraft slices on two streams: copies overlap the physics of the other slice)",
+                           "(4 aircraft slices, one stream each: copies overlap the physics of the other slices)",
                     "steps": Ke},
             "roofline": {"bound": "fp64", "achieved": achieved_tflops, "peak": peak_tflops, "unit": "TFLOP/s",
                          "frac": achieved_tflops / peak_tflops, "traffic": traffic, "traffic_source": traffic_src,
