@@ -282,6 +282,7 @@ __device__ __forceinline__ float uniform24(uint64_t key, uint32_t idx) {
 
 struct Smem {
   uint64_t x_full, act_empty, acc_full, act_ready, tmem_empty, drain, logp_bar;
+  uint64_t act_lo;                               // a 512-wide layer's first 256 activations stored
   uint64_t acc_h0;                               // a 512-wide hidden layer's first 256 columns done
   uint64_t full[STAGES], empty[STAGES];
   uint32_t tmem_base;
@@ -546,6 +547,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
     mbar_init(smem_u32(&S->acc_full), 1);
     mbar_init(smem_u32(&S->acc_h0), 1);
     mbar_init(smem_u32(&S->act_ready), 32 * EPI_WARPS);
+    mbar_init(smem_u32(&S->act_lo), 32 * EPI_WARPS);
     mbar_init(smem_u32(&S->tmem_empty), 32 * EPI_WARPS);
     mbar_init(smem_u32(&S->logp_bar), TILE_M * (EPI_PER_Q - 1));
     mbar_init(smem_u32(&S->drain), 1);
@@ -610,7 +612,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      uint32_t it = 0, acts = 0;
+      uint32_t it = 0, acts = 0, los = 0;
       int64_t jn = 0;
       for (int64_t j = blockIdx.x; j < njobs; j += gridDim.x) {
         Job J;
@@ -619,16 +621,25 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
         bool ok = mbar_wait(smem_u32(&S->x_full), (uint32_t)(jn & 1), abort_flag) &&
                   mbar_wait(smem_u32(&S->tmem_empty), (uint32_t)((jn & 1) ^ 1), abort_flag);
         for (int l = 0; l < P.n_layers && ok; l++) {
-          if (l > 0) {
-            if (!mbar_wait(smem_u32(&S->act_ready), acts & 1, abort_flag)) { ok = false; break; }
-            acts++;
-          }
-          tc_fence_after();
           int K = (l == 0) ? P.in_pad : P.width_pad[l - 1];
           int N = P.width_pad[l];
           const bool split = split_layer(P, l);
           const uint32_t box_bytes = (uint32_t)((N < NCHUNK ? N : NCHUNK) * 128);
           const int cps = chunks_per_stage(N, K);
+          // After a split layer the epilogue releases its first 256 activations (and the TMEM
+          // columns they came from) before the second half: this layer's K-chunks below K/2 can
+          // start on act_lo, the rest wait for act_ready -- when K/2 falls on a stage boundary.
+          const bool lo_first = l > 0 && split_layer(P, l - 1);
+          const int k_hi = (lo_first && (K / 2) % (cps * KCHUNK) == 0) ? K / 2 : 0;
+          if (lo_first) {
+            if (!mbar_wait(smem_u32(&S->act_lo), los & 1, abort_flag)) { ok = false; break; }
+            los++;
+          }
+          if (l > 0 && k_hi == 0) {
+            if (!mbar_wait(smem_u32(&S->act_ready), acts & 1, abort_flag)) { ok = false; break; }
+            acts++;
+          }
+          tc_fence_after();
           for (int n0 = 0; n0 < N && ok; n0 += NCHUNK) {
             int nc = (N - n0) < NCHUNK ? (N - n0) : NCHUNK;
             uint32_t idesc = idesc_f16<FP16>(nc);
@@ -636,6 +647,10 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
               int s = it % STAGES;
               uint32_t round = it / STAGES;
               const int nk = (K - k0) / KCHUNK < cps ? (K - k0) / KCHUNK : cps;
+              if (n0 == 0 && k0 == k_hi && k_hi > 0) {
+                if (!mbar_wait(smem_u32(&S->act_ready), acts & 1, abort_flag)) { ok = false; break; }
+                acts++;
+              }
               if (!mbar_wait(smem_u32(&S->full[s]), round & 1, abort_flag)) { ok = false; break; }
               tc_fence_after();
               for (int c = 0; c < nk; c++) {
@@ -718,6 +733,11 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             tc_fence_after();
 #pragma unroll
             for (int i = 0; i < NH; i++) store32(held[i], rowbase, cstart + i * STEP, m);
+            // the first half's activations are in place and its TMEM columns read: the next
+            // layer's MMAs over them may start while the second half is converted
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(smem_u32(&S->act_lo));
             cstart += NCHUNK;
           }
           if (EPI_PER_Q >= 4) {
