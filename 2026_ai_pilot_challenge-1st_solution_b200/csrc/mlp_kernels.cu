@@ -618,8 +618,14 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
         Job J;
         if (!decode_job(L, j, J)) continue;
         const NetParams& P = nets[J.net];
-        bool ok = mbar_wait(smem_u32(&S->x_full), (uint32_t)(jn & 1), abort_flag) &&
-                  mbar_wait(smem_u32(&S->tmem_empty), (uint32_t)((jn & 1) ^ 1), abort_flag);
+        // Accumulator halves alternate between jobs: this job's first 256 output columns go to TMEM
+        // columns side..side+255, the rest (and nothing of the previous job's head, which sat in
+        // the other half) to the other half.  So the first layer's first half can be issued
+        // while the previous job's output head is still being read, and only the first MMA
+        // into the other half waits for that head (tmem_empty).
+        const uint32_t side = (uint32_t)(jn & 1) << 8;
+        bool tmem_ok = false;
+        bool ok = mbar_wait(smem_u32(&S->x_full), (uint32_t)(jn & 1), abort_flag);
         for (int l = 0; l < P.n_layers && ok; l++) {
           int K = (l == 0) ? P.in_pad : P.width_pad[l - 1];
           int N = P.width_pad[l];
@@ -643,6 +649,10 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           for (int n0 = 0; n0 < N && ok; n0 += NCHUNK) {
             int nc = (N - n0) < NCHUNK ? (N - n0) : NCHUNK;
             uint32_t idesc = idesc_f16<FP16>(nc);
+            if (!tmem_ok && n0 >= NCHUNK) {
+              if (!mbar_wait(smem_u32(&S->tmem_empty), (uint32_t)((jn & 1) ^ 1), abort_flag)) { ok = false; break; }
+              tmem_ok = true;
+            }
             for (int k0 = 0; k0 < K; k0 += cps * KCHUNK, it++) {
               int s = it % STAGES;
               uint32_t round = it / STAGES;
@@ -658,7 +668,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
                 uint32_t b_base = smem_u32(stages + s * STAGE_BYTES + c * box_bytes);
 #pragma unroll
                 for (int kk = 0; kk < KCHUNK / 16; kk++)
-                  tc_mma(tmem + (uint32_t)n0, sdesc(a_base + kk * 32), sdesc(b_base + kk * 32), idesc,
+                  tc_mma(tmem + ((uint32_t)n0 ^ side), sdesc(a_base + kk * 32), sdesc(b_base + kk * 32), idesc,
                          (k0 > 0 || c > 0 || kk > 0) ? 1u : 0u);
               }
               tc_commit(smem_u32(&S->empty[s]));
@@ -667,6 +677,8 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           }
           tc_commit(smem_u32(&S->acc_full));
         }
+        // a job that never wrote the other half still consumes its tmem_empty phase
+        if (ok && !tmem_ok && !mbar_wait(smem_u32(&S->tmem_empty), (uint32_t)((jn & 1) ^ 1), abort_flag)) ok = false;
         tc_commit(smem_u32(&S->act_empty));
         if (!ok) break;
         jn++;
@@ -693,6 +705,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
       if (!decode_job(L, j, J)) continue;
       const NetParams& P = nets[J.net];
       bool ok = true;
+      const uint32_t side = (uint32_t)(jn & 1) << 8;   // the MMA issuer's per-job accumulator half
       for (int l = 0; l < P.n_layers; l++) {
         const bool split = split_layer(P, l);
         bool got = split ? mbar_wait(smem_u32(&S->acc_h0), h0s & 1, abort_flag)
@@ -721,7 +734,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             for (int i = 0; i < NH; i++) {
               const int c = cstart + i * STEP;
               uint32_t ra[32];
-              tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
+              tmem_ld32_nowait(lane_addr + ((uint32_t)c ^ side), ra);
               tmem_wait_ld();
               pack32<FP16>(ra, bias, c, relu, held[i]);
             }
@@ -744,7 +757,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             // enough warps per scheduler to hide the TMEM load latency: one chunk at a time
             for (int c = cstart; c < N; c += STEP) {
               uint32_t ra[32];
-              tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
+              tmem_ld32_nowait(lane_addr + ((uint32_t)c ^ side), ra);
               tmem_wait_ld();
               convert32<FP16>(ra, bias, c, rowbase, m, relu);
             }
@@ -753,16 +766,16 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             uint32_t ra[32], rb[32];
             int c = cstart;
             if (c < N) {
-              tmem_ld32_nowait(lane_addr + (uint32_t)c, ra);
+              tmem_ld32_nowait(lane_addr + ((uint32_t)c ^ side), ra);
               tmem_wait_ld();
             }
             while (c < N) {
-              if (c + STEP < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + STEP), rb);
+              if (c + STEP < N) tmem_ld32_nowait(lane_addr + ((uint32_t)(c + STEP) ^ side), rb);
               convert32<FP16>(ra, bias, c, rowbase, m, relu);
               tmem_wait_ld();
               c += STEP;
               if (c >= N) break;
-              if (c + STEP < N) tmem_ld32_nowait(lane_addr + (uint32_t)(c + STEP), ra);
+              if (c + STEP < N) tmem_ld32_nowait(lane_addr + ((uint32_t)(c + STEP) ^ side), ra);
               convert32<FP16>(rb, bias, c, rowbase, m, relu);
               tmem_wait_ld();
               c += STEP;
@@ -777,7 +790,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           if (P.head == HEAD_VALUE) {
             if (h == 0) {
               float v[32];
-              tmem_ld32(lane_addr, v);
+              tmem_ld32(lane_addr + side, v);
               float val = v[0] + __ldg(bias);
               if (valid) {
                 if (L.value) L.value[row] = val;
@@ -789,14 +802,14 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             // through shared memory
             if (h != 0) {
               float part;
-              if (EPI_PER_Q == 2) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr, bias, L, row, valid);
-              else if (h == 1) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr, bias, L, row, valid);
-              else if (h == 2) part = cat_head<4, 21, 2 % EPI_PER_Q, EPI_PER_Q>(lane_addr, bias, L, row, valid);
-              else part = cat_head<4, 21, 3 % EPI_PER_Q, EPI_PER_Q>(lane_addr, bias, L, row, valid);
+              if (EPI_PER_Q == 2) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr + side, bias, L, row, valid);
+              else if (h == 1) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr + side, bias, L, row, valid);
+              else if (h == 2) part = cat_head<4, 21, 2 % EPI_PER_Q, EPI_PER_Q>(lane_addr + side, bias, L, row, valid);
+              else part = cat_head<4, 21, 3 % EPI_PER_Q, EPI_PER_Q>(lane_addr + side, bias, L, row, valid);
               S->logp_part[h - 1][m] = part;
               mbar_arrive(smem_u32(&S->logp_bar));
             } else {
-              float part = cat_head<4, 21, 0, EPI_PER_Q>(lane_addr, bias, L, row, valid);
+              float part = cat_head<4, 21, 0, EPI_PER_Q>(lane_addr + side, bias, L, row, valid);
               if (!mbar_wait(smem_u32(&S->logp_bar), heads & 1, abort_flag)) {
                 ok = false;
               } else if (valid && L.logp) {
@@ -807,7 +820,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             }
             heads++;
           } else if (h == 0) {
-            cat_head_generic(lane_addr, bias, L, P, row, valid);
+            cat_head_generic(lane_addr + side, bias, L, P, row, valid);
           }
           tc_fence_before();
           mbar_arrive(smem_u32(&S->tmem_empty));
