@@ -26,6 +26,7 @@
 // leave their loops, so a malformed launch returns an error instead of hanging.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
@@ -73,6 +74,20 @@ struct NetParams {
   int head;                                      // Head
   int num_bins, act_dim;                         // categorical head: act_dim groups of num_bins
   int fp16;                                      // operands: 0 bf16, 1 fp16 (one type per set)
+  // A width-1 value head after at least one hidden layer is not run on the tensor cores: the
+  // last hidden layer's epilogue keeps its activations in fp32 and dots them with the head's
+  // weight row (head_w32 when given, else the 16-bit row head_w16 converted), so the head needs
+  // no MMA, no 16-bit activation tile and no extra pass over TMEM.
+  int fold;
+  const float* head_w32;
+  const void* head_w16;
+};
+
+// Every network's parameters travel in the kernel's parameter space (constant bank): each role
+// reads the current job's fields there with uniform, cached loads instead of global-memory
+// loads whose latency sat between a job's layers.
+struct NetTable {
+  NetParams p[MAX_NETS];
 };
 
 struct Launch {
@@ -290,6 +305,7 @@ struct Smem {
   float logp_part[EPI_PER_Q - 1][TILE_M];        // the other parts' channel log-probs per tile row
 };
 static_assert(sizeof(Smem) <= CTRL_BYTES, "control block");
+static_assert(sizeof(NetTable) + sizeof(Launch) + sizeof(CUtensorMap) + sizeof(void*) <= 4096, "kernel parameters");
 
 // tanh for hidden activations that are rounded to bf16 right after: the hardware approximation
 // (max relative error about 2^-11) is well below the bf16 rounding step (2^-9).
@@ -396,6 +412,56 @@ __device__ __forceinline__ void convert32(const uint32_t (&r)[32], const float* 
     w.w = pack_x2<FP16>(x[4 * u + 3], relu);
     *reinterpret_cast<uint4*>(rowp + (((unit0 + u) ^ (m & 7)) * 16)) = w;
   }
+}
+
+// Folded value head, one 32-column chunk [c0, c0+32) of one row: bias + activation in fp32 (ReLU
+// keeps NaN, as torch's does; tanh is the accurate fp32 tanhf, since nothing is rounded to 16
+// bits here) dotted with the head's weights, accumulated onto `acc` in column order.
+template <bool FP16>
+__device__ __forceinline__ float fold32(const uint32_t (&r)[32], const float* __restrict__ bias, const NetParams& P,
+                                        int c0, bool relu, float acc) {
+  const float4* b4 = reinterpret_cast<const float4*>(bias + c0);
+  float h[32];                                   // the chunk's fp32 activations
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const float4 b = __ldg(b4 + i);
+    h[4 * i] = __uint_as_float(r[4 * i]) + b.x;
+    h[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + b.y;
+    h[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + b.z;
+    h[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + b.w;
+  }
+  // one activation branch per chunk (a per-element select would evaluate tanhf for ReLU too)
+  if (relu) {
+#pragma unroll
+    for (int i = 0; i < 32; i++) h[i] = h[i] < 0.0f ? 0.0f : h[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; i++) h[i] = tanhf(h[i]);
+  }
+  auto step = [&](int i, const float4& w) {
+    acc = fmaf(h[4 * i], w.x, acc);
+    acc = fmaf(h[4 * i + 1], w.y, acc);
+    acc = fmaf(h[4 * i + 2], w.z, acc);
+    acc = fmaf(h[4 * i + 3], w.w, acc);
+  };
+  if (P.head_w32) {
+    const float4* w4 = reinterpret_cast<const float4*>(P.head_w32 + c0);
+#pragma unroll
+    for (int i = 0; i < 8; i++) step(i, __ldg(w4 + i));
+  } else {
+    const uint2* h2 = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(P.head_w16) + c0);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const uint2 t = __ldg(h2 + i);
+      const unsigned short e[4] = {(unsigned short)(t.x & 0xFFFFu), (unsigned short)(t.x >> 16),
+                                   (unsigned short)(t.y & 0xFFFFu), (unsigned short)(t.y >> 16)};
+      float f[4];
+#pragma unroll
+      for (int k = 0; k < 4; k++) f[k] = FP16 ? __half2float(__ushort_as_half(e[k])) : __uint_as_float((uint32_t)e[k] << 16);
+      step(i, make_float4(f[0], f[1], f[2], f[3]));
+    }
+  }
+  return acc;
 }
 
 // Per-row outputs of one sampled channel: bins / int32 index / fp64 env command.
@@ -532,7 +598,7 @@ __device__ __noinline__ void cat_head_generic(uint32_t lane_addr, const float* _
 template <bool FP16>
 __global__ void __launch_bounds__(THREADS, 1)
 k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ nets_dev,
-         const NetParams* __restrict__ nets, const __grid_constant__ Launch L) {
+         const __grid_constant__ NetTable nets, const __grid_constant__ Launch L) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* act = base;
@@ -577,15 +643,24 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
       for (int64_t j = blockIdx.x; j < njobs; j += gridDim.x) {
         Job J;
         if (!decode_job(L, j, J)) continue;
-        const NetParams& P = nets[J.net];
+        const NetParams& P = nets.p[J.net];
         const NetDev& D = nets_dev[J.net];
-        if (!mbar_wait(smem_u32(&S->act_empty), (uint32_t)((jn & 1) ^ 1), abort_flag)) break;
-        int kc0 = P.in_pad / KCHUNK;
-        mbar_expect_tx(smem_u32(&S->x_full), (uint32_t)(kc0 * TILE_M * 128));
-        for (int c = 0; c < kc0; c++)
-          tma_load_2d(smem_u32(act + c * TILE_M * 128), &xmap, c * KCHUNK, (int)J.row0, smem_u32(&S->x_full));
+        // The input tile replaces the previous job's activations, so it waits until that job's
+        // MMAs are done (act_empty); the weight ring does not: the first STAGES weight stages of
+        // this job are requested before that wait, while the previous job's last layer runs.
+        int sidx = 0;
+        bool x_sent = false;
+        auto send_x = [&]() -> bool {
+          if (!mbar_wait(smem_u32(&S->act_empty), (uint32_t)((jn & 1) ^ 1), abort_flag)) return false;
+          const int kc0 = P.in_pad / KCHUNK;
+          mbar_expect_tx(smem_u32(&S->x_full), (uint32_t)(kc0 * TILE_M * 128));
+          for (int c = 0; c < kc0; c++)
+            tma_load_2d(smem_u32(act + c * TILE_M * 128), &xmap, c * KCHUNK, (int)J.row0, smem_u32(&S->x_full));
+          x_sent = true;
+          return true;
+        };
         bool ok = true;
-        for (int l = 0; l < P.n_layers && ok; l++) {
+        for (int l = 0; l < P.n_layers - P.fold && ok; l++) {
           int K = (l == 0) ? P.in_pad : P.width_pad[l - 1];
           int N = P.width_pad[l];
           // every box of this layer's map moves box_rows x 128 B (rows past N arrive zero-filled);
@@ -597,6 +672,8 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
               int s = it % STAGES;
               uint32_t round = it / STAGES;
               const int nk = (K - k0) / KCHUNK < cps ? (K - k0) / KCHUNK : cps;
+              if (!x_sent && sidx == STAGES && !send_x()) { ok = false; break; }
+              sidx++;
               if (!mbar_wait(smem_u32(&S->empty[s]), (round & 1) ^ 1, abort_flag)) { ok = false; break; }
               mbar_expect_tx(smem_u32(&S->full[s]), box_bytes * (uint32_t)nk);
               for (int c = 0; c < nk; c++)
@@ -605,6 +682,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             }
           }
         }
+        if (ok && !x_sent && !send_x()) ok = false;
         if (!ok) break;
         jn++;
       }
@@ -613,11 +691,12 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       uint32_t it = 0, acts = 0, los = 0;
+      bool prev_fold = false;
       int64_t jn = 0;
       for (int64_t j = blockIdx.x; j < njobs; j += gridDim.x) {
         Job J;
         if (!decode_job(L, j, J)) continue;
-        const NetParams& P = nets[J.net];
+        const NetParams& P = nets.p[J.net];
         // Accumulator halves alternate between jobs: this job's first 256 output columns go to TMEM
         // columns side..side+255, the rest (and nothing of the previous job's head, which sat in
         // the other half) to the other half.  So the first layer's first half can be issued
@@ -626,7 +705,13 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
         const uint32_t side = (uint32_t)(jn & 1) << 8;
         bool tmem_ok = false;
         bool ok = mbar_wait(smem_u32(&S->x_full), (uint32_t)(jn & 1), abort_flag);
-        for (int l = 0; l < P.n_layers && ok; l++) {
+        // a folded value head kept both accumulator halves until its epilogue finished: no MMA of
+        // this job before that epilogue has released them
+        if (ok && prev_fold) {
+          ok = mbar_wait(smem_u32(&S->tmem_empty), (uint32_t)((jn & 1) ^ 1), abort_flag);
+          tmem_ok = true;
+        }
+        for (int l = 0; l < P.n_layers - P.fold && ok; l++) {
           int K = (l == 0) ? P.in_pad : P.width_pad[l - 1];
           int N = P.width_pad[l];
           const bool split = split_layer(P, l);
@@ -681,6 +766,7 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
         if (ok && !tmem_ok && !mbar_wait(smem_u32(&S->tmem_empty), (uint32_t)((jn & 1) ^ 1), abort_flag)) ok = false;
         tc_commit(smem_u32(&S->act_empty));
         if (!ok) break;
+        prev_fold = P.fold != 0;
         jn++;
       }
       // drain: wait (bounded) until every MMA this thread issued has completed
@@ -703,10 +789,10 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
     for (int64_t j = blockIdx.x; j < njobs; j += gridDim.x) {
       Job J;
       if (!decode_job(L, j, J)) continue;
-      const NetParams& P = nets[J.net];
+      const NetParams& P = nets.p[J.net];
       bool ok = true;
       const uint32_t side = (uint32_t)(jn & 1) << 8;   // the MMA issuer's per-job accumulator half
-      for (int l = 0; l < P.n_layers; l++) {
+      for (int l = 0; l < P.n_layers - P.fold; l++) {
         const bool split = split_layer(P, l);
         bool got = split ? mbar_wait(smem_u32(&S->acc_h0), h0s & 1, abort_flag)
                          : mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
@@ -717,7 +803,53 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
         tc_fence_after();
         const float* bias = P.bias[l];
         const bool last = (l == P.n_layers - 1);
-        if (!last) {
+        if (P.fold && l == P.n_layers - 2) {
+          // the value head folded into the last hidden layer: each part dots its chunks' fp32
+          // activations with the head's weights (the first half while the second half's MMAs
+          // run), the quarter's parts join through shared memory, and both accumulator halves
+          // are released together
+          const int N = P.width_pad[l];
+          const bool relu = P.act == 0;
+          constexpr int STEP = 32 * EPI_PER_Q;
+          float part = 0.0f;
+          int c = 32 * h;
+          for (; c < (split ? NCHUNK : N); c += STEP) {
+            uint32_t ra[32];
+            tmem_ld32_nowait(lane_addr + ((uint32_t)c ^ side), ra);
+            tmem_wait_ld();
+            part = fold32<FP16>(ra, bias, P, c, relu, part);
+          }
+          if (split) {
+            bool got2 = mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
+            __syncwarp();
+            if (!got2 || *abort_flag) { ok = false; break; }
+            accs++;
+            tc_fence_after();
+            for (; c < N; c += STEP) {
+              uint32_t ra[32];
+              tmem_ld32_nowait(lane_addr + ((uint32_t)c ^ side), ra);
+              tmem_wait_ld();
+              part = fold32<FP16>(ra, bias, P, c, relu, part);
+            }
+          }
+          const int64_t row = J.row0 + m;
+          if (h != 0) {
+            S->logp_part[h - 1][m] = part;
+            mbar_arrive(smem_u32(&S->logp_bar));
+          } else if (!mbar_wait(smem_u32(&S->logp_bar), heads & 1, abort_flag)) {
+            ok = false;
+          } else if (m < J.rows) {
+#pragma unroll
+            for (int k = 0; k < EPI_PER_Q - 1; k++) part += S->logp_part[k][m];
+            const float val = part + __ldg(P.bias[P.n_layers - 1]);
+            if (L.value) L.value[row] = val;
+            if (L.logits) L.logits[row * L.logits_ld] = val;
+          }
+          heads++;
+          tc_fence_before();
+          mbar_arrive(smem_u32(&S->tmem_empty));
+          if (!ok) break;
+        } else if (!last) {
           // bias + activation -> bf16 into the swizzled A region of the next layer.  32-column
           // chunks, the TMEM load of the next chunk in flight while this one is converted.
           const int N = P.width_pad[l];
@@ -887,7 +1019,7 @@ struct f16_mlp_set_s {
   int n;
   int fp16;                        // operand type of every network in the set
   f16::mlp::NetDev* dev_maps;      // device [n]
-  f16::mlp::NetParams* dev_params; // device [n]
+  // host copy of every network's parameters, passed to each launch by value
   f16::mlp::NetParams host_params[f16::mlp::MAX_NETS];
 };
 
@@ -941,16 +1073,17 @@ extern "C" int f16_mlp_set_create(const f16_mlp_desc* descs, int n, f16_mlp_set*
       }
       in_l = w;
     }
+    P.fold = (d.head == HEAD_VALUE && d.n_layers >= 2) ? 1 : 0;
+    P.head_w16 = d.weight[d.n_layers - 1];
+    P.head_w32 = d.head_weight_f32;
+    if (P.head_w32 && !aligned(P.head_w32, 16)) { delete s; return F16_ERR_ALIGN; }
   }
-  if (cudaMalloc(&s->dev_maps, sizeof(NetDev) * n) != cudaSuccess ||
-      cudaMalloc(&s->dev_params, sizeof(NetParams) * n) != cudaSuccess) {
+  if (cudaMalloc(&s->dev_maps, sizeof(NetDev) * n) != cudaSuccess) {
     delete s;
     return F16_ERR_CUDA;
   }
-  if (cudaMemcpy(s->dev_maps, maps, sizeof(NetDev) * n, cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemcpy(s->dev_params, s->host_params, sizeof(NetParams) * n, cudaMemcpyHostToDevice) != cudaSuccess) {
+  if (cudaMemcpy(s->dev_maps, maps, sizeof(NetDev) * n, cudaMemcpyHostToDevice) != cudaSuccess) {
     cudaFree(s->dev_maps);
-    cudaFree(s->dev_params);
     delete s;
     return F16_ERR_CUDA;
   }
@@ -961,7 +1094,6 @@ extern "C" int f16_mlp_set_create(const f16_mlp_desc* descs, int n, f16_mlp_set*
 extern "C" int f16_mlp_set_destroy(f16_mlp_set* s) {
   if (!s) return F16_ERR_ARG;
   cudaFree(s->dev_maps);
-  cudaFree(s->dev_params);
   delete s;
   return F16_OK;
 }
@@ -1030,7 +1162,10 @@ extern "C" int f16_policy_forward(const f16_mlp_set* set, const f16_policy_args*
   }
   int grid = (int)(njobs < sm_count() ? njobs : sm_count());
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (t) k_policy<true><<<grid, THREADS, SMEM_BYTES, st>>>(xmap, set->dev_maps, set->dev_params, L);
-  else k_policy<false><<<grid, THREADS, SMEM_BYTES, st>>>(xmap, set->dev_maps, set->dev_params, L);
+  NetTable nets;
+  memset(&nets, 0, sizeof(nets));
+  memcpy(nets.p, set->host_params, sizeof(NetParams) * set->n);
+  if (t) k_policy<true><<<grid, THREADS, SMEM_BYTES, st>>>(xmap, set->dev_maps, nets, L);
+  else k_policy<false><<<grid, THREADS, SMEM_BYTES, st>>>(xmap, set->dev_maps, nets, L);
   return launch_status();
 }

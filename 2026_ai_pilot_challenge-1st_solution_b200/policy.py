@@ -27,7 +27,7 @@ ACTIVATIONS = {"relu": 0, "tanh": 1}
 class MlpDesc(C.Structure):
     _fields_ = [("in_dim", C.c_int), ("n_layers", C.c_int), ("width", C.c_int * 4), ("activation", C.c_int),
                 ("head", C.c_int), ("act_dim", C.c_int), ("num_bins", C.c_int), ("weight", C.c_void_p * 4),
-                ("bias", C.c_void_p * 4), ("operand", C.c_int)]
+                ("bias", C.c_void_p * 4), ("operand", C.c_int), ("head_weight_f32", C.c_void_p)]
 
 
 class PolicyArgs(C.Structure):
@@ -72,6 +72,10 @@ class MlpWeights:
         self.head = head
         self.act_dim, self.num_bins = act_dim, num_bins
         self.in_dim = self.weights[0].shape[1]
+        # a value head after a hidden layer runs in fp32 in that layer's epilogue: its weight
+        # row is also kept in fp32
+        self.head_w32 = (weights[-1].detach().to(device=self.weights[-1].device, dtype=torch.float32).contiguous()
+                         if head == HEAD_VALUE and len(self.weights) >= 2 else None)
 
     @classmethod
     def from_sequential(cls, seq, head, device, act_dim=4, num_bins=21, in_width=None, operand="bf16"):
@@ -96,6 +100,8 @@ class MlpWeights:
                 raise ValueError("layer shape differs from the registered network")
             w[:, :cols].copy_(lin.weight)
             b.copy_(lin.bias)
+        if self.head_w32 is not None:
+            self.head_w32.copy_(linears[-1].weight)
 
     def desc(self):
         d = MlpDesc()
@@ -109,6 +115,7 @@ class MlpWeights:
         d.head = self.head
         d.act_dim, d.num_bins = self.act_dim, self.num_bins
         d.operand = OPERANDS[self.operand][0]
+        d.head_weight_f32 = self.head_w32.data_ptr() if self.head_w32 is not None else None
         return d
 
 

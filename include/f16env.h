@@ -259,6 +259,11 @@ typedef struct {
   int operand;              /* F16_OPERAND_BF16 (0, a zero-initialised descriptor) or
                                F16_OPERAND_FP16: the type of the weights, of the policy input x
                                and of the hidden activations; one type for every network of a set */
+  const float* head_weight_f32;  /* optional, value head (head 2) with n_layers >= 2: the head's
+                               weight row in fp32, device, 16-byte aligned [width[n_layers-2]].
+                               Such a head is computed in fp32 from the last hidden layer's fp32
+                               activations (bias + activation, then the dot product with this row);
+                               NULL: the same with weight[n_layers-1] converted to fp32 */
 } f16_mlp_desc;
 
 #define F16_OPERAND_BF16 0

@@ -45,17 +45,25 @@ def make_seq(in_dim, hidden, out, act, seed, device):
     return seq.to(device)
 
 
-def emulate(seq, xb):
+def emulate(seq, xb, head_w32=True):
     """The kernel's numerics in torch: weights in xb's 16-bit type, fp32 accumulation, hidden
-    activations rounded to that type."""
+    activations rounded to that type -- except a width-1 value head after a hidden layer, which
+    takes the last hidden layer's fp32 activations and its fp32 weight row (the 16-bit row
+    widened when the descriptor carries no fp32 copy, head_w32=False)."""
     dt = xb.dtype
     lin = [m for m in seq if isinstance(m, nn.Linear)]
     act = [m for m in seq if not isinstance(m, nn.Linear)]
+    fold = lin[-1].out_features == 1 and len(lin) >= 2
     h = xb.float()
     for i, l in enumerate(lin):
-        h = h @ l.weight.detach().to(dt).float().T + l.bias.detach().float()
-        if i < len(lin) - 1:
-            h = act[i](h).to(dt).float()
+        last = i == len(lin) - 1
+        w = l.weight.detach()
+        w = w.float() if (last and fold and head_w32) else w.to(dt).float()
+        h = h @ w.T + l.bias.detach().float()
+        if not last:
+            h = act[i](h)
+            if not (fold and i == len(lin) - 2):
+                h = h.to(dt).float()
     return h
 
 
@@ -213,6 +221,48 @@ def test_other_head_shape(P, cuda):
 
 # contract bound per operand type: logits (fraction of max |logit|) and summed log-prob (relative)
 CONTRACT = {"fp16": 1e-3, "bf16": 1e-2}
+
+
+@pytest.mark.parametrize("operand", ["fp16", "bf16"])
+@pytest.mark.parametrize("fp32_row", [True, False])
+def test_value_head_against_fp32_torch(P, cuda, operand, fp32_row):
+    """The critic's width-1 head runs in the last hidden layer's epilogue in fp32: values against
+    the fp32 network within the operand's contract bound (fraction of max |value|), against the
+    kernel-numerics emulation within a quarter of it, with the descriptor's fp32 weight row and
+    without it (the 16-bit row widened); a partial last tile, tanh and a 384-wide hidden layer
+    (not split into accumulator halves) included."""
+    bound = CONTRACT[operand]
+    dt = torch.float16 if operand == "fp16" else torch.bfloat16
+    for hidden, act, seed in (((512, 512), "relu", 41), ((384, 384, 384), "tanh", 42), ((512,), "relu", 43)):
+        critic = make_seq(184, hidden, 1, act, seed, cuda)
+        net = P.MlpWeights.from_sequential(critic, P.HEAD_VALUE, cuda, operand=operand)
+        if not fp32_row:
+            net.head_w32 = None
+        actor = make_seq(184, (512, 512), 84, "relu", seed + 100, cuda)
+        ps = P.PolicySet([P.MlpWeights.from_sequential(actor, P.HEAD_CATEGORICAL, cuda, operand=operand), net])
+        rows = 3000                                  # 23 full tiles + a partial one
+        x, xb = make_x(rows, cuda, seed=seed, dtype=dt)
+        value = torch.full((rows,), float("nan"), device=cuda)
+        ps.forward(xb, [(rows, [1])], value=value)
+        # fused with the actor (the rollout's launch) the values are the same bits
+        value2 = torch.full((rows,), float("nan"), device=cuda)
+        logp = torch.zeros(rows, device=cuda)
+        ps.forward(xb, [(rows, [0, 1])], nets_per_group=2, value=value2, logp=logp, seed=3, step=1)
+        torch.cuda.synchronize()
+        ps.check_error()
+        assert torch.equal(value, value2)
+        with torch.no_grad():
+            f32 = critic(x)[:, 0]
+        em = emulate(critic, xb[:, :184], head_w32=fp32_row)[:, 0]
+        scale = f32.abs().max().item()
+        err = (value - f32).abs().max().item() / scale
+        em_err = (value - em).abs().max().item() / em.abs().max().item()
+        print(f"{operand} {hidden} {act} fp32 row {fp32_row}: value {err:.2e} of max |value| vs fp32 torch, "
+              f"{em_err:.2e} vs emulation")
+        assert err <= bound
+        # the emulation rounds the 16-bit hidden layers as the kernel does, but its fp32 sums run in
+        # another order (and tanh is not the kernel's fast tanh), so a few 16-bit roundings differ
+        assert em_err <= bound / 4
 
 
 @pytest.mark.parametrize("operand", ["fp16", "bf16"])
