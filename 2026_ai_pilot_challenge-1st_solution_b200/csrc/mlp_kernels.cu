@@ -181,7 +181,34 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 8 consecutive fp32 columns of this warp's 32 TMEM lanes, without the completion wait
+__device__ __forceinline__ void tmem_ld8_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 16 packed 32-bit words of this warp's 32 TMEM lanes: store / load (load waits for completion)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint4 (&w)[4]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(w[0].x), "r"(w[0].y), "r"(w[0].z), "r"(w[0].w), "r"(w[1].x), "r"(w[1].y), "r"(w[1].z),
+        "r"(w[1].w), "r"(w[2].x), "r"(w[2].y), "r"(w[2].z), "r"(w[2].w), "r"(w[3].x), "r"(w[3].y), "r"(w[3].z),
+        "r"(w[3].w)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint4 (&w)[4]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(w[0].x), "=r"(w[0].y), "=r"(w[0].z), "=r"(w[0].w), "=r"(w[1].x), "=r"(w[1].y), "=r"(w[1].z),
+        "=r"(w[1].w), "=r"(w[2].x), "=r"(w[2].y), "=r"(w[2].z), "=r"(w[2].w), "=r"(w[3].x), "=r"(w[3].y),
+        "=r"(w[3].z), "=r"(w[3].w)
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 
 // 32 consecutive fp32 columns of this warp's 32 TMEM lanes
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
@@ -227,8 +254,9 @@ struct Job {
 };
 // A hidden layer two weight boxes wide (512 outputs): the MMA issuer signals its first 256
 // accumulator columns (acc_h0) before issuing the second half, and the epilogue converts that
-// half into registers while the second half's MMAs run; it stores them once the layer's MMAs
-// are done reading the activations they replace (acc_full).
+// half while the second half's MMAs run, parking the packed 16-bit values in the columns it has
+// read; it stores them to shared memory once the layer's MMAs are done reading the activations
+// they replace (acc_full).
 __device__ __forceinline__ bool split_layer(const NetParams& P, int l) {
   return l < P.n_layers - 1 && P.width_pad[l] == 2 * NCHUNK;
 }
@@ -344,12 +372,8 @@ __device__ __forceinline__ uint32_t pack_x2(uint64_t v, bool relu) {
 // ReLU fused into the conversion
 // bias + activation of one 32-column chunk packed as the four 16-byte units it stores
 template <bool FP16>
-__device__ __forceinline__ void pack32(const uint32_t (&r)[32], const float* __restrict__ bias, int c0, bool relu,
+__device__ __forceinline__ void pack32(const uint32_t (&r)[32], const ulonglong2 (&bv)[8], bool relu,
                                        uint4 (&w)[4]) {
-  const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(bias + c0);
-  ulonglong2 bv[8];
-#pragma unroll
-  for (int i = 0; i < 8; i++) bv[i] = __ldg(b2 + i);
   uint64_t x[16];
 #pragma unroll
   for (int i = 0; i < 8; i++) {
@@ -372,6 +396,12 @@ __device__ __forceinline__ void pack32(const uint32_t (&r)[32], const float* __r
     w[u].w = pack_x2<FP16>(x[4 * u + 3], relu);
   }
 }
+// the 32 biases of a chunk, loaded before its TMEM load so that the two latencies overlap
+__device__ __forceinline__ void load_bias32(const float* __restrict__ bias, int c0, ulonglong2 (&bv)[8]) {
+  const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(bias + c0);
+#pragma unroll
+  for (int i = 0; i < 8; i++) bv[i] = __ldg(b2 + i);
+}
 // the packed chunk into the swizzled A region of the next layer (row m, columns c0..c0+31)
 __device__ __forceinline__ void store32(const uint4 (&w)[4], uint8_t* rowbase, int c0, int m) {
   uint8_t* rowp = rowbase + (c0 / KCHUNK) * TILE_M * 128;
@@ -381,12 +411,8 @@ __device__ __forceinline__ void store32(const uint4 (&w)[4], uint8_t* rowbase, i
 }
 
 template <bool FP16>
-__device__ __forceinline__ void convert32(const uint32_t (&r)[32], const float* __restrict__ bias, int c0,
-                                          uint8_t* rowbase, int m, bool relu) {
-  const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(bias + c0);
-  ulonglong2 bv[8];
-#pragma unroll
-  for (int i = 0; i < 8; i++) bv[i] = __ldg(b2 + i);
+__device__ __forceinline__ void convert32(const uint32_t (&r)[32], const ulonglong2 (&bv)[8], int c0, uint8_t* rowbase,
+                                          int m, bool relu) {
   uint64_t x[16];
 #pragma unroll
   for (int i = 0; i < 8; i++) {
@@ -414,52 +440,59 @@ __device__ __forceinline__ void convert32(const uint32_t (&r)[32], const float* 
   }
 }
 
-// Folded value head, one 32-column chunk [c0, c0+32) of one row: bias + activation in fp32 (ReLU
-// keeps NaN, as torch's does; tanh is the accurate fp32 tanhf, since nothing is rounded to 16
-// bits here) dotted with the head's weights, accumulated onto `acc` in column order.
+// Folded value head over 16 columns [c0, c0+16) of one row: the biases and head weights (fp32
+// row, or the 16-bit row widened) are loaded before the columns' TMEM load so the latencies
+// overlap; then bias + activation in fp32 (ReLU keeps NaN, as torch's does; tanh is the accurate
+// tanhf, since nothing here is rounded to 16 bits) and the dot product accumulated onto `acc` in
+// column order.
+struct Fold16 {
+  float4 b[4], w[4];
+};
 template <bool FP16>
-__device__ __forceinline__ float fold32(const uint32_t (&r)[32], const float* __restrict__ bias, const NetParams& P,
-                                        int c0, bool relu, float acc) {
+__device__ __forceinline__ void fold16_load(const float* __restrict__ bias, const NetParams& P, int c0, Fold16& f) {
   const float4* b4 = reinterpret_cast<const float4*>(bias + c0);
-  float h[32];                                   // the chunk's fp32 activations
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
-    const float4 b = __ldg(b4 + i);
-    h[4 * i] = __uint_as_float(r[4 * i]) + b.x;
-    h[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + b.y;
-    h[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + b.z;
-    h[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + b.w;
-  }
-  // one activation branch per chunk (a per-element select would evaluate tanhf for ReLU too)
-  if (relu) {
-#pragma unroll
-    for (int i = 0; i < 32; i++) h[i] = h[i] < 0.0f ? 0.0f : h[i];
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; i++) h[i] = tanhf(h[i]);
-  }
-  auto step = [&](int i, const float4& w) {
-    acc = fmaf(h[4 * i], w.x, acc);
-    acc = fmaf(h[4 * i + 1], w.y, acc);
-    acc = fmaf(h[4 * i + 2], w.z, acc);
-    acc = fmaf(h[4 * i + 3], w.w, acc);
-  };
+  for (int i = 0; i < 4; i++) f.b[i] = __ldg(b4 + i);
   if (P.head_w32) {
     const float4* w4 = reinterpret_cast<const float4*>(P.head_w32 + c0);
 #pragma unroll
-    for (int i = 0; i < 8; i++) step(i, __ldg(w4 + i));
+    for (int i = 0; i < 4; i++) f.w[i] = __ldg(w4 + i);
   } else {
     const uint2* h2 = reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(P.head_w16) + c0);
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
+    for (int i = 0; i < 4; i++) {
       const uint2 t = __ldg(h2 + i);
       const unsigned short e[4] = {(unsigned short)(t.x & 0xFFFFu), (unsigned short)(t.x >> 16),
                                    (unsigned short)(t.y & 0xFFFFu), (unsigned short)(t.y >> 16)};
-      float f[4];
+      float v[4];
 #pragma unroll
-      for (int k = 0; k < 4; k++) f[k] = FP16 ? __half2float(__ushort_as_half(e[k])) : __uint_as_float((uint32_t)e[k] << 16);
-      step(i, make_float4(f[0], f[1], f[2], f[3]));
+      for (int k = 0; k < 4; k++) v[k] = FP16 ? __half2float(__ushort_as_half(e[k])) : __uint_as_float((uint32_t)e[k] << 16);
+      f.w[i] = make_float4(v[0], v[1], v[2], v[3]);
     }
+  }
+}
+__device__ __forceinline__ float fold16(const uint4 (&q)[4], const Fold16& f, bool relu, float acc) {
+  const uint32_t r[16] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
+                          q[2].x, q[2].y, q[2].z, q[2].w, q[3].x, q[3].y, q[3].z, q[3].w};
+  float h[16];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    h[4 * i] = __uint_as_float(r[4 * i]) + f.b[i].x;
+    h[4 * i + 1] = __uint_as_float(r[4 * i + 1]) + f.b[i].y;
+    h[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + f.b[i].z;
+    h[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + f.b[i].w;
+  }
+  if (relu) {
+#pragma unroll
+    for (int i = 0; i < 16; i++) h[i] = h[i] < 0.0f ? 0.0f : h[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; i++) h[i] = tanhf(h[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    acc = fmaf(h[4 * i], f.w[i].x, acc); acc = fmaf(h[4 * i + 1], f.w[i].y, acc);
+    acc = fmaf(h[4 * i + 2], f.w[i].z, acc); acc = fmaf(h[4 * i + 3], f.w[i].w, acc);
   }
   return acc;
 }
@@ -487,15 +520,17 @@ __device__ __forceinline__ float cat_head(uint32_t lane_addr, const float* __res
   constexpr int GA = A / PARTS;                  // channels of this part
   constexpr int W = GA * NB;
   constexpr int C0 = H * W;                      // first logit column of this half
-  constexpr int LB = C0 / 32 * 32;               // first TMEM column loaded
-  constexpr int NL = (C0 + W - 1) / 32 - C0 / 32 + 1;
-  uint32_t r[NL * 32];
-#pragma unroll
-  for (int c = 0; c < NL; c++) tmem_ld32_nowait(lane_addr + (uint32_t)(LB + 32 * c), r + 32 * c);
-  tmem_wait_ld();
+  constexpr int LB = C0 / 8 * 8;                 // first TMEM column loaded (8-column blocks)
+  constexpr int NL = (C0 + W - 1) / 8 - C0 / 8 + 1;
   float lg[W];
 #pragma unroll
-  for (int i = 0; i < W; i++) lg[i] = __uint_as_float(r[C0 - LB + i]) + __ldg(bias + C0 + i);
+  for (int i = 0; i < W; i++) lg[i] = __ldg(bias + C0 + i);     // issued before the TMEM loads
+  uint32_t r[NL * 8];
+#pragma unroll
+  for (int c = 0; c < NL; c++) tmem_ld8_nowait(lane_addr + (uint32_t)(LB + 8 * c), r + 8 * c);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < W; i++) lg[i] += __uint_as_float(r[C0 - LB + i]);
   const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step + (L.step_dev ? *L.step_dev : 0ull), row);
   float logp = 0.0f;
 #pragma unroll
@@ -814,10 +849,14 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           float part = 0.0f;
           int c = 32 * h;
           for (; c < (split ? NCHUNK : N); c += STEP) {
-            uint32_t ra[32];
-            tmem_ld32_nowait(lane_addr + ((uint32_t)c ^ side), ra);
-            tmem_wait_ld();
-            part = fold32<FP16>(ra, bias, P, c, relu, part);
+            uint4 ra[4];
+            Fold16 f;
+            fold16_load<FP16>(bias, P, c, f);
+            tmem_ld16(lane_addr + ((uint32_t)c ^ side), ra);
+            part = fold16(ra, f, relu, part);
+            fold16_load<FP16>(bias, P, c + 16, f);
+            tmem_ld16(lane_addr + ((uint32_t)(c + 16) ^ side), ra);
+            part = fold16(ra, f, relu, part);
           }
           if (split) {
             bool got2 = mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
@@ -826,10 +865,14 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             accs++;
             tc_fence_after();
             for (; c < N; c += STEP) {
-              uint32_t ra[32];
-              tmem_ld32_nowait(lane_addr + ((uint32_t)c ^ side), ra);
-              tmem_wait_ld();
-              part = fold32<FP16>(ra, bias, P, c, relu, part);
+              uint4 ra[4];
+              Fold16 f;
+              fold16_load<FP16>(bias, P, c, f);
+              tmem_ld16(lane_addr + ((uint32_t)c ^ side), ra);
+              part = fold16(ra, f, relu, part);
+              fold16_load<FP16>(bias, P, c + 16, f);
+              tmem_ld16(lane_addr + ((uint32_t)(c + 16) ^ side), ra);
+              part = fold16(ra, f, relu, part);
             }
           }
           const int64_t row = J.row0 + m;
@@ -858,26 +901,34 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           constexpr int STEP = 32 * EPI_PER_Q;           // this warp's chunks: c, c + STEP, ...
           int cstart = 32 * h;
           if (split) {
-            // first half: packed into registers (one chunk loaded at a time: the held half
-            // takes the registers a second load buffer would)
+            // first half: packed to 16 bits and parked in the chunk's own (already read) TMEM
+            // columns until the second half's MMAs are done with the activations being replaced
             constexpr int NH = NCHUNK / STEP;
-            uint4 held[NH][4];
 #pragma unroll
             for (int i = 0; i < NH; i++) {
               const int c = cstart + i * STEP;
+              ulonglong2 bv[8];
+              load_bias32(bias, c, bv);
               uint32_t ra[32];
               tmem_ld32_nowait(lane_addr + ((uint32_t)c ^ side), ra);
               tmem_wait_ld();
-              pack32<FP16>(ra, bias, c, relu, held[i]);
+              uint4 w[4];
+              pack32<FP16>(ra, bv, relu, w);
+              tmem_st16(lane_addr + ((uint32_t)c ^ side), w);
             }
-            // the layer's second-half MMAs are done with the activations being replaced
+            tmem_wait_st();
             bool got2 = mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
             __syncwarp();
             if (!got2 || *abort_flag) { ok = false; break; }
             accs++;
             tc_fence_after();
 #pragma unroll
-            for (int i = 0; i < NH; i++) store32(held[i], rowbase, cstart + i * STEP, m);
+            for (int i = 0; i < NH; i++) {
+              const int c = cstart + i * STEP;
+              uint4 w[4];
+              tmem_ld16(lane_addr + ((uint32_t)c ^ side), w);
+              store32(w, rowbase, c, m);
+            }
             // the first half's activations are in place and its TMEM columns read: the next
             // layer's MMAs over them may start while the second half is converted
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -888,10 +939,12 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           if (EPI_PER_Q >= 4) {
             // enough warps per scheduler to hide the TMEM load latency: one chunk at a time
             for (int c = cstart; c < N; c += STEP) {
+              ulonglong2 bv[8];
+              load_bias32(bias, c, bv);
               uint32_t ra[32];
               tmem_ld32_nowait(lane_addr + ((uint32_t)c ^ side), ra);
               tmem_wait_ld();
-              convert32<FP16>(ra, bias, c, rowbase, m, relu);
+              convert32<FP16>(ra, bv, c, rowbase, m, relu);
             }
           } else {
             // the next chunk's TMEM load in flight while this one is converted
@@ -903,12 +956,12 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             }
             while (c < N) {
               if (c + STEP < N) tmem_ld32_nowait(lane_addr + ((uint32_t)(c + STEP) ^ side), rb);
-              convert32<FP16>(ra, bias, c, rowbase, m, relu);
+              { ulonglong2 bv[8]; load_bias32(bias, c, bv); convert32<FP16>(ra, bv, c, rowbase, m, relu); }
               tmem_wait_ld();
               c += STEP;
               if (c >= N) break;
               if (c + STEP < N) tmem_ld32_nowait(lane_addr + ((uint32_t)(c + STEP) ^ side), ra);
-              convert32<FP16>(rb, bias, c, rowbase, m, relu);
+              { ulonglong2 bv[8]; load_bias32(bias, c, bv); convert32<FP16>(rb, bv, c, rowbase, m, relu); }
               tmem_wait_ld();
               c += STEP;
             }
