@@ -471,7 +471,8 @@ __device__ __forceinline__ void fold16_load(const float* __restrict__ bias, cons
     }
   }
 }
-__device__ __forceinline__ float fold16(const uint4 (&q)[4], const Fold16& f, bool relu, float acc) {
+template <bool RELU>
+__device__ __forceinline__ float fold16(const uint4 (&q)[4], const Fold16& f, float acc) {
   const uint32_t r[16] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
                           q[2].x, q[2].y, q[2].z, q[2].w, q[3].x, q[3].y, q[3].z, q[3].w};
   float h[16];
@@ -482,13 +483,8 @@ __device__ __forceinline__ float fold16(const uint4 (&q)[4], const Fold16& f, bo
     h[4 * i + 2] = __uint_as_float(r[4 * i + 2]) + f.b[i].z;
     h[4 * i + 3] = __uint_as_float(r[4 * i + 3]) + f.b[i].w;
   }
-  if (relu) {
 #pragma unroll
-    for (int i = 0; i < 16; i++) h[i] = h[i] < 0.0f ? 0.0f : h[i];
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; i++) h[i] = tanhf(h[i]);
-  }
+  for (int i = 0; i < 16; i++) h[i] = RELU ? (h[i] < 0.0f ? 0.0f : h[i]) : tanhf(h[i]);
 #pragma unroll
   for (int i = 0; i < 4; i++) {
     acc = fmaf(h[4 * i], f.w[i].x, acc); acc = fmaf(h[4 * i + 1], f.w[i].y, acc);
@@ -497,41 +493,66 @@ __device__ __forceinline__ float fold16(const uint4 (&q)[4], const Fold16& f, bo
   return acc;
 }
 
+// The folded head over this warp's chunks c0, c0 + step, ... below c_end, in 16-column steps.
+// The activation is a template parameter: a runtime select would issue the tanhf code for ReLU
+// networks as well.
+template <bool FP16, bool RELU>
+__device__ __forceinline__ float fold_chunks(uint32_t lane_addr, uint32_t side, const float* __restrict__ bias,
+                                             const NetParams& P, int c0, int c_end, int step, float part) {
+  for (int c = c0; c < c_end; c += step) {
+#pragma unroll
+    for (int k = 0; k < 32; k += 16) {
+      uint4 ra[4];
+      Fold16 f;
+      fold16_load<FP16>(bias, P, c + k, f);
+      tmem_ld16(lane_addr + ((uint32_t)(c + k) ^ side), ra);
+      part = fold16<RELU>(ra, f, part);
+    }
+  }
+  return part;
+}
+
 // Per-row outputs of one sampled channel: bins / int32 index / fp64 env command.
-__device__ __forceinline__ void emit_choice(const Launch& L, int act_dim, int64_t row, int g, int best) {
+// gv: the action grid's value at `best` (read only when env commands are written).
+__device__ __forceinline__ void emit_choice(const Launch& L, int act_dim, int64_t row, int g, int best, float gv) {
   if (L.bins) L.bins[row * L.bins_stride + L.bins_offset + g] = (uint8_t)best;
   if (L.act_idx) L.act_idx[row * act_dim + g] = best;
   if (L.cmd) {
     // action_to_env in fp32: grid value, throttle (channel 3) 0.5 * v + 0.5
-    const float gv = __ldg(L.grid + best);
     const float cv = g == 3 ? __fadd_rn(__fmul_rn(0.5f, gv), 0.5f) : gv;
     L.cmd[row * L.cmd_stride + L.cmd_offset + g] = (double)cv;
   }
+}
+__device__ __forceinline__ void emit_choice(const Launch& L, int act_dim, int64_t row, int g, int best) {
+  emit_choice(L, act_dim, row, g, best, L.cmd ? __ldg(L.grid + best) : 0.0f);
 }
 
 // Categorical head with compile-time shape (the reference's 4 channels x 21 bins), split over
 // the PARTS epilogue warps of a lane quarter: part H handles channels [H*A/PARTS, (H+1)*A/PARTS).
 // Logits stay in registers; per channel max, log-sum-exp, inverse-CDF sample (or argmax);
 // returns this part's share of the summed log-prob.
+// grid_lane: this lane's entry of the action grid (lane < NB), so the chosen bin's value comes
+// by one warp shuffle instead of a dependent load.
 template <int A, int NB, int H, int PARTS>
 __device__ __forceinline__ float cat_head(uint32_t lane_addr, const float* __restrict__ bias, const Launch& L,
-                                          int64_t row, bool valid) {
+                                          int64_t row, bool valid, float grid_lane) {
   static_assert(A % PARTS == 0, "channels split evenly over the parts");
   constexpr int GA = A / PARTS;                  // channels of this part
   constexpr int W = GA * NB;
   constexpr int C0 = H * W;                      // first logit column of this half
   constexpr int LB = C0 / 8 * 8;                 // first TMEM column loaded (8-column blocks)
   constexpr int NL = (C0 + W - 1) / 8 - C0 / 8 + 1;
+  // the row's sampling key and the biases before the TMEM loads
+  const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step + (L.step_dev ? *L.step_dev : 0ull), row);
   float lg[W];
 #pragma unroll
-  for (int i = 0; i < W; i++) lg[i] = __ldg(bias + C0 + i);     // issued before the TMEM loads
+  for (int i = 0; i < W; i++) lg[i] = __ldg(bias + C0 + i);
   uint32_t r[NL * 8];
 #pragma unroll
   for (int c = 0; c < NL; c++) tmem_ld8_nowait(lane_addr + (uint32_t)(LB + 8 * c), r + 8 * c);
   tmem_wait_ld();
 #pragma unroll
   for (int i = 0; i < W; i++) lg[i] += __uint_as_float(r[C0 - LB + i]);
-  const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step + (L.step_dev ? *L.step_dev : 0ull), row);
   float logp = 0.0f;
 #pragma unroll
   for (int gl = 0; gl < GA; gl++) {
@@ -571,7 +592,8 @@ __device__ __forceinline__ float cat_head(uint32_t lane_addr, const float* __res
 #pragma unroll
     for (int b = 1; b < NB; b++) chosen = (b == best) ? x[b] : chosen;
     logp += chosen - lse;
-    if (valid) emit_choice(L, A, row, g, best);
+    const float gv = __shfl_sync(0xffffffffu, grid_lane, best);
+    if (valid) emit_choice(L, A, row, g, best, gv);
   }
   if (valid && L.logits)
 #pragma unroll
@@ -819,6 +841,8 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
     const int h = (warp - 2) >> 2;
     const int m = q * 32 + lane;                  // tile row of this thread
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    // the action grid, one entry per lane, for the categorical head's env commands
+    const float grid_lane = (L.cmd && lane < 21) ? __ldg(L.grid + lane) : 0.0f;
     uint32_t accs = 0, heads = 0, h0s = 0;
     int64_t jn = 0;
     for (int64_t j = blockIdx.x; j < njobs; j += gridDim.x) {
@@ -846,34 +870,17 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           const int N = P.width_pad[l];
           const bool relu = P.act == 0;
           constexpr int STEP = 32 * EPI_PER_Q;
-          float part = 0.0f;
-          int c = 32 * h;
-          for (; c < (split ? NCHUNK : N); c += STEP) {
-            uint4 ra[4];
-            Fold16 f;
-            fold16_load<FP16>(bias, P, c, f);
-            tmem_ld16(lane_addr + ((uint32_t)c ^ side), ra);
-            part = fold16(ra, f, relu, part);
-            fold16_load<FP16>(bias, P, c + 16, f);
-            tmem_ld16(lane_addr + ((uint32_t)(c + 16) ^ side), ra);
-            part = fold16(ra, f, relu, part);
-          }
+          const int n_first = split ? NCHUNK : N;
+          float part = relu ? fold_chunks<FP16, true>(lane_addr, side, bias, P, 32 * h, n_first, STEP, 0.0f)
+                            : fold_chunks<FP16, false>(lane_addr, side, bias, P, 32 * h, n_first, STEP, 0.0f);
           if (split) {
             bool got2 = mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
             __syncwarp();
             if (!got2 || *abort_flag) { ok = false; break; }
             accs++;
             tc_fence_after();
-            for (; c < N; c += STEP) {
-              uint4 ra[4];
-              Fold16 f;
-              fold16_load<FP16>(bias, P, c, f);
-              tmem_ld16(lane_addr + ((uint32_t)c ^ side), ra);
-              part = fold16(ra, f, relu, part);
-              fold16_load<FP16>(bias, P, c + 16, f);
-              tmem_ld16(lane_addr + ((uint32_t)(c + 16) ^ side), ra);
-              part = fold16(ra, f, relu, part);
-            }
+            part = relu ? fold_chunks<FP16, true>(lane_addr, side, bias, P, 32 * h + NCHUNK, N, STEP, part)
+                        : fold_chunks<FP16, false>(lane_addr, side, bias, P, 32 * h + NCHUNK, N, STEP, part);
           }
           const int64_t row = J.row0 + m;
           if (h != 0) {
@@ -987,14 +994,14 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             // through shared memory
             if (h != 0) {
               float part;
-              if (EPI_PER_Q == 2) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr + side, bias, L, row, valid);
-              else if (h == 1) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr + side, bias, L, row, valid);
-              else if (h == 2) part = cat_head<4, 21, 2 % EPI_PER_Q, EPI_PER_Q>(lane_addr + side, bias, L, row, valid);
-              else part = cat_head<4, 21, 3 % EPI_PER_Q, EPI_PER_Q>(lane_addr + side, bias, L, row, valid);
+              if (EPI_PER_Q == 2) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
+              else if (h == 1) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
+              else if (h == 2) part = cat_head<4, 21, 2 % EPI_PER_Q, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
+              else part = cat_head<4, 21, 3 % EPI_PER_Q, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
               S->logp_part[h - 1][m] = part;
               mbar_arrive(smem_u32(&S->logp_bar));
             } else {
-              float part = cat_head<4, 21, 0, EPI_PER_Q>(lane_addr + side, bias, L, row, valid);
+              float part = cat_head<4, 21, 0, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
               if (!mbar_wait(smem_u32(&S->logp_bar), heads & 1, abort_flag)) {
                 ok = false;
               } else if (valid && L.logp) {
