@@ -52,6 +52,13 @@ constexpr double DT = 1.0 / 60.0;
 constexpr double ROT = F16C_ROTATION_RATE;
 
 // Reference table1d (fdm.cuh:50-60) with the span division replaced by the staged reciprocal.
+// Out-of-line calls of the library's fp64 exp and log: the frame body is instantiated twice
+// (with and without its outputs) and each inline expansion carries the whole function; one body
+// each shortens the code the warps fetch (-0.7% per step, same results bit for bit).  atan2 stays
+// inline: out of line it measured slower (+1.6%).
+static __device__ __noinline__ double exp_ool(double x) { return exp(x); }
+static __device__ __noinline__ double log_ool(double x) { return log(x); }
+
 __device__ __forceinline__ double lut1(const double* __restrict__ T, int xo, int yo, int n, double k) {
   const double* x = T + xo;
   const double* y = T + yo;
@@ -175,9 +182,9 @@ __device__ __forceinline__ void isa(const double* __restrict__ S, double h, Air&
   double P;
   if (L != 0.0) {
     // (Tb / (Tb + L dh))^e as exp(e (log Tb - log(Tb + L dh))), log Tb staged per layer
-    P = S[F16T_ATM_PBRK + b] * exp(S[ATM_EXPP + b] * (S[ATM_LTB + b] - log(Tb + L * dh)));
+    P = S[F16T_ATM_PBRK + b] * exp_ool(S[ATM_EXPP + b] * (S[ATM_LTB + b] - log_ool(Tb + L * dh)));
   } else {
-    P = S[F16T_ATM_PBRK + b] * exp(dh * S[ATM_KISO + b]);
+    P = S[F16T_ATM_PBRK + b] * exp_ool(dh * S[ATM_KISO + b]);
   }
   const double ia = rsqrt(F16C_SHRatio * F16C_Reng * T);
   double rho = P * (F16C_SHRatio * ia * ia);          // P / (R T), with 1 / (R T) = gamma ia^2
@@ -194,8 +201,8 @@ __device__ __forceinline__ void isa(const double* __restrict__ S, double h, Air&
   double Hb = AL[d], Ld = S[F16T_ATM_LAPSE + d];
   double da;
   double ratio = rho * S[ATM_RDB + d];
-  if (Ld != 0.0) da = Hb + S[ATM_TOL + d] * (exp(S[ATM_EXPD + d] * log(ratio)) - 1.0);
-  else da = Hb + S[ATM_KDISO + d] * log(ratio);
+  if (Ld != 0.0) da = Hb + S[ATM_TOL + d] * (exp_ool(S[ATM_EXPD + d] * log_ool(ratio)) - 1.0);
+  else da = Hb + S[ATM_KDISO + d] * log_ool(ratio);
   o.densalt = geomet(da);
 }
 
@@ -440,7 +447,7 @@ __device__ __forceinline__ double turbine(const double* __restrict__ S, double* 
 // ---------------- calibrated airspeed (fdm.cuh:457-470) ----------------
 __device__ __forceinline__ double mach_from_qc(double qc) {
   double A = qc * (1.0 / F16C_StdDaySLpressure) + 1.0;
-  double m = sqrt(5.0 * (exp(log(A) * (1.0 / 3.5)) - 1.0));
+  double m = sqrt(5.0 * (exp_ool(log_ool(A) * (1.0 / 3.5)) - 1.0));
   if (m > 1.0) {
     for (int i = 0; i < 10; i++) {
       double t = 1.0 - 1.0 / (7.0 * m * m);
