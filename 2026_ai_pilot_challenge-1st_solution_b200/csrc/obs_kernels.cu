@@ -262,6 +262,41 @@ __global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_obs_init_reward
   rc.prev_alt_log[pl.a] = alt_log(-L.own(F_S + 2));
 }
 
+// k_env_post's autoreset of one aircraft (both lanes of the environment run it): the pool row,
+// fresh reconstruction state, anchored reward trackers, restaged geometry.
+template <int LAYOUT>
+__device__ __forceinline__ void env_reset_row(const Lanes<PT>& L, const PairLane& pl, double* __restrict__ st,
+                                              int64_t ld, const double* __restrict__ pool, int64_t pool_size,
+                                              const int64_t* __restrict__ pick, const f16_recon& rc, const Origin& O,
+                                              Los& g) {
+  const int64_t a = pl.a, e = pl.e;
+  // autoreset: this aircraft's row from the pool, fresh reconstruction state, anchored trackers
+  int64_t row = pick[e];
+  row = row < 0 ? 0 : (row >= pool_size ? pool_size - 1 : row);
+  const double* src = pool + (row * 2 + pl.k) * F16_STATE_N;
+  for (int c = 0; c < F16_STATE_N; c++) {
+    const double v = src[c];
+    if (LAYOUT == F16_LAYOUT_SOA) st[(int64_t)c * ld + a] = v;
+    else st[a * F16_STATE_N + c] = v;
+  }
+  rc.hp[a] = 1.0; rc.fuel[a] = 1.0;
+  rc.prev_att[a * 3] = 0.0; rc.prev_att[a * 3 + 1] = 0.0; rc.prev_att[a * 3 + 2] = 0.0;
+  rc.prev_valid[a] = 0;
+  rc.pqr[a * 3] = 0.0; rc.pqr[a * 3 + 1] = 0.0; rc.pqr[a * 3 + 2] = 0.0;
+  rc.dmg_dealt[a] = 0.0; rc.dmg_taken[a] = 0.0; rc.hp_loss[a] = 0.0;
+  double2* h = reinterpret_cast<double2*>(rc.act_hist + a * 20);
+  for (int i = 0; i < 10; i++) h[i] = make_double2(0.0, 0.0);
+  if (pl.k == 0) rc.t_sec[e] = 0.0;
+  L.sync();                                     // the partner's rows are written: restage
+  g = stage_pair<LAYOUT>(L, st, ld, a, pl.k, O);
+  const double gx = geometry_advantage(L, pl.k, g, 0.0);
+  rc.prev_x[a] = gx;
+  rc.prev_x_valid[a] = 1;
+  rc.prev_alt_log[a] = alt_log(-L.own(F_S + 2));
+  stage_fresh(L);
+  L.sync();
+}
+
 // Everything GpuDogfightVecEnv.step does after the physics step (R/cuda_fdm/rl_env.py:514-551),
 // in one launch: advance, terminal observations, terminal HP / MSL altitude, and for finished
 // environments the autoreset from the IC pool (state rows, reconstruction reset, reward-tracker
@@ -304,37 +339,11 @@ __global__ void __launch_bounds__(PT, F16_OBS_PAIR_MIN_BLOCKS) k_env_post(double
   L.sync();
   double* ax = (aux && pl.k == 0) ? aux + e * 21 : nullptr;
   if (terminal_obs) obs_row(L, pl.k, g, A.t, HIST_DONE, nullptr, terminal_obs + a * 184, nullptr);
-  if (!fin) {
-    obs_row(L, pl.k, g, A.t, HIST_DONE, nullptr, obs + a * 184, ax);
-    return;
-  }
-  // autoreset: this aircraft's row from the pool, fresh reconstruction state, anchored trackers
-  int64_t row = pick[e];
-  row = row < 0 ? 0 : (row >= pool_size ? pool_size - 1 : row);
-  const double* src = pool + (row * 2 + pl.k) * F16_STATE_N;
-  for (int c = 0; c < F16_STATE_N; c++) {
-    const double v = src[c];
-    if (LAYOUT == F16_LAYOUT_SOA) st[(int64_t)c * ld + a] = v;
-    else st[a * F16_STATE_N + c] = v;
-  }
-  rc.hp[a] = 1.0; rc.fuel[a] = 1.0;
-  rc.prev_att[a * 3] = 0.0; rc.prev_att[a * 3 + 1] = 0.0; rc.prev_att[a * 3 + 2] = 0.0;
-  rc.prev_valid[a] = 0;
-  rc.pqr[a * 3] = 0.0; rc.pqr[a * 3 + 1] = 0.0; rc.pqr[a * 3 + 2] = 0.0;
-  rc.dmg_dealt[a] = 0.0; rc.dmg_taken[a] = 0.0; rc.hp_loss[a] = 0.0;
-  double2* h = reinterpret_cast<double2*>(rc.act_hist + a * 20);
-  for (int i = 0; i < 10; i++) h[i] = make_double2(0.0, 0.0);
-  if (pl.k == 0) rc.t_sec[e] = 0.0;
-  L.sync();                                     // the partner's rows are written: restage
-  g = stage_pair<LAYOUT>(L, st, ld, a, pl.k, O);
-  const double gx = geometry_advantage(L, pl.k, g, 0.0);
-  rc.prev_x[a] = gx;
-  rc.prev_x_valid[a] = 1;
-  rc.prev_alt_log[a] = alt_log(-L.own(F_S + 2));
-  stage_fresh(L);
-  L.sync();
-  obs_row(L, pl.k, g, 0.0, HIST_ZERO, nullptr, obs + a * 184, ax);
+  if (fin) env_reset_row<LAYOUT>(L, pl, st, ld, pool, pool_size, pick, rc, O, g);
+  // one row-builder call for both outcomes (a finished environment's row after its reset)
+  obs_row(L, pl.k, g, fin ? 0.0 : A.t, fin ? HIST_ZERO : HIST_DONE, nullptr, obs + a * 184, ax);
 }
+
 
 // 9-DoF export (R/cuda_fdm/rl_env.py:558-566 state9_flat): one thread per aircraft
 template <int LAYOUT>
