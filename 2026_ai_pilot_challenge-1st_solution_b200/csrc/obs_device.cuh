@@ -333,12 +333,11 @@ enum StageField : int {
   F_FL = 37,     // dir_frame(line of sight from this aircraft to the other)
   F_PROJ = 46,   // body-frame unit line of sight to the other aircraft
   F_ATA = 49,    // ATA at the other aircraft (deg)
-  F_HP = 50,     // reconstruction values of the row: HP, fuel, damage dealt / taken rates
+  F_HP = 50,     // reconstruction values of the row: HP, fuel (the damage rates, read by the
+                 // own lane only, are passed to obs_row as arguments)
   F_FUEL = 51,
-  F_DEALT = 52,
-  F_TAKEN = 53,
-  F_PQR = 54,    // body rates from the attitude change
-  NFIELD = 57
+  F_PQR = 52,    // body rates from the attitude change
+  NFIELD = 55
 };
 
 template <int T>
@@ -486,7 +485,8 @@ enum HistMode : int { HIST_READ = 0, HIST_ZERO = 1, HIST_DONE = 2 };
 // reconstruction fields are staged on both lanes; aux: the 21 future-position features or NULL.
 template <int T>
 __device__ __forceinline__ void obs_row(const Lanes<T>& L, int k, const Los& g, double t, int hist_mode,
-                                       const double* hist, float* __restrict__ out, double* __restrict__ aux) {
+                                       const double* hist, float* __restrict__ out, double* __restrict__ aux,
+                                       double dealt, double taken) {
   const int o = k, p = 1 - k;
   const M3 Ro = L.mat(F_R, o);
   const V3 ovn = L.vec(F_VN, o), tvn = L.vec(F_VN, p);
@@ -586,8 +586,8 @@ __device__ __forceinline__ void obs_row(const Lanes<T>& L, int k, const Los& g, 
   }
   wr.put(normz_k(L.col(F_FUEL, o), 0.0, 1.0));
   wr.put(normz_k(L.col(F_FUEL, p), 0.0, 1.0));
-  wr.put(clampd(2.0 * L.col(F_DEALT, o) - 1.0, -1.0, 1.0));
-  wr.put(clampd(2.0 * L.col(F_TAKEN, o) - 1.0, -1.0, 1.0));
+  wr.put(clampd(2.0 * dealt - 1.0, -1.0, 1.0));
+  wr.put(clampd(2.0 * taken - 1.0, -1.0, 1.0));
   wr.put(2.0 * (pa * pr) - 1.0);
   wr.put(normz_k(oalt, 0.0, MAX_ALT_M));
   wr.put(normz_k(talt, 0.0, MAX_ALT_M));
