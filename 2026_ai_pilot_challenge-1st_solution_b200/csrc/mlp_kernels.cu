@@ -601,6 +601,76 @@ __device__ __forceinline__ float cat_head(uint32_t lane_addr, const float* __res
   return logp;
 }
 
+// One channel of NB bins per part (the reference's 4 x 21 shape with four parts per quarter): the
+// same code for every part, the channel g a runtime value.  Each part's 21 logit columns start
+// at a column offset 21g whose position inside an 8-column block (21g mod 8: 0, 5, 2, 7) picks
+// one of four unrolled extractions; everything after them is a single instance.  (A separate
+// instance per part put four copies of the head on every scheduler's instruction stream.)
+template <int NB, int OFF>
+__device__ __forceinline__ void head_extract(const uint32_t (&r)[32], float (&lg)[NB]) {
+#pragma unroll
+  for (int i = 0; i < NB; i++) lg[i] += __uint_as_float(r[OFF + i]);
+}
+template <int A, int NB>
+__device__ __forceinline__ float cat_head1(uint32_t lane_addr, const float* __restrict__ bias, const Launch& L,
+                                           int64_t row, bool valid, float grid_lane, int g) {
+  static_assert(NB + 7 <= 32, "a channel's logits fit the four loaded 8-column blocks");
+  const int C0 = g * NB, LB = C0 & ~7, off = C0 - LB;
+  const uint64_t key = L.deterministic ? 0ull : row_key(L.seed, L.step + (L.step_dev ? *L.step_dev : 0ull), row);
+  float x[NB];
+#pragma unroll
+  for (int i = 0; i < NB; i++) x[i] = __ldg(bias + C0 + i);
+  uint32_t r[32];
+#pragma unroll
+  for (int c = 0; c < 4; c++) tmem_ld8_nowait(lane_addr + (uint32_t)(LB + 8 * c), r + 8 * c);
+  tmem_wait_ld();
+  switch (off) {
+    case 0: head_extract<NB, 0>(r, x); break;
+    case 2: head_extract<NB, 2>(r, x); break;
+    case 5: head_extract<NB, 5>(r, x); break;
+    default: head_extract<NB, 7>(r, x); break;
+  }
+  float mx = x[0];
+#pragma unroll
+  for (int b = 1; b < NB; b++) mx = fmaxf(mx, x[b]);
+  float ex[NB];
+  float se = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NB; b++) {
+    ex[b] = __expf(x[b] - mx);
+    se += ex[b];
+  }
+  const float lse = mx + logf(se);
+  int best = 0;
+  if (L.deterministic) {
+    float bestv = -INFINITY;
+#pragma unroll
+    for (int b = 0; b < NB; b++)
+      if (x[b] > bestv) { bestv = x[b]; best = b; }
+  } else {
+    // the first bin whose running weight exceeds u * total = the number of bins whose running
+    // weight does not (running sums never decrease); the last bin if rounding leaves none
+    const float target = uniform24(key, (uint32_t)(g * 64)) * se;
+    float cum = 0.0f;
+    int below = 0;
+#pragma unroll
+    for (int b = 0; b < NB; b++) {
+      cum += ex[b];
+      below += cum <= target ? 1 : 0;
+    }
+    best = below < NB - 1 ? below : NB - 1;
+  }
+  float chosen = x[0];
+#pragma unroll
+  for (int b = 1; b < NB; b++) chosen = (b == best) ? x[b] : chosen;
+  const float gv = __shfl_sync(0xffffffffu, grid_lane, best);
+  if (valid) emit_choice(L, A, row, g, best, gv);
+  if (valid && L.logits)
+#pragma unroll
+    for (int i = 0; i < NB; i++) L.logits[row * L.logits_ld + C0 + i] = x[i];
+  return chosen - lse;
+}
+
 // One fp32 column of this warp's 32 TMEM lanes.
 __device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
   uint32_t r;
@@ -994,14 +1064,13 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
             // through shared memory
             if (h != 0) {
               float part;
-              if (EPI_PER_Q == 2) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
-              else if (h == 1) part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
-              else if (h == 2) part = cat_head<4, 21, 2 % EPI_PER_Q, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
-              else part = cat_head<4, 21, 3 % EPI_PER_Q, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
+              if (EPI_PER_Q == 4) part = cat_head1<4, 21>(lane_addr + side, bias, L, row, valid, grid_lane, h);
+              else part = cat_head<4, 21, 1, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
               S->logp_part[h - 1][m] = part;
               mbar_arrive(smem_u32(&S->logp_bar));
             } else {
-              float part = cat_head<4, 21, 0, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
+              float part = EPI_PER_Q == 4 ? cat_head1<4, 21>(lane_addr + side, bias, L, row, valid, grid_lane, 0)
+                                          : cat_head<4, 21, 0, EPI_PER_Q>(lane_addr + side, bias, L, row, valid, grid_lane);
               if (!mbar_wait(smem_u32(&S->logp_bar), heads & 1, abort_flag)) {
                 ok = false;
               } else if (valid && L.logp) {
