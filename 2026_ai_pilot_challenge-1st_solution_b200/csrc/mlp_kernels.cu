@@ -940,18 +940,24 @@ k_policy(const __grid_constant__ CUtensorMap xmap, const NetDev* __restrict__ ne
           const int N = P.width_pad[l];
           const bool relu = P.act == 0;
           constexpr int STEP = 32 * EPI_PER_Q;
-          const int n_first = split ? NCHUNK : N;
-          float part = relu ? fold_chunks<FP16, true>(lane_addr, side, bias, P, 32 * h, n_first, STEP, 0.0f)
-                            : fold_chunks<FP16, false>(lane_addr, side, bias, P, 32 * h, n_first, STEP, 0.0f);
-          if (split) {
-            bool got2 = mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
-            __syncwarp();
-            if (!got2 || *abort_flag) { ok = false; break; }
-            accs++;
-            tc_fence_after();
-            part = relu ? fold_chunks<FP16, true>(lane_addr, side, bias, P, 32 * h + NCHUNK, N, STEP, part)
-                        : fold_chunks<FP16, false>(lane_addr, side, bias, P, 32 * h + NCHUNK, N, STEP, part);
+          // a split layer in two passes (the second after its last MMAs), one call site per
+          // activation either way (compact code)
+          float part = 0.0f;
+          const int passes = split ? 2 : 1;
+#pragma unroll 1
+          for (int pass = 0; pass < passes; pass++) {
+            if (pass == 1) {
+              bool got2 = mbar_wait(smem_u32(&S->acc_full), accs & 1, abort_flag);
+              __syncwarp();
+              if (!got2 || *abort_flag) { ok = false; break; }
+              accs++;
+              tc_fence_after();
+            }
+            const int c0 = 32 * h + pass * NCHUNK, c1 = split ? (pass + 1) * NCHUNK : N;
+            part = relu ? fold_chunks<FP16, true>(lane_addr, side, bias, P, c0, c1, STEP, part)
+                        : fold_chunks<FP16, false>(lane_addr, side, bias, P, c0, c1, STEP, part);
           }
+          if (!ok) break;
           const int64_t row = J.row0 + m;
           if (h != 0) {
             S->logp_part[h - 1][m] = part;
