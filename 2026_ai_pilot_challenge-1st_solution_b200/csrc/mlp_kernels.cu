@@ -51,7 +51,7 @@ constexpr int STAGE_BYTES = NCHUNK * 128;        // 32 KB
 #define F16_MLP_EPI_PER_QUARTER 4
 #endif
 constexpr int EPI_PER_Q = F16_MLP_EPI_PER_QUARTER;   // epilogue warps per TMEM lane quarter (2 or 4)
-constexpr int CTRL_BYTES = 2048;                 // barriers, TMEM base, head partial log-probs
+constexpr int CTRL_BYTES = 2048;                 // barriers, TMEM base, the heads' per-part partials
 constexpr int SMEM_BYTES = ACT_BYTES + STAGES * STAGE_BYTES + CTRL_BYTES + 1024;
 constexpr int EPI_WARPS = 4 * EPI_PER_Q;         // the warps of a quarter split the columns
 constexpr int THREADS = 64 + 32 * EPI_WARPS;     // warp 0 TMA, warp 1 MMA + TMEM, then the epilogue
@@ -330,7 +330,7 @@ struct Smem {
   uint64_t full[STAGES], empty[STAGES];
   uint32_t tmem_base;
   int abort_flag;
-  float logp_part[EPI_PER_Q - 1][TILE_M];        // the other parts' channel log-probs per tile row
+  float logp_part[EPI_PER_Q - 1][TILE_M];        // the other parts' log-probs (or value partial sums) per row
 };
 static_assert(sizeof(Smem) <= CTRL_BYTES, "control block");
 static_assert(sizeof(NetTable) + sizeof(Launch) + sizeof(CUtensorMap) + sizeof(void*) <= 4096, "kernel parameters");
