@@ -229,24 +229,27 @@ k_norm_apply(const float* __restrict__ x, int64_t B, int D, int64_t ldx, const f
 // the per-element arithmetic is k_norm_apply's, so the outputs are identical.  The fp32 rows are
 // stored with the evict-first hint: in a rollout they are the stored observations, read again only
 // by the update, while the 16-bit rows (the policy's next input) and the environment state that the
-// next step reads stay in L2 (-0.6% per rollout, the environment step -1.3%).
-constexpr int APPLY4_ROWS = 64;
+// next step reads stay in L2 (-0.6% per rollout, the environment step -1.3%).  Blocks take an
+// equal share of rows (rpb each, at least APPLY4_MIN_ROWS) so that the grid fills APPLY4_WAVES
+// waves of APPLY4_BLOCKS_PER_SM blocks per SM exactly: no partly filled last wave (-1.0% per
+// rollout against fixed 64-row blocks at five blocks per SM).
+constexpr int APPLY4_MIN_ROWS = 16, APPLY4_BLOCKS_PER_SM = 8, APPLY4_WAVES = 3;
 __device__ __forceinline__ float norm_elem(float v, float mu, float den, bool norm, float clip) {
   if (!norm) return v;
   float o = __fdiv_rn(__fsub_rn(v, mu), den);
   return o < -clip ? -clip : (o > clip ? clip : o);
 }
 template <bool FP16>
-__global__ void __launch_bounds__(NORM_THREADS)
+__global__ void __launch_bounds__(NORM_THREADS, APPLY4_BLOCKS_PER_SM)
 k_norm_apply4(const float4* __restrict__ x, int64_t B, int D, int64_t ldx4, const float* __restrict__ mean,
               const float* __restrict__ var, float eps, float clip, float4* __restrict__ y, int64_t ldy4,
-              uint2* __restrict__ yb, int64_t ldb4, unsigned* __restrict__ nonfinite) {
+              uint2* __restrict__ yb, int64_t ldb4, unsigned* __restrict__ nonfinite, int64_t rpb) {
   const int dg = D >> 2;
   const int G = yb ? (int)ldb4 : dg;
   const int S = NORM_THREADS / G;
   const int cg = threadIdx.x % G, st = threadIdx.x / G;
-  const int64_t r0 = (int64_t)blockIdx.x * APPLY4_ROWS;
-  const int64_t r1 = r0 + APPLY4_ROWS < B ? r0 + APPLY4_ROWS : B;
+  const int64_t r0 = (int64_t)blockIdx.x * rpb;
+  const int64_t r1 = r0 + rpb < B ? r0 + rpb : B;
   const bool norm = mean != nullptr;
   bool bad = false;
   if (st < S) {
@@ -298,15 +301,18 @@ inline void launch_apply(const float* x, int64_t B, int D, int64_t ldx, const fl
                                                            nonfinite);
     return;
   }
-  const unsigned grid = (unsigned)((B + APPLY4_ROWS - 1) / APPLY4_ROWS);
+  const int64_t slots = (int64_t)sm_count() * APPLY4_BLOCKS_PER_SM * APPLY4_WAVES;
+  int64_t rpb = (B + slots - 1) / slots;
+  if (rpb < APPLY4_MIN_ROWS) rpb = APPLY4_MIN_ROWS;
+  const unsigned grid = (unsigned)((B + rpb - 1) / rpb);
   if (fp16)
     k_norm_apply4<true><<<grid, NORM_THREADS, 0, s>>>(reinterpret_cast<const float4*>(x), B, D, ldx / 4, mean, var,
                                                       eps, clip, reinterpret_cast<float4*>(y), ldy / 4,
-                                                      reinterpret_cast<uint2*>(yb), ldb / 4, nonfinite);
+                                                      reinterpret_cast<uint2*>(yb), ldb / 4, nonfinite, rpb);
   else
     k_norm_apply4<false><<<grid, NORM_THREADS, 0, s>>>(reinterpret_cast<const float4*>(x), B, D, ldx / 4, mean, var,
                                                        eps, clip, reinterpret_cast<float4*>(y), ldy / 4,
-                                                       reinterpret_cast<uint2*>(yb), ldb / 4, nonfinite);
+                                                       reinterpret_cast<uint2*>(yb), ldb / 4, nonfinite, rpb);
 }
 
 // ---------------------------------------------------------------- rollout bookkeeping

@@ -98,6 +98,30 @@ def test_checked_normalise_cast_and_nonfinite_count(cuda):
     assert int(cnt) >= 1 and bool(torch.isnan(y2[17, 5]))
 
 
+@pytest.mark.parametrize("rows", [131_075, 70_001])
+def test_normalise_rollout_batch_bit_exact(cuda, rows):
+    """At rollout sizes (each block then takes more than the minimum row share, and the last block
+    a ragged remainder) the fp32 rows equal torch's (x - mean) / sqrt(var + eps) clamped, bit for
+    bit, and the 16-bit rows are those values rounded, with zero padding, for both operands."""
+    ro = pkg_module("rollout")
+    g = torch.Generator(device=cuda).manual_seed(rows)
+    src = torch.randn(rows, 368, device=cuda, generator=g) * 3.0 + 0.5
+    x = src[:, 184:]                                      # the opponent half of a (nenv, 2, 184) view
+    rn = ro.RunningNorm(184, cuda)
+    rn.update(x)
+    ref = ((x - rn.mean) / torch.sqrt(rn.var + rn.eps)).clamp(-rn.clip, rn.clip)
+    for dtype in (torch.float16, torch.bfloat16):
+        yf = torch.full((rows, 184), 3.0, device=cuda)
+        yh = rn.normalize_half(x, out_f32=yf, dtype=dtype)
+        torch.cuda.synchronize()
+        assert torch.equal(yf, ref)
+        assert torch.equal(yh[:, :184], ref.to(dtype)) and bool((yh[:, 184:] == 0).all())
+        c = torch.full((rows, 192), 5.0, device=cuda).to(dtype)        # the cast without a normaliser
+        ro.cast_half(x, c)
+        torch.cuda.synchronize()
+        assert torch.equal(c[:, :184], x.to(dtype)) and bool((c[:, 184:] == 0).all())
+
+
 def test_norm_apply_half_fp16(cuda):
     """f16_norm_apply_half with the fp16 operand: the fp16 rows are the fp32 rows rounded to
     nearest (zero padding beyond the features), values past fp16's range saturate at +-65504,
