@@ -166,3 +166,24 @@ def test_rollout_pool_assignment(cuda):
     # the assignment follows opp_weights (1 : 1.5 : 2 over three opponents, 512 envs resampled)
     freq = torch.bincount(t._sample_opp(200_000), minlength=3).float() / 200_000
     assert torch.allclose(freq.cpu(), torch.tensor([1.0, 1.5, 2.0]) / 4.5, atol=0.01)
+
+
+@pytest.mark.parametrize("opp_mode,n_opp", [("blocks", 2), ("pool", 3)])
+def test_side_stream_rollout_bit_identical(cuda, opp_mode, n_opp):
+    """The opponents' input prepared on a side stream gives the single-stream rollout's buffers,
+    advantages and commands bit for bit (two rollouts, so the second starts from the first's
+    end state; one opponent has its own normaliser)."""
+    out = []
+    for side in (False, True):
+        t, tr = make_trainer(cuda, 768, n_opp, opp_mode, 9)
+        t.side_stream_opponents = side
+        t.reset(stagger=False)
+        t.collect_rollout()
+        adv, ret, stats = t.collect_rollout()
+        torch.cuda.synchronize()
+        out.append([t.b_obs.clone(), t.b_act.clone(), t.b_logp.clone(), t.b_val.clone(), t.b_rew.clone(),
+                    t.b_done.clone(), adv, ret, t.env.action_buffer.clone(), t.x_opp.clone(), t.opp_assign.clone(),
+                    stats["ep_count"].clone()])
+        del t
+    for i, (a, b) in enumerate(zip(*out)):
+        assert torch.equal(a, b), f"buffer {i} differs between the side-stream and single-stream rollouts"
