@@ -65,11 +65,12 @@ k_norm_partial(const float* __restrict__ x, int64_t B, int D, int64_t ldx, doubl
 
 // The same partial sums with 16-byte loads, for D % 4 == 0 and a 16-byte aligned, 4-float
 // strided x: thread t sums columns 4c..4c+3 (c = t mod D/4) of the rows r0 + j, r0 + j + S, ...
-// (stripe j = t div D/4, S = PART4_THREADS div D/4 stripes), so two resident blocks per SM keep
-// ~64 KB of loads in flight instead of one 4-byte load per column; the stripes' fp64 sums meet
-// in shared memory and are added in stripe order (deterministic).
-constexpr int PART4_THREADS = 512;
-__global__ void __launch_bounds__(PART4_THREADS)
+// (stripe j = t div D/4, S = PART4_THREADS div D/4 stripes), so two resident blocks of 768
+// threads per SM keep ~94 KB of loads in flight instead of one 4-byte load per column (512-thread
+// blocks: the update 11% slower); the stripes' fp64 sums meet in shared memory (at most 48 KB per
+// block) and are added in stripe order (deterministic).
+constexpr int PART4_THREADS = 768;
+__global__ void __launch_bounds__(PART4_THREADS, 2)
 k_norm_partial4(const float4* __restrict__ x, int64_t B, int D, int64_t ldx4, double2* __restrict__ partial) {
   extern __shared__ double2 stripes[];              // [S][D]
   const int ncg = D >> 2;

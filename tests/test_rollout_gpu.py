@@ -98,6 +98,31 @@ def test_checked_normalise_cast_and_nonfinite_count(cuda):
     assert int(cnt) >= 1 and bool(torch.isnan(y2[17, 5]))
 
 
+@pytest.mark.parametrize("rows,dim", [(131_072, 184), (5_000, 184), (777, 12), (4_096, 1_024), (333, 7)])
+def test_sums_then_merge_equals_update(cuda, rows, dim):
+    """The data-parallel form of the norm update (per-feature fp64 sums, then a merge of the
+    summed pairs: f16_norm_sums + f16_norm_merge_sums, what each rank runs around its
+    all-reduce) gives f16_norm_update's mean, var and count bit for bit on one rank, over three
+    updates; the partial sums of both come from the same kernel in the same order."""
+    ro = pkg_module("rollout")
+    L = pkg_module("_lib")
+    lib = L.load()
+    g = torch.Generator(device=cuda).manual_seed(rows + dim)
+    a, b = ro.RunningNorm(dim, cuda), ro.RunningNorm(dim, cuda)
+    scratch = torch.empty(int(lib.f16_norm_scratch_doubles(rows, dim)), dtype=torch.float64, device=cuda)
+    sums = torch.empty(2 * dim, dtype=torch.float64, device=cuda)
+    for i in range(3):
+        x = torch.randn(rows, dim, device=cuda, generator=g) * (1.0 + i) + 0.25 * i
+        a.update(x)
+        s = L.stream_of(x)
+        L.check(lib.f16_norm_sums(L.ptr(x), rows, dim, x.stride(0), L.ptr(sums), L.ptr(scratch), scratch.numel(), s),
+                "sums")
+        L.check(lib.f16_norm_merge_sums(L.ptr(sums), rows, dim, L.ptr(b.mean), L.ptr(b.var), L.ptr(b.count), s),
+                "merge_sums")
+        torch.cuda.synchronize()
+        assert torch.equal(a.mean, b.mean) and torch.equal(a.var, b.var) and torch.equal(a.count, b.count)
+
+
 @pytest.mark.parametrize("rows", [131_075, 70_001])
 def test_normalise_rollout_batch_bit_exact(cuda, rows):
     """At rollout sizes (each block then takes more than the minimum row share, and the last block
