@@ -62,12 +62,13 @@ def parse():
     p.add_argument("--breakdown", action="store_true", help="ppo workload: print the per-kernel device time of "
                                                               "one extra, untimed iteration to stderr")
     p.add_argument("--workload", default="fdm",
-                   choices=["fdm", "obs", "rollout", "ppo", "mlp", "seed", "external", "warmup", "payoff"],
+                   choices=["fdm", "obs", "rollout", "ppo", "mlp", "norm", "seed", "external", "warmup", "payoff"],
                    help="fdm = configs[1] headline (default); obs = configs[2] fused obs/reward kernel; "
                         "rollout = configs[3] full 64-step rollout (env + obs/reward + actor/critic/opponents + GAE); "
                         "ppo = configs[4] PPO league iteration (rollout + 4x16 minibatch update, NCCL gradient "
                         "allreduce across ranks); mlp = the rollout's actor+critic launch alone (k_policy, "
-                        "131,072 rows); seed / external / warmup / payoff = the next rows: GPU IC "
+                        "131,072 rows); norm = one decision's RunningNorm work (update, normalise, the "
+                        "opponents' cast) on 131,072 envs; seed / external / warmup / payoff = the next rows: GPU IC "
                         "seeder, 214-D external observation, device-side staggered warm-up, batched payoff "
                         "evaluation")
     return p.parse_args()
@@ -836,6 +837,83 @@ def run_aux(args, dev, world, rank):
     return 0
 
 
+# Algorithmic bytes per environment of one decision's RunningNorm work on the rollout's rows:
+# the update reads the learner's 184 fp32 features (736 B); the normalise reads them again and
+# writes the fp32 rollout row (736 B) and the 16-bit policy row padded to 192 (384 B); the
+# opponents' cast reads their 736 B and writes 384 B.
+NORM_BYTES_PER_ENV = 736 + (736 + 736 + 384) + (736 + 384)
+
+
+def run_norm(args, dev, world, rank):
+    """The rollout's RunningNorm launches alone (rollout.RunningNorm / cast_half, as
+    PPOTrainer.collect_rollout issues them each decision) on configs[3]'s 131,072 envs: update
+    (partial sums, merge, count), normalise into the fp32 rollout row and the fp16 policy input,
+    and the fp16 cast of the opponents' rows.  Each call timed with CUDA events on the launching
+    stream, the 256 MB L2 flush before every call outside the events; one step = the three."""
+    import torch
+    rollout = importlib.import_module(PKG + ".rollout")
+    K, W = max(1, args.steps), max(3, args.warmup)
+    stream = torch.cuda.current_stream(dev)
+    n = ROLL_NENV
+    g = torch.Generator(device=dev).manual_seed(20260106 + rank)
+    obs = torch.randn(n, 2, 184, device=dev, generator=g) * 3.0 + 0.5      # the env's (nenv, 2, 184) rows
+    x, xo = obs[:, 0, :], obs[:, 1, :]
+    rn = rollout.RunningNorm(184, dev)
+    rn.update(x)
+    yf = torch.empty(n, 184, device=dev)
+    yh = torch.empty(n, 192, dtype=torch.float16, device=dev)
+    yo = torch.empty(n, 192, dtype=torch.float16, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    calls = {"update": lambda: rn.update(x),
+             "normalise": lambda: rn.normalize_half(x, out_f32=yf, out_half=yh),
+             "cast": lambda: rollout.cast_half(xo, yo)}
+    for _ in range(W):
+        for fn in calls.values():
+            fn()
+    ev = {k: [] for k in calls}
+    torch.cuda.synchronize(dev)
+    with ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0")))) as clk:
+        for _ in range(K):
+            for k, fn in calls.items():
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                fn()
+                b.record(stream)
+                ev[k].append((a, b))
+        torch.cuda.synchronize(dev)
+    per = {k: float(np.mean([a.elapsed_time(b) for a, b in v])) for k, v in ev.items()}
+    t = torch.tensor([sum(per.values())], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    peak, peak_src = peak_of("hbm_gbs")
+    bytes_per_call = {"update": 736 * n, "normalise": (736 + 736 + 384) * n, "cast": (736 + 384) * n}
+    gbs = {k: bytes_per_call[k] / (per[k] * 1e-3) / 1e9 for k in per}
+    if rank == 0:
+        achieved = NORM_BYTES_PER_ENV * n / (ms * 1e-3) / 1e9
+        line = {"metric": "RunningNorm decision rows/s (update + normalise + opponents' cast)",
+                "value": world * n / (ms * 1e-3), "unit": "envs/s", "n_gpus": world, "steps": K, "warmup": W,
+                "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 (fp64 sums)", "data": "synthetic",
+                "config": {"workload": "configs[3] RunningNorm launches of one decision, 131,072 envs x 184 features",
+                           "l2": "flushed before every call (256 MB write, outside the events)",
+                           "per_call_ms": per, "per_call_gbs": gbs},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak if peak else None, "traffic": None,
+                             "kernel": "k_norm_partial4 / k_norm_merge / k_norm_count / k_norm_apply4 x 2",
+                             "bytes_per_unit": NORM_BYTES_PER_ENV, "unit_basis": "environment",
+                             "per_call_frac": {k: gbs[k] / peak for k in gbs} if peak else None,
+                             "peak_source": peak_src},
+                "gpu_launches": 5 * K, "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
 def run_mlp(args, dev, world, rank):
     """The rollout's main policy launch alone: actor 184-512-512-84 ReLU with Gumbel-max sampling,
     log-prob and env commands, and critic 184-512-512-1, on 131,072 16-bit rows (k_policy, one
@@ -949,6 +1027,8 @@ def main():
         return run_ppo(args, dev, world, rank)
     if args.workload == "mlp":
         return run_mlp(args, dev, world, rank)
+    if args.workload == "norm":
+        return run_norm(args, dev, world, rank)
     if args.workload in ("seed", "external", "warmup", "payoff"):
         return run_aux(args, dev, world, rank)
 
