@@ -38,6 +38,17 @@ def test_profile_traffic_refuses_a_stale_summary(tmp_path, monkeypatch):
     assert v is None and "predates" in why
 
 
+def test_reference_arm_sampler_steps_the_reference():
+    """The --impl reference arm's sampler: the reference's fdm.cuh compiled here (or, where
+    that build is absent, the C restatement on one core) steps a bounded sample and reports a
+    rate; with the reference present every host core of the affinity set is used."""
+    b = _bench()
+    run, threads, n, kind = b.cpu_reference_sampler(nsample_per_thread=8)
+    rate, reps = run(0.2)
+    assert rate > 0 and reps >= 1 and n >= 64
+    assert (kind, threads) == ("port", 1) or (kind == "reference" and threads == b.host_cores())
+
+
 @pytest.mark.gpu
 def test_driver_command_line_prints_the_contract_line(cuda):
     r = subprocess.run([sys.executable, "bench.py", "--gpus", "1", "--steps", "20", "--warmup", "5"],
